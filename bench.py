@@ -1,0 +1,403 @@
+"""Benchmark of the routed-MoE hot path on B200 (one JSON line on rank 0).
+
+Headline workload: a Qwen3.8-Max-shaped MoE layer decoding one token per
+GPU -- hidden 8192, 512 MXFP4 experts (SwiGLU 8192->2048->8192), softmax top-10, gated shared
+expert, all experts resident in HBM. Metric: microseconds per token for the whole layer (lower
+is better). Each timed step is one full layer forward (router, top-k, dispatch, expert GEMVs,
+combine) on a fresh token already resident in HBM; L2 is flushed between steps.
+
+Also reported on the same line: prefill tokens/s (config 2, 2048 tokens), the dominant kernel's
+roofline (algorithmic bytes / CUDA-event duration vs the measured HBM copy peak), the end-to-end
+number through the host-buffer C entry point (rmoe_moe_forward_host, copies included), and the
+reference path restated in C (AVX-512 tier, oracle/) timed on this host's cores.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rmoe|reference]
+
+With N > 1 (torchrun, one process per GPU) every rank runs its own replica of the layer on its
+own tokens (weak scaling; the expert-parallel path is separate): value = max-over-ranks time /
+all tokens processed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from rabbit_b200 import synth  # noqa: E402
+
+DECODE_CFG = "c1_qwen_decode"
+PREFILL_CFG = "c2_qwen_prefill"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = f"/tmp/rmoe_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ CPU path
+def cpu_decode_setup(cfg, n_tokens=4, seed=0):
+    """Tokens + the experts they route to, on the host, for the C restatement."""
+    from oracle import oracle as orc
+
+    x = synth.activations(cfg, tokens=n_tokens, token_offset=10_000)
+    router = synth.router_weights(cfg, seed)
+    logits = orc.matmul(x, router, n_tokens, cfg.hidden, cfg.n_experts)
+    logits = (logits + synth.logit_bias(cfg, seed)[None, :]).astype(np.float32)
+    need = set()
+    for t in range(n_tokens):
+        need.update(i for i, _ in orc.qwen_route(logits[t], cfg.topk))
+    experts = {e: synth.expert(cfg, e, seed) for e in sorted(need)}
+    shared = synth.expert(cfg, cfg.n_experts, seed)
+    return x, router, experts, shared
+
+
+def cpu_decode_time(cfg, budget_s=12.0, min_tokens=3, threads=None, setup=None):
+    """Seconds per token of the reference path restated in C (AVX-512 tier, all row-parallel
+    threads), decoding the setup's tokens round-robin until the time budget is spent."""
+    from oracle import oracle as orc
+
+    if threads:
+        orc.set_threads(threads)
+    x, router, experts, shared = setup or cpu_decode_setup(cfg)
+    sg, lb = synth.shared_gate(cfg), synth.logit_bias(cfg)
+    # warm once (page faults, thread pool)
+    orc.moe_forward_qwen(x[:1], router, experts, cfg.n_experts, cfg.topk, cfg.inter, shared=shared,
+                         shared_gate=sg, logit_bias=lb, shared_inter=cfg.shared_inter, tier="avx512")
+    n, t0 = 0, time.perf_counter()
+    while True:
+        t = n % x.shape[0]
+        orc.moe_forward_qwen(x[t:t + 1], router, experts, cfg.n_experts, cfg.topk, cfg.inter,
+                             shared=shared, shared_gate=sg, logit_bias=lb,
+                             shared_inter=cfg.shared_inter, tier="avx512")
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= min_tokens and el >= budget_s:
+            break
+    return el / n, n, orc.get_threads()
+
+
+def physical_cores():
+    try:
+        import psutil
+
+        return psutil.cpu_count(logical=False) or os.cpu_count()
+    except ImportError:
+        return os.cpu_count()
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    cfg = synth.CONFIGS[DECODE_CFG]
+    threads = physical_cores()
+    from oracle import oracle as orc
+
+    orc.build()
+    orc.set_threads(threads)
+    setup = cpu_decode_setup(cfg)
+    # warmup steps, then K timed steps; each step is one token through the whole layer
+    sec, n, used = cpu_decode_time(cfg, budget_s=0.0, min_tokens=max(1, args.warmup), setup=setup)
+    sec, n, used = cpu_decode_time(cfg, budget_s=0.0, min_tokens=max(1, args.steps), setup=setup)
+    us = sec * 1e6
+    line = {
+        "impl": "reference", "metric": "moe_layer_decode_us_per_token", "value": us,
+        "unit": "us/token", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": DECODE_CFG, "tokens_per_step": 1, "hidden": cfg.hidden,
+                   "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+                   "weights": "mxfp4", "cpu": cpu_model()},
+        "cpu_baseline": {"value": us, "unit": "us/token", "cores": used, "kind": "port",
+                         "sample": f"{n} decode tokens round-robin over 4 seeded tokens; C "
+                                   "restatement of rabbit's AVX-512 MXFP4 tier + f32 router, "
+                                   "OpenMP over output rows"},
+        "e2e": {"value": us, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------ GPU path
+def expert_touch_bytes(cfg, ids_np, with_shared=True):
+    """Algorithmic bytes of one forward: distinct touched experts (+ shared) + router + x + out."""
+    distinct = len(np.unique(ids_np[ids_np >= 0]))
+    eb = cfg.expert_bytes()
+    T = ids_np.shape[0]
+    total = (distinct + (1 if with_shared else 0)) * eb
+    total += cfg.n_experts * cfg.hidden * 2 + T * cfg.hidden * 2 + T * cfg.hidden * 4
+    gu = (distinct + (1 if with_shared else 0)) * (2 * cfg.inter * (cfg.hidden // 2 + cfg.hidden // 32))
+    return total, gu, distinct
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    import rabbit_b200 as rb
+
+    from rabbit_b200.synth import build_layer, x_device
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = rb.Context(local)
+    cfg = synth.CONFIGS[PREFILL_CFG]  # same weights as config 1; sized for the prefill run
+    dcfg = synth.CONFIGS[DECODE_CFG]
+    layer = build_layer(ctx, cfg, max_tokens=cfg.tokens)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    n_steps = args.warmup + args.steps
+    xs = synth.activations(dcfg, tokens=n_steps, token_offset=rank * n_steps)
+    xd = x_device(dcfg, xs)
+    out = torch.empty((1, cfg.hidden), dtype=torch.float32, device=dev)
+    ids_all = torch.empty((n_steps, cfg.topk), dtype=torch.int32, device=dev)
+    w_all = torch.empty((n_steps, cfg.topk), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        layer.moe_forward(xd[i:i + 1], out=out)
+
+    for i in range(args.warmup):
+        flush.zero_()
+        step(i)
+    torch.cuda.synchronize()
+    layer.set_profiling(True)
+    layer.profile()
+    launches0 = layer.stats()["kernel_launches"]
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for j in range(args.steps):
+        flush.zero_()
+        ev[j][0].record(stream)
+        step(args.warmup + j)
+        ev[j][1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+    prof = layer.profile()
+    layer.set_profiling(False)
+    launches = (layer.stats()["kernel_launches"] - launches0) // args.steps
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    us_per_token = total_ms * 1e3 / (args.steps * world)
+
+    # routing of the timed tokens -> algorithmic bytes (every step touches k distinct + shared)
+    layer.route(xd[args.warmup:])  # warm path check; ids below from one extra forward each
+    ids_np = layer.route(xd[args.warmup:])[0].cpu().numpy()
+    per_step = [expert_touch_bytes(dcfg, ids_np[j:j + 1]) for j in range(args.steps)]
+    layer_bytes = float(np.mean([p[0] for p in per_step]))
+    gu_bytes = float(np.mean([p[1] for p in per_step]))
+    hbm_peak, _, peak_kind = peaks()
+    gu_ms = prof["gate_up"] / max(1, prof["calls"])
+    dn_ms = prof["down"] / max(1, prof["calls"])
+    stages_us = {k: prof[k] * 1e3 / max(1, prof["calls"]) for k in prof if k != "calls"}
+
+    # end to end through the host-buffer entry point (pinned host in/out, copies inside)
+    x_host = torch.from_numpy(synth.f32_to_bf16_bits(xs).view(np.int16)).pin_memory().view(torch.bfloat16)
+    out_host = torch.empty((1, cfg.hidden), dtype=torch.float32).pin_memory()
+    for i in range(min(3, n_steps)):
+        layer.moe_forward_host(x_host[i:i + 1], out=out_host)
+    e2e = []
+    for j in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        layer.moe_forward_host(x_host[args.warmup + j:args.warmup + j + 1], out=out_host)
+        e2e.append(time.perf_counter() - t0)
+    e2e_t = torch.tensor([sum(e2e)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_us = float(e2e_t.item()) * 1e6 / (args.steps * world)
+
+    # prefill (config 2): 2048 tokens per step
+    pre = None
+    if not args.no_prefill:
+        xp = x_device(cfg, synth.activations(cfg, tokens=cfg.tokens, token_offset=100_000 + rank * cfg.tokens))
+        outp = torch.empty((cfg.tokens, cfg.hidden), dtype=torch.float32, device=dev)
+        for _ in range(2):
+            flush.zero_()
+            layer.moe_forward(xp, out=outp)
+        torch.cuda.synchronize()
+        layer.set_profiling(True)
+        layer.profile()
+        pev = []
+        for _ in range(args.prefill_steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            layer.moe_forward(xp, out=outp)
+            b.record(stream)
+            pev.append((a, b))
+        torch.cuda.synchronize()
+        pprof = layer.profile()
+        layer.set_profiling(False)
+        pms = sum(a.elapsed_time(b) for a, b in pev) / args.prefill_steps
+        pt = torch.tensor([pms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        pms = float(pt.item())
+        pids = layer.route(xp)[0].cpu().numpy()
+        pbytes, pgu, pdistinct = expert_touch_bytes(cfg, pids)
+        flops = 2.0 * (cfg.tokens * cfg.topk + cfg.tokens) * 3 * cfg.hidden * cfg.inter + \
+            2.0 * cfg.tokens * cfg.n_experts * cfg.hidden
+        pre = {"metric": "moe_layer_prefill_tokens_per_s",
+               "value": cfg.tokens * world / (pms / 1e3), "unit": "tokens/s",
+               "ms_per_step": pms, "tokens_per_step_per_gpu": cfg.tokens,
+               "distinct_experts": pdistinct, "algorithmic_bytes": pbytes,
+               "achieved_gbs": pbytes / (pms / 1e3) / 1e9, "hbm_frac": pbytes / (pms / 1e3) / 1e9 / hbm_peak,
+               "tflops": flops / (pms / 1e3) / 1e12,
+               "stages_ms": {k: pprof[k] / max(1, pprof["calls"]) for k in pprof if k != "calls"}}
+
+    line = {
+        "metric": "moe_layer_decode_us_per_token", "value": us_per_token, "unit": "us/token",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 weights x f16 activations, f32 accumulate", "data": "synthetic",
+        "config": {"workload": DECODE_CFG, "tokens_per_step_per_gpu": 1, "hidden": cfg.hidden,
+                   "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+                   "shared_inter": cfg.shared_inter, "weights": "mxfp4 (E2M1 + E8M0/32)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
+                   "l2": "flushed (256 MiB write) between timed steps",
+                   "layer_algorithmic_bytes": layer_bytes},
+        "roofline": {"bound": "hbm", "kernel": "gemv_gate_up (fused gate/up + SwiGLU)",
+                     "achieved": gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None,
+                     "peak": hbm_peak, "unit": "GB/s", "peak_kind": peak_kind,
+                     "frac": (gu_bytes / (gu_ms / 1e3) / 1e9 / hbm_peak) if gu_ms > 0 else None,
+                     "traffic": None, "kernel_us": gu_ms * 1e3, "kernel_bytes": gu_bytes,
+                     "layer_achieved_gbs": layer_bytes / (ms_per_step / 1e3) / 1e9,
+                     "layer_frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / hbm_peak,
+                     "down_us": dn_ms * 1e3},
+        "stages_us": stages_us,
+        "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": cfg.hidden * 2,
+                "d2h_bytes_per_step": cfg.hidden * 4,
+                "api": "rmoe_moe_forward_host (pinned host x/out, copies + sync inside)"},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "prefill": pre,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, n, used = cpu_decode_time(dcfg, budget_s=args.cpu_budget, threads=physical_cores())
+        line["cpu_baseline"] = {
+            "value": sec * 1e6, "unit": "us/token", "cores": used, "kind": "port",
+            "cpu": cpu_model(),
+            "sample": f"{n} decode tokens round-robin over 4 seeded tokens (~{args.cpu_budget:.0f} s); "
+                      "C restatement of rabbit's AVX-512 MXFP4 tier + f32 router, OpenMP over rows"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    layer.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="rmoe", choices=["rmoe", "reference"])
+    ap.add_argument("--prefill-steps", type=int, default=3)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,218 @@
+/*
+ * rmoe.h -- C ABI of the B200-native routed-MoE layer (the drop-in boundary).
+ *
+ * Plain pointers and sizes only; no CUDA or torch types. `stream` arguments are a
+ * cudaStream_t passed as void* (NULL = the legacy default stream). Device-pointer entry points
+ * are asynchronous and stream-ordered; the *_host entry points synchronize before returning.
+ * Every function returns rmoe_status; on failure rmoe_last_error() (thread-local) says why.
+ * Nothing aborts or throws across this boundary.
+ *
+ * Each entry point names the reference interface it replaces (ferrumox/rabbit v0.29.1, paths
+ * relative to that crate).
+ */
+#ifndef RMOE_H
+#define RMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define RMOE_API __attribute__((visibility("default")))
+#else
+#define RMOE_API
+#endif
+
+#define RMOE_ABI_VERSION 1
+#define RMOE_MAX_TOPK 32
+
+typedef enum rmoe_status {
+  RMOE_OK = 0,
+  RMOE_INVALID_ARG = 1,     /* null pointer, out-of-range id, bad enum */
+  RMOE_SHAPE_MISMATCH = 2,  /* byte counts that do not match the declared shape */
+  RMOE_CUDA_ERROR = 3,
+  RMOE_NCCL_ERROR = 4,
+  RMOE_TIMEOUT = 5,         /* a bounded device-side wait gave up */
+  RMOE_NOT_SUPPORTED = 6,   /* a shape the kernels do not handle (see rmoe_layer_create) */
+  RMOE_OUT_OF_MEMORY = 7
+} rmoe_status;
+
+typedef enum rmoe_router_kind {
+  /* qwen38::moe::route: top-k of the logits, softmax over the k winners (weights sum to 1) */
+  RMOE_ROUTER_SOFTMAX_TOPK = 0,
+  /* glm52::moe::route: sigmoid scores + correction bias, grouped top-k, norm_topk, scale */
+  RMOE_ROUTER_SIGMOID_GROUPED = 1
+} rmoe_router_kind;
+
+typedef enum rmoe_weight_format {
+  RMOE_FMT_MXFP4 = 0,      /* QTKind::MxFp4: E2M1 nibbles low-first + E8M0 byte per 32 */
+  RMOE_FMT_I4_GROUPED = 1  /* QTKind::I4Grouped: offset-binary nibbles + scale per group */
+} rmoe_weight_format;
+
+typedef enum rmoe_dtype { RMOE_F32 = 0, RMOE_BF16 = 1 } rmoe_dtype;
+
+typedef struct rmoe_ctx rmoe_ctx;
+typedef struct rmoe_layer rmoe_layer;
+
+/* Mirrors the routing/expert fields of qwen38::config::Cfg (src/qwen38/config.rs:71-102) and
+ * glm52::config::Cfg (src/glm52/config.rs:26-46). */
+typedef struct rmoe_layer_desc {
+  int32_t hidden;         /* H: cfg.hidden (multiple of 32) */
+  int32_t moe_inter;      /* I: cfg.moe_inter (multiple of 32) */
+  int32_t shared_inter;   /* shared expert width (Qwen shared_inter, GLM moe_inter*n_shared); 0 = none */
+  int32_t n_experts;      /* E: routed experts in the whole model (all EP ranks) */
+  int32_t topk;           /* k: cfg.topk (<= RMOE_MAX_TOPK, <= n_experts) */
+  int32_t router_kind;    /* rmoe_router_kind */
+  int32_t n_group;        /* GLM n_group (<= 1 = ungrouped); must divide n_experts */
+  int32_t topk_group;     /* GLM topk_group */
+  int32_t norm_topk;      /* GLM norm_topk_prob (Qwen always renormalizes) */
+  float routed_scale;     /* GLM routed_scaling_factor (Qwen: 1) */
+  int32_t weight_format;  /* rmoe_weight_format, for routed and shared experts alike */
+  int32_t group_size;     /* I4_GROUPED: elements per scale (multiple of 32); MXFP4: 32 */
+  int32_t scale_dtype;    /* I4_GROUPED scale storage: RMOE_F32 (reference .qs) or RMOE_BF16 */
+  int32_t shared_gated;   /* Qwen: shared expert scaled by sigmoid(x . shared_gate) */
+  int32_t max_tokens;     /* largest T any call will pass (sizes the workspace) */
+  int32_t ep_rank;        /* expert parallel rank (0 when unsharded) */
+  int32_t ep_size;        /* expert parallel world size (1 when unsharded) */
+} rmoe_layer_desc;
+
+typedef struct rmoe_layer_stats {
+  uint64_t forward_calls;
+  uint64_t tokens_routed;
+  uint64_t kernel_launches;      /* this library's kernels launched by forward calls */
+  uint64_t device_bytes;         /* resident expert + router bytes */
+  int32_t local_expert_begin;    /* experts [begin, end) are resident on this device */
+  int32_t local_expert_end;
+} rmoe_layer_stats;
+
+/* Stages of one forward call, in launch order (rmoe_layer_get_profile). */
+typedef enum rmoe_stage {
+  RMOE_STAGE_ROUTER_LOGITS = 0,
+  RMOE_STAGE_TOPK = 1,
+  RMOE_STAGE_PREP = 2,
+  RMOE_STAGE_DISPATCH = 3,
+  RMOE_STAGE_GATE_UP = 4,
+  RMOE_STAGE_QUANT_H = 5,
+  RMOE_STAGE_DOWN = 6,
+  RMOE_STAGE_COMBINE = 7,
+  RMOE_NUM_STAGES = 8
+} rmoe_stage;
+
+typedef struct rmoe_profile {
+  uint64_t calls;                       /* forward calls profiled since the last read */
+  double stage_ms[RMOE_NUM_STAGES];     /* summed device time per stage (CUDA events) */
+} rmoe_profile;
+
+RMOE_API const char* rmoe_last_error(void);
+RMOE_API const char* rmoe_status_string(rmoe_status s);
+RMOE_API int rmoe_abi_version(void);
+
+/* ---- context / layer lifetime (replaces ExpertCache construction, src/expert_cache.rs:698-760:
+ *      all experts become HBM-resident instead of an LRU of streamed ones) ---- */
+RMOE_API rmoe_status rmoe_init(int device, rmoe_ctx** out);
+RMOE_API rmoe_status rmoe_shutdown(rmoe_ctx* ctx);
+RMOE_API rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* desc, rmoe_layer** out);
+RMOE_API rmoe_status rmoe_layer_destroy(rmoe_layer* layer);
+RMOE_API rmoe_status rmoe_layer_get_stats(const rmoe_layer* layer, rmoe_layer_stats* out);
+/* Per-stage CUDA-event timing of forward calls (no counterpart in the reference, whose
+ * Phases/StepProfile timers in src/generate.rs:192-203 play this role on the CPU). While on,
+ * every forward records one event per stage boundary on its stream. get_profile waits for
+ * those events, returns the sums since the last read and resets them. */
+RMOE_API rmoe_status rmoe_layer_set_profiling(rmoe_layer* layer, int on);
+RMOE_API rmoe_status rmoe_layer_get_profile(rmoe_layer* layer, rmoe_profile* out);
+
+/* ---- weights, taken in the reference's byte layout verbatim. Pointers may be host or device
+ *      memory (unified addressing). Byte counts are checked like mxfp4_from_raw
+ *      (src/expert_cache.rs:1245-1256): MXFP4 data = rows*ceil(cols/2), scales =
+ *      rows*ceil(cols/32); I4_GROUPED scales = rows*ceil(cols/gs)*sizeof(scale). ---- */
+
+/* MoeWeights::router (src/qwen38/model.rs:89-92, src/glm52/model.rs:50): [E, H] row-major. */
+RMOE_API rmoe_status rmoe_upload_router(rmoe_layer* layer, const void* w, int32_t dtype, size_t bytes);
+/* SIGMOID_GROUPED: MoeWeights::router_bias [E] (selection-only correction bias).
+ * SOFTMAX_TOPK: optional f32 bias added to every logit before selection and softmax (the
+ * Qwen router itself has none; this carries a harness popularity skew). */
+RMOE_API rmoe_status rmoe_upload_router_bias(rmoe_layer* layer, const float* bias, size_t n);
+/* ExpertSlot{gate_up: GateUp::Separate{gate, up}, down} (src/expert_cache.rs:640-650).
+ * gate/up are [I, H], down is [H, I]. eid is global; only this rank's experts are accepted. */
+RMOE_API rmoe_status rmoe_upload_expert(rmoe_layer* layer, int32_t eid,
+                               const void* gate, size_t gate_bytes,
+                               const void* gate_scale, size_t gate_scale_bytes,
+                               const void* up, size_t up_bytes,
+                               const void* up_scale, size_t up_scale_bytes,
+                               const void* down, size_t down_bytes,
+                               const void* down_scale, size_t down_scale_bytes);
+/* GateUp::Fused{gate_up} [2I, H]: gate rows 0..I, then up rows I..2I (expert_cache.rs:69-74). */
+RMOE_API rmoe_status rmoe_upload_expert_fused(rmoe_layer* layer, int32_t eid,
+                                     const void* gate_up, size_t gate_up_bytes,
+                                     const void* gate_up_scale, size_t gate_up_scale_bytes,
+                                     const void* down, size_t down_bytes,
+                                     const void* down_scale, size_t down_scale_bytes);
+/* MoeWeights::{sh_gate, sh_up, sh_down, shared_gate} (src/qwen38/model.rs:93-99). shared_gate
+ * ([H] f32) may be NULL when desc.shared_gated == 0. Same format as the routed experts. */
+RMOE_API rmoe_status rmoe_upload_shared(rmoe_layer* layer,
+                               const void* gate, size_t gate_bytes,
+                               const void* gate_scale, size_t gate_scale_bytes,
+                               const void* up, size_t up_bytes,
+                               const void* up_scale, size_t up_scale_bytes,
+                               const void* down, size_t down_bytes,
+                               const void* down_scale, size_t down_scale_bytes,
+                               const float* shared_gate);
+
+/* ---- the hot path (device pointers) ---- */
+
+/* Router matmul + top-k for T tokens: replaces kernels::matmul (src/kernels.rs:113-124) +
+ * qwen38::moe::route (src/qwen38/moe.rs:41-76) or glm52::moe::route (src/glm52/moe.rs:247-260).
+ * x: [T, H] of x_dtype. ids/weights: [T, k], in the reference's rank order. */
+RMOE_API rmoe_status rmoe_route(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                       int32_t* ids, float* weights, void* stream);
+
+/* Token -> expert dispatch from a routing: unique_experts (src/glm52/moe.rs:333-344) and the
+ * per-expert ascending-token row lists of apply_single_expert (:465-470). ids: [T, k].
+ * counts: [E] tokens per expert; offsets: [E+1] exclusive prefix; perm_token: [T*k] tokens of
+ * expert e at perm_token[offsets[e] .. offsets[e+1]) ascending; uniq: [E] experts in
+ * first-occurrence order, n_uniq: [1]. All device pointers; any output may be NULL. */
+RMOE_API rmoe_status rmoe_dispatch(rmoe_layer* layer, const int32_t* ids, int32_t T, int32_t* counts,
+                          int32_t* offsets, int32_t* perm_token, int32_t* uniq, int32_t* n_uniq,
+                          void* stream);
+
+/* The whole MoE block for T tokens: qwen38::generate::moe_forward (src/qwen38/generate.rs:
+ * 262-351) or glm52::moe::moe (src/glm52/moe.rs:350-451). out [T, H] f32 is overwritten.
+ * ids_out/w_out ([T, k]) receive the routing when non-NULL. */
+RMOE_API rmoe_status rmoe_moe_forward(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                             float* out, int32_t* ids_out, float* w_out, void* stream);
+
+/* Same, with HOST buffers as the Rust call sites hold them (x: &[f32] / bf16 bits, out:
+ * &mut [f32]): copies in, runs, copies out and synchronizes. The drop-in for moe_forward's
+ * signature. */
+RMOE_API rmoe_status rmoe_moe_forward_host(rmoe_layer* layer, const void* x_host, int32_t x_dtype,
+                                  int32_t T, float* out_host, int32_t* ids_host,
+                                  float* w_host);
+
+/* ---- generic expert-format GEMMs, y[S,O] = x[S,I] . W^T (device pointers) ---- */
+
+/* kernels::matmul_mxfp4 (src/kernels.rs:233-244) */
+RMOE_API rmoe_status rmoe_matmul_mxfp4(float* y, const void* x, int32_t x_dtype, const uint8_t* data,
+                              const uint8_t* block_scale, int32_t s, int32_t i, int32_t o,
+                              void* stream);
+/* kernels::matmul_i4_grouped (src/kernels.rs:276-296) */
+RMOE_API rmoe_status rmoe_matmul_i4_grouped(float* y, const void* x, int32_t x_dtype, const uint8_t* q4,
+                                   const void* scale, int32_t scale_dtype, int32_t group_size,
+                                   int32_t s, int32_t i, int32_t o, void* stream);
+/* kernels::matmul (src/kernels.rs:113-124) for f32/bf16 weights: each y element is the
+ * reference's exact left-to-right f32 chain (separate multiply and add, from -0.0). */
+RMOE_API rmoe_status rmoe_matmul_f32(float* y, const void* x, int32_t x_dtype, const void* w,
+                            int32_t w_dtype, int32_t s, int32_t i, int32_t o, void* stream);
+
+/* ---- seeded synthetic bytes for benches/tests (SplitMix64 counter stream; identical to the
+ *      host generator rabbit_b200/synth.py). mode 0: uniform bytes; mode 1: E8M0 bytes
+ *      127+lo .. 127+hi. ---- */
+RMOE_API rmoe_status rmoe_synth_bytes(void* dst, size_t n, uint64_t key, int32_t mode, int32_t lo,
+                             int32_t hi, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RMOE_H */

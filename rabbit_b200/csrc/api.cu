@@ -1,0 +1,727 @@
+// api.cu -- the C ABI (include/rmoe.h): contexts, layers with HBM-resident experts, uploads
+// in the reference byte layout, and the stream-ordered forward pipeline.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "rmoe.h"
+
+using namespace rmoe;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+rmoe_status fail(rmoe_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+rmoe_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? RMOE_OUT_OF_MEMORY : RMOE_CUDA_ERROR, "%s: %s",
+              what, cudaGetErrorString(e));
+}
+
+#define RMOE_CUDA(call, what)                         \
+  do {                                                \
+    cudaError_t _e = (call);                          \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device allocations of one layer, freed together.
+struct DevArena {
+  std::vector<void*> ptrs;
+  ~DevArena() {
+    for (void* p : ptrs) cudaFree(p);
+  }
+  template <typename T>
+  cudaError_t alloc(T** out, size_t count) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, std::max<size_t>(count * sizeof(T), 16));
+    if (e != cudaSuccess) return e;
+    ptrs.push_back(p);
+    *out = static_cast<T*>(p);
+    return cudaSuccess;
+  }
+};
+
+}  // namespace
+
+struct rmoe_ctx {
+  int device;
+};
+
+struct rmoe_layer {
+  rmoe_ctx* ctx = nullptr;
+  rmoe_layer_desc desc{};
+  int e_begin = 0, e_end = 0, n_loc = 0;
+  bool has_shared = false;
+  ExpertFormat fmt{};
+  DevArena arena;
+  // weights
+  void* router = nullptr;
+  int router_dtype = kF32;
+  float* router_bias = nullptr;
+  bool has_router = false, has_bias = false, has_shared_w = false;
+  uint8_t* experts = nullptr;
+  ExpertTable tab{};
+  uint8_t* shared = nullptr;
+  float* shared_gate_vec = nullptr;
+  std::vector<uint8_t> uploaded;
+  // workspace
+  int max_tokens = 0, P_max = 0, h_ld = 0;
+  float* logits = nullptr;
+  int32_t* ids = nullptr;
+  float* rw = nullptr;
+  DispatchBuffers d{};
+  uint16_t* xq = nullptr;
+  int32_t* xexp = nullptr;
+  float* gate = nullptr;
+  float* h = nullptr;
+  uint32_t* hmax = nullptr;
+  uint16_t* hq = nullptr;
+  int32_t* hexp = nullptr;
+  float* y = nullptr;
+  // host-buffer entry point
+  cudaStream_t stream = nullptr;
+  void* x_dev = nullptr;
+  float* out_dev = nullptr;
+  rmoe_layer_stats stats{};
+  // profiling: one event per stage boundary per profiled call
+  bool profiling = false;
+  std::vector<cudaEvent_t> ev_free, ev_pending;  // pending: groups of RMOE_NUM_STAGES + 1
+  uint64_t prof_calls = 0;
+  double prof_ms[RMOE_NUM_STAGES] = {};
+  ~rmoe_layer() {
+    for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
+    for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
+  }
+};
+
+namespace {
+// Records a stage boundary when profiling is on.
+struct StageMarks {
+  rmoe_layer* L;
+  cudaStream_t st;
+  std::vector<cudaEvent_t> evs;
+  StageMarks(rmoe_layer* l, cudaStream_t s) : L(l), st(s) {}
+  void mark() {
+    if (!L->profiling) return;
+    cudaEvent_t e;
+    if (!L->ev_free.empty()) {
+      e = L->ev_free.back();
+      L->ev_free.pop_back();
+    } else if (cudaEventCreate(&e) != cudaSuccess) {
+      return;
+    }
+    cudaEventRecord(e, st);
+    evs.push_back(e);
+  }
+  void commit() {
+    if (!L->profiling) return;
+    if (evs.size() == RMOE_NUM_STAGES + 1) {
+      L->ev_pending.insert(L->ev_pending.end(), evs.begin(), evs.end());
+    } else {
+      L->ev_free.insert(L->ev_free.end(), evs.begin(), evs.end());
+    }
+    evs.clear();
+  }
+};
+}  // namespace
+
+// ------------------------------------------------------------------------------ misc
+extern "C" const char* rmoe_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" const char* rmoe_status_string(rmoe_status s) {
+  switch (s) {
+    case RMOE_OK: return "ok";
+    case RMOE_INVALID_ARG: return "invalid argument";
+    case RMOE_SHAPE_MISMATCH: return "shape mismatch";
+    case RMOE_CUDA_ERROR: return "cuda error";
+    case RMOE_NCCL_ERROR: return "nccl error";
+    case RMOE_TIMEOUT: return "timeout";
+    case RMOE_NOT_SUPPORTED: return "not supported";
+    case RMOE_OUT_OF_MEMORY: return "out of memory";
+  }
+  return "unknown status";
+}
+
+extern "C" int rmoe_abi_version(void) { return RMOE_ABI_VERSION; }
+
+extern "C" rmoe_status rmoe_init(int device, rmoe_ctx** out) {
+  if (!out) return fail(RMOE_INVALID_ARG, "rmoe_init: out is null");
+  int n = 0;
+  RMOE_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(RMOE_INVALID_ARG, "rmoe_init: device %d of %d", device, n);
+  RMOE_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  rmoe_ctx* c = new (std::nothrow) rmoe_ctx{device};
+  if (!c) return fail(RMOE_OUT_OF_MEMORY, "rmoe_init: host allocation");
+  *out = c;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_shutdown(rmoe_ctx* ctx) {
+  delete ctx;
+  return RMOE_OK;
+}
+
+// ------------------------------------------------------------------------------ layer
+static size_t scale_bytes_for(const ExpertFormat& f, size_t rows, size_t cols) {
+  if (f.fmt == kMxfp4) return rows * ((cols + 31) / 32);
+  return rows * ((cols + f.group_size - 1) / f.group_size) * (f.scale_dtype == kBF16 ? 2 : 4);
+}
+
+extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* desc,
+                                         rmoe_layer** out) {
+  if (!ctx || !desc || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_create: null argument");
+  const rmoe_layer_desc& D = *desc;
+  if (D.hidden <= 0 || D.moe_inter <= 0 || D.n_experts <= 0 || D.topk <= 0 || D.max_tokens <= 0)
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: hidden, moe_inter, n_experts, topk, max_tokens must be > 0");
+  if (D.topk > RMOE_MAX_TOPK || D.topk > D.n_experts)
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: topk %d (max %d, n_experts %d)", D.topk, RMOE_MAX_TOPK, D.n_experts);
+  if (D.n_experts > 1024) return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: n_experts %d > 1024", D.n_experts);
+  if (D.hidden % 32 || D.moe_inter % 32 || D.shared_inter % 32 || D.shared_inter < 0)
+    return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: hidden/moe_inter/shared_inter must be multiples of 32");
+  if (D.router_kind != RMOE_ROUTER_SOFTMAX_TOPK && D.router_kind != RMOE_ROUTER_SIGMOID_GROUPED)
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: router_kind %d", D.router_kind);
+  if (D.router_kind == RMOE_ROUTER_SIGMOID_GROUPED && D.n_group > 1) {
+    if (D.n_group > 32 || D.n_experts % D.n_group)
+      return fail(RMOE_INVALID_ARG, "rmoe_layer_create: n_group %d must divide n_experts and be <= 32", D.n_group);
+    if (D.topk_group < 1 || D.topk_group > D.n_group)
+      return fail(RMOE_INVALID_ARG, "rmoe_layer_create: topk_group %d", D.topk_group);
+  }
+  ExpertFormat f{};
+  if (D.weight_format == RMOE_FMT_MXFP4) {
+    f = ExpertFormat{kMxfp4, 32, kF32};
+  } else if (D.weight_format == RMOE_FMT_I4_GROUPED) {
+    if (D.group_size <= 0 || D.group_size % 32)
+      return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: int4 group_size %d must be a multiple of 32", D.group_size);
+    if (D.hidden % D.group_size || D.moe_inter % D.group_size || (D.shared_inter && D.shared_inter % D.group_size))
+      return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: group_size must divide hidden and inter");
+    if (D.scale_dtype != RMOE_F32 && D.scale_dtype != RMOE_BF16)
+      return fail(RMOE_INVALID_ARG, "rmoe_layer_create: scale_dtype %d", D.scale_dtype);
+    f = ExpertFormat{kInt4g, D.group_size, D.scale_dtype == RMOE_BF16 ? kBF16 : kF32};
+  } else {
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: weight_format %d", D.weight_format);
+  }
+  const int ep_size = D.ep_size <= 0 ? 1 : D.ep_size;
+  if (D.n_experts % ep_size || D.ep_rank < 0 || D.ep_rank >= ep_size)
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: ep_rank %d / ep_size %d / n_experts %d", D.ep_rank, ep_size, D.n_experts);
+
+  RMOE_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+  rmoe_layer* L = new (std::nothrow) rmoe_layer();
+  if (!L) return fail(RMOE_OUT_OF_MEMORY, "rmoe_layer_create: host allocation");
+  L->ctx = ctx;
+  L->desc = D;
+  L->desc.ep_size = ep_size;
+  L->fmt = f;
+  L->n_loc = D.n_experts / ep_size;
+  L->e_begin = D.ep_rank * L->n_loc;
+  L->e_end = L->e_begin + L->n_loc;
+  L->has_shared = D.shared_inter > 0;
+  L->uploaded.assign(L->n_loc, 0);
+  auto cleanup = [&](rmoe_status s) {
+    if (L->stream) cudaStreamDestroy(L->stream);
+    delete L;
+    return s;
+  };
+#define ALLOC(ptr, n)                                                          \
+  do {                                                                         \
+    cudaError_t _e = L->arena.alloc(&(ptr), (n));                              \
+    if (_e != cudaSuccess) return cleanup(cuda_fail(_e, "cudaMalloc " #ptr)); \
+  } while (0)
+
+  const size_t H = D.hidden, I = D.moe_inter, Is = D.shared_inter, E = D.n_experts;
+  // expert table: [gate][up][down][gate sc][up sc][down sc], each region 256-byte aligned
+  const size_t gd = I * (H / 2), dd = H * (I / 2);
+  size_t off = 0;
+  const size_t o_gate = off; off = align_up(off + gd, 256);
+  const size_t o_up = off; off = align_up(off + gd, 256);
+  const size_t o_down = off; off = align_up(off + dd, 256);
+  const size_t o_gs = off; off = align_up(off + scale_bytes_for(f, I, H), 256);
+  const size_t o_us = off; off = align_up(off + scale_bytes_for(f, I, H), 256);
+  const size_t o_ds = off; off = align_up(off + scale_bytes_for(f, H, I), 256);
+  const size_t stride = off;
+  ALLOC(L->experts, stride * L->n_loc);
+  L->tab.base = L->experts;
+  L->tab.stride = stride;
+  L->tab.off_up = o_up - o_gate;
+  L->tab.off_down = o_down;
+  L->tab.off_gs = o_gs;
+  L->tab.off_us = o_us;
+  L->tab.off_ds = o_ds;
+  L->tab.n_local = L->n_loc;
+  L->tab.inter = static_cast<int>(I);
+  L->tab.shared_inter = static_cast<int>(Is);
+  if (L->has_shared) {
+    const size_t sgd = Is * (H / 2), sdd = H * (Is / 2);
+    size_t so = 0;
+    const size_t s_up = so = align_up(sgd, 256);
+    const size_t s_down = so = align_up(so + sgd, 256);
+    const size_t s_gs = so = align_up(so + sdd, 256);
+    const size_t s_us = so = align_up(so + scale_bytes_for(f, Is, H), 256);
+    const size_t s_ds = so = align_up(so + scale_bytes_for(f, Is, H), 256);
+    so = align_up(so + scale_bytes_for(f, H, Is), 256);
+    ALLOC(L->shared, so);
+    L->tab.shared = ExpertPtrs{L->shared, L->shared + s_up, L->shared + s_down, L->shared + s_gs,
+                               L->shared + s_us, L->shared + s_ds};
+    ALLOC(L->shared_gate_vec, H);
+  }
+  ALLOC(L->router_bias, E);
+  {
+    uint8_t* r = nullptr;
+    ALLOC(r, E * H * 4);
+    L->router = r;
+  }
+  // workspace
+  const int T = D.max_tokens, k = D.topk;
+  const int n_slots = L->n_loc + (L->has_shared ? 1 : 0);
+  L->max_tokens = T;
+  L->P_max = T * k + (L->has_shared ? T : 0);
+  L->h_ld = static_cast<int>(std::max(I, Is));
+  const int words = (T + 31) / 32;
+  const int max_chunks = L->P_max + n_slots + 1;
+  ALLOC(L->logits, static_cast<size_t>(T) * E);
+  ALLOC(L->ids, static_cast<size_t>(T) * k);
+  ALLOC(L->rw, static_cast<size_t>(T) * k);
+  DispatchBuffers& d = L->d;
+  d.words = words;
+  d.max_chunks = max_chunks;
+  ALLOC(d.bits, static_cast<size_t>(L->n_loc) * words);
+  ALLOC(d.first_occ, L->n_loc);
+  ALLOC(d.wpre, static_cast<size_t>(L->n_loc) * words);
+  ALLOC(d.counts, n_slots + 1);
+  ALLOC(d.offsets, n_slots + 2);
+  ALLOC(d.uniq, L->n_loc);
+  ALLOC(d.n_uniq, 1);
+  ALLOC(d.perm_tok, L->P_max);
+  ALLOC(d.perm_w, L->P_max);
+  ALLOC(d.inv, static_cast<size_t>(T) * k);
+  ALLOC(d.ch_expert, max_chunks);
+  ALLOC(d.ch_pos, max_chunks);
+  ALLOC(d.ch_n, max_chunks);
+  ALLOC(d.ch_task_gu, max_chunks + 1);
+  ALLOC(d.ch_task_dn, max_chunks + 1);
+  ALLOC(d.n_chunks, 1);
+  ALLOC(L->xq, static_cast<size_t>(T) * H);
+  ALLOC(L->xexp, T);
+  ALLOC(L->gate, T);
+  ALLOC(L->h, static_cast<size_t>(L->P_max) * L->h_ld);
+  ALLOC(L->hmax, L->P_max);
+  ALLOC(L->hq, static_cast<size_t>(L->P_max) * L->h_ld);
+  ALLOC(L->hexp, L->P_max);
+  ALLOC(L->y, static_cast<size_t>(L->P_max) * H);
+  {
+    uint8_t* xd = nullptr;
+    ALLOC(xd, static_cast<size_t>(T) * H * 4);
+    L->x_dev = xd;
+  }
+  ALLOC(L->out_dev, static_cast<size_t>(T) * H);
+  {
+    cudaError_t e = cudaStreamCreateWithFlags(&L->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaStreamCreate"));
+  }
+#undef ALLOC
+  L->stats.local_expert_begin = L->e_begin;
+  L->stats.local_expert_end = L->e_end;
+  L->stats.device_bytes = stride * L->n_loc + E * H * 4;
+  *out = L;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_layer_destroy(rmoe_layer* L) {
+  if (!L) return RMOE_OK;
+  cudaSetDevice(L->ctx->device);
+  if (L->stream) {
+    cudaStreamSynchronize(L->stream);
+    cudaStreamDestroy(L->stream);
+  }
+  delete L;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stats* out) {
+  if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_stats: null argument");
+  *out = L->stats;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_layer_set_profiling(rmoe_layer* L, int on) {
+  if (!L) return fail(RMOE_INVALID_ARG, "rmoe_layer_set_profiling: null layer");
+  L->profiling = on != 0;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_layer_get_profile(rmoe_layer* L, rmoe_profile* out) {
+  if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_profile: null argument");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const size_t G = RMOE_NUM_STAGES + 1;
+  for (size_t g = 0; g + G <= L->ev_pending.size(); g += G) {
+    RMOE_CUDA(cudaEventSynchronize(L->ev_pending[g + G - 1]), "profile event");
+    for (int s = 0; s < RMOE_NUM_STAGES; s++) {
+      float ms = 0.0f;
+      RMOE_CUDA(cudaEventElapsedTime(&ms, L->ev_pending[g + s], L->ev_pending[g + s + 1]), "profile elapsed");
+      L->prof_ms[s] += ms;
+    }
+    L->prof_calls++;
+  }
+  L->ev_free.insert(L->ev_free.end(), L->ev_pending.begin(), L->ev_pending.end());
+  L->ev_pending.clear();
+  out->calls = L->prof_calls;
+  for (int s = 0; s < RMOE_NUM_STAGES; s++) out->stage_ms[s] = L->prof_ms[s];
+  L->prof_calls = 0;
+  for (double& v : L->prof_ms) v = 0.0;
+  return RMOE_OK;
+}
+
+// ------------------------------------------------------------------------------ uploads
+extern "C" rmoe_status rmoe_upload_router(rmoe_layer* L, const void* w, int32_t dtype, size_t bytes) {
+  if (!L || !w) return fail(RMOE_INVALID_ARG, "rmoe_upload_router: null argument");
+  if (dtype != RMOE_F32 && dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "rmoe_upload_router: dtype %d", dtype);
+  const size_t want = static_cast<size_t>(L->desc.n_experts) * L->desc.hidden * (dtype == RMOE_BF16 ? 2 : 4);
+  if (bytes != want)
+    return fail(RMOE_SHAPE_MISMATCH, "rmoe_upload_router: %zu bytes, [%d, %d] needs %zu", bytes,
+                L->desc.n_experts, L->desc.hidden, want);
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  RMOE_CUDA(cudaMemcpy(L->router, w, bytes, cudaMemcpyDefault), "rmoe_upload_router copy");
+  L->router_dtype = dtype == RMOE_BF16 ? kBF16 : kF32;
+  L->has_router = true;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_upload_router_bias(rmoe_layer* L, const float* bias, size_t n) {
+  if (!L || !bias) return fail(RMOE_INVALID_ARG, "rmoe_upload_router_bias: null argument");
+  if (n != static_cast<size_t>(L->desc.n_experts))
+    return fail(RMOE_SHAPE_MISMATCH, "rmoe_upload_router_bias: %zu values for %d experts", n, L->desc.n_experts);
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  RMOE_CUDA(cudaMemcpy(L->router_bias, bias, n * 4, cudaMemcpyDefault), "rmoe_upload_router_bias copy");
+  L->has_bias = true;
+  return RMOE_OK;
+}
+
+// Checks (data, scale) byte counts of one [rows, cols] matrix like mxfp4_from_raw
+// (src/expert_cache.rs:1245-1256) and copies them.
+static rmoe_status put_matrix(const rmoe_layer* L, const char* what, size_t rows, size_t cols,
+                              const void* data, size_t data_bytes, const void* scale,
+                              size_t scale_bytes, uint8_t* ddst, uint8_t* sdst) {
+  if (!data || !scale) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  const size_t want_d = rows * ((cols + 1) / 2);
+  const size_t want_s = scale_bytes_for(L->fmt, rows, cols);
+  if (data_bytes != want_d)
+    return fail(RMOE_SHAPE_MISMATCH, "%s: %zu data bytes, [%zu, %zu] needs %zu", what, data_bytes, rows, cols, want_d);
+  if (scale_bytes != want_s)
+    return fail(RMOE_SHAPE_MISMATCH, "%s: %zu scale bytes, [%zu, %zu] needs %zu", what, scale_bytes, rows, cols, want_s);
+  RMOE_CUDA(cudaMemcpy(ddst, data, data_bytes, cudaMemcpyDefault), what);
+  RMOE_CUDA(cudaMemcpy(sdst, scale, scale_bytes, cudaMemcpyDefault), what);
+  return RMOE_OK;
+}
+
+static rmoe_status local_slot(const rmoe_layer* L, int32_t eid, const char* what, int* slot) {
+  if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
+  if (eid < 0 || eid >= L->desc.n_experts)
+    return fail(RMOE_INVALID_ARG, "%s: expert %d out of range [0, %d)", what, eid, L->desc.n_experts);
+  if (eid < L->e_begin || eid >= L->e_end)
+    return fail(RMOE_INVALID_ARG, "%s: expert %d is not resident on EP rank %d (experts %d..%d)", what, eid,
+                L->desc.ep_rank, L->e_begin, L->e_end - 1);
+  *slot = eid - L->e_begin;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_upload_expert(rmoe_layer* L, int32_t eid, const void* gate,
+                                          size_t gate_bytes, const void* gate_scale,
+                                          size_t gate_scale_bytes, const void* up, size_t up_bytes,
+                                          const void* up_scale, size_t up_scale_bytes,
+                                          const void* down, size_t down_bytes,
+                                          const void* down_scale, size_t down_scale_bytes) {
+  int slot = 0;
+  rmoe_status s = local_slot(L, eid, "rmoe_upload_expert", &slot);
+  if (s != RMOE_OK) return s;
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const size_t H = L->desc.hidden, I = L->desc.moe_inter;
+  uint8_t* b = L->experts + L->tab.stride * slot;
+  if ((s = put_matrix(L, "rmoe_upload_expert gate", I, H, gate, gate_bytes, gate_scale,
+                      gate_scale_bytes, b, b + L->tab.off_gs)) != RMOE_OK)
+    return s;
+  if ((s = put_matrix(L, "rmoe_upload_expert up", I, H, up, up_bytes, up_scale, up_scale_bytes,
+                      b + L->tab.off_up, b + L->tab.off_us)) != RMOE_OK)
+    return s;
+  if ((s = put_matrix(L, "rmoe_upload_expert down", H, I, down, down_bytes, down_scale,
+                      down_scale_bytes, b + L->tab.off_down, b + L->tab.off_ds)) != RMOE_OK)
+    return s;
+  L->uploaded[slot] = 1;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_upload_expert_fused(rmoe_layer* L, int32_t eid, const void* gate_up,
+                                                size_t gate_up_bytes, const void* gate_up_scale,
+                                                size_t gate_up_scale_bytes, const void* down,
+                                                size_t down_bytes, const void* down_scale,
+                                                size_t down_scale_bytes) {
+  if (!L || !gate_up || !gate_up_scale) return fail(RMOE_INVALID_ARG, "rmoe_upload_expert_fused: null argument");
+  const size_t H = L->desc.hidden, I = L->desc.moe_inter;
+  const size_t half_d = I * ((H + 1) / 2), half_s = scale_bytes_for(L->fmt, I, H);
+  if (gate_up_bytes != 2 * half_d || gate_up_scale_bytes != 2 * half_s)
+    return fail(RMOE_SHAPE_MISMATCH, "rmoe_upload_expert_fused: %zu/%zu bytes, [2*%zu, %zu] needs %zu/%zu",
+                gate_up_bytes, gate_up_scale_bytes, I, H, 2 * half_d, 2 * half_s);
+  // gate rows 0..I then up rows I..2I: the same bytes as Separate{gate, up} back to back
+  const uint8_t* gu = static_cast<const uint8_t*>(gate_up);
+  const uint8_t* gus = static_cast<const uint8_t*>(gate_up_scale);
+  return rmoe_upload_expert(L, eid, gu, half_d, gus, half_s, gu + half_d, half_d, gus + half_s,
+                            half_s, down, down_bytes, down_scale, down_scale_bytes);
+}
+
+extern "C" rmoe_status rmoe_upload_shared(rmoe_layer* L, const void* gate, size_t gate_bytes,
+                                          const void* gate_scale, size_t gate_scale_bytes,
+                                          const void* up, size_t up_bytes, const void* up_scale,
+                                          size_t up_scale_bytes, const void* down,
+                                          size_t down_bytes, const void* down_scale,
+                                          size_t down_scale_bytes, const float* shared_gate) {
+  if (!L) return fail(RMOE_INVALID_ARG, "rmoe_upload_shared: null layer");
+  if (!L->has_shared) return fail(RMOE_INVALID_ARG, "rmoe_upload_shared: layer was created with shared_inter = 0");
+  if (L->desc.shared_gated && !shared_gate)
+    return fail(RMOE_INVALID_ARG, "rmoe_upload_shared: shared_gated layer needs shared_gate");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const size_t H = L->desc.hidden, Is = L->desc.shared_inter;
+  const ExpertPtrs& p = L->tab.shared;
+  rmoe_status s;
+  if ((s = put_matrix(L, "rmoe_upload_shared gate", Is, H, gate, gate_bytes, gate_scale, gate_scale_bytes,
+                      const_cast<uint8_t*>(p.gate), (uint8_t*)p.gate_scale)) != RMOE_OK)
+    return s;
+  if ((s = put_matrix(L, "rmoe_upload_shared up", Is, H, up, up_bytes, up_scale, up_scale_bytes,
+                      const_cast<uint8_t*>(p.up), (uint8_t*)p.up_scale)) != RMOE_OK)
+    return s;
+  if ((s = put_matrix(L, "rmoe_upload_shared down", H, Is, down, down_bytes, down_scale, down_scale_bytes,
+                      const_cast<uint8_t*>(p.down), (uint8_t*)p.down_scale)) != RMOE_OK)
+    return s;
+  if (shared_gate && L->desc.shared_gated)
+    RMOE_CUDA(cudaMemcpy(L->shared_gate_vec, shared_gate, H * 4, cudaMemcpyDefault), "rmoe_upload_shared gate vector");
+  L->has_shared_w = true;
+  return RMOE_OK;
+}
+
+// ------------------------------------------------------------------------------ forward
+static rmoe_status check_ready(const rmoe_layer* L, const char* what, int T, int x_dtype) {
+  if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
+  if (T < 0 || T > L->max_tokens)
+    return fail(RMOE_INVALID_ARG, "%s: T = %d outside [0, max_tokens = %d]", what, T, L->max_tokens);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  if (!L->has_router) return fail(RMOE_INVALID_ARG, "%s: router weights were never uploaded", what);
+  if (L->desc.router_kind == RMOE_ROUTER_SIGMOID_GROUPED && !L->has_bias)
+    return fail(RMOE_INVALID_ARG, "%s: sigmoid router needs rmoe_upload_router_bias", what);
+  return RMOE_OK;
+}
+
+static rmoe_status route_into(rmoe_layer* L, const void* x, int x_dtype, int T, cudaStream_t st,
+                              StageMarks* marks = nullptr) {
+  const rmoe_layer_desc& D = L->desc;
+  cudaError_t e = launch_router_logits_exact(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, L->router,
+                                             L->router_dtype, L->logits, T, D.hidden, D.n_experts, st);
+  if (e != cudaSuccess) return cuda_fail(e, "router logits");
+  if (marks) marks->mark();
+  if (D.router_kind == RMOE_ROUTER_SOFTMAX_TOPK)
+    e = launch_topk_softmax(L->logits, L->has_bias ? L->router_bias : nullptr, T, D.n_experts, D.topk,
+                            L->ids, L->rw, st);
+  else
+    e = launch_topk_grouped(L->logits, L->router_bias, T, D.n_experts, D.topk, D.n_group,
+                            D.topk_group, D.norm_topk, D.routed_scale, L->ids, L->rw, st);
+  if (e != cudaSuccess) return cuda_fail(e, "router top-k");
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_route(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T,
+                                  int32_t* ids, float* weights, void* stream) {
+  rmoe_status s = check_ready(L, "rmoe_route", T, x_dtype);
+  if (s != RMOE_OK) return s;
+  if (T == 0) return RMOE_OK;
+  if (!x || !ids || !weights) return fail(RMOE_INVALID_ARG, "rmoe_route: null pointer");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((s = route_into(L, x, x_dtype, T, st)) != RMOE_OK) return s;
+  const size_t n = static_cast<size_t>(T) * L->desc.topk;
+  RMOE_CUDA(cudaMemcpyAsync(ids, L->ids, n * 4, cudaMemcpyDeviceToDevice, st), "rmoe_route ids");
+  RMOE_CUDA(cudaMemcpyAsync(weights, L->rw, n * 4, cudaMemcpyDeviceToDevice, st), "rmoe_route weights");
+  return RMOE_OK;
+}
+
+static int chunk_tokens(int T) { return T >= 8 ? 8 : (T >= 4 ? 4 : (T >= 2 ? 2 : 1)); }
+
+static rmoe_status dispatch_into(rmoe_layer* L, int T, int mt, const float* gate, cudaStream_t st) {
+  const rmoe_layer_desc& D = L->desc;
+  cudaError_t e = launch_dispatch(L->ids, L->rw, T, D.topk, L->e_begin, L->e_end, mt,
+                                  L->has_shared ? 1 : 0, gate, D.moe_inter, D.shared_inter,
+                                  D.hidden, 2, 4, L->d, st);
+  if (e != cudaSuccess) return cuda_fail(e, "dispatch");
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_dispatch(rmoe_layer* L, const int32_t* ids, int32_t T, int32_t* counts,
+                                     int32_t* offsets, int32_t* perm_token, int32_t* uniq,
+                                     int32_t* n_uniq, void* stream) {
+  if (!L || !ids) return fail(RMOE_INVALID_ARG, "rmoe_dispatch: null argument");
+  if (T < 0 || T > L->max_tokens) return fail(RMOE_INVALID_ARG, "rmoe_dispatch: T = %d", T);
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t n = static_cast<size_t>(T) * L->desc.topk;
+  RMOE_CUDA(cudaMemcpyAsync(L->ids, ids, n * 4, cudaMemcpyDeviceToDevice, st), "rmoe_dispatch ids");
+  RMOE_CUDA(cudaMemsetAsync(L->rw, 0, n * 4, st), "rmoe_dispatch weights");
+  rmoe_status s = dispatch_into(L, T, chunk_tokens(T), nullptr, st);
+  if (s != RMOE_OK) return s;
+  const int E = L->n_loc;
+  if (counts) RMOE_CUDA(cudaMemcpyAsync(counts, L->d.counts, E * 4, cudaMemcpyDeviceToDevice, st), "counts");
+  if (offsets) RMOE_CUDA(cudaMemcpyAsync(offsets, L->d.offsets, (E + 1) * 4, cudaMemcpyDeviceToDevice, st), "offsets");
+  if (perm_token) RMOE_CUDA(cudaMemcpyAsync(perm_token, L->d.perm_tok, n * 4, cudaMemcpyDeviceToDevice, st), "perm");
+  if (uniq) RMOE_CUDA(cudaMemcpyAsync(uniq, L->d.uniq, E * 4, cudaMemcpyDeviceToDevice, st), "uniq");
+  if (n_uniq) RMOE_CUDA(cudaMemcpyAsync(n_uniq, L->d.n_uniq, 4, cudaMemcpyDeviceToDevice, st), "n_uniq");
+  return RMOE_OK;
+}
+
+static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
+                                int32_t* ids_out, float* w_out, cudaStream_t st) {
+  const rmoe_layer_desc& D = L->desc;
+  const int H = D.hidden, k = D.topk;
+  for (int s = 0; s < L->n_loc; s++)
+    if (!L->uploaded[s])
+      return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: expert %d was never uploaded", L->e_begin + s);
+  if (L->has_shared && !L->has_shared_w) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: shared expert never uploaded");
+  StageMarks marks(L, st);
+  marks.mark();
+  rmoe_status s = route_into(L, x, x_dtype, T, st, &marks);
+  if (s != RMOE_OK) return s;
+  marks.mark();  // end of top-k
+  const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
+  const bool gated = L->has_shared && D.shared_gated;
+  cudaError_t e = launch_prep_tokens(x, xdt, T, H, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr,
+                                     L->xq, L->xexp, L->gate, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
+  marks.mark();
+  const int mt = chunk_tokens(T);
+  if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st)) != RMOE_OK) return s;
+  const int P = T * k + (L->has_shared ? T : 0);
+  RMOE_CUDA(cudaMemsetAsync(L->hmax, 0, static_cast<size_t>(P) * 4, st), "hmax reset");
+  const int n_slots = L->n_loc + (L->has_shared ? 1 : 0);
+  const int max_chunks = std::min(T * k, L->n_loc) + (T * k + mt - 1) / mt + (L->has_shared ? (T + mt - 1) / mt : 0);
+  const int tasks_gu = max_chunks * (std::max(D.moe_inter, D.shared_inter) / 2);
+  const int tasks_dn = max_chunks * (H / 4);
+  marks.mark();
+  e = launch_gemv_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, tasks_gu, L->h, L->hmax, L->h_ld, st);
+  if (e != cudaSuccess) return cuda_fail(e, "gate/up");
+  marks.mark();
+  e = launch_quant_h(L->h, L->hmax, L->d.offsets + n_slots, P, L->h_ld, L->fmt.fmt, L->hq, L->hexp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "h quantize");
+  marks.mark();
+  e = launch_gemv_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, tasks_dn, L->h_ld, L->y, st);
+  if (e != cudaSuccess) return cuda_fail(e, "down");
+  marks.mark();
+  e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
+  if (e != cudaSuccess) return cuda_fail(e, "combine");
+  marks.mark();
+  marks.commit();
+  // router logits, top-k, prep, dispatch (mark/scan/place), gate/up, quantize h, down, combine
+  L->stats.kernel_launches += 10;
+  const size_t n = static_cast<size_t>(T) * k;
+  if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, L->ids, n * 4, cudaMemcpyDefault, st), "ids out");
+  if (w_out) RMOE_CUDA(cudaMemcpyAsync(w_out, L->rw, n * 4, cudaMemcpyDefault, st), "weights out");
+  L->stats.forward_calls++;
+  L->stats.tokens_routed += T;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_moe_forward(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T,
+                                        float* out, int32_t* ids_out, float* w_out, void* stream) {
+  rmoe_status s = check_ready(L, "rmoe_moe_forward", T, x_dtype);
+  if (s != RMOE_OK) return s;
+  if (T == 0) return RMOE_OK;
+  if (!x || !out) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: null x/out");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  return forward_into(L, x, x_dtype, T, out, ids_out, w_out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, int32_t x_dtype,
+                                             int32_t T, float* out_host, int32_t* ids_host,
+                                             float* w_host) {
+  rmoe_status s = check_ready(L, "rmoe_moe_forward_host", T, x_dtype);
+  if (s != RMOE_OK) return s;
+  if (T == 0) return RMOE_OK;
+  if (!x_host || !out_host) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward_host: null x/out");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const size_t H = L->desc.hidden;
+  const size_t xb = static_cast<size_t>(T) * H * (x_dtype == RMOE_BF16 ? 2 : 4);
+  RMOE_CUDA(cudaMemcpyAsync(L->x_dev, x_host, xb, cudaMemcpyHostToDevice, L->stream), "x to device");
+  if ((s = forward_into(L, L->x_dev, x_dtype, T, L->out_dev, ids_host, w_host, L->stream)) != RMOE_OK)
+    return s;
+  RMOE_CUDA(cudaMemcpyAsync(out_host, L->out_dev, static_cast<size_t>(T) * H * 4, cudaMemcpyDeviceToHost, L->stream),
+            "out to host");
+  RMOE_CUDA(cudaStreamSynchronize(L->stream), "rmoe_moe_forward_host synchronize");
+  return RMOE_OK;
+}
+
+// ------------------------------------------------------------------------------ matmuls
+static rmoe_status matmul_q(const char* what, float* y, const void* x, int32_t x_dtype,
+                            const uint8_t* data, const void* scale, const ExpertFormat& f, int32_t s,
+                            int32_t i, int32_t o, void* stream) {
+  if (!y || !x || !data || !scale) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  if (s < 0 || i <= 0 || o < 0) return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d o=%d", what, s, i, o);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t ws = matmul_q_workspace_bytes(s, i);
+  void* buf = nullptr;
+  RMOE_CUDA(cudaMallocAsync(&buf, ws, st), "matmul workspace");
+  cudaError_t e = launch_matmul_q(y, x, x_dtype == RMOE_BF16 ? kBF16 : kF32, data, scale, f, s, i, o, buf, ws, st);
+  cudaError_t e2 = cudaFreeAsync(buf, st);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  if (e2 != cudaSuccess) return cuda_fail(e2, what);
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_matmul_mxfp4(float* y, const void* x, int32_t x_dtype,
+                                         const uint8_t* data, const uint8_t* block_scale, int32_t s,
+                                         int32_t i, int32_t o, void* stream) {
+  return matmul_q("rmoe_matmul_mxfp4", y, x, x_dtype, data, block_scale, ExpertFormat{kMxfp4, 32, kF32},
+                  s, i, o, stream);
+}
+
+extern "C" rmoe_status rmoe_matmul_i4_grouped(float* y, const void* x, int32_t x_dtype,
+                                              const uint8_t* q4, const void* scale,
+                                              int32_t scale_dtype, int32_t group_size, int32_t s,
+                                              int32_t i, int32_t o, void* stream) {
+  if (group_size <= 0) return fail(RMOE_INVALID_ARG, "rmoe_matmul_i4_grouped: group_size %d", group_size);
+  if (scale_dtype != RMOE_F32 && scale_dtype != RMOE_BF16)
+    return fail(RMOE_INVALID_ARG, "rmoe_matmul_i4_grouped: scale_dtype %d", scale_dtype);
+  return matmul_q("rmoe_matmul_i4_grouped", y, x, x_dtype, q4, scale,
+                  ExpertFormat{kInt4g, group_size, scale_dtype == RMOE_BF16 ? kBF16 : kF32}, s, i, o, stream);
+}
+
+extern "C" rmoe_status rmoe_matmul_f32(float* y, const void* x, int32_t x_dtype, const void* w,
+                                       int32_t w_dtype, int32_t s, int32_t i, int32_t o, void* stream) {
+  if (!y || !x || !w) return fail(RMOE_INVALID_ARG, "rmoe_matmul_f32: null pointer");
+  if (s < 0 || i <= 0 || o < 0) return fail(RMOE_INVALID_ARG, "rmoe_matmul_f32: s=%d i=%d o=%d", s, i, o);
+  cudaError_t e = launch_router_logits_exact(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, w,
+                                             w_dtype == RMOE_BF16 ? kBF16 : kF32, y, s, i, o,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmoe_matmul_f32");
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_synth_bytes(void* dst, size_t n, uint64_t key, int32_t mode, int32_t lo,
+                                        int32_t hi, void* stream) {
+  if (!dst && n) return fail(RMOE_INVALID_ARG, "rmoe_synth_bytes: null dst");
+  if (mode != 0 && mode != 1) return fail(RMOE_INVALID_ARG, "rmoe_synth_bytes: mode %d", mode);
+  cudaError_t e = launch_synth_bytes(dst, n, key, mode, lo, hi, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmoe_synth_bytes");
+  return RMOE_OK;
+}

@@ -1,0 +1,117 @@
+// kernels.h -- host-side launchers of the routed-MoE kernels (internal to librmoe.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace rmoe {
+
+// Where one expert's six tensors live on the device. gate/up: [inter, hidden]; down:
+// [hidden, inter]. scales are E8M0 bytes (MXFP4) or f32/bf16 per group (int4).
+struct ExpertPtrs {
+  const uint8_t* gate;
+  const uint8_t* up;
+  const uint8_t* down;
+  const void* gate_scale;
+  const void* up_scale;
+  const void* down_scale;
+};
+
+// Format of every expert of a layer.
+struct ExpertFormat {
+  int fmt;          // kMxfp4 | kInt4g
+  int group_size;   // int4 elements per scale (multiple of 32); 32 for MXFP4
+  int scale_dtype;  // int4 scale storage kF32 | kBF16
+};
+
+// Device-side expert table: local routed experts are contiguous, `stride` bytes apart, each
+// laid out [gate data][up data][down data][gate scales][up scales][down scales]; the shared
+// expert (if any) has its own pointers and width.
+struct ExpertTable {
+  const uint8_t* base;
+  size_t stride;
+  size_t off_up, off_down, off_gs, off_us, off_ds;  // byte offsets inside one expert
+  int n_local;                                      // local routed experts
+  int inter;                                        // routed expert width
+  ExpertPtrs shared;
+  int shared_inter;                                 // 0 = no shared expert
+};
+
+// One group of up to MT positions of one expert ("chunk"), the unit the GEMV kernels stream
+// an expert's weights for. Built on the device by the dispatch kernel.
+struct DispatchBuffers {
+  // sizes: E_loc = local routed experts (+1 slot for the shared expert)
+  uint32_t* bits;       // [E_loc][words] token bitmap per expert
+  int32_t* first_occ;   // [E_loc] first (t*k+j) that picked the expert
+  int32_t* wpre;        // [E_loc][words] exclusive popcount prefix per word
+  int32_t* counts;      // [E_loc + 1]
+  int32_t* offsets;     // [E_loc + 2]
+  int32_t* uniq;        // [E_loc]
+  int32_t* n_uniq;      // [1]
+  int32_t* perm_tok;    // [P] token of each position
+  float* perm_w;        // [P] combine weight of each position (routing weight or shared gate)
+  int32_t* inv;         // [T][k] position of (t, j); -1 when the slot is not local
+  int32_t* ch_expert;   // [max_chunks] local expert index (n_local = the shared expert)
+  int32_t* ch_pos;      // [max_chunks] first position
+  int32_t* ch_n;        // [max_chunks] positions in the chunk (<= MT)
+  int32_t* ch_task_gu;  // [max_chunks + 1] prefix of gate/up warp tasks
+  int32_t* ch_task_dn;  // [max_chunks + 1] prefix of down warp tasks
+  int32_t* n_chunks;    // [1]
+  int words;            // ceil(max_tokens / 32)
+  int max_chunks;
+};
+
+// ---- router (router.cu) ----
+// logits[T][E] = exact reference chain of x[t] . w[e] (fmul then fadd per element, from -0.0)
+cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
+                                       float* logits, int T, int H, int E, cudaStream_t st);
+// Qwen: top-k by (logit+bias desc, id asc), softmax over the winners.
+cudaError_t launch_topk_softmax(const float* logits, const float* bias, int T, int E, int k,
+                                int32_t* ids, float* w, cudaStream_t st);
+// GLM noaux_tc: sigmoid, +bias for selection, group top-2 sums, grouped top-k, normalize.
+cudaError_t launch_topk_grouped(const float* logits, const float* bias, int T, int E, int k,
+                                int n_group, int topk_group, int norm_topk, float routed_scale,
+                                int32_t* ids, float* w, cudaStream_t st);
+
+// ---- dispatch (dispatch.cu) ----
+// e_begin/e_end: the local routed expert range. mt: positions per chunk. has_shared: append
+// the shared expert's T positions (weights from shared_gate[t], or 1).
+cudaError_t launch_dispatch(const int32_t* ids, const float* w, int T, int k, int e_begin,
+                            int e_end, int mt, int has_shared, const float* shared_gate_w,
+                            int inter, int shared_inter, int hidden, int rows_per_task_gu,
+                            int rows_per_task_dn, const DispatchBuffers& d, cudaStream_t st);
+
+// ---- expert compute (experts.cu) ----
+// x[T][H] -> xq[T][H] f16 (power-of-two scaled, format pairing), xexp[T] (the exponent), and
+// the Qwen shared gate sigmoid(x . g) (g may be null -> 1).
+cudaError_t launch_prep_tokens(const void* x, int x_dtype, int T, int H, int fmt,
+                               const float* shared_gate_vec, uint16_t* xq, int32_t* xexp,
+                               float* gate_out, cudaStream_t st);
+cudaError_t launch_gemv_gate_up(const ExpertTable& tab, const ExpertFormat& f,
+                                const DispatchBuffers& d, const uint16_t* xq,
+                                const int32_t* xexp, int H, int mt, int max_tasks, float* h,
+                                uint32_t* hmax, int h_ld, cudaStream_t st);
+// total_pos: device int holding the number of positions (offsets[n_slots]).
+cudaError_t launch_quant_h(const float* h, const uint32_t* hmax, const int32_t* total_pos,
+                           int P_max, int inter_ld, int fmt, uint16_t* hq, int32_t* hexp,
+                           cudaStream_t st);
+cudaError_t launch_gemv_down(const ExpertTable& tab, const ExpertFormat& f,
+                             const DispatchBuffers& d, const uint16_t* hq, const int32_t* hexp,
+                             int H, int mt, int max_tasks, int h_ld, float* y, cudaStream_t st);
+// shared_slot: index of the shared expert in d.offsets (= local routed experts).
+cudaError_t launch_combine(const float* y, const DispatchBuffers& d, const float* rw, int T,
+                           int k, int H, int shared_slot, int has_shared, float* out,
+                           cudaStream_t st);
+
+// ---- generic GEMM entry points (experts.cu) ----
+cudaError_t launch_matmul_q(float* y, const void* x, int x_dtype, const uint8_t* data,
+                            const void* scale, const ExpertFormat& f, int s, int i, int o,
+                            void* workspace, size_t ws_bytes, cudaStream_t st);
+size_t matmul_q_workspace_bytes(int s, int i);
+
+// ---- synthetic bytes (synth.cu) ----
+cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,
+                               cudaStream_t st);
+
+}  // namespace rmoe

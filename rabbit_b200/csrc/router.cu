@@ -1,0 +1,371 @@
+// router.cu -- router logits (bit-exact with the reference's sequential f32 dot) and the
+// warp-per-token top-k selectors (softmax/renormalise for Qwen, sigmoid+bias grouped for GLM).
+#include <float.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rmoe {
+
+// ---------------------------------------------------------------------------------------
+// Exact router logits. rabbit's kernels::matmul (src/kernels.rs:113-124) computes every logit
+// as `xs.iter().zip(wr).map(|(a, b)| a * b).sum()`: a left-to-right chain of separately rounded
+// f32 multiplies and adds starting from -0.0. Routing indices are only bit-exact if every logit
+// is, so each output element here is exactly that chain (__fmul_rn / __fadd_rn cannot be
+// contracted into FMAs). Parallelism comes from the (token, expert) grid, never from the sum.
+// ---------------------------------------------------------------------------------------
+
+// Small T: a block is 32 experts (lanes) x BT tokens (warps). The [32 x KC] weight tile and
+// [BT x KC] token tile are staged in shared memory.
+template <int BT>
+__global__ void __launch_bounds__(32 * BT) router_exact_small_kernel(
+    const void* __restrict__ x, int x_dtype, const void* __restrict__ w, int w_dtype,
+    float* __restrict__ logits, int T, int H, int E) {
+  constexpr int KC = 64;
+  __shared__ float ws[32][KC + 1];
+  __shared__ float xs[BT][KC];
+  const int lane = threadIdx.x, ty = threadIdx.y;
+  const int tid = ty * 32 + lane;
+  const int e0 = blockIdx.x * 32, t0 = blockIdx.y * BT;
+  const int e = e0 + lane, t = t0 + ty;
+  float acc = -0.0f;
+  constexpr int NT = 32 * BT;
+  for (int k0 = 0; k0 < H; k0 += KC) {
+    const int kc = min(KC, H - k0);
+    __syncthreads();
+    for (int q = tid; q < 32 * KC; q += NT) {
+      int r = q / KC, c = q % KC;
+      float v = 0.0f;
+      if (e0 + r < E && c < kc) v = load_elem(w, w_dtype, static_cast<size_t>(e0 + r) * H + k0 + c);
+      ws[r][c] = v;
+    }
+    for (int q = tid; q < BT * KC; q += NT) {
+      int r = q / KC, c = q % KC;
+      float v = 0.0f;
+      if (t0 + r < T && c < kc) v = load_elem(x, x_dtype, static_cast<size_t>(t0 + r) * H + k0 + c);
+      xs[r][c] = v;
+    }
+    __syncthreads();
+    for (int c = 0; c < kc; c++) acc = __fadd_rn(acc, __fmul_rn(xs[ty][c], ws[lane][c]));
+  }
+  if (e < E && t < T) logits[static_cast<size_t>(t) * E + e] = acc;
+}
+
+// Large T: 64 tokens x 64 experts per 256-thread block, each thread 4x4 independent chains
+// (register tiling only re-uses operands; every chain still walks k in order).
+__global__ void __launch_bounds__(256) router_exact_tiled_kernel(
+    const void* __restrict__ x, int x_dtype, const void* __restrict__ w, int w_dtype,
+    float* __restrict__ logits, int T, int H, int E) {
+  constexpr int BM = 64, BN = 64, KC = 16;
+  __shared__ __align__(16) float xs[KC][BM + 4];
+  __shared__ __align__(16) float ws[KC][BN + 4];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int t0 = blockIdx.y * BM, e0 = blockIdx.x * BN;
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; a++)
+#pragma unroll
+    for (int b = 0; b < 4; b++) acc[a][b] = -0.0f;
+  // each thread stages 4 elements of each tile: row = tid / 4, cols 4*(tid%4) .. +3
+  const int lr = threadIdx.x / 4, lc = (threadIdx.x % 4) * 4;
+  for (int k0 = 0; k0 < H; k0 += KC) {
+    float xv[4], wv[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      int kk = k0 + lc + q;
+      xv[q] = (t0 + lr < T && kk < H) ? load_elem(x, x_dtype, static_cast<size_t>(t0 + lr) * H + kk) : 0.0f;
+      wv[q] = (e0 + lr < E && kk < H) ? load_elem(w, w_dtype, static_cast<size_t>(e0 + lr) * H + kk) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      xs[lc + q][lr] = xv[q];
+      ws[lc + q][lr] = wv[q];
+    }
+    __syncthreads();
+    const int kc = min(KC, H - k0);
+    if (kc == KC) {
+#pragma unroll
+      for (int c = 0; c < KC; c++) {
+        float4 xa = *reinterpret_cast<const float4*>(&xs[c][ty * 4]);
+        float4 wb = *reinterpret_cast<const float4*>(&ws[c][tx * 4]);
+        const float xr[4] = {xa.x, xa.y, xa.z, xa.w};
+        const float wr[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int b = 0; b < 4; b++) acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(xr[a], wr[b]));
+      }
+    } else {
+      for (int c = 0; c < kc; c++) {
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int b = 0; b < 4; b++)
+            acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(xs[c][ty * 4 + a], ws[c][tx * 4 + b]));
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; a++) {
+    int t = t0 + ty * 4 + a;
+    if (t >= T) continue;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      int e = e0 + tx * 4 + b;
+      if (e < E) logits[static_cast<size_t>(t) * E + e] = acc[a][b];
+    }
+  }
+}
+
+cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
+                                       float* logits, int T, int H, int E, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (T >= 64) {
+    dim3 grid((E + 63) / 64, (T + 63) / 64);
+    router_exact_tiled_kernel<<<grid, 256, 0, st>>>(x, x_dtype, w, w_dtype, logits, T, H, E);
+  } else if (T == 1) {
+    dim3 grid((E + 31) / 32, 1);
+    router_exact_small_kernel<1><<<grid, dim3(32, 1), 0, st>>>(x, x_dtype, w, w_dtype, logits, T, H, E);
+  } else {
+    dim3 grid((E + 31) / 32, (T + 7) / 8);
+    router_exact_small_kernel<8><<<grid, dim3(32, 8), 0, st>>>(x, x_dtype, w, w_dtype, logits, T, H, E);
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Top-k selection, one warp per token.
+// ---------------------------------------------------------------------------------------
+
+// (value desc, id asc) total order: true when (va, ia) ranks ahead of (vb, ib).
+__device__ __forceinline__ bool ranks_ahead(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+// Warp argmax over per-lane candidates under ranks_ahead; returns the winner to all lanes.
+__device__ __forceinline__ void warp_argmax(float& v, int& id) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(kFull, v, o);
+    int oid = __shfl_xor_sync(kFull, id, o);
+    if (ranks_ahead(ov, oid, v, id)) {
+      v = ov;
+      id = oid;
+    }
+  }
+}
+
+constexpr int kMaxE = 1024;  // experts per token held in registers: 32 lanes x PL
+
+// qwen38::moe::route (src/qwen38/moe.rs:41-76). Its strict-'>' running insertion keeps the k
+// largest logits ordered by (logit desc, id asc) -- a total order, so k rounds of a warp argmax
+// pick the same ids in the same rank order. Weights: exp(l - l_max) over the k winners, summed
+// left to right from +0.0, each divided by the sum.
+template <int PL>
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                    int T, int E, int k, int32_t* __restrict__ ids,
+                                    float* __restrict__ wout) {
+  const int warps = blockDim.x / 32;
+  const int t = blockIdx.x * warps + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  float v[PL];
+  const float* row = logits + static_cast<size_t>(t) * E;
+#pragma unroll
+  for (int q = 0; q < PL; q++) {
+    int e = q * 32 + lane;
+    float l = -INFINITY;
+    if (e < E) {
+      l = row[e];
+      if (bias) l = __fadd_rn(l, bias[e]);
+    }
+    v[q] = l;
+  }
+  unsigned taken = 0;
+  float sel_v = 0.0f;  // lane j keeps the j-th winner
+  int sel_id = -1;
+  const int kk = min(k, E);
+  for (int r = 0; r < kk; r++) {
+    float bv = -INFINITY;
+    int bid = 0x7fffffff;
+#pragma unroll
+    for (int q = 0; q < PL; q++) {
+      int e = q * 32 + lane;
+      if (e < E && !((taken >> q) & 1) && ranks_ahead(v[q], e, bv, bid)) {
+        bv = v[q];
+        bid = e;
+      }
+    }
+    warp_argmax(bv, bid);
+    if (lane == r) {
+      sel_v = bv;
+      sel_id = bid;
+    }
+    if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
+  }
+  const float mx = __shfl_sync(kFull, sel_v, 0);
+  float ex = (lane < kk) ? exp_f32(__fsub_rn(sel_v, mx)) : 0.0f;
+  float sum = 0.0f;
+  for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, ex, j));
+  if (lane < kk) {
+    ids[static_cast<size_t>(t) * k + lane] = sel_id;
+    wout[static_cast<size_t>(t) * k + lane] = __fdiv_rn(ex, sum);
+  } else if (lane < k) {
+    ids[static_cast<size_t>(t) * k + lane] = -1;
+    wout[static_cast<size_t>(t) * k + lane] = 0.0f;
+  }
+}
+
+template <int PL>
+static void launch_softmax_pl(const float* logits, const float* bias, int T, int E, int k,
+                              int32_t* ids, float* w, cudaStream_t st) {
+  const int warps = 8;
+  topk_softmax_kernel<PL><<<(T + warps - 1) / warps, warps * 32, 0, st>>>(logits, bias, T, E, k, ids, w);
+}
+
+cudaError_t launch_topk_softmax(const float* logits, const float* bias, int T, int E, int k,
+                                int32_t* ids, float* w, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (E > kMaxE || k > 32 || k < 1) return cudaErrorInvalidValue;
+  if (E <= 32) launch_softmax_pl<1>(logits, bias, T, E, k, ids, w, st);
+  else if (E <= 64) launch_softmax_pl<2>(logits, bias, T, E, k, ids, w, st);
+  else if (E <= 128) launch_softmax_pl<4>(logits, bias, T, E, k, ids, w, st);
+  else if (E <= 256) launch_softmax_pl<8>(logits, bias, T, E, k, ids, w, st);
+  else if (E <= 512) launch_softmax_pl<16>(logits, bias, T, E, k, ids, w, st);
+  else launch_softmax_pl<32>(logits, bias, T, E, k, ids, w, st);
+  return cudaGetLastError();
+}
+
+// glm52::moe::route (src/glm52/moe.rs:131-260) for one token per warp:
+//   logit_e = sigmoid(l_e) (1/(1+exp(-l)) in f32), choice_e = logit_e + bias_e;
+//   group score = top2_sum of choice over each of n_group contiguous groups (:193-205);
+//   keep the topk_group best groups, ties to the lower group index (:214-229);
+//   k rounds of a strict '>' scan from -1e30 over allowed, untaken experts (ties -> lower id);
+//   weight = plain logit; norm_topk: divide by (sum from -0.0) + 1e-20; times routed_scale.
+template <int PL>
+__global__ void topk_grouped_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                    int T, int E, int k, int n_group, int topk_group,
+                                    int norm_topk, float routed_scale, int32_t* __restrict__ ids,
+                                    float* __restrict__ wout) {
+  extern __shared__ float choice_smem[];  // [warps][E]
+  const int warps = blockDim.x / 32;
+  const int wi = threadIdx.x / 32;
+  const int t = blockIdx.x * warps + wi;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  float* cs = choice_smem + static_cast<size_t>(wi) * E;
+  float sg[PL], ch[PL];
+  const float* row = logits + static_cast<size_t>(t) * E;
+#pragma unroll
+  for (int q = 0; q < PL; q++) {
+    int e = q * 32 + lane;
+    float s = 0.0f, c = -INFINITY;
+    if (e < E) {
+      s = sigmoid_ref(row[e]);
+      c = __fadd_rn(s, bias ? bias[e] : 0.0f);
+      cs[e] = c;
+    }
+    sg[q] = s;
+    ch[q] = c;
+  }
+  __syncwarp();
+  unsigned allowed_groups = 0xffffffffu;
+  const int gsz = n_group > 1 ? E / n_group : E;
+  if (n_group > 1) {
+    // lane g scans group g in index order exactly as top2_sum does
+    float score = -INFINITY;
+    if (lane < n_group) {
+      float t1 = -INFINITY, t2 = -INFINITY;
+      for (int i = 0; i < gsz; i++) {
+        float val = cs[lane * gsz + i];
+        if (val > t1) {
+          t2 = t1;
+          t1 = val;
+        } else if (val > t2) {
+          t2 = val;
+        }
+      }
+      score = isfinite(t2) ? __fadd_rn(t1, t2) : t1;
+    }
+    allowed_groups = 0;
+    for (int r = 0; r < topk_group && r < n_group; r++) {
+      bool cand = lane < n_group && !((allowed_groups >> lane) & 1);
+      float bv = cand ? score : -INFINITY;
+      int bid = cand ? lane : 0x7fffffff;
+      warp_argmax(bv, bid);
+      if (bid < n_group) allowed_groups |= 1u << bid;
+    }
+  }
+  const int n_allowed = n_group > 1 ? __popc(allowed_groups) * gsz : E;
+  const int kk = min(k, n_allowed);
+  float sel_w = 0.0f;
+  int sel_id = -1;
+  unsigned taken = 0;
+  for (int r = 0; r < kk; r++) {
+    float bv = -1e30f;
+    int bid = 0x7fffffff;
+#pragma unroll
+    for (int q = 0; q < PL; q++) {
+      int e = q * 32 + lane;
+      if (e >= E || ((taken >> q) & 1)) continue;
+      if (n_group > 1 && !((allowed_groups >> (e / gsz)) & 1)) continue;
+      if (ch[q] > bv) {  // strict '>' from -1e30, ids ascending within the lane
+        bv = ch[q];
+        bid = e;
+      }
+    }
+    warp_argmax(bv, bid);
+    float wv = 0.0f;
+    const bool found = bid != 0x7fffffff;
+    if (found && (bid & 31) == lane) {
+      taken |= 1u << (bid >> 5);
+#pragma unroll
+      for (int q = 0; q < PL; q++)
+        if (q == (bid >> 5)) wv = sg[q];
+    }
+    wv = __shfl_sync(kFull, wv, found ? (bid & 31) : 0);
+    if (lane == r) {
+      sel_id = found ? bid : -1;
+      sel_w = found ? wv : 0.0f;
+    }
+  }
+  if (norm_topk) {
+    float sum = -0.0f;
+    for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, sel_w, j));
+    sum = __fadd_rn(sum, 1e-20f);
+    sel_w = __fdiv_rn(sel_w, sum);
+  }
+  sel_w = __fmul_rn(sel_w, routed_scale);
+  if (lane < k) {
+    ids[static_cast<size_t>(t) * k + lane] = lane < kk ? sel_id : -1;
+    wout[static_cast<size_t>(t) * k + lane] = lane < kk ? sel_w : 0.0f;
+  }
+}
+
+template <int PL>
+static void launch_grouped_pl(const float* logits, const float* bias, int T, int E, int k,
+                              int n_group, int topk_group, int norm_topk, float routed_scale,
+                              int32_t* ids, float* w, cudaStream_t st) {
+  const int warps = 8;
+  size_t smem = static_cast<size_t>(warps) * E * sizeof(float);
+  topk_grouped_kernel<PL><<<(T + warps - 1) / warps, warps * 32, smem, st>>>(
+      logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w);
+}
+
+cudaError_t launch_topk_grouped(const float* logits, const float* bias, int T, int E, int k,
+                                int n_group, int topk_group, int norm_topk, float routed_scale,
+                                int32_t* ids, float* w, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (E > kMaxE || k > 32 || k < 1 || n_group > 32) return cudaErrorInvalidValue;
+  if (n_group > 1 && E % n_group != 0) return cudaErrorInvalidValue;
+  if (E <= 32) launch_grouped_pl<1>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 64) launch_grouped_pl<2>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 128) launch_grouped_pl<4>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 256) launch_grouped_pl<8>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 512) launch_grouped_pl<16>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
+  else launch_grouped_pl<32>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
+  return cudaGetLastError();
+}
+
+}  // namespace rmoe

@@ -1,0 +1,124 @@
+"""Whole-layer GPU parity against the CPU oracle on the BASELINE configs: routing bit-exact,
+layer output within 1e-2 relative L2 (the north star's bf16-accumulation tolerance)."""
+import numpy as np
+import pytest
+
+from helpers import build_layer, oracle_forward, oracle_routing, x_device
+from rabbit_b200 import synth
+from refvec import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+OUT_RTOL = 1e-2  # relative L2 of the layer output vs the reference
+
+
+@pytest.fixture(scope="module")
+def qwen_layer(cuda_ctx):
+    cfg = synth.CONFIGS["c2_qwen_prefill"]
+    L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    yield cfg, L
+    L.close()
+
+
+def test_c0_tiny_layer_matches_oracle(cuda_ctx):
+    cfg = synth.CONFIGS["c0_tiny"]
+    L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    x = synth.activations(cfg)
+    out, ids, w = L.moe_forward(x_device(cfg, x), return_routing=True)
+    want, want_ids, want_w = oracle_forward(cfg, x)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.max(np.abs(w.cpu().numpy() - want_w)) < 1e-6
+    assert rel_l2(out.cpu().numpy(), want) < OUT_RTOL
+    L.close()
+
+
+def test_c0_tiny_ragged_token_counts(cuda_ctx):
+    """T = 1..4 on a max_tokens = 4 layer: every prefix routes and combines like the oracle."""
+    cfg = synth.CONFIGS["c0_tiny"]
+    L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    xa = synth.activations(cfg)
+    for T in range(1, cfg.tokens + 1):
+        x = xa[:T]
+        out, ids, _ = L.moe_forward(x_device(cfg, x), return_routing=True)
+        want, want_ids, _ = oracle_forward(cfg, x)
+        assert np.array_equal(ids.cpu().numpy(), want_ids)
+        assert rel_l2(out.cpu().numpy(), want) < OUT_RTOL
+    L.close()
+
+
+def test_c1_decode_one_token_matches_oracle(qwen_layer):
+    cfg, L = qwen_layer
+    c1 = synth.CONFIGS["c1_qwen_decode"]
+    x = synth.activations(c1)
+    out, ids, w = L.moe_forward(x_device(c1, x), return_routing=True)
+    want, want_ids, want_w = oracle_forward(c1, x)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.max(np.abs(w.cpu().numpy() - want_w)) < 1e-6
+    assert rel_l2(out.cpu().numpy(), want) < OUT_RTOL
+
+
+def test_c2_prefill_routing_exact_and_output_subset(qwen_layer):
+    """All 2048 tokens route bit-exactly; the output of a token subset matches the oracle (the
+    layer is per-token independent, so the subset's reference output is the same)."""
+    cfg, L = qwen_layer
+    x = synth.activations(cfg)
+    out, ids, w = L.moe_forward(x_device(cfg, x), return_routing=True)
+    want_ids, want_w = oracle_routing(cfg, x)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.max(np.abs(w.cpu().numpy() - want_w)) < 1e-6
+    sel = [0, 777, 2047]
+    want, _, _ = oracle_forward(cfg, x[sel])
+    assert rel_l2(out.cpu().numpy()[sel], want) < OUT_RTOL
+
+
+def test_host_entry_point_matches_device_path(qwen_layer):
+    """rmoe_moe_forward_host (the Rust call-site signature: host slices in and out)."""
+    import torch
+
+    cfg, L = qwen_layer
+    x = synth.activations(cfg, tokens=4)
+    dev = L.moe_forward(x_device(cfg, x)).cpu().numpy()
+    host = L.moe_forward_host(synth.f32_to_bf16_bits(x))
+    assert np.array_equal(dev, host)
+    pinned = torch.from_numpy(synth.f32_to_bf16_bits(x).view(np.int16)).pin_memory()
+    out = L.moe_forward_host(pinned.view(torch.bfloat16))
+    assert np.array_equal(dev, out)
+
+
+def test_c4_glm_int4_layer(cuda_ctx):
+    cfg = synth.CONFIGS["c4_glm_int4"]
+    L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens, scale_dtype="bf16")
+    x = synth.activations(cfg)
+    out, ids, w = L.moe_forward(x_device(cfg, x), return_routing=True)
+    want_ids, want_w = oracle_routing(cfg, x)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.max(np.abs(w.cpu().numpy() - want_w)) < 1e-5
+    sel = [3, 300]
+    want, _, _ = oracle_forward(cfg, x[sel])
+    assert rel_l2(out.cpu().numpy()[sel], want) < OUT_RTOL
+    L.close()
+
+
+def test_shape_and_argument_errors(cuda_ctx):
+    import torch
+
+    import rabbit_b200 as rb
+
+    cfg = synth.CONFIGS["c0_tiny"]
+    L = rb.MoeLayer(cuda_ctx, cfg.hidden, cfg.inter, cfg.n_experts, cfg.topk, max_tokens=2)
+    good = synth.expert(cfg, 0)
+    with pytest.raises(rb.RmoeError, match="SHAPE_MISMATCH"):
+        L.upload_expert(0, good["gate"][:-1], good["gate_scale"], good["up"], good["up_scale"],
+                        good["down"], good["down_scale"])
+    with pytest.raises(rb.RmoeError, match="INVALID_ARG"):
+        L.upload_expert_dict(cfg.n_experts, good)
+    with pytest.raises(rb.RmoeError, match="INVALID_ARG"):  # router never uploaded
+        L.route(torch.zeros((1, cfg.hidden), device="cuda"))
+    L.upload_router(synth.router_weights(cfg))
+    with pytest.raises(rb.RmoeError, match="INVALID_ARG"):  # T > max_tokens
+        L.route(torch.zeros((3, cfg.hidden), device="cuda"))
+    with pytest.raises(rb.RmoeError, match="INVALID_ARG"):  # experts missing
+        L.moe_forward(torch.zeros((1, cfg.hidden), device="cuda"))
+    with pytest.raises(rb.RmoeError, match="NOT_SUPPORTED"):
+        rb.MoeLayer(cuda_ctx, 100, 32, 4, 2)
+    L.close()
