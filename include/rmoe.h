@@ -83,6 +83,8 @@ typedef struct rmoe_layer_stats {
   uint64_t forward_calls;
   uint64_t tokens_routed;
   uint64_t kernel_launches;      /* this library's kernels launched by forward calls */
+  uint64_t router_fallbacks;     /* tokens whose fast-router certificate failed and were
+                                    re-ranked on exact reference-order logits */
   uint64_t device_bytes;         /* resident expert + router bytes */
   int32_t local_expert_begin;    /* experts [begin, end) are resident on this device */
   int32_t local_expert_end;

@@ -86,6 +86,8 @@ struct rmoe_layer {
   // workspace
   int max_tokens = 0, P_max = 0, h_ld = 0;
   float* logits = nullptr;
+  float* logit_err = nullptr;
+  unsigned* fallbacks = nullptr;
   int32_t* ids = nullptr;
   float* rw = nullptr;
   DispatchBuffers d{};
@@ -297,6 +299,12 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   const int words = (T + 31) / 32;
   const int max_chunks = L->P_max + n_slots + 1;
   ALLOC(L->logits, static_cast<size_t>(T) * E);
+  ALLOC(L->logit_err, static_cast<size_t>(std::min(T, 32)) * E);
+  ALLOC(L->fallbacks, 1);
+  {
+    cudaError_t e = cudaMemset(L->fallbacks, 0, 4);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset"));
+  }
   ALLOC(L->ids, static_cast<size_t>(T) * k);
   ALLOC(L->rw, static_cast<size_t>(T) * k);
   DispatchBuffers& d = L->d;
@@ -358,6 +366,10 @@ extern "C" rmoe_status rmoe_layer_destroy(rmoe_layer* L) {
 extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stats* out) {
   if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_stats: null argument");
   *out = L->stats;
+  unsigned fb = 0;
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  RMOE_CUDA(cudaMemcpy(&fb, L->fallbacks, 4, cudaMemcpyDeviceToHost), "read fallback counter");
+  out->router_fallbacks = fb;
   return RMOE_OK;
 }
 
@@ -558,6 +570,12 @@ extern "C" rmoe_status rmoe_route(rmoe_layer* L, const void* x, int32_t x_dtype,
   return RMOE_OK;
 }
 
+// The decode-sized front end: softmax router, T <= 32, H a multiple of 256.
+static bool small_path(const rmoe_layer* L, int T) {
+  return T <= 32 && L->desc.router_kind == RMOE_ROUTER_SOFTMAX_TOPK && L->desc.hidden % 256 == 0 &&
+         L->desc.topk <= 32;
+}
+
 static int chunk_tokens(int T) { return T >= 8 ? 8 : (T >= 4 ? 4 : (T >= 2 ? 2 : 1)); }
 
 static rmoe_status dispatch_into(rmoe_layer* L, int T, int mt, const float* gate, cudaStream_t st) {
@@ -599,18 +617,44 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
       return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: expert %d was never uploaded", L->e_begin + s);
   if (L->has_shared && !L->has_shared_w) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: shared expert never uploaded");
   StageMarks marks(L, st);
-  marks.mark();
-  rmoe_status s = route_into(L, x, x_dtype, T, st, &marks);
-  if (s != RMOE_OK) return s;
-  marks.mark();  // end of top-k
   const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
   const bool gated = L->has_shared && D.shared_gated;
-  cudaError_t e = launch_prep_tokens(x, xdt, T, H, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr,
-                                     L->xq, L->xexp, L->gate, st);
-  if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
-  marks.mark();
   const int mt = chunk_tokens(T);
-  if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st)) != RMOE_OK) return s;
+  rmoe_status s = RMOE_OK;
+  cudaError_t e = cudaSuccess;
+  int launches = 10;
+  if (small_path(L, T)) {
+    // certified router + one-block front end (top-k, dispatch, activation prep)
+    marks.mark();
+    e = launch_router_certified(x, xdt, L->router, L->router_dtype, L->logits, L->logit_err, T, H,
+                                D.n_experts, st);
+    if (e != cudaSuccess) return cuda_fail(e, "certified router");
+    marks.mark();
+    SmallPrologue a{};
+    a.T = T; a.E = D.n_experts; a.k = k; a.H = H; a.mt = mt;
+    a.e_begin = L->e_begin; a.e_end = L->e_end; a.n_loc = L->n_loc;
+    a.has_shared = L->has_shared ? 1 : 0; a.fmt = L->fmt.fmt;
+    a.tpc_gu = D.moe_inter / 2; a.tpc_gu_shared = D.shared_inter / 2; a.tpc_dn = H / 4;
+    a.mid = L->logits; a.err = L->logit_err; a.bias = L->has_bias ? L->router_bias : nullptr;
+    a.x = x; a.x_dtype = xdt; a.w = L->router; a.w_dtype = L->router_dtype;
+    a.gvec = gated ? L->shared_gate_vec : nullptr;
+    a.ids = L->ids; a.rw = L->rw; a.xq = L->xq; a.xexp = L->xexp; a.gate = L->gate;
+    a.fallback_count = L->fallbacks;
+    e = launch_prologue_small(a, L->d, st);
+    if (e != cudaSuccess) return cuda_fail(e, "small-T prologue");
+    marks.mark();  // prep and dispatch are folded into the prologue
+    launches = 6;
+  } else {
+    marks.mark();
+    s = route_into(L, x, x_dtype, T, st, &marks);
+    if (s != RMOE_OK) return s;
+    marks.mark();  // end of top-k
+    e = launch_prep_tokens(x, xdt, T, H, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr,
+                           L->xq, L->xexp, L->gate, st);
+    if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
+    marks.mark();
+    if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st)) != RMOE_OK) return s;
+  }
   const int P = T * k + (L->has_shared ? T : 0);
   RMOE_CUDA(cudaMemsetAsync(L->hmax, 0, static_cast<size_t>(P) * 4, st), "hmax reset");
   const int n_slots = L->n_loc + (L->has_shared ? 1 : 0);
@@ -631,8 +675,9 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
   if (e != cudaSuccess) return cuda_fail(e, "combine");
   marks.mark();
   marks.commit();
-  // router logits, top-k, prep, dispatch (mark/scan/place), gate/up, quantize h, down, combine
-  L->stats.kernel_launches += 10;
+  // generic: router logits, top-k, prep, dispatch (mark/scan/place), gate/up, quantize h,
+  // down, combine; small-T: certified router, prologue, gate/up, quantize h, down, combine
+  L->stats.kernel_launches += launches;
   const size_t n = static_cast<size_t>(T) * k;
   if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, L->ids, n * 4, cudaMemcpyDefault, st), "ids out");
   if (w_out) RMOE_CUDA(cudaMemcpyAsync(w_out, L->rw, n * 4, cudaMemcpyDefault, st), "weights out");

@@ -62,7 +62,36 @@ struct DispatchBuffers {
   int max_chunks;
 };
 
-// ---- router (router.cu) ----
+constexpr int RMOE_MAX_TOPK_DEV = 32;
+
+// Inputs/outputs of the fused small-T front end (route_small.cu).
+struct SmallPrologue {
+  int T, E, k, H, mt;
+  int e_begin, e_end, n_loc, has_shared, fmt;
+  int tpc_gu, tpc_gu_shared, tpc_dn;  // warp tasks per chunk (gate/up routed, shared; down)
+  const float* mid;                   // [T][E] certified logit values
+  const float* err;                   // [T][E] their error bounds
+  const float* bias;                  // [E] logit bias or null
+  const void* x;
+  int x_dtype;
+  const void* w;                      // router [E][H] (exact fallback chains)
+  int w_dtype;
+  const float* gvec;                  // shared-expert gate vector [H] or null
+  int32_t* ids;                       // [T][k]
+  float* rw;                          // [T][k]
+  uint16_t* xq;                       // [T][H] f16
+  int32_t* xexp;                      // [T]
+  float* gate;                        // [T]
+  unsigned* fallback_count;           // tokens whose certificate failed (exact recompute)
+};
+
+// ---- router (router.cu, route_small.cu) ----
+// Certified logits for T <= 32 tokens (H % 256 == 0): value + rigorous error bound.
+cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, int w_dtype,
+                                    float* mid, float* err, int T, int H, int E, cudaStream_t st);
+// Top-k + certificate (+ exact fallback), dispatch, activation prep in one block.
+cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers& d,
+                                  cudaStream_t st);
 // logits[T][E] = exact reference chain of x[t] . w[e] (fmul then fadd per element, from -0.0)
 cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
                                        float* logits, int T, int H, int E, cudaStream_t st);

@@ -1,0 +1,405 @@
+// route_small.cu -- the decode-sized (T <= 32) front end of the layer in two launches:
+//
+//  1. router_certified_kernel: every router logit as a value plus a rigorous bound on how far
+//     the reference's own sequential f32 chain (kernels::matmul, src/kernels.rs:113-124) can be
+//     from it. A warp per expert, each lane owning one contiguous H/32 slice of the dot product.
+//  2. prologue_small_kernel (one block): top-k with a certificate that the reference picks the
+//     same experts in the same order; tokens whose certificate fails recompute the contending
+//     logits with the exact chain, so routing indices stay bit-exact. Then the dispatch
+//     (positions grouped by expert, ascending token), the chunk lists, and the f16 activations.
+//
+// The bound. The reference computes S^_j = fl(S^_{j-1} + p^_j) with p^_j = fl(x_j w_j), so
+// |S^_n - sum p_j| <= u/(1-u) * sum_j |S^_j| + u * sum_j |p_j| (u = 2^-24). With lane l's slice
+// starting at the exact prefix O_l and local prefixes b_j, sum over the slice of |S_j| is at
+// most c*|O_l| + sum_j |b_j| (c = slice length). The kernel's own f32 evaluation adds at most
+// u * sum_l sum_j |b^_j| (local chains) + 6u * sum_l |B_l| (the 32-lane scan), so
+//   err = (1.01 + 2nu) * u * ( sum_l (c|O_l| + 2 A_l + 6 |B_l|) + P (1 + nu) )
+// with A_l = sum |b_j|, B_l the slice sum, P = sum |p_j|, n = H. Second-order terms are covered
+// by the 1.01 and 2nu factors for any H with n*u < 0.01.
+#include <float.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rmoe {
+
+constexpr int kSmallT = 32;
+
+// 8 consecutive elements of an f32 / bf16 row as f32.
+__device__ __forceinline__ void load8(const void* p, int dtype, size_t idx, float (&v)[8]) {
+  if (dtype == kBF16) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + idx));
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      v[2 * q] = __uint_as_float(w[q] << 16);
+      v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+    }
+  } else {
+    const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(p) + idx);
+    const float4 a = __ldg(f), b = __ldg(f + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// grid: ceil(E/8) blocks of 8 warps; warp = one expert, all T tokens (groups of TB).
+template <int TB>
+__global__ void __launch_bounds__(256) router_certified_kernel(
+    const void* __restrict__ x, int x_dtype, const void* __restrict__ w, int w_dtype,
+    float* __restrict__ mid, float* __restrict__ err, int T, int H, int E) {
+  const int e = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (e >= E) return;
+  const int c = H / 32;  // slice length (multiple of 8)
+  const size_t wrow = static_cast<size_t>(e) * H + static_cast<size_t>(lane) * c;
+  const float u = 5.9604645e-08f;  // 2^-24
+  const float n = static_cast<float>(H);
+  const float safety = 1.01f + 2.0f * n * u;
+  for (int t0 = 0; t0 < T; t0 += TB) {
+    float b[TB], A[TB], P[TB];
+#pragma unroll
+    for (int q = 0; q < TB; q++) b[q] = A[q] = P[q] = 0.0f;
+    for (int j = 0; j < c; j += 8) {
+      float wv[8];
+      load8(w, w_dtype, wrow + j, wv);
+#pragma unroll
+      for (int q = 0; q < TB; q++) {
+        if (t0 + q >= T) break;
+        float xv[8];
+        load8(x, x_dtype, static_cast<size_t>(t0 + q) * H + static_cast<size_t>(lane) * c + j, xv);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float p = __fmul_rn(xv[i], wv[i]);
+          b[q] = __fadd_rn(b[q], p);
+          A[q] += fabsf(b[q]);
+          P[q] += fabsf(p);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < TB; q++) {
+      if (t0 + q >= T) break;
+      // inclusive scan of slice sums across lanes -> exclusive prefix O_l and the total S
+      float incl = b[q];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const float O = incl - b[q];
+      const float S = __shfl_sync(kFull, incl, 31);
+      float term = static_cast<float>(c) * fabsf(O) + 2.0f * A[q] + 6.0f * fabsf(b[q]);
+      float Pt = P[q];
+      term = warp_sum(term);
+      Pt = warp_sum(Pt);
+      if (lane == 0) {
+        const size_t o = static_cast<size_t>(t0 + q) * E + e;
+        mid[o] = S;
+        err[o] = safety * u * (term + Pt * (1.0f + n * u)) + 1e-37f;
+      }
+    }
+  }
+}
+
+cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, int w_dtype,
+                                    float* mid, float* err, int T, int H, int E,
+                                    cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (H % 256 != 0 || T > kSmallT) return cudaErrorInvalidValue;
+  const int blocks = (E + 7) / 8;
+  if (T == 1) router_certified_kernel<1><<<blocks, 256, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
+  else router_certified_kernel<4><<<blocks, 256, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ bool ahead(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+__device__ __forceinline__ void warp_best(float& v, int& id) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(kFull, v, o);
+    const int oid = __shfl_xor_sync(kFull, id, o);
+    if (ahead(ov, oid, v, id)) {
+      v = ov;
+      id = oid;
+    }
+  }
+}
+
+// The reference chain for one (token, expert): a = -0.0; a = fl(a + fl(x_k * w_k)), k ascending.
+__device__ float exact_logit(const void* x, int x_dtype, const void* w, int w_dtype, int t, int e,
+                             int H) {
+  float a = -0.0f;
+  const size_t xo = static_cast<size_t>(t) * H, wo = static_cast<size_t>(e) * H;
+  for (int k = 0; k < H; k += 8) {
+    float xv[8], wv[8];
+    load8(x, x_dtype, xo + k, xv);
+    load8(w, w_dtype, wo + k, wv);
+#pragma unroll
+    for (int i = 0; i < 8; i++) a = __fadd_rn(a, __fmul_rn(xv[i], wv[i]));
+  }
+  return a;
+}
+
+constexpr int kMaxPL = 32;  // experts per lane (E <= 1024)
+
+// One block of 512 threads. Warp w routes tokens w, w + 16, ...; then the block builds the dispatch and
+// converts the activations. Produces exactly what the generic route/dispatch/prep kernels do.
+template <int PL>
+__global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, DispatchBuffers d) {
+  __shared__ int s_ids[kSmallT * RMOE_MAX_TOPK_DEV];
+  __shared__ float s_w[kSmallT * RMOE_MAX_TOPK_DEV];
+  __shared__ int s_pos[kSmallT * RMOE_MAX_TOPK_DEV];
+  __shared__ int s_nch[kSmallT * RMOE_MAX_TOPK_DEV];
+  __shared__ int s_misc[4];
+  const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int T = a.T, E = a.E, k = a.k;
+  const int kk = min(k, E);
+
+  // ---------------- 1. route (warp per token)
+  for (int t = wi; t < T; t += blockDim.x / 32) {
+    float lo[PL], hi[PL], v[PL];
+#pragma unroll
+    for (int q = 0; q < PL; q++) {
+      const int e = q * 32 + lane;
+      if (e < E) {
+        const float m = a.mid[static_cast<size_t>(t) * E + e];
+        const float r = a.err[static_cast<size_t>(t) * E + e];
+        float l = __fsub_rd(m, r), h = __fadd_ru(m, r), vv = m;
+        if (a.bias) {
+          const float bb = a.bias[e];
+          l = __fadd_rn(l, bb);
+          h = __fadd_rn(h, bb);
+          vv = __fadd_rn(vv, bb);
+        }
+        lo[q] = l;
+        hi[q] = h;
+        v[q] = vv;
+      } else {
+        lo[q] = hi[q] = v[q] = -INFINITY;
+      }
+    }
+    // k-th largest lower bound
+    unsigned taken = 0;
+    float Lk = INFINITY;
+    for (int r = 0; r < kk; r++) {
+      float bv = -INFINITY;
+      int bid = 0x7fffffff;
+#pragma unroll
+      for (int q = 0; q < PL; q++) {
+        const int e = q * 32 + lane;
+        if (e < E && !((taken >> q) & 1) && ahead(lo[q], e, bv, bid)) {
+          bv = lo[q];
+          bid = e;
+        }
+      }
+      warp_best(bv, bid);
+      if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
+      Lk = bv;
+    }
+    // contenders: hi >= Lk
+    int n_cont = 0;
+#pragma unroll
+    for (int q = 0; q < PL; q++) {
+      const int e = q * 32 + lane;
+      n_cont += __popc(__ballot_sync(kFull, e < E && hi[q] >= Lk));
+    }
+    // selection by value, then the order certificate
+    auto select = [&](int* sel_id, float* sel_v) {
+      unsigned tk = 0;
+      for (int r = 0; r < kk; r++) {
+        float bv = -INFINITY;
+        int bid = 0x7fffffff;
+#pragma unroll
+        for (int q = 0; q < PL; q++) {
+          const int e = q * 32 + lane;
+          if (e < E && !((tk >> q) & 1) && ahead(v[q], e, bv, bid)) {
+            bv = v[q];
+            bid = e;
+          }
+        }
+        warp_best(bv, bid);
+        if ((bid & 31) == lane) tk |= 1u << (bid >> 5);
+        if (lane == r) {
+          *sel_id = bid;
+          *sel_v = bv;
+        }
+      }
+    };
+    int sel_id = -1;
+    float sel_v = -INFINITY;
+    select(&sel_id, &sel_v);
+    // interval of the winner of each rank
+    float my_lo = -INFINITY, my_hi = INFINITY;
+#pragma unroll
+    for (int q = 0; q < PL; q++) {
+      // fetch lo/hi of expert sel_id: it lives in lane sel_id%32, slot sel_id/32
+      const int src = sel_id >= 0 ? (sel_id & 31) : 0;
+      const float l = __shfl_sync(kFull, lo[q], src);
+      const float h = __shfl_sync(kFull, hi[q], src);
+      if (sel_id >= 0 && q == (sel_id >> 5)) {
+        my_lo = l;
+        my_hi = h;
+      }
+    }
+    const float next_hi = __shfl_down_sync(kFull, my_hi, 1);
+    const bool pair_ok = (lane >= kk - 1) || (my_lo > next_hi);
+    const bool certified = (n_cont == kk) && __all_sync(kFull, pair_ok);
+    if (!certified) {
+      // exact chains for every contender, then select on exact values among them
+      for (int q = 0; q < PL; q++) {
+        const int e = q * 32 + lane;
+        const bool cont = e < E && hi[q] >= Lk;
+        if (cont) {
+          float ex = exact_logit(a.x, a.x_dtype, a.w, a.w_dtype, t, e, a.H);
+          if (a.bias) ex = __fadd_rn(ex, a.bias[e]);
+          v[q] = ex;
+        } else {
+          v[q] = -INFINITY;
+        }
+      }
+      select(&sel_id, &sel_v);
+      if (lane == 0) atomicAdd(a.fallback_count, 1u);
+    }
+    // softmax over the winners (qwen38/moe.rs:64-75): exp(l - max), sum from +0.0, divide
+    const float mx = __shfl_sync(kFull, sel_v, 0);
+    const float exv = lane < kk ? exp_f32(__fsub_rn(sel_v, mx)) : 0.0f;
+    float sum = 0.0f;
+    for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, exv, j));
+    if (lane < k) {
+      const float wv = lane < kk ? __fdiv_rn(exv, sum) : 0.0f;
+      const int id = lane < kk ? sel_id : -1;
+      s_ids[t * k + lane] = id;
+      s_w[t * k + lane] = wv;
+      a.ids[t * k + lane] = id;
+      a.rw[t * k + lane] = wv;
+    }
+  }
+  __syncthreads();
+
+  // ---------------- 2. dispatch: positions grouped by expert id, ascending token inside
+  const int n = T * k;
+  for (int q = threadIdx.x; q < n; q += blockDim.x) {
+    const int e = s_ids[q];
+    const bool local = e >= a.e_begin && e < a.e_end;
+    int pos = -1, nch = 0;
+    if (local) {
+      int less = 0, same = 0, first = 1;
+      const int t = q / k;
+      for (int r = 0; r < n; r++) {
+        const int e2 = s_ids[r];
+        if (e2 < a.e_begin || e2 >= a.e_end) continue;
+        if (e2 < e || (e2 == e && r / k < t)) less++;
+        if (e2 == e) {
+          same++;
+          if (r / k < t) first = 0;
+        }
+      }
+      pos = less;
+      if (first) nch = (same + a.mt - 1) / a.mt;
+    }
+    s_pos[q] = pos;
+    s_nch[q] = nch;  // chunks, counted once per expert on its first (lowest-token) entry
+    d.inv[q] = pos;
+    if (local) {
+      d.perm_tok[pos] = q / k;
+      d.perm_w[pos] = s_w[q];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int routed = 0, chunks = 0;
+    for (int q = 0; q < n; q++) {
+      routed += s_pos[q] >= 0;
+      chunks += s_nch[q];
+    }
+    s_misc[0] = routed;
+    s_misc[1] = chunks;
+  }
+  __syncthreads();
+  const int routed = s_misc[0], routed_chunks = s_misc[1];
+  // chunk lists: each expert's first entry writes its chunks; chunk base = chunks of experts
+  // with a lower position
+  for (int q = threadIdx.x; q < n; q += blockDim.x) {
+    if (s_nch[q] == 0) continue;
+    int base = 0;
+    for (int r = 0; r < n; r++)
+      if (s_nch[r] > 0 && s_pos[r] < s_pos[q]) base += s_nch[r];
+    int cnt = 0;
+    const int e = s_ids[q];
+    for (int r = 0; r < n; r++) cnt += s_ids[r] == e;
+    for (int i = 0; i < s_nch[q]; i++) {
+      const int c = base + i;
+      d.ch_expert[c] = e - a.e_begin;
+      d.ch_pos[c] = s_pos[q] + i * a.mt;
+      d.ch_n[c] = min(a.mt, cnt - i * a.mt);
+      d.ch_task_gu[c] = c * a.tpc_gu;
+      d.ch_task_dn[c] = c * a.tpc_dn;
+    }
+  }
+  const int sh_chunks = a.has_shared ? (T + a.mt - 1) / a.mt : 0;
+  for (int i = threadIdx.x; i < sh_chunks; i += blockDim.x) {
+    const int c = routed_chunks + i;
+    d.ch_expert[c] = a.n_loc;
+    d.ch_pos[c] = routed + i * a.mt;
+    d.ch_n[c] = min(a.mt, T - i * a.mt);
+    d.ch_task_gu[c] = routed_chunks * a.tpc_gu + i * a.tpc_gu_shared;
+    d.ch_task_dn[c] = c * a.tpc_dn;
+  }
+  if (threadIdx.x == 0) {
+    const int nc = routed_chunks + sh_chunks;
+    d.n_chunks[0] = nc;
+    d.ch_task_gu[nc] = routed_chunks * a.tpc_gu + sh_chunks * a.tpc_gu_shared;
+    d.ch_task_dn[nc] = nc * a.tpc_dn;
+    d.offsets[a.n_loc] = routed;                             // first shared position
+    d.offsets[a.n_loc + (a.has_shared ? 1 : 0)] = routed + (a.has_shared ? T : 0);  // total
+  }
+
+  // ---------------- 3. activations: f16 copy with a power-of-two scale, shared gate
+  for (int t = wi; t < T; t += blockDim.x / 32) {
+    float amax = 0.0f, dot = 0.0f;
+    for (int i = lane; i < a.H; i += 32) {
+      const float xv = load_elem(a.x, a.x_dtype, static_cast<size_t>(t) * a.H + i);
+      amax = fmaxf(amax, fabsf(xv));
+      if (a.gvec) dot = fmaf(xv, a.gvec[i], dot);
+    }
+    amax = warp_max(amax);
+    dot = warp_sum(dot);
+    const int ex = f16_row_exponent(amax);
+    const float g = a.gvec ? sigmoid_ref(dot) : 1.0f;
+    if (lane == 0) {
+      a.xexp[t] = ex;
+      a.gate[t] = g;
+    }
+    if (a.has_shared)
+      if (lane == 0) d.perm_w[routed + t] = g;
+    if (a.has_shared && lane == 0) d.perm_tok[routed + t] = t;
+    const float sc = exp2i(ex);
+    for (int i = lane; i < a.H; i += 32) {
+      const float xv = load_elem(a.x, a.x_dtype, static_cast<size_t>(t) * a.H + i) * sc;
+      int dst = i;
+      if (a.fmt == kInt4g) {
+        const int gq = i & ~7, qq = i & 7;
+        dst = gq + (qq < 4 ? 2 * qq : 2 * (qq - 4) + 1);
+      }
+      a.xq[static_cast<size_t>(t) * a.H + dst] = __half_as_ushort(__float2half_rn(xv));
+    }
+  }
+}
+
+cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers& d,
+                                  cudaStream_t st) {
+  if (a.T <= 0) return cudaSuccess;
+  if (a.T > kSmallT || a.k > RMOE_MAX_TOPK_DEV || a.E > 1024) return cudaErrorInvalidValue;
+  if (a.E <= 64) prologue_small_kernel<2><<<1, 512, 0, st>>>(a, d);
+  else if (a.E <= 256) prologue_small_kernel<8><<<1, 512, 0, st>>>(a, d);
+  else if (a.E <= 512) prologue_small_kernel<16><<<1, 512, 0, st>>>(a, d);
+  else prologue_small_kernel<32><<<1, 512, 0, st>>>(a, d);
+  return cudaGetLastError();
+}
+
+}  // namespace rmoe

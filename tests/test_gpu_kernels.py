@@ -222,7 +222,7 @@ def test_dispatch_matches_reference_order(cuda_ctx, T, k, E):
     import rabbit_b200 as rb
 
     rng = np.random.default_rng(T * 31 + E)
-    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32).reshape(T, k)
+    ids = np.array([rng.choice(E, k, replace=False) for _ in range(T)], np.int32).reshape(T, k)
     L = rb.MoeLayer(cuda_ctx, 32, 32, E, k, max_tokens=max(T, 1))
     res = L.dispatch(_t(ids) if T else torch.zeros((0, k), dtype=torch.int32, device="cuda"))
     torch.cuda.synchronize()
