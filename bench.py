@@ -362,6 +362,8 @@ def run_gpu(args):
                 "d2h_bytes_per_step": cfg.hidden * 4,
                 "api": "rmoe_moe_forward_host (pinned host x/out, copies + sync inside)"},
         "gpu_launches": int(launches),
+        "router_fallbacks": layer.stats()["router_fallbacks"],
+        "device_error_flags": layer.stats()["device_error_flags"],
         "clocks": clk,
         "prefill": pre,
     }

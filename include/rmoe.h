@@ -85,6 +85,8 @@ typedef struct rmoe_layer_stats {
   uint64_t kernel_launches;      /* this library's kernels launched by forward calls */
   uint64_t router_fallbacks;     /* tokens whose fast-router certificate failed and were
                                     re-ranked on exact reference-order logits */
+  uint64_t device_error_flags;   /* nonzero: a bounded device-side wait gave up (bit 0 producer,
+                                    bit 1 consumer); the results of that call are invalid */
   uint64_t device_bytes;         /* resident expert + router bytes */
   int32_t local_expert_begin;    /* experts [begin, end) are resident on this device */
   int32_t local_expert_end;

@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -88,6 +89,9 @@ struct rmoe_layer {
   float* logits = nullptr;
   float* logit_err = nullptr;
   unsigned* fallbacks = nullptr;
+  unsigned* dev_err = nullptr;   // bounded-wait failures of the pipelined kernels
+  bool use_pipe = false;         // TMA-staged GEMVs (shape permitting)
+  int rpt_gu = 2, rpt_dn = 4;    // rows per warp task of the gate/up and down GEMVs
   int32_t* ids = nullptr;
   float* rw = nullptr;
   DispatchBuffers d{};
@@ -301,9 +305,18 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->logits, static_cast<size_t>(T) * E);
   ALLOC(L->logit_err, static_cast<size_t>(std::min(T, 32)) * E);
   ALLOC(L->fallbacks, 1);
+  ALLOC(L->dev_err, 1);
   {
     cudaError_t e = cudaMemset(L->fallbacks, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(L->dev_err, 0, 4);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset"));
+  }
+  {
+    const char* off = getenv("RMOE_DISABLE_PIPE");
+    L->use_pipe = pipe_supported(f, static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is)) &&
+                  !(off && off[0] == '1');
+    L->rpt_gu = L->use_pipe ? 1 : 2;
+    L->rpt_dn = L->use_pipe ? 8 : 4;
   }
   ALLOC(L->ids, static_cast<size_t>(T) * k);
   ALLOC(L->rw, static_cast<size_t>(T) * k);
@@ -370,6 +383,9 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   RMOE_CUDA(cudaMemcpy(&fb, L->fallbacks, 4, cudaMemcpyDeviceToHost), "read fallback counter");
   out->router_fallbacks = fb;
+  unsigned ef = 0;
+  RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
+  out->device_error_flags = ef;
   return RMOE_OK;
 }
 
@@ -582,7 +598,7 @@ static rmoe_status dispatch_into(rmoe_layer* L, int T, int mt, const float* gate
   const rmoe_layer_desc& D = L->desc;
   cudaError_t e = launch_dispatch(L->ids, L->rw, T, D.topk, L->e_begin, L->e_end, mt,
                                   L->has_shared ? 1 : 0, gate, D.moe_inter, D.shared_inter,
-                                  D.hidden, 2, 4, L->d, st);
+                                  D.hidden, L->rpt_gu, L->rpt_dn, L->d, st);
   if (e != cudaSuccess) return cuda_fail(e, "dispatch");
   return RMOE_OK;
 }
@@ -590,7 +606,7 @@ static rmoe_status dispatch_into(rmoe_layer* L, int T, int mt, const float* gate
 extern "C" rmoe_status rmoe_dispatch(rmoe_layer* L, const int32_t* ids, int32_t T, int32_t* counts,
                                      int32_t* offsets, int32_t* perm_token, int32_t* uniq,
                                      int32_t* n_uniq, void* stream) {
-  if (!L || !ids) return fail(RMOE_INVALID_ARG, "rmoe_dispatch: null argument");
+  if (!L || (!ids && T > 0)) return fail(RMOE_INVALID_ARG, "rmoe_dispatch: null argument");
   if (T < 0 || T > L->max_tokens) return fail(RMOE_INVALID_ARG, "rmoe_dispatch: T = %d", T);
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -634,7 +650,8 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
     a.T = T; a.E = D.n_experts; a.k = k; a.H = H; a.mt = mt;
     a.e_begin = L->e_begin; a.e_end = L->e_end; a.n_loc = L->n_loc;
     a.has_shared = L->has_shared ? 1 : 0; a.fmt = L->fmt.fmt;
-    a.tpc_gu = D.moe_inter / 2; a.tpc_gu_shared = D.shared_inter / 2; a.tpc_dn = H / 4;
+    a.tpc_gu = D.moe_inter / L->rpt_gu; a.tpc_gu_shared = D.shared_inter / L->rpt_gu;
+    a.tpc_dn = H / L->rpt_dn;
     a.mid = L->logits; a.err = L->logit_err; a.bias = L->has_bias ? L->router_bias : nullptr;
     a.x = x; a.x_dtype = xdt; a.w = L->router; a.w_dtype = L->router_dtype;
     a.gvec = gated ? L->shared_gate_vec : nullptr;
@@ -662,13 +679,21 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
   const int tasks_gu = max_chunks * (std::max(D.moe_inter, D.shared_inter) / 2);
   const int tasks_dn = max_chunks * (H / 4);
   marks.mark();
-  e = launch_gemv_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, tasks_gu, L->h, L->hmax, L->h_ld, st);
+  if (L->use_pipe)
+    e = launch_pipe_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, L->h, L->hmax, L->h_ld,
+                            L->dev_err, st);
+  else
+    e = launch_gemv_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, tasks_gu, L->h, L->hmax,
+                            L->h_ld, st);
   if (e != cudaSuccess) return cuda_fail(e, "gate/up");
   marks.mark();
   e = launch_quant_h(L->h, L->hmax, L->d.offsets + n_slots, P, L->h_ld, L->fmt.fmt, L->hq, L->hexp, st);
   if (e != cudaSuccess) return cuda_fail(e, "h quantize");
   marks.mark();
-  e = launch_gemv_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, tasks_dn, L->h_ld, L->y, st);
+  if (L->use_pipe)
+    e = launch_pipe_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, L->h_ld, L->y, L->dev_err, st);
+  else
+    e = launch_gemv_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, tasks_dn, L->h_ld, L->y, st);
   if (e != cudaSuccess) return cuda_fail(e, "down");
   marks.mark();
   e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);

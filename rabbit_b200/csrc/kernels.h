@@ -133,6 +133,18 @@ cudaError_t launch_combine(const float* y, const DispatchBuffers& d, const float
                            int k, int H, int shared_slot, int has_shared, float* out,
                            cudaStream_t st);
 
+// ---- TMA-staged expert GEMVs (gemv_pipe.cu): one task = one gate/up row index, or 8 down
+//      rows; tasks per chunk are therefore inter (gate/up) and hidden / 8 (down) ----
+bool pipe_supported(const ExpertFormat& f, int H, int inter, int shared_inter);
+cudaError_t launch_pipe_gate_up(const ExpertTable& tab, const ExpertFormat& f,
+                                const DispatchBuffers& d, const uint16_t* xq,
+                                const int32_t* xexp, int H, int mt, float* h, uint32_t* hmax,
+                                int h_ld, unsigned* err_flag, cudaStream_t st);
+cudaError_t launch_pipe_down(const ExpertTable& tab, const ExpertFormat& f,
+                             const DispatchBuffers& d, const uint16_t* hq, const int32_t* hexp,
+                             int H, int mt, int h_ld, float* y, unsigned* err_flag,
+                             cudaStream_t st);
+
 // ---- generic GEMM entry points (experts.cu) ----
 cudaError_t launch_matmul_q(float* y, const void* x, int x_dtype, const uint8_t* data,
                             const void* scale, const ExpertFormat& f, int s, int i, int o,
