@@ -363,6 +363,7 @@ def run_gpu(args):
                 "api": "rmoe_moe_forward_host (pinned host x/out, copies + sync inside)"},
         "gpu_launches": int(launches),
         "router_fallbacks": layer.stats()["router_fallbacks"],
+        "router_order_resolved": layer.stats()["router_order_resolved"],
         "device_error_flags": layer.stats()["device_error_flags"],
         "clocks": clk,
         "prefill": pre,

@@ -83,8 +83,10 @@ typedef struct rmoe_layer_stats {
   uint64_t forward_calls;
   uint64_t tokens_routed;
   uint64_t kernel_launches;      /* this library's kernels launched by forward calls */
-  uint64_t router_fallbacks;     /* tokens whose fast-router certificate failed and were
-                                    re-ranked on exact reference-order logits */
+  uint64_t router_fallbacks;     /* tokens whose fast-router expert set was uncertain and
+                                    were re-ranked on exact reference-order logits */
+  uint64_t router_order_resolved; /* tokens whose set was certain but whose rank order was
+                                    settled on exact logits beside the expert products */
   uint64_t device_error_flags;   /* nonzero: a bounded device-side wait gave up (bit 0 producer,
                                     bit 1 consumer); the results of that call are invalid */
   uint64_t device_bytes;         /* resident expert + router bytes */

@@ -36,7 +36,7 @@ class LayerDesc(C.Structure):
 
 class LayerStats(C.Structure):
     _fields_ = [("forward_calls", C.c_uint64), ("tokens_routed", C.c_uint64),
-                ("kernel_launches", C.c_uint64), ("router_fallbacks", C.c_uint64),
+                ("kernel_launches", C.c_uint64), ("router_fallbacks", C.c_uint64), ("router_order_resolved", C.c_uint64),
                 ("device_error_flags", C.c_uint64),
                 ("device_bytes", C.c_uint64), ("local_expert_begin", C.c_int32),
                 ("local_expert_end", C.c_int32)]

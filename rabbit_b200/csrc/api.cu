@@ -90,6 +90,12 @@ struct rmoe_layer {
   float* logit_err = nullptr;
   unsigned* fallbacks = nullptr;
   unsigned* dev_err = nullptr;   // bounded-wait failures of the pipelined kernels
+  unsigned* order_pending = nullptr;  // tokens whose rank order was resolved beside the GEMVs
+  int32_t* pending = nullptr;    // [min(T, 32)] per-token order-pending flags
+  int32_t* ids_final = nullptr;  // [T][k] routing in the reference's rank order
+  float* w_final = nullptr;
+  cudaStream_t side = nullptr;   // resolves rank order concurrently with the expert GEMVs
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   bool use_pipe = false;         // TMA-staged GEMVs (shape permitting)
   int rpt_gu = 2, rpt_dn = 4;    // rows per warp task of the gate/up and down GEMVs
   int32_t* ids = nullptr;
@@ -243,6 +249,9 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   L->uploaded.assign(L->n_loc, 0);
   auto cleanup = [&](rmoe_status s) {
     if (L->stream) cudaStreamDestroy(L->stream);
+    if (L->side) cudaStreamDestroy(L->side);
+    if (L->ev_fork) cudaEventDestroy(L->ev_fork);
+    if (L->ev_join) cudaEventDestroy(L->ev_join);
     delete L;
     return s;
   };
@@ -306,9 +315,14 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->logit_err, static_cast<size_t>(std::min(T, 32)) * E);
   ALLOC(L->fallbacks, 1);
   ALLOC(L->dev_err, 1);
+  ALLOC(L->order_pending, 1);
+  ALLOC(L->pending, std::min(T, 32));
+  ALLOC(L->ids_final, static_cast<size_t>(T) * k);
+  ALLOC(L->w_final, static_cast<size_t>(T) * k);
   {
     cudaError_t e = cudaMemset(L->fallbacks, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(L->dev_err, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(L->order_pending, 0, 4);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset"));
   }
   {
@@ -355,6 +369,9 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->out_dev, static_cast<size_t>(T) * H);
   {
     cudaError_t e = cudaStreamCreateWithFlags(&L->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&L->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_join, cudaEventDisableTiming);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaStreamCreate"));
   }
 #undef ALLOC
@@ -372,6 +389,12 @@ extern "C" rmoe_status rmoe_layer_destroy(rmoe_layer* L) {
     cudaStreamSynchronize(L->stream);
     cudaStreamDestroy(L->stream);
   }
+  if (L->side) {
+    cudaStreamSynchronize(L->side);
+    cudaStreamDestroy(L->side);
+  }
+  if (L->ev_fork) cudaEventDestroy(L->ev_fork);
+  if (L->ev_join) cudaEventDestroy(L->ev_join);
   delete L;
   return RMOE_OK;
 }
@@ -386,6 +409,9 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
   unsigned ef = 0;
   RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
   out->device_error_flags = ef;
+  unsigned op = 0;
+  RMOE_CUDA(cudaMemcpy(&op, L->order_pending, 4, cudaMemcpyDeviceToHost), "read order counter");
+  out->router_order_resolved = op;
   return RMOE_OK;
 }
 
@@ -639,6 +665,7 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
   rmoe_status s = RMOE_OK;
   cudaError_t e = cudaSuccess;
   int launches = 10;
+  bool resolved = false;
   if (small_path(L, T)) {
     // certified router + one-block front end (top-k, dispatch, activation prep)
     marks.mark();
@@ -657,10 +684,20 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
     a.gvec = gated ? L->shared_gate_vec : nullptr;
     a.ids = L->ids; a.rw = L->rw; a.xq = L->xq; a.xexp = L->xexp; a.gate = L->gate;
     a.fallback_count = L->fallbacks;
+    a.order_pending_count = L->order_pending;
+    a.pending = L->pending;
     e = launch_prologue_small(a, L->d, st);
     if (e != cudaSuccess) return cuda_fail(e, "small-T prologue");
-    marks.mark();  // prep and dispatch are folded into the prologue
-    launches = 6;
+    marks.mark();  // top-k, certificate, dispatch and activation prep
+    marks.mark();  // (prep and dispatch are folded into the prologue)
+    // rank order of near-tied winners: resolved on a side stream, joined before returning
+    RMOE_CUDA(cudaEventRecord(L->ev_fork, st), "fork");
+    RMOE_CUDA(cudaStreamWaitEvent(L->side, L->ev_fork, 0), "fork wait");
+    e = launch_resolve_order(a, L->ids_final, L->w_final, L->side);
+    if (e != cudaSuccess) return cuda_fail(e, "order resolve");
+    RMOE_CUDA(cudaEventRecord(L->ev_join, L->side), "join");
+    resolved = true;
+    launches = 7;
   } else {
     marks.mark();
     s = route_into(L, x, x_dtype, T, st, &marks);
@@ -704,8 +741,11 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
   // down, combine; small-T: certified router, prologue, gate/up, quantize h, down, combine
   L->stats.kernel_launches += launches;
   const size_t n = static_cast<size_t>(T) * k;
-  if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, L->ids, n * 4, cudaMemcpyDefault, st), "ids out");
-  if (w_out) RMOE_CUDA(cudaMemcpyAsync(w_out, L->rw, n * 4, cudaMemcpyDefault, st), "weights out");
+  if (resolved) RMOE_CUDA(cudaStreamWaitEvent(st, L->ev_join, 0), "join wait");
+  const int32_t* ids_src = resolved ? L->ids_final : L->ids;
+  const float* w_src = resolved ? L->w_final : L->rw;
+  if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, ids_src, n * 4, cudaMemcpyDefault, st), "ids out");
+  if (w_out) RMOE_CUDA(cudaMemcpyAsync(w_out, w_src, n * 4, cudaMemcpyDefault, st), "weights out");
   L->stats.forward_calls++;
   L->stats.tokens_routed += T;
   return RMOE_OK;

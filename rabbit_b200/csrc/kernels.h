@@ -82,7 +82,9 @@ struct SmallPrologue {
   uint16_t* xq;                       // [T][H] f16
   int32_t* xexp;                      // [T]
   float* gate;                        // [T]
-  unsigned* fallback_count;           // tokens whose certificate failed (exact recompute)
+  unsigned* fallback_count;           // tokens whose expert set was uncertain (exact recompute)
+  unsigned* order_pending_count;      // tokens whose rank order was resolved off the critical path
+  int32_t* pending;                   // [T] 1 = order to be resolved by launch_resolve_order
 };
 
 // ---- router (router.cu, route_small.cu) ----
@@ -92,6 +94,9 @@ cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, i
 // Top-k + certificate (+ exact fallback), dispatch, activation prep in one block.
 cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers& d,
                                   cudaStream_t st);
+// Final reference-order routing (exact chains for order-pending tokens); one warp per token.
+cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final,
+                                 cudaStream_t st);
 // logits[T][E] = exact reference chain of x[t] . w[e] (fmul then fadd per element, from -0.0)
 cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
                                        float* logits, int T, int H, int E, cudaStream_t st);

@@ -131,16 +131,40 @@ __device__ __forceinline__ void warp_best(float& v, int& id) {
 }
 
 // The reference chain for one (token, expert): a = -0.0; a = fl(a + fl(x_k * w_k)), k ascending.
+// The 8192 adds are inherently serial; the loads run 32 elements ahead of the chain so only the
+// add latency remains (~4 cycles per element).
 __device__ float exact_logit(const void* x, int x_dtype, const void* w, int w_dtype, int t, int e,
                              int H) {
   float a = -0.0f;
   const size_t xo = static_cast<size_t>(t) * H, wo = static_cast<size_t>(e) * H;
-  for (int k = 0; k < H; k += 8) {
-    float xv[8], wv[8];
-    load8(x, x_dtype, xo + k, xv);
-    load8(w, w_dtype, wo + k, wv);
+  float xc[32], wc[32];
 #pragma unroll
-    for (int i = 0; i < 8; i++) a = __fadd_rn(a, __fmul_rn(xv[i], wv[i]));
+  for (int q = 0; q < 4; q++) {
+    load8(x, x_dtype, xo + 8 * q, *reinterpret_cast<float(*)[8]>(&xc[8 * q]));
+    load8(w, w_dtype, wo + 8 * q, *reinterpret_cast<float(*)[8]>(&wc[8 * q]));
+  }
+  for (int k = 0; k < H; k += 32) {
+    float xn[32], wn[32];
+    const bool more = k + 32 < H;
+    if (more) {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        load8(x, x_dtype, xo + k + 32 + 8 * q, *reinterpret_cast<float(*)[8]>(&xn[8 * q]));
+        load8(w, w_dtype, wo + k + 32 + 8 * q, *reinterpret_cast<float(*)[8]>(&wn[8 * q]));
+      }
+    }
+    float p[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) p[i] = __fmul_rn(xc[i], wc[i]);
+#pragma unroll
+    for (int i = 0; i < 32; i++) a = __fadd_rn(a, p[i]);
+    if (more) {
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        xc[i] = xn[i];
+        wc[i] = wn[i];
+      }
+    }
   }
   return a;
 }
@@ -248,8 +272,19 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
     }
     const float next_hi = __shfl_down_sync(kFull, my_hi, 1);
     const bool pair_ok = (lane >= kk - 1) || (my_lo > next_hi);
-    const bool certified = (n_cont == kk) && __all_sync(kFull, pair_ok);
-    if (!certified) {
+    const bool set_ok = n_cont == kk;
+    const bool order_ok = __all_sync(kFull, pair_ok);
+    if (set_ok && !order_ok) {
+      // the expert set is certain, only the rank order of near-tied winners is not: the expert
+      // products do not depend on it, so the exact order is resolved off the critical path
+      if (lane == 0) {
+        a.pending[t] = 1;
+        atomicAdd(a.order_pending_count, 1u);
+      }
+    } else if (lane == 0) {
+      a.pending[t] = 0;
+    }
+    if (!set_ok) {
       // exact chains for every contender, then select on exact values among them
       for (int q = 0; q < PL; q++) {
         const int e = q * 32 + lane;
@@ -286,6 +321,7 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
   for (int q = threadIdx.x; q < n; q += blockDim.x) {
     const int e = s_ids[q];
     const bool local = e >= a.e_begin && e < a.e_end;
+    // (rank-order-independent: positions depend only on the expert set of each token)
     int pos = -1, nch = 0;
     if (local) {
       int less = 0, same = 0, first = 1;
@@ -389,6 +425,56 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
       a.xq[static_cast<size_t>(t) * a.H + dst] = __half_as_ushort(__float2half_rn(xv));
     }
   }
+}
+
+// Final routing in the reference's rank order. Tokens whose order certificate failed get exact
+// chains for their k winners (the set is already certain) and are re-ranked on those values;
+// the others are copied. Runs beside the expert GEMVs.
+__global__ void __launch_bounds__(32) resolve_order_kernel(SmallPrologue a, int32_t* ids_final,
+                                                           float* w_final) {
+  const int t = blockIdx.x, lane = threadIdx.x;
+  const int k = a.k, kk = min(a.k, a.E);
+  if (!a.pending[t]) {
+    if (lane < k) {
+      ids_final[t * k + lane] = a.ids[t * k + lane];
+      w_final[t * k + lane] = a.rw[t * k + lane];
+    }
+    return;
+  }
+  const int e = lane < kk ? a.ids[t * k + lane] : -1;
+  float v = -INFINITY;
+  if (e >= 0) {
+    v = exact_logit(a.x, a.x_dtype, a.w, a.w_dtype, t, e, a.H);
+    if (a.bias) v = __fadd_rn(v, a.bias[e]);
+  }
+  unsigned tk = 0;
+  int sel_id = -1;
+  float sel_v = -INFINITY;
+  for (int r = 0; r < kk; r++) {
+    float bv = (e >= 0 && !tk) ? v : -INFINITY;
+    int bid = (e >= 0 && !tk) ? e : 0x7fffffff;
+    warp_best(bv, bid);
+    if (bid == e) tk = 1;
+    if (lane == r) {
+      sel_id = bid;
+      sel_v = bv;
+    }
+  }
+  const float mx = __shfl_sync(kFull, sel_v, 0);
+  const float exv = lane < kk ? exp_f32(__fsub_rn(sel_v, mx)) : 0.0f;
+  float sum = 0.0f;
+  for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, exv, j));
+  if (lane < k) {
+    ids_final[t * k + lane] = lane < kk ? sel_id : -1;
+    w_final[t * k + lane] = lane < kk ? __fdiv_rn(exv, sum) : 0.0f;
+  }
+}
+
+cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final,
+                                 cudaStream_t st) {
+  if (a.T <= 0) return cudaSuccess;
+  resolve_order_kernel<<<a.T, 32, 0, st>>>(a, ids_final, w_final);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers& d,
