@@ -50,13 +50,22 @@ struct PipeGeom<1> {
   static constexpr int kRows = 8;  // 8 down rows
 };
 
+// What the consumers of one slot need besides the weights, written by the producer so that no
+// consumer waits on a dependent global load: chunk, row index, expert slot, first position,
+// positions in the chunk, and each position's activation row and power-of-two exponent.
+struct SlotMeta {
+  int c, r, eslot, p0, n;
+  int row[8];
+  int xe[8];
+};
+
 template <int FMT, int MT, int MODE>
 __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NR = PipeGeom<MODE>::kRows;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * a.slot_bytes);
   uint64_t* empty = full + kStages;
-  int2* meta = reinterpret_cast<int2*>(empty + kStages);  // (chunk, task row index) per slot
+  SlotMeta* meta = reinterpret_cast<SlotMeta*>(empty + kStages);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int32_t* task0 = MODE == 0 ? a.d.ch_task_gu : a.d.ch_task_dn;
   const int n_chunks = *a.d.n_chunks;
@@ -76,18 +85,39 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
 
   if (warp == kConsumers) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if (lane == 0 && my_tasks > 0) {
+      // tasks of this CTA are contiguous: one search, then the chunk index only moves forward
+      int c = find_chunk(task0, n_chunks, t_begin);
+      SlotMeta cm;
+      int c_end = 0;
+      ExpertPtrs ep{};
+      auto enter_chunk = [&](int cc) {
+        c_end = task0[cc + 1];
+        cm.c = cc;
+        cm.eslot = a.d.ch_expert[cc];
+        cm.p0 = a.d.ch_pos[cc];
+        cm.n = a.d.ch_n[cc];
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+          const int mm = m < cm.n ? m : 0;
+          const int row = MODE == 0 ? a.d.perm_tok[cm.p0 + mm] : cm.p0 + mm;
+          cm.row[m] = row;
+          cm.xe[m] = a.xexp[row];
+        }
+        ep = expert_ptrs(a.tab, cm.eslot);
+      };
+      enter_chunk(c);
       for (int i = 0; i < my_tasks; i++) {
         const int slot = i % kStages;
+        const int task = t_begin + i;
+        while (task >= c_end) enter_chunk(++c);
+        const int r = task - task0[c];
+        const int eslot = cm.eslot;
         if (i >= kStages && !mbar_wait_bounded(&empty[slot], ((i / kStages) - 1) & 1, a.err_flag, 1u))
           return;
-        const int task = t_begin + i;
-        const int c = find_chunk(task0, n_chunks, task);
-        const int r = task - task0[c];
-        const int eslot = a.d.ch_expert[c];
-        const ExpertPtrs ep = expert_ptrs(a.tab, eslot);
         uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes;
-        meta[slot] = make_int2(c, r);
+        cm.r = r;
+        meta[slot] = cm;
         if (MODE == 0) {
           const uint32_t rb = a.H / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, a.H));
           mbar_arrive_expect_tx(&full[slot], 2 * (rb + sb));
@@ -114,10 +144,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
   for (int i = warp; i < my_tasks; i += kConsumers) {
     const int slot = i % kStages;
     if (!mbar_wait_bounded(&full[slot], (i / kStages) & 1, a.err_flag, 2u)) return;
-    const int2 cr = meta[slot];
-    const int c = cr.x, r = cr.y;
-    const int eslot = a.d.ch_expert[c];
-    const int p0 = a.d.ch_pos[c], n = a.d.ch_n[c];
+    const SlotMeta& sm = meta[slot];
+    const int r = sm.r;
+    const int eslot = sm.eslot;
+    const int p0 = sm.p0, n = sm.n;
     const int K = MODE == 0 ? a.H : (eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter);
     const uint32_t rb = K / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, K));
     const uint8_t* base = smem + static_cast<size_t>(slot) * a.slot_bytes;
@@ -125,10 +155,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
     int xe[MT];
 #pragma unroll
     for (int m = 0; m < MT; m++) {
-      const int mm = m < n ? m : 0;
-      const int row = MODE == 0 ? a.d.perm_tok[p0 + mm] : p0 + mm;
-      xr[m] = a.xin + static_cast<size_t>(row) * a.x_ld;
-      xe[m] = a.xexp[row];
+      xr[m] = a.xin + static_cast<size_t>(sm.row[m]) * a.x_ld;
+      xe[m] = sm.xe[m];
     }
     float acc[NR][MT];
 #pragma unroll
@@ -251,7 +279,7 @@ cudaError_t launch_pipe_gate_up(const ExpertTable& tab, const ExpertFormat& f,
   PipeArgs a{tab, f, d, xq, xexp, H, h, h_ld, hmax, H, 0, err_flag};
   a.slot_bytes = static_cast<int>(2 * (H / 2 + scale_row_bytes_host(f, H)));
   a.slot_bytes = (a.slot_bytes + 127) / 128 * 128;
-  const size_t smem = static_cast<size_t>(kStages) * a.slot_bytes + kStages * 16 + kStages * 8;
+  const size_t smem = static_cast<size_t>(kStages) * a.slot_bytes + kStages * 16 + kStages * sizeof(SlotMeta);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (f.fmt == kMxfp4) return launch_pipe_fmt<kMxfp4, 0>(mt, a, num_sms(), smem, st);
   return launch_pipe_fmt<kInt4g, 0>(mt, a, num_sms(), smem, st);
@@ -265,7 +293,7 @@ cudaError_t launch_pipe_down(const ExpertTable& tab, const ExpertFormat& f,
   const int K = std::max(tab.inter, tab.shared_inter);
   a.slot_bytes = static_cast<int>(PipeGeom<1>::kRows * (K / 2 + scale_row_bytes_host(f, K)));
   a.slot_bytes = (a.slot_bytes + 127) / 128 * 128;
-  const size_t smem = static_cast<size_t>(kStages) * a.slot_bytes + kStages * 16 + kStages * 8;
+  const size_t smem = static_cast<size_t>(kStages) * a.slot_bytes + kStages * 16 + kStages * sizeof(SlotMeta);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (f.fmt == kMxfp4) return launch_pipe_fmt<kMxfp4, 1>(mt, a, num_sms(), smem, st);
   return launch_pipe_fmt<kInt4g, 1>(mt, a, num_sms(), smem, st);

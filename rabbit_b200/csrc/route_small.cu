@@ -43,12 +43,15 @@ __device__ __forceinline__ void load8(const void* p, int dtype, size_t idx, floa
   }
 }
 
-// grid: ceil(E/8) blocks of 8 warps; warp = one expert, all T tokens (groups of TB).
+// grid: ceil(E/4) blocks of 4 warps; warp = one expert, all T tokens (groups of TB). Each
+// lane's weight slice streams in batches of NB x 8 elements whose loads are all issued before
+// the (serial) local chain consumes them.
 template <int TB>
-__global__ void __launch_bounds__(256) router_certified_kernel(
+__global__ void __launch_bounds__(128) router_certified_kernel(
     const void* __restrict__ x, int x_dtype, const void* __restrict__ w, int w_dtype,
     float* __restrict__ mid, float* __restrict__ err, int T, int H, int E) {
-  const int e = blockIdx.x * 8 + threadIdx.x / 32;
+  constexpr int NB = TB == 1 ? 8 : 4;
+  const int e = blockIdx.x * 4 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (e >= E) return;
   const int c = H / 32;  // slice length (multiple of 8)
@@ -60,20 +63,32 @@ __global__ void __launch_bounds__(256) router_certified_kernel(
     float b[TB], A[TB], P[TB];
 #pragma unroll
     for (int q = 0; q < TB; q++) b[q] = A[q] = P[q] = 0.0f;
-    for (int j = 0; j < c; j += 8) {
-      float wv[8];
-      load8(w, w_dtype, wrow + j, wv);
+    for (int j0 = 0; j0 < c; j0 += 8 * NB) {
+      float wv[NB][8], xv[NB][TB][8];
 #pragma unroll
-      for (int q = 0; q < TB; q++) {
-        if (t0 + q >= T) break;
-        float xv[8];
-        load8(x, x_dtype, static_cast<size_t>(t0 + q) * H + static_cast<size_t>(lane) * c + j, xv);
+      for (int bb = 0; bb < NB; bb++) {
+        const int j = j0 + 8 * bb;
+        if (j < c) {
+          load8(w, w_dtype, wrow + j, wv[bb]);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const float p = __fmul_rn(xv[i], wv[i]);
-          b[q] = __fadd_rn(b[q], p);
-          A[q] += fabsf(b[q]);
-          P[q] += fabsf(p);
+          for (int q = 0; q < TB; q++)
+            if (t0 + q < T)
+              load8(x, x_dtype, static_cast<size_t>(t0 + q) * H + static_cast<size_t>(lane) * c + j, xv[bb][q]);
+        }
+      }
+#pragma unroll
+      for (int bb = 0; bb < NB; bb++) {
+        if (j0 + 8 * bb >= c) break;
+#pragma unroll
+        for (int q = 0; q < TB; q++) {
+          if (t0 + q >= T) break;
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float p = __fmul_rn(xv[bb][q][i], wv[bb][i]);
+            b[q] = __fadd_rn(b[q], p);
+            A[q] += fabsf(b[q]);
+            P[q] += fabsf(p);
+          }
         }
       }
     }
@@ -107,9 +122,9 @@ cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, i
                                     cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   if (H % 256 != 0 || T > kSmallT) return cudaErrorInvalidValue;
-  const int blocks = (E + 7) / 8;
-  if (T == 1) router_certified_kernel<1><<<blocks, 256, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
-  else router_certified_kernel<4><<<blocks, 256, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
+  const int blocks = (E + 3) / 4;
+  if (T == 1) router_certified_kernel<1><<<blocks, 128, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
+  else router_certified_kernel<4><<<blocks, 128, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
   return cudaGetLastError();
 }
 
@@ -395,35 +410,67 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
     d.offsets[a.n_loc + (a.has_shared ? 1 : 0)] = routed + (a.has_shared ? T : 0);  // total
   }
 
-  // ---------------- 3. activations: f16 copy with a power-of-two scale, shared gate
-  for (int t = wi; t < T; t += blockDim.x / 32) {
+  // ---------------- 3. activations: f16 copy with a power-of-two scale, shared gate.
+  // The whole block works on one token at a time, 8 consecutive elements per thread.
+  __shared__ float red[2][16];
+  for (int t = 0; t < T; t++) {
     float amax = 0.0f, dot = 0.0f;
-    for (int i = lane; i < a.H; i += 32) {
-      const float xv = load_elem(a.x, a.x_dtype, static_cast<size_t>(t) * a.H + i);
-      amax = fmaxf(amax, fabsf(xv));
-      if (a.gvec) dot = fmaf(xv, a.gvec[i], dot);
+    for (int i = threadIdx.x * 8; i < a.H; i += blockDim.x * 8) {
+      float xv[8];
+      load8(a.x, a.x_dtype, static_cast<size_t>(t) * a.H + i, xv);
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        amax = fmaxf(amax, fabsf(xv[q]));
+        if (a.gvec) dot = fmaf(xv[q], a.gvec[i + q], dot);
+      }
     }
     amax = warp_max(amax);
     dot = warp_sum(dot);
-    const int ex = f16_row_exponent(amax);
-    const float g = a.gvec ? sigmoid_ref(dot) : 1.0f;
     if (lane == 0) {
+      red[0][wi] = amax;
+      red[1][wi] = dot;
+    }
+    __syncthreads();
+    if (wi == 0) {
+      float am = lane < (int)(blockDim.x / 32) ? red[0][lane] : 0.0f;
+      float dt = lane < (int)(blockDim.x / 32) ? red[1][lane] : 0.0f;
+      am = warp_max(am);
+      dt = warp_sum(dt);
+      if (lane == 0) {
+        red[0][0] = am;
+        red[1][0] = dt;
+      }
+    }
+    __syncthreads();
+    const int ex = f16_row_exponent(red[0][0]);
+    const float g = a.gvec ? sigmoid_ref(red[1][0]) : 1.0f;
+    if (threadIdx.x == 0) {
       a.xexp[t] = ex;
       a.gate[t] = g;
-    }
-    if (a.has_shared)
-      if (lane == 0) d.perm_w[routed + t] = g;
-    if (a.has_shared && lane == 0) d.perm_tok[routed + t] = t;
-    const float sc = exp2i(ex);
-    for (int i = lane; i < a.H; i += 32) {
-      const float xv = load_elem(a.x, a.x_dtype, static_cast<size_t>(t) * a.H + i) * sc;
-      int dst = i;
-      if (a.fmt == kInt4g) {
-        const int gq = i & ~7, qq = i & 7;
-        dst = gq + (qq < 4 ? 2 * qq : 2 * (qq - 4) + 1);
+      if (a.has_shared) {
+        d.perm_w[routed + t] = g;
+        d.perm_tok[routed + t] = t;
       }
-      a.xq[static_cast<size_t>(t) * a.H + dst] = __half_as_ushort(__float2half_rn(xv));
     }
+    const float sc = exp2i(ex);
+    for (int i = threadIdx.x * 8; i < a.H; i += blockDim.x * 8) {
+      float xv[8];
+      load8(a.x, a.x_dtype, static_cast<size_t>(t) * a.H + i, xv);
+      uint16_t hv[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        // int4 layout pairs (0,4),(1,5),(2,6),(3,7) inside each 8-group
+        const int dst = a.fmt == kInt4g ? (q < 4 ? 2 * q : 2 * (q - 4) + 1) : q;
+        hv[dst] = __half_as_ushort(__float2half_rn(xv[q] * sc));
+      }
+      uint4 pk;
+      pk.x = hv[0] | (static_cast<uint32_t>(hv[1]) << 16);
+      pk.y = hv[2] | (static_cast<uint32_t>(hv[3]) << 16);
+      pk.z = hv[4] | (static_cast<uint32_t>(hv[5]) << 16);
+      pk.w = hv[6] | (static_cast<uint32_t>(hv[7]) << 16);
+      *reinterpret_cast<uint4*>(a.xq + static_cast<size_t>(t) * a.H + i) = pk;
+    }
+    __syncthreads();
   }
 }
 
