@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <new>
 #include <string>
 #include <vector>
@@ -67,6 +68,19 @@ struct rmoe_ctx {
   int device;
 };
 
+// One captured forward (CUDA graph) for a (T, dtype, routing-out, profiling) combination. The
+// caller's buffers are reached through memcpy nodes whose pointers are set per launch.
+struct GraphEntry {
+  cudaGraphExec_t exec = nullptr;
+  cudaGraphNode_t in_node = nullptr, out_node = nullptr, ids_node = nullptr, w_node = nullptr;
+  size_t x_bytes = 0, out_bytes = 0, rt_bytes = 0;
+  const void* ids_src = nullptr;
+  const void* w_src = nullptr;
+  bool profiled = false, pending = false;
+  cudaEvent_t ev[RMOE_NUM_STAGES + 1] = {};
+  int launches = 0;
+};
+
 struct rmoe_layer {
   rmoe_ctx* ctx = nullptr;
   rmoe_layer_desc desc{};
@@ -119,9 +133,24 @@ struct rmoe_layer {
   std::vector<cudaEvent_t> ev_free, ev_pending;  // pending: groups of RMOE_NUM_STAGES + 1
   uint64_t prof_calls = 0;
   double prof_ms[RMOE_NUM_STAGES] = {};
+  // CUDA graphs of the small-T forward
+  bool use_graphs = true;
+  std::map<uint64_t, GraphEntry> graphs;
+  cudaStream_t cap = nullptr;    // capture stream
+  void* x_stage = nullptr;       // host entry point: H2D target, copied into x_dev by the graph
+  float* out_stage = nullptr;    // host entry point: graph output, copied to the host
+  int32_t* ids_host_stage = nullptr;
+  float* w_host_stage = nullptr;
+  int last_launches = 0;         // kernels launched by the last forward_into
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
+    for (auto& kv : graphs) {
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+      for (cudaEvent_t e : kv.second.ev)
+        if (e) cudaEventDestroy(e);
+    }
+    if (cap) cudaStreamDestroy(cap);
   }
 };
 
@@ -131,9 +160,15 @@ struct StageMarks {
   rmoe_layer* L;
   cudaStream_t st;
   std::vector<cudaEvent_t> evs;
+  const cudaEvent_t* fixed = nullptr;  // graph capture: the entry's own events
+  int n_fixed = 0;
   StageMarks(rmoe_layer* l, cudaStream_t s) : L(l), st(s) {}
   void mark() {
     if (!L->profiling) return;
+    if (fixed) {
+      if (n_fixed < RMOE_NUM_STAGES + 1) cudaEventRecord(fixed[n_fixed++], st);
+      return;
+    }
     cudaEvent_t e;
     if (!L->ev_free.empty()) {
       e = L->ev_free.back();
@@ -145,7 +180,7 @@ struct StageMarks {
     evs.push_back(e);
   }
   void commit() {
-    if (!L->profiling) return;
+    if (!L->profiling || fixed) return;
     if (evs.size() == RMOE_NUM_STAGES + 1) {
       L->ev_pending.insert(L->ev_pending.end(), evs.begin(), evs.end());
     } else {
@@ -329,6 +364,8 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     const char* off = getenv("RMOE_DISABLE_PIPE");
     L->use_pipe = pipe_supported(f, static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is)) &&
                   !(off && off[0] == '1');
+    const char* nog = getenv("RMOE_DISABLE_GRAPH");
+    L->use_graphs = !(nog && nog[0] == '1');
     L->rpt_gu = L->use_pipe ? 1 : 2;
     L->rpt_dn = L->use_pipe ? 8 : 4;
   }
@@ -367,9 +404,18 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     L->x_dev = xd;
   }
   ALLOC(L->out_dev, static_cast<size_t>(T) * H);
+  ALLOC(L->out_stage, static_cast<size_t>(T) * H);
+  {
+    uint8_t* xs = nullptr;
+    ALLOC(xs, static_cast<size_t>(T) * H * 4);
+    L->x_stage = xs;
+  }
+  ALLOC(L->ids_host_stage, static_cast<size_t>(T) * k);
+  ALLOC(L->w_host_stage, static_cast<size_t>(T) * k);
   {
     cudaError_t e = cudaStreamCreateWithFlags(&L->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&L->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&L->cap, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_join, cudaEventDisableTiming);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaStreamCreate"));
@@ -421,9 +467,15 @@ extern "C" rmoe_status rmoe_layer_set_profiling(rmoe_layer* L, int on) {
   return RMOE_OK;
 }
 
+static rmoe_status drain_graph_profile(rmoe_layer* L, GraphEntry& g);
+
 extern "C" rmoe_status rmoe_layer_get_profile(rmoe_layer* L, rmoe_profile* out) {
   if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_profile: null argument");
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  for (auto& kv : L->graphs) {
+    rmoe_status s = drain_graph_profile(L, kv.second);
+    if (s != RMOE_OK) return s;
+  }
   const size_t G = RMOE_NUM_STAGES + 1;
   for (size_t g = 0; g + G <= L->ev_pending.size(); g += G) {
     RMOE_CUDA(cudaEventSynchronize(L->ev_pending[g + G - 1]), "profile event");
@@ -650,15 +702,13 @@ extern "C" rmoe_status rmoe_dispatch(rmoe_layer* L, const int32_t* ids, int32_t 
   return RMOE_OK;
 }
 
-static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
-                                int32_t* ids_out, float* w_out, cudaStream_t st) {
+// Enqueues one forward on `st` (stream-ordered, capturable): x -> out, routing left in
+// *ids_src / *w_src (reference rank order). L->last_launches = kernels it launched.
+static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
+                                   cudaStream_t st, StageMarks& marks, const int32_t** ids_src,
+                                   const float** w_src) {
   const rmoe_layer_desc& D = L->desc;
   const int H = D.hidden, k = D.topk;
-  for (int s = 0; s < L->n_loc; s++)
-    if (!L->uploaded[s])
-      return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: expert %d was never uploaded", L->e_begin + s);
-  if (L->has_shared && !L->has_shared_w) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: shared expert never uploaded");
-  StageMarks marks(L, st);
   const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
   const bool gated = L->has_shared && D.shared_gated;
   const int mt = chunk_tokens(T);
@@ -724,32 +774,198 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
                             L->h_ld, st);
   if (e != cudaSuccess) return cuda_fail(e, "gate/up");
   marks.mark();
-  e = launch_quant_h(L->h, L->hmax, L->d.offsets + n_slots, P, L->h_ld, L->fmt.fmt, L->hq, L->hexp, st);
-  if (e != cudaSuccess) return cuda_fail(e, "h quantize");
-  marks.mark();
-  if (L->use_pipe)
-    e = launch_pipe_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, L->h_ld, L->y, L->dev_err, st);
-  else
+  if (L->use_pipe && small_path(L, T)) {
+    // down projection + weighted combine + gated shared expert in one kernel
+    marks.mark();  // (h quantization happens inside the down kernel)
+    e = launch_pipe_down_combine(L->tab, L->fmt, L->d, L->h, L->hmax, L->ids, T, k, L->e_begin,
+                                 H, L->h_ld, out, L->dev_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "down + combine");
+    marks.mark();
+    launches -= 2;
+  } else if (L->use_pipe) {
+    marks.mark();  // (h quantization happens inside the down kernel)
+    e = launch_pipe_down(L->tab, L->fmt, L->d, L->h, L->hmax, H, mt, L->h_ld, L->y, L->dev_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "down");
+    marks.mark();
+    e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "combine");
+    launches -= 1;
+  } else {
+    e = launch_quant_h(L->h, L->hmax, L->d.offsets + n_slots, P, L->h_ld, L->fmt.fmt, L->hq, L->hexp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "h quantize");
+    marks.mark();
     e = launch_gemv_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, tasks_dn, L->h_ld, L->y, st);
-  if (e != cudaSuccess) return cuda_fail(e, "down");
+    if (e != cudaSuccess) return cuda_fail(e, "down");
+    marks.mark();
+    e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "combine");
+  }
   marks.mark();
-  e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
-  if (e != cudaSuccess) return cuda_fail(e, "combine");
-  marks.mark();
-  marks.commit();
-  // generic: router logits, top-k, prep, dispatch (mark/scan/place), gate/up, quantize h,
-  // down, combine; small-T: certified router, prologue, gate/up, quantize h, down, combine
-  L->stats.kernel_launches += launches;
-  const size_t n = static_cast<size_t>(T) * k;
+  // the rank-order resolver joins back before the forward counts as done
   if (resolved) RMOE_CUDA(cudaStreamWaitEvent(st, L->ev_join, 0), "join wait");
-  const int32_t* ids_src = resolved ? L->ids_final : L->ids;
-  const float* w_src = resolved ? L->w_final : L->rw;
+  *ids_src = resolved ? L->ids_final : L->ids;
+  *w_src = resolved ? L->w_final : L->rw;
+  L->last_launches = launches;
+  return RMOE_OK;
+}
+
+static rmoe_status check_uploaded(const rmoe_layer* L) {
+  for (int s = 0; s < L->n_loc; s++)
+    if (!L->uploaded[s])
+      return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: expert %d was never uploaded", L->e_begin + s);
+  if (L->has_shared && !L->has_shared_w) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: shared expert never uploaded");
+  return RMOE_OK;
+}
+
+// Direct launches (large T, or graphs disabled).
+static rmoe_status forward_direct(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
+                                  int32_t* ids_out, float* w_out, cudaStream_t st) {
+  StageMarks marks(L, st);
+  const int32_t* ids_src = nullptr;
+  const float* w_src = nullptr;
+  rmoe_status s = enqueue_forward(L, x, x_dtype, T, out, st, marks, &ids_src, &w_src);
+  if (s != RMOE_OK) return s;
+  marks.commit();
+  const size_t n = static_cast<size_t>(T) * L->desc.topk;
   if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, ids_src, n * 4, cudaMemcpyDefault, st), "ids out");
   if (w_out) RMOE_CUDA(cudaMemcpyAsync(w_out, w_src, n * 4, cudaMemcpyDefault, st), "weights out");
+  L->stats.kernel_launches += L->last_launches;
   L->stats.forward_calls++;
   L->stats.tokens_routed += T;
   return RMOE_OK;
 }
+
+// Folds the stage events of a profiled graph launch into the profile (waits for them).
+static rmoe_status drain_graph_profile(rmoe_layer* L, GraphEntry& g) {
+  if (!g.pending) return RMOE_OK;
+  RMOE_CUDA(cudaEventSynchronize(g.ev[RMOE_NUM_STAGES]), "profile event");
+  for (int s = 0; s < RMOE_NUM_STAGES; s++) {
+    float ms = 0.0f;
+    RMOE_CUDA(cudaEventElapsedTime(&ms, g.ev[s], g.ev[s + 1]), "profile elapsed");
+    L->prof_ms[s] += ms;
+  }
+  L->prof_calls++;
+  g.pending = false;
+  return RMOE_OK;
+}
+
+// Captures the forward for (T, dtype, routing out, profiling) once; the caller's x / out /
+// routing buffers are bound per launch through memcpy nodes at the graph's ends.
+static rmoe_status capture_graph(rmoe_layer* L, int x_dtype, int T, bool want_rt, GraphEntry& g) {
+  const size_t H = L->desc.hidden;
+  g.x_bytes = static_cast<size_t>(T) * H * (x_dtype == RMOE_BF16 ? 2 : 4);
+  g.out_bytes = static_cast<size_t>(T) * H * 4;
+  g.rt_bytes = static_cast<size_t>(T) * L->desc.topk * 4;
+  g.profiled = L->profiling;
+  StageMarks marks(L, L->cap);
+  if (g.profiled) {
+    for (cudaEvent_t& e : g.ev) RMOE_CUDA(cudaEventCreate(&e), "graph profile event");
+    marks.fixed = g.ev;
+  }
+  const int32_t* ids_src = nullptr;
+  const float* w_src = nullptr;
+  RMOE_CUDA(cudaStreamBeginCapture(L->cap, cudaStreamCaptureModeThreadLocal), "begin capture");
+  rmoe_status s = enqueue_forward(L, L->x_dev, x_dtype, T, L->out_dev, L->cap, marks, &ids_src, &w_src);
+  cudaGraph_t graph = nullptr;
+  cudaError_t ce = cudaStreamEndCapture(L->cap, &graph);
+  if (s != RMOE_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return s;
+  }
+  if (ce != cudaSuccess) return cuda_fail(ce, "end capture");
+  g.ids_src = ids_src;
+  g.w_src = w_src;
+  g.launches = L->last_launches;
+  auto done = [&](cudaError_t e, const char* what) {
+    cudaGraphDestroy(graph);
+    return cuda_fail(e, what);
+  };
+  size_t n_roots = 0, n_nodes = 0;
+  cudaError_t e = cudaGraphGetRootNodes(graph, nullptr, &n_roots);
+  if (e != cudaSuccess) return done(e, "graph roots");
+  std::vector<cudaGraphNode_t> roots(n_roots);
+  if ((e = cudaGraphGetRootNodes(graph, roots.data(), &n_roots)) != cudaSuccess) return done(e, "graph roots");
+  if ((e = cudaGraphGetNodes(graph, nullptr, &n_nodes)) != cudaSuccess) return done(e, "graph nodes");
+  std::vector<cudaGraphNode_t> nodes(n_nodes), leaves;
+  if ((e = cudaGraphGetNodes(graph, nodes.data(), &n_nodes)) != cudaSuccess) return done(e, "graph nodes");
+  for (cudaGraphNode_t nd : nodes) {
+    size_t nd_out = 0;
+    if ((e = cudaGraphNodeGetDependentNodes(nd, nullptr, &nd_out)) != cudaSuccess) return done(e, "graph deps");
+    if (nd_out == 0) leaves.push_back(nd);
+  }
+  if ((e = cudaGraphAddMemcpyNode1D(&g.in_node, graph, nullptr, 0, L->x_dev, L->x_stage, g.x_bytes,
+                                    cudaMemcpyDeviceToDevice)) != cudaSuccess)
+    return done(e, "graph input node");
+  for (cudaGraphNode_t r : roots)
+    if ((e = cudaGraphAddDependencies(graph, &g.in_node, &r, 1)) != cudaSuccess) return done(e, "graph input deps");
+  if ((e = cudaGraphAddMemcpyNode1D(&g.out_node, graph, leaves.data(), leaves.size(), L->out_stage,
+                                    L->out_dev, g.out_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+    return done(e, "graph output node");
+  if (want_rt) {
+    if ((e = cudaGraphAddMemcpyNode1D(&g.ids_node, graph, leaves.data(), leaves.size(), L->ids_host_stage,
+                                      g.ids_src, g.rt_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+      return done(e, "graph ids node");
+    if ((e = cudaGraphAddMemcpyNode1D(&g.w_node, graph, leaves.data(), leaves.size(), L->w_host_stage,
+                                      g.w_src, g.rt_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+      return done(e, "graph weights node");
+  }
+  if ((e = cudaGraphInstantiate(&g.exec, graph, 0)) != cudaSuccess) return done(e, "graph instantiate");
+  cudaGraphDestroy(graph);
+  return RMOE_OK;
+}
+
+// One graph launch per call; x/out/ids/w are device pointers of the caller.
+static rmoe_status forward_graph(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
+                                 int32_t* ids_out, float* w_out, cudaStream_t st) {
+  const bool want_rt = ids_out || w_out;
+  const uint64_t key = static_cast<uint64_t>(T) | (static_cast<uint64_t>(x_dtype) << 24) |
+                       (static_cast<uint64_t>(want_rt) << 28) |
+                       (static_cast<uint64_t>(L->profiling) << 29);
+  auto it = L->graphs.find(key);
+  if (it == L->graphs.end()) {
+    GraphEntry g;
+    rmoe_status s = capture_graph(L, x_dtype, T, want_rt, g);
+    if (s != RMOE_OK) {
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+      for (cudaEvent_t e : g.ev)
+        if (e) cudaEventDestroy(e);
+      return s;
+    }
+    it = L->graphs.emplace(key, g).first;
+  }
+  GraphEntry& g = it->second;
+  rmoe_status s = drain_graph_profile(L, g);
+  if (s != RMOE_OK) return s;
+  RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.in_node, L->x_dev, x, g.x_bytes, cudaMemcpyDeviceToDevice),
+            "bind x");
+  RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.out_node, out, L->out_dev, g.out_bytes, cudaMemcpyDeviceToDevice),
+            "bind out");
+  if (want_rt) {
+    RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.ids_node, ids_out ? static_cast<void*>(ids_out) : L->ids_host_stage,
+                                                 g.ids_src, g.rt_bytes, cudaMemcpyDeviceToDevice),
+              "bind ids");
+    RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.w_node, w_out ? static_cast<void*>(w_out) : L->w_host_stage,
+                                                 g.w_src, g.rt_bytes, cudaMemcpyDeviceToDevice),
+              "bind weights");
+  }
+  RMOE_CUDA(cudaGraphLaunch(g.exec, st), "graph launch");
+  g.pending = g.profiled;
+  L->stats.kernel_launches += g.launches;
+  L->stats.forward_calls++;
+  L->stats.tokens_routed += T;
+  return RMOE_OK;
+}
+
+static bool graph_path(const rmoe_layer* L, int T) { return L->use_graphs && small_path(L, T); }
+
+static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
+                                int32_t* ids_out, float* w_out, cudaStream_t st) {
+  rmoe_status s = check_uploaded(L);
+  if (s != RMOE_OK) return s;
+  if (graph_path(L, T)) return forward_graph(L, x, x_dtype, T, out, ids_out, w_out, st);
+  return forward_direct(L, x, x_dtype, T, out, ids_out, w_out, st);
+}
+
 
 extern "C" rmoe_status rmoe_moe_forward(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T,
                                         float* out, int32_t* ids_out, float* w_out, void* stream) {
@@ -771,11 +987,16 @@ extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, 
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   const size_t H = L->desc.hidden;
   const size_t xb = static_cast<size_t>(T) * H * (x_dtype == RMOE_BF16 ? 2 : 4);
-  RMOE_CUDA(cudaMemcpyAsync(L->x_dev, x_host, xb, cudaMemcpyHostToDevice, L->stream), "x to device");
-  if ((s = forward_into(L, L->x_dev, x_dtype, T, L->out_dev, ids_host, w_host, L->stream)) != RMOE_OK)
+  RMOE_CUDA(cudaMemcpyAsync(L->x_stage, x_host, xb, cudaMemcpyHostToDevice, L->stream), "x to device");
+  const size_t n = static_cast<size_t>(T) * L->desc.topk;
+  const bool rt = ids_host || w_host;
+  if ((s = forward_into(L, L->x_stage, x_dtype, T, L->out_stage, rt ? L->ids_host_stage : nullptr,
+                        rt ? L->w_host_stage : nullptr, L->stream)) != RMOE_OK)
     return s;
-  RMOE_CUDA(cudaMemcpyAsync(out_host, L->out_dev, static_cast<size_t>(T) * H * 4, cudaMemcpyDeviceToHost, L->stream),
+  RMOE_CUDA(cudaMemcpyAsync(out_host, L->out_stage, static_cast<size_t>(T) * H * 4, cudaMemcpyDeviceToHost, L->stream),
             "out to host");
+  if (ids_host) RMOE_CUDA(cudaMemcpyAsync(ids_host, L->ids_host_stage, n * 4, cudaMemcpyDeviceToHost, L->stream), "ids to host");
+  if (w_host) RMOE_CUDA(cudaMemcpyAsync(w_host, L->w_host_stage, n * 4, cudaMemcpyDeviceToHost, L->stream), "weights to host");
   RMOE_CUDA(cudaStreamSynchronize(L->stream), "rmoe_moe_forward_host synchronize");
   return RMOE_OK;
 }

@@ -7,10 +7,14 @@
 // bytes and finish together; ~140 KB per SM is in flight, enough to cover HBM latency at full
 // bandwidth. No spin is unbounded: a wait that exceeds its limit sets a flag and returns.
 //
-//   MODE 0 (gate/up): task = one row index r of one chunk: gate row r and up row r (K = H);
-//                     epilogue h = silu(g) * u per token (glm52/moe.rs:58-70), |h| max per row.
-//   MODE 1 (down):    task = 8 consecutive rows of the chunk expert's down matrix (K = inter);
-//                     epilogue y[position][row] for the chunk's positions.
+//   MODE 0 (gate/up):  stage = gate row r + up row r of a chunk's expert (K = H); epilogue
+//                      h = silu(g) * u per token (glm52/moe.rs:58-70) and |h| max per position.
+//   MODE 1 (down):     stage = 8 down rows of a chunk's expert (K = inter); h enters as f32 and
+//                      is scaled into f16 on the fly; epilogue y[position][row].
+//   MODE 2 (down + combine, one token per stage): task = (token, 8 output rows); its stages
+//                      are the 8 down rows of each of the token's k experts and of the shared
+//                      expert, accumulated in rank order with their routing weight / shared gate
+//                      into out[token][rows] (glm52/moe.rs:508-512, qwen38/generate.rs:346-349).
 #include <algorithm>
 
 #include "common.cuh"
@@ -23,56 +27,83 @@ namespace rmoe {
 constexpr int kStages = 16;
 constexpr int kConsumers = 8;
 constexpr int kPipeThreads = (kConsumers + 1) * 32;
+constexpr int kDownRows = 8;
 
 struct PipeArgs {
   ExpertTable tab;
   ExpertFormat f;
   DispatchBuffers d;
-  const uint16_t* xin;   // MODE 0: xq [T][x_ld] by token; MODE 1: hq [P][x_ld] by position
-  const int32_t* xexp;   // MODE 0: per token; MODE 1: per position
+  const void* xin;       // MODE 0: xq f16 [T][x_ld] by token; MODE 1/2: h f32 [P][x_ld]
+  const int32_t* xexp;   // MODE 0: per-token exponent
+  const uint32_t* hmax;  // MODE 0: written (|h| max per position); MODE 1/2: read
   int x_ld;
-  float* out;            // MODE 0: h [P][out_ld]; MODE 1: y [P][out_ld]
+  float* out;            // MODE 0: h [P][out_ld]; MODE 1: y [P][out_ld]; MODE 2: out [T][out_ld]
   int out_ld;
-  uint32_t* hmax;        // MODE 0 only
   int H;
   int slot_bytes;
+  int T, k;              // MODE 2
+  const int32_t* ids;    // MODE 2: routing [T][k] (positions from d.inv)
+  int e_begin;           // MODE 2
   unsigned* err_flag;
 };
 
-template <int MODE>
-struct PipeGeom;
-template <>
-struct PipeGeom<0> {
-  static constexpr int kRows = 2;  // gate row + up row
-};
-template <>
-struct PipeGeom<1> {
-  static constexpr int kRows = 8;  // 8 down rows
+// What the consumers of one slot need besides the weights, written by the producer so that no
+// consumer waits on a dependent global load.
+struct SlotMeta {
+  int r, eslot, p0, n;
+  int row[8];   // activation row of each chunk position (token for MODE 0, position otherwise)
+  int xe[8];    // its power-of-two exponent
+  float w;      // MODE 2: routing weight / shared gate of this stage's position
+  int last;     // MODE 2: 1 on the task's final stage
 };
 
-// What the consumers of one slot need besides the weights, written by the producer so that no
-// consumer waits on a dependent global load: chunk, row index, expert slot, first position,
-// positions in the chunk, and each position's activation row and power-of-two exponent.
-struct SlotMeta {
-  int c, r, eslot, p0, n;
-  int row[8];
-  int xe[8];
-};
+__device__ __forceinline__ void load_x_f16(const void* xin, int row, int x_ld, int b,
+                                           uint32_t (&xv)[16]) {
+  const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xin) +
+                                                   static_cast<size_t>(row) * x_ld + b * 32);
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const uint4 v = __ldg(xp + q);
+    xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
+  }
+}
+
+// 32 f32 activations scaled by 2^e into f16 pairs in the format's pair order.
+template <int FMT>
+__device__ __forceinline__ void load_x_f32(const void* xin, int row, int x_ld, int b, float sc,
+                                           uint32_t (&xv)[16]) {
+  const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(xin) +
+                                                     static_cast<size_t>(row) * x_ld + b * 32);
+#pragma unroll
+  for (int g = 0; g < 4; g++) {  // 8-element groups
+    const float4 lo = __ldg(xp + 2 * g), hi = __ldg(xp + 2 * g + 1);
+    const float v[8] = {lo.x * sc, lo.y * sc, lo.z * sc, lo.w * sc,
+                        hi.x * sc, hi.y * sc, hi.z * sc, hi.w * sc};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      __half2 h2 = FMT == kMxfp4 ? __floats2half2_rn(v[2 * q], v[2 * q + 1])
+                                 : __floats2half2_rn(v[q], v[q + 4]);
+      xv[4 * g + q] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+  }
+}
 
 template <int FMT, int MT, int MODE>
 __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int NR = PipeGeom<MODE>::kRows;
+  constexpr int NR = MODE == 0 ? 2 : kDownRows;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * a.slot_bytes);
   uint64_t* empty = full + kStages;
   SlotMeta* meta = reinterpret_cast<SlotMeta*>(empty + kStages);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int32_t* task0 = MODE == 0 ? a.d.ch_task_gu : a.d.ch_task_dn;
   const int n_chunks = *a.d.n_chunks;
-  const int n_tasks = task0[n_chunks];
+  const int has_shared = a.tab.shared_inter > 0;
+  const int S = MODE == 2 ? a.k + has_shared : 1;  // stages per task
+  const int n_tasks = MODE == 2 ? a.T * (a.H / kDownRows) : task0[n_chunks];
   const int t_begin = static_cast<int>((static_cast<long long>(n_tasks) * blockIdx.x) / gridDim.x);
   const int t_end = static_cast<int>((static_cast<long long>(n_tasks) * (blockIdx.x + 1)) / gridDim.x);
-  const int my_tasks = t_end - t_begin;
+  const int my_stages = (t_end - t_begin) * S;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -85,15 +116,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
 
   if (warp == kConsumers) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && my_tasks > 0) {
-      // tasks of this CTA are contiguous: one search, then the chunk index only moves forward
-      int c = find_chunk(task0, n_chunks, t_begin);
-      SlotMeta cm;
-      int c_end = 0;
+    if (lane == 0 && my_stages > 0) {
+      int c = 0, c_end = 0;
+      SlotMeta cm{};
       ExpertPtrs ep{};
       auto enter_chunk = [&](int cc) {
         c_end = task0[cc + 1];
-        cm.c = cc;
         cm.eslot = a.d.ch_expert[cc];
         cm.p0 = a.d.ch_pos[cc];
         cm.n = a.d.ch_n[cc];
@@ -102,17 +130,41 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
           const int mm = m < cm.n ? m : 0;
           const int row = MODE == 0 ? a.d.perm_tok[cm.p0 + mm] : cm.p0 + mm;
           cm.row[m] = row;
-          cm.xe[m] = a.xexp[row];
+          cm.xe[m] = MODE == 0 ? a.xexp[row] : f16_row_exponent(__uint_as_float(a.hmax[row]));
         }
         ep = expert_ptrs(a.tab, cm.eslot);
       };
-      enter_chunk(c);
-      for (int i = 0; i < my_tasks; i++) {
+      if (MODE != 2) {
+        c = find_chunk(task0, n_chunks, t_begin);
+        enter_chunk(c);
+      }
+      for (int i = 0; i < my_stages; i++) {
         const int slot = i % kStages;
-        const int task = t_begin + i;
-        while (task >= c_end) enter_chunk(++c);
-        const int r = task - task0[c];
-        const int eslot = cm.eslot;
+        const int task = t_begin + i / S;
+        int r = 0;
+        if (MODE == 2) {
+          const int t = task / (a.H / kDownRows), j = i % S;
+          r = task % (a.H / kDownRows);
+          int p = -1, eslot = 0;
+          if (j < a.k) {
+            p = a.d.inv[t * a.k + j];
+            if (p >= 0) eslot = a.ids[t * a.k + j] - a.e_begin;
+          } else {
+            p = a.d.offsets[a.tab.n_local] + t;
+            eslot = a.tab.n_local;
+          }
+          cm.eslot = eslot;
+          cm.p0 = p;
+          cm.n = p >= 0 ? 1 : 0;
+          cm.row[0] = p;
+          cm.xe[0] = p >= 0 ? f16_row_exponent(__uint_as_float(a.hmax[p])) : 0;
+          cm.w = p >= 0 ? a.d.perm_w[p] : 0.0f;
+          cm.last = j == S - 1;
+          ep = expert_ptrs(a.tab, eslot);
+        } else {
+          while (task >= c_end) enter_chunk(++c);
+          r = task - task0[c];
+        }
         if (i >= kStages && !mbar_wait_bounded(&empty[slot], ((i / kStages) - 1) & 1, a.err_flag, 1u))
           return;
         uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes;
@@ -127,8 +179,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
                    &full[slot]);
           bulk_g2s(dst + 2 * rb + sb, static_cast<const uint8_t*>(ep.up_scale) + static_cast<size_t>(r) * sb, sb,
                    &full[slot]);
+        } else if (cm.n == 0) {
+          mbar_arrive(&full[slot]);  // nothing to load for a position on another EP rank
         } else {
-          const int K = eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter;
+          const int K = cm.eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter;
           const uint32_t rb = K / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, K));
           const size_t row0 = static_cast<size_t>(r) * NR;
           mbar_arrive_expect_tx(&full[slot], NR * (rb + sb));
@@ -141,93 +195,115 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
   }
 
   // -------------------------------------------------------------- consumers
-  for (int i = warp; i < my_tasks; i += kConsumers) {
-    const int slot = i % kStages;
-    if (!mbar_wait_bounded(&full[slot], (i / kStages) & 1, a.err_flag, 2u)) return;
-    const SlotMeta& sm = meta[slot];
-    const int r = sm.r;
-    const int eslot = sm.eslot;
-    const int p0 = sm.p0, n = sm.n;
-    const int K = MODE == 0 ? a.H : (eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter);
-    const uint32_t rb = K / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, K));
-    const uint8_t* base = smem + static_cast<size_t>(slot) * a.slot_bytes;
-    const uint16_t* xr[MT];
-    int xe[MT];
+  const int my_tasks = t_end - t_begin;
+  for (int tk = warp; tk < my_tasks; tk += kConsumers) {
+    float comb[NR];  // MODE 2: weighted sum over the task's stages (per-lane partials)
 #pragma unroll
-    for (int m = 0; m < MT; m++) {
-      xr[m] = a.xin + static_cast<size_t>(sm.row[m]) * a.x_ld;
-      xe[m] = sm.xe[m];
-    }
-    float acc[NR][MT];
+    for (int q = 0; q < NR; q++) comb[q] = 0.0f;
+    for (int j = 0; j < S; j++) {
+      const int i = tk * S + j;
+      const int slot = i % kStages;
+      if (!mbar_wait_bounded(&full[slot], (i / kStages) & 1, a.err_flag, 2u)) return;
+      const SlotMeta& sm = meta[slot];
+      const int r = sm.r, eslot = sm.eslot, p0 = sm.p0, n = sm.n;
+      const int K = MODE == 0 ? a.H : (eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter);
+      const uint32_t rb = K / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, K));
+      const uint8_t* base = smem + static_cast<size_t>(slot) * a.slot_bytes;
+      int rows[MT], xe[MT];
 #pragma unroll
-    for (int q = 0; q < NR; q++)
+      for (int m = 0; m < MT; m++) {
+        rows[m] = sm.row[m];
+        xe[m] = sm.xe[m];
+      }
+      const float wstage = sm.w;
+      const int last = sm.last;
+      float acc[NR][MT];
 #pragma unroll
-      for (int m = 0; m < MT; m++) acc[q][m] = 0.0f;
-    const int nblk = K / 32;
-    // rows in groups of (at most) 4 keep the decoded nibbles in registers
+      for (int q = 0; q < NR; q++)
 #pragma unroll
-    for (int g0 = 0; g0 < NR; g0 += 4) {
-      constexpr int G = NR < 4 ? NR : 4;
-      for (int b = lane; b < nblk; b += 32) {
-        uint32_t hw[G][16];
-        float sc[G];
+        for (int m = 0; m < MT; m++) acc[q][m] = 0.0f;
+      const int nblk = K / 32;
+      // rows in groups of (at most) 4 keep the decoded nibbles in registers
 #pragma unroll
-        for (int q = 0; q < G; q++) {
-          const uint4 w = *reinterpret_cast<const uint4*>(base + (g0 + q) * rb + b * 16);
-          decode_block<FMT>(w, hw[q]);
-          sc[q] = block_scale_smem<FMT>(base + NR * rb + (g0 + q) * sb, b, a.f);
+      for (int g0 = 0; g0 < NR; g0 += 4) {
+        constexpr int G = NR < 4 ? NR : 4;
+        for (int b = lane; b < nblk; b += 32) {
+          uint32_t hw[G][16];
+          float sc[G];
+#pragma unroll
+          for (int q = 0; q < G; q++) {
+            const uint4 w = *reinterpret_cast<const uint4*>(base + (g0 + q) * rb + b * 16);
+            decode_block<FMT>(w, hw[q]);
+            sc[q] = block_scale_smem<FMT>(base + NR * rb + (g0 + q) * sb, b, a.f);
+          }
+#pragma unroll
+          for (int m = 0; m < MT; m++) {
+            if (m >= n) break;
+            uint32_t xv[16];
+            if (MODE == 0) load_x_f16(a.xin, rows[m], a.x_ld, b, xv);
+            else load_x_f32<FMT>(a.xin, rows[m], a.x_ld, b, exp2i(xe[m]), xv);
+#pragma unroll
+            for (int q = 0; q < G; q++) {
+              uint32_t a0 = 0, a1 = 0;
+#pragma unroll
+              for (int e = 0; e < 16; e += 2) {
+                a0 = hfma2u(hw[q][e], xv[e], a0);
+                a1 = hfma2u(hw[q][e + 1], xv[e + 1], a1);
+              }
+              acc[g0 + q][m] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[q], acc[g0 + q][m]);
+            }
+          }
         }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // this slot's shared memory is no longer read
+      if (MODE == 2) {
+        if (n > 0) {
+          const float wu = wstage * exp2i(-xe[0]);
+#pragma unroll
+          for (int q = 0; q < NR; q++) comb[q] = fmaf(wu, acc[q][0], comb[q]);
+        }
+        if (last) {
+#pragma unroll
+          for (int q = 0; q < NR; q++) comb[q] = warp_sum(comb[q]);
+          const int t = (t_begin + tk) / (a.H / kDownRows);
+          if (lane < NR) {
+            float v = comb[0];
+#pragma unroll
+            for (int q = 1; q < NR; q++)
+              if (lane == q) v = comb[q];
+            a.out[static_cast<size_t>(t) * a.out_ld + r * NR + lane] = v;
+          }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int q = 0; q < NR; q++)
+#pragma unroll
+        for (int m = 0; m < MT; m++) acc[q][m] = warp_sum(acc[q][m]);
+      if (MODE == 0) {
 #pragma unroll
         for (int m = 0; m < MT; m++) {
           if (m >= n) break;
-          const uint4* xp = reinterpret_cast<const uint4*>(xr[m] + static_cast<size_t>(b) * 32);
-          uint32_t xv[16];
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            const uint4 v = __ldg(xp + q);
-            xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
-          }
-#pragma unroll
-          for (int q = 0; q < G; q++) {
-            uint32_t a0 = 0, a1 = 0;
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              a0 = hfma2u(hw[q][e], xv[e], a0);
-              a1 = hfma2u(hw[q][e + 1], xv[e + 1], a1);
-            }
-            acc[g0 + q][m] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[q], acc[g0 + q][m]);
+          if (lane == m) {
+            const float unscale = exp2i(-xe[m]);
+            const float g = acc[0][m] * unscale, u = acc[1][m] * unscale;
+            const float hv = __fmul_rn(silu_ref(g), u);
+            a.out[static_cast<size_t>(p0 + m) * a.out_ld + r] = hv;
+            atomicMax(const_cast<uint32_t*>(a.hmax) + p0 + m, __float_as_uint(fabsf(hv)));
           }
         }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);  // shared memory of this slot is no longer read
+      } else {
 #pragma unroll
-    for (int q = 0; q < NR; q++)
+        for (int m = 0; m < MT; m++) {
+          if (m >= n) break;
+          if (lane < NR) {
+            float v = acc[0][m];
 #pragma unroll
-      for (int m = 0; m < MT; m++) acc[q][m] = warp_sum(acc[q][m]);
-    if (MODE == 0) {
-#pragma unroll
-      for (int m = 0; m < MT; m++) {
-        if (m >= n) break;
-        if (lane == m) {
-          const float unscale = exp2i(-xe[m]);
-          const float g = acc[0][m] * unscale, u = acc[1][m] * unscale;
-          const float hv = __fmul_rn(silu_ref(g), u);
-          a.out[static_cast<size_t>(p0 + m) * a.out_ld + r] = hv;
-          atomicMax(a.hmax + p0 + m, __float_as_uint(fabsf(hv)));
-        }
-      }
-    } else {
-#pragma unroll
-      for (int m = 0; m < MT; m++) {
-        if (m >= n) break;
-        if (lane < NR) {
-          float v = acc[0][m];
-#pragma unroll
-          for (int q = 1; q < NR; q++)
-            if (lane == q) v = acc[q][m];
-          a.out[static_cast<size_t>(p0 + m) * a.out_ld + r * NR + lane] = v * exp2i(-xe[m]);
+            for (int q = 1; q < NR; q++)
+              if (lane == q) v = acc[q][m];
+            a.out[static_cast<size_t>(p0 + m) * a.out_ld + r * NR + lane] = v * exp2i(-xe[m]);
+          }
         }
       }
     }
@@ -242,6 +318,7 @@ static cudaError_t launch_pipe_fmt(int mt, const PipeArgs& a, int grid, size_t s
     kern<<<grid, kPipeThreads, smem, st>>>(a);
     return cudaGetLastError();
   };
+  if (MODE == 2) return go(gemv_pipe_kernel<FMT, 1, MODE>);
   switch (mt) {
     case 1: return go(gemv_pipe_kernel<FMT, 1, MODE>);
     case 2: return go(gemv_pipe_kernel<FMT, 2, MODE>);
@@ -255,9 +332,9 @@ bool pipe_supported(const ExpertFormat& f, int H, int inter, int shared_inter) {
   auto ok_k = [&](int K, int rows) {
     return K % 32 == 0 && (K / 2) % 16 == 0 && (scale_row_bytes_host(f, K) * rows) % 16 == 0;
   };
-  if (!ok_k(H, 1)) return false;
-  if (!ok_k(inter, PipeGeom<1>::kRows)) return false;
-  if (shared_inter && !ok_k(shared_inter, PipeGeom<1>::kRows)) return false;
+  if (H % kDownRows || !ok_k(H, 1)) return false;
+  if (!ok_k(inter, kDownRows)) return false;
+  if (shared_inter && !ok_k(shared_inter, kDownRows)) return false;
   return true;
 }
 
@@ -272,31 +349,57 @@ static int num_sms() {
   return n;
 }
 
+static size_t pipe_smem(int slot_bytes) {
+  return static_cast<size_t>(kStages) * slot_bytes + kStages * 16 + kStages * sizeof(SlotMeta);
+}
+
 cudaError_t launch_pipe_gate_up(const ExpertTable& tab, const ExpertFormat& f,
                                 const DispatchBuffers& d, const uint16_t* xq,
                                 const int32_t* xexp, int H, int mt, float* h, uint32_t* hmax,
                                 int h_ld, unsigned* err_flag, cudaStream_t st) {
-  PipeArgs a{tab, f, d, xq, xexp, H, h, h_ld, hmax, H, 0, err_flag};
-  a.slot_bytes = static_cast<int>(2 * (H / 2 + scale_row_bytes_host(f, H)));
-  a.slot_bytes = (a.slot_bytes + 127) / 128 * 128;
-  const size_t smem = static_cast<size_t>(kStages) * a.slot_bytes + kStages * 16 + kStages * sizeof(SlotMeta);
+  PipeArgs a{};
+  a.tab = tab; a.f = f; a.d = d; a.xin = xq; a.xexp = xexp; a.hmax = hmax; a.x_ld = H;
+  a.out = h; a.out_ld = h_ld; a.H = H; a.err_flag = err_flag;
+  a.slot_bytes = static_cast<int>((2 * (H / 2 + scale_row_bytes_host(f, H)) + 127) / 128 * 128);
+  const size_t smem = pipe_smem(a.slot_bytes);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (f.fmt == kMxfp4) return launch_pipe_fmt<kMxfp4, 0>(mt, a, num_sms(), smem, st);
   return launch_pipe_fmt<kInt4g, 0>(mt, a, num_sms(), smem, st);
 }
 
+static int down_slot_bytes(const ExpertTable& tab, const ExpertFormat& f) {
+  const int K = std::max(tab.inter, tab.shared_inter);
+  return static_cast<int>((kDownRows * (K / 2 + scale_row_bytes_host(f, K)) + 127) / 128 * 128);
+}
+
 cudaError_t launch_pipe_down(const ExpertTable& tab, const ExpertFormat& f,
-                             const DispatchBuffers& d, const uint16_t* hq, const int32_t* hexp,
+                             const DispatchBuffers& d, const float* h, const uint32_t* hmax,
                              int H, int mt, int h_ld, float* y, unsigned* err_flag,
                              cudaStream_t st) {
-  PipeArgs a{tab, f, d, hq, hexp, h_ld, y, H, nullptr, H, 0, err_flag};
-  const int K = std::max(tab.inter, tab.shared_inter);
-  a.slot_bytes = static_cast<int>(PipeGeom<1>::kRows * (K / 2 + scale_row_bytes_host(f, K)));
-  a.slot_bytes = (a.slot_bytes + 127) / 128 * 128;
-  const size_t smem = static_cast<size_t>(kStages) * a.slot_bytes + kStages * 16 + kStages * sizeof(SlotMeta);
+  PipeArgs a{};
+  a.tab = tab; a.f = f; a.d = d; a.xin = h; a.hmax = hmax; a.x_ld = h_ld;
+  a.out = y; a.out_ld = H; a.H = H; a.err_flag = err_flag;
+  a.slot_bytes = down_slot_bytes(tab, f);
+  const size_t smem = pipe_smem(a.slot_bytes);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (f.fmt == kMxfp4) return launch_pipe_fmt<kMxfp4, 1>(mt, a, num_sms(), smem, st);
   return launch_pipe_fmt<kInt4g, 1>(mt, a, num_sms(), smem, st);
+}
+
+cudaError_t launch_pipe_down_combine(const ExpertTable& tab, const ExpertFormat& f,
+                                     const DispatchBuffers& d, const float* h,
+                                     const uint32_t* hmax, const int32_t* ids, int T, int k,
+                                     int e_begin, int H, int h_ld, float* out, unsigned* err_flag,
+                                     cudaStream_t st) {
+  PipeArgs a{};
+  a.tab = tab; a.f = f; a.d = d; a.xin = h; a.hmax = hmax; a.x_ld = h_ld;
+  a.out = out; a.out_ld = H; a.H = H; a.err_flag = err_flag;
+  a.T = T; a.k = k; a.ids = ids; a.e_begin = e_begin;
+  a.slot_bytes = down_slot_bytes(tab, f);
+  const size_t smem = pipe_smem(a.slot_bytes);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (f.fmt == kMxfp4) return launch_pipe_fmt<kMxfp4, 2>(1, a, num_sms(), smem, st);
+  return launch_pipe_fmt<kInt4g, 2>(1, a, num_sms(), smem, st);
 }
 
 }  // namespace rmoe

@@ -145,10 +145,17 @@ cudaError_t launch_pipe_gate_up(const ExpertTable& tab, const ExpertFormat& f,
                                 const DispatchBuffers& d, const uint16_t* xq,
                                 const int32_t* xexp, int H, int mt, float* h, uint32_t* hmax,
                                 int h_ld, unsigned* err_flag, cudaStream_t st);
+// h enters as f32 [P][h_ld] with its per-position |h| max; scaled to f16 inside the kernel.
 cudaError_t launch_pipe_down(const ExpertTable& tab, const ExpertFormat& f,
-                             const DispatchBuffers& d, const uint16_t* hq, const int32_t* hexp,
+                             const DispatchBuffers& d, const float* h, const uint32_t* hmax,
                              int H, int mt, int h_ld, float* y, unsigned* err_flag,
                              cudaStream_t st);
+// Down projection fused with the weighted combine and the gated shared expert (small T).
+cudaError_t launch_pipe_down_combine(const ExpertTable& tab, const ExpertFormat& f,
+                                     const DispatchBuffers& d, const float* h,
+                                     const uint32_t* hmax, const int32_t* ids, int T, int k,
+                                     int e_begin, int H, int h_ld, float* out, unsigned* err_flag,
+                                     cudaStream_t st);
 
 // ---- generic GEMM entry points (experts.cu) ----
 cudaError_t launch_matmul_q(float* y, const void* x, int x_dtype, const uint8_t* data,
