@@ -33,6 +33,7 @@ rmoe_status fail(rmoe_status s, const char* fmt, ...) {
 }
 
 rmoe_status cuda_fail(cudaError_t e, const char* what) {
+  cudaGetLastError();  // a handled (non-sticky) error must not resurface in a later check
   return fail(e == cudaErrorMemoryAllocation ? RMOE_OUT_OF_MEMORY : RMOE_CUDA_ERROR, "%s: %s",
               what, cudaGetErrorString(e));
 }
@@ -71,6 +72,7 @@ struct rmoe_ctx {
 // One captured forward (CUDA graph) for a (T, dtype, routing-out, profiling) combination. The
 // caller's buffers are reached through memcpy nodes whose pointers are set per launch.
 struct GraphEntry {
+  cudaGraph_t graph = nullptr;  // kept alive: its node handles address the exec's nodes
   cudaGraphExec_t exec = nullptr;
   cudaGraphNode_t in_node = nullptr, out_node = nullptr, ids_node = nullptr, w_node = nullptr;
   size_t x_bytes = 0, out_bytes = 0, rt_bytes = 0;
@@ -147,6 +149,7 @@ struct rmoe_layer {
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
     for (auto& kv : graphs) {
       if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+      if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
       for (cudaEvent_t e : kv.second.ev)
         if (e) cudaEventDestroy(e);
     }
@@ -910,7 +913,7 @@ static rmoe_status capture_graph(rmoe_layer* L, int x_dtype, int T, bool want_rt
       return done(e, "graph weights node");
   }
   if ((e = cudaGraphInstantiate(&g.exec, graph, 0)) != cudaSuccess) return done(e, "graph instantiate");
-  cudaGraphDestroy(graph);
+  g.graph = graph;
   return RMOE_OK;
 }
 
@@ -927,6 +930,7 @@ static rmoe_status forward_graph(rmoe_layer* L, const void* x, int x_dtype, int 
     rmoe_status s = capture_graph(L, x_dtype, T, want_rt, g);
     if (s != RMOE_OK) {
       if (g.exec) cudaGraphExecDestroy(g.exec);
+      if (g.graph) cudaGraphDestroy(g.graph);
       for (cudaEvent_t e : g.ev)
         if (e) cudaEventDestroy(e);
       return s;

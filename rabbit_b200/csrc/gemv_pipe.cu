@@ -103,7 +103,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
   const int n_tasks = MODE == 2 ? a.T * (a.H / kDownRows) : task0[n_chunks];
   const int t_begin = static_cast<int>((static_cast<long long>(n_tasks) * blockIdx.x) / gridDim.x);
   const int t_end = static_cast<int>((static_cast<long long>(n_tasks) * (blockIdx.x + 1)) / gridDim.x);
-  const int my_stages = (t_end - t_begin) * S;
+  const int my_tasks = t_end - t_begin;
+  // Consumer warp w owns local tasks w, w + 8, ... and ring slots 2w and 2w + 1; its q-th stage
+  // (task w + 8 * (q / S), sub-stage q % S) lives in slot 2w + (q & 1), phase q / 2. Every slot
+  // therefore has exactly one consumer, which never waits more than one phase ahead.
+  auto warp_stages = [&](int w) { return w < my_tasks ? ((my_tasks - 1 - w) / kConsumers + 1) * S : 0; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -115,8 +119,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
   __syncthreads();
 
   if (warp == kConsumers) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && my_stages > 0) {
+    // ------------------------------------------------------------ producer (round-robin)
+    if (lane == 0 && my_tasks > 0) {
       int c = 0, c_end = 0;
       SlotMeta cm{};
       ExpertPtrs ep{};
@@ -138,56 +142,60 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
         c = find_chunk(task0, n_chunks, t_begin);
         enter_chunk(c);
       }
-      for (int i = 0; i < my_stages; i++) {
-        const int slot = i % kStages;
-        const int task = t_begin + i / S;
-        int r = 0;
-        if (MODE == 2) {
-          const int t = task / (a.H / kDownRows), j = i % S;
-          r = task % (a.H / kDownRows);
-          int p = -1, eslot = 0;
-          if (j < a.k) {
-            p = a.d.inv[t * a.k + j];
-            if (p >= 0) eslot = a.ids[t * a.k + j] - a.e_begin;
+      const int rounds = warp_stages(0);
+      for (int q = 0; q < rounds; q++) {
+        for (int w = 0; w < kConsumers; w++) {
+          if (q >= warp_stages(w)) continue;
+          const int task = t_begin + w + kConsumers * (q / S);
+          const int j = q % S;
+          const int slot = 2 * w + (q & 1);
+          int r = 0;
+          if (MODE == 2) {
+            const int t = task / (a.H / kDownRows);
+            r = task % (a.H / kDownRows);
+            int p = -1, eslot = 0;
+            if (j < a.k) {
+              p = a.d.inv[t * a.k + j];
+              if (p >= 0) eslot = a.ids[t * a.k + j] - a.e_begin;
+            } else {
+              p = a.d.offsets[a.tab.n_local] + t;
+              eslot = a.tab.n_local;
+            }
+            cm.eslot = eslot;
+            cm.p0 = p;
+            cm.n = p >= 0 ? 1 : 0;
+            cm.row[0] = p;
+            cm.xe[0] = p >= 0 ? f16_row_exponent(__uint_as_float(a.hmax[p])) : 0;
+            cm.w = p >= 0 ? a.d.perm_w[p] : 0.0f;
+            cm.last = j == S - 1;
+            ep = expert_ptrs(a.tab, eslot);
           } else {
-            p = a.d.offsets[a.tab.n_local] + t;
-            eslot = a.tab.n_local;
+            while (task >= c_end) enter_chunk(++c);
+            r = task - task0[c];
           }
-          cm.eslot = eslot;
-          cm.p0 = p;
-          cm.n = p >= 0 ? 1 : 0;
-          cm.row[0] = p;
-          cm.xe[0] = p >= 0 ? f16_row_exponent(__uint_as_float(a.hmax[p])) : 0;
-          cm.w = p >= 0 ? a.d.perm_w[p] : 0.0f;
-          cm.last = j == S - 1;
-          ep = expert_ptrs(a.tab, eslot);
-        } else {
-          while (task >= c_end) enter_chunk(++c);
-          r = task - task0[c];
-        }
-        if (i >= kStages && !mbar_wait_bounded(&empty[slot], ((i / kStages) - 1) & 1, a.err_flag, 1u))
-          return;
-        uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes;
-        cm.r = r;
-        meta[slot] = cm;
-        if (MODE == 0) {
-          const uint32_t rb = a.H / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, a.H));
-          mbar_arrive_expect_tx(&full[slot], 2 * (rb + sb));
-          bulk_g2s(dst, ep.gate + static_cast<size_t>(r) * rb, rb, &full[slot]);
-          bulk_g2s(dst + rb, ep.up + static_cast<size_t>(r) * rb, rb, &full[slot]);
-          bulk_g2s(dst + 2 * rb, static_cast<const uint8_t*>(ep.gate_scale) + static_cast<size_t>(r) * sb, sb,
-                   &full[slot]);
-          bulk_g2s(dst + 2 * rb + sb, static_cast<const uint8_t*>(ep.up_scale) + static_cast<size_t>(r) * sb, sb,
-                   &full[slot]);
-        } else if (cm.n == 0) {
-          mbar_arrive(&full[slot]);  // nothing to load for a position on another EP rank
-        } else {
-          const int K = cm.eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter;
-          const uint32_t rb = K / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, K));
-          const size_t row0 = static_cast<size_t>(r) * NR;
-          mbar_arrive_expect_tx(&full[slot], NR * (rb + sb));
-          bulk_g2s(dst, ep.down + row0 * rb, NR * rb, &full[slot]);
-          bulk_g2s(dst + NR * rb, static_cast<const uint8_t*>(ep.down_scale) + row0 * sb, NR * sb, &full[slot]);
+          if (q >= 2 && !mbar_wait_bounded(&empty[slot], ((q / 2) - 1) & 1, a.err_flag, 1u)) return;
+          uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes;
+          cm.r = r;
+          meta[slot] = cm;
+          if (MODE == 0) {
+            const uint32_t rb = a.H / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, a.H));
+            mbar_arrive_expect_tx(&full[slot], 2 * (rb + sb));
+            bulk_g2s(dst, ep.gate + static_cast<size_t>(r) * rb, rb, &full[slot]);
+            bulk_g2s(dst + rb, ep.up + static_cast<size_t>(r) * rb, rb, &full[slot]);
+            bulk_g2s(dst + 2 * rb, static_cast<const uint8_t*>(ep.gate_scale) + static_cast<size_t>(r) * sb, sb,
+                     &full[slot]);
+            bulk_g2s(dst + 2 * rb + sb, static_cast<const uint8_t*>(ep.up_scale) + static_cast<size_t>(r) * sb,
+                     sb, &full[slot]);
+          } else if (cm.n == 0) {
+            mbar_arrive(&full[slot]);  // nothing to load for a position on another EP rank
+          } else {
+            const int K = cm.eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter;
+            const uint32_t rb = K / 2, sb = static_cast<uint32_t>(scale_row_bytes(a.f, K));
+            const size_t row0 = static_cast<size_t>(r) * NR;
+            mbar_arrive_expect_tx(&full[slot], NR * (rb + sb));
+            bulk_g2s(dst, ep.down + row0 * rb, NR * rb, &full[slot]);
+            bulk_g2s(dst + NR * rb, static_cast<const uint8_t*>(ep.down_scale) + row0 * sb, NR * sb, &full[slot]);
+          }
         }
       }
     }
@@ -195,15 +203,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
   }
 
   // -------------------------------------------------------------- consumers
-  const int my_tasks = t_end - t_begin;
+  int q = 0;  // this warp's stage counter
   for (int tk = warp; tk < my_tasks; tk += kConsumers) {
     float comb[NR];  // MODE 2: weighted sum over the task's stages (per-lane partials)
 #pragma unroll
-    for (int q = 0; q < NR; q++) comb[q] = 0.0f;
-    for (int j = 0; j < S; j++) {
-      const int i = tk * S + j;
-      const int slot = i % kStages;
-      if (!mbar_wait_bounded(&full[slot], (i / kStages) & 1, a.err_flag, 2u)) return;
+    for (int qq = 0; qq < NR; qq++) comb[qq] = 0.0f;
+    for (int j = 0; j < S; j++, q++) {
+      const int slot = 2 * warp + (q & 1);
+      if (!mbar_wait_bounded(&full[slot], (q / 2) & 1, a.err_flag, 2u)) return;
       const SlotMeta& sm = meta[slot];
       const int r = sm.r, eslot = sm.eslot, p0 = sm.p0, n = sm.n;
       const int K = MODE == 0 ? a.H : (eslot >= a.tab.n_local ? a.tab.shared_inter : a.tab.inter);
@@ -219,9 +226,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
       const int last = sm.last;
       float acc[NR][MT];
 #pragma unroll
-      for (int q = 0; q < NR; q++)
+      for (int qq = 0; qq < NR; qq++)
 #pragma unroll
-        for (int m = 0; m < MT; m++) acc[q][m] = 0.0f;
+        for (int m = 0; m < MT; m++) acc[qq][m] = 0.0f;
       const int nblk = K / 32;
       // rows in groups of (at most) 4 keep the decoded nibbles in registers
 #pragma unroll
@@ -231,10 +238,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
           uint32_t hw[G][16];
           float sc[G];
 #pragma unroll
-          for (int q = 0; q < G; q++) {
-            const uint4 w = *reinterpret_cast<const uint4*>(base + (g0 + q) * rb + b * 16);
-            decode_block<FMT>(w, hw[q]);
-            sc[q] = block_scale_smem<FMT>(base + NR * rb + (g0 + q) * sb, b, a.f);
+          for (int qq = 0; qq < G; qq++) {
+            const uint4 w = *reinterpret_cast<const uint4*>(base + (g0 + qq) * rb + b * 16);
+            decode_block<FMT>(w, hw[qq]);
+            sc[qq] = block_scale_smem<FMT>(base + NR * rb + (g0 + qq) * sb, b, a.f);
           }
 #pragma unroll
           for (int m = 0; m < MT; m++) {
@@ -243,14 +250,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
             if (MODE == 0) load_x_f16(a.xin, rows[m], a.x_ld, b, xv);
             else load_x_f32<FMT>(a.xin, rows[m], a.x_ld, b, exp2i(xe[m]), xv);
 #pragma unroll
-            for (int q = 0; q < G; q++) {
+            for (int qq = 0; qq < G; qq++) {
               uint32_t a0 = 0, a1 = 0;
 #pragma unroll
               for (int e = 0; e < 16; e += 2) {
-                a0 = hfma2u(hw[q][e], xv[e], a0);
-                a1 = hfma2u(hw[q][e + 1], xv[e + 1], a1);
+                a0 = hfma2u(hw[qq][e], xv[e], a0);
+                a1 = hfma2u(hw[qq][e + 1], xv[e + 1], a1);
               }
-              acc[g0 + q][m] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[q], acc[g0 + q][m]);
+              acc[g0 + qq][m] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[qq], acc[g0 + qq][m]);
             }
           }
         }
@@ -261,26 +268,26 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
         if (n > 0) {
           const float wu = wstage * exp2i(-xe[0]);
 #pragma unroll
-          for (int q = 0; q < NR; q++) comb[q] = fmaf(wu, acc[q][0], comb[q]);
+          for (int qq = 0; qq < NR; qq++) comb[qq] = fmaf(wu, acc[qq][0], comb[qq]);
         }
         if (last) {
 #pragma unroll
-          for (int q = 0; q < NR; q++) comb[q] = warp_sum(comb[q]);
+          for (int qq = 0; qq < NR; qq++) comb[qq] = warp_sum(comb[qq]);
           const int t = (t_begin + tk) / (a.H / kDownRows);
           if (lane < NR) {
             float v = comb[0];
 #pragma unroll
-            for (int q = 1; q < NR; q++)
-              if (lane == q) v = comb[q];
+            for (int qq = 1; qq < NR; qq++)
+              if (lane == qq) v = comb[qq];
             a.out[static_cast<size_t>(t) * a.out_ld + r * NR + lane] = v;
           }
         }
         continue;
       }
 #pragma unroll
-      for (int q = 0; q < NR; q++)
+      for (int qq = 0; qq < NR; qq++)
 #pragma unroll
-        for (int m = 0; m < MT; m++) acc[q][m] = warp_sum(acc[q][m]);
+        for (int m = 0; m < MT; m++) acc[qq][m] = warp_sum(acc[qq][m]);
       if (MODE == 0) {
 #pragma unroll
         for (int m = 0; m < MT; m++) {
@@ -300,8 +307,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
           if (lane < NR) {
             float v = acc[0][m];
 #pragma unroll
-            for (int q = 1; q < NR; q++)
-              if (lane == q) v = acc[q][m];
+            for (int qq = 1; qq < NR; qq++)
+              if (lane == qq) v = acc[qq][m];
             a.out[static_cast<size_t>(p0 + m) * a.out_ld + r * NR + lane] = v * exp2i(-xe[m]);
           }
         }
