@@ -169,7 +169,8 @@ struct StageMarks {
   void mark() {
     if (!L->profiling) return;
     if (fixed) {
-      if (n_fixed < RMOE_NUM_STAGES + 1) cudaEventRecord(fixed[n_fixed++], st);
+      // inside stream capture only an "external" record becomes an event node of the graph
+      if (n_fixed < RMOE_NUM_STAGES + 1) cudaEventRecordWithFlags(fixed[n_fixed++], st, cudaEventRecordExternal);
       return;
     }
     cudaEvent_t e;
