@@ -222,6 +222,12 @@ def run_gpu(args):
     ctx = rb.Context(local)
     cfg = synth.CONFIGS[PREFILL_CFG]  # same weights as config 1; sized for the prefill run
     dcfg = synth.CONFIGS[DECODE_CFG]
+    if args.small_experts:
+        # profiling-size variant: identical shapes and kernels, fewer resident experts
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, n_experts=args.small_experts)
+        dcfg = dataclasses.replace(dcfg, n_experts=args.small_experts)
     layer = build_layer(ctx, cfg, max_tokens=cfg.tokens)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     n_steps = args.warmup + args.steps
@@ -393,6 +399,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--small-experts", type=int, default=0,
+                    help="profiling only: resident experts (same shapes); not a bench config")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

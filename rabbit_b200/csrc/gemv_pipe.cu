@@ -44,6 +44,7 @@ struct PipeArgs {
   int T, k;              // MODE 2
   const int32_t* ids;    // MODE 2: routing [T][k] (positions from d.inv)
   int e_begin;           // MODE 2
+  int hbuf_ok;           // MODE 2: the h rows of one token fit in the shared-memory cache
   unsigned* err_flag;
 };
 
@@ -203,11 +204,58 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
   }
 
   // -------------------------------------------------------------- consumers
+  // MODE 2: the h rows (f16, scaled) of the first token this CTA serves live in shared memory,
+  // loaded once; stages of that token read them from there.
+  uint16_t* hbuf = reinterpret_cast<uint16_t*>(meta + kStages);
+  int h_tok = -1;
+  const int kmax = max(a.tab.inter, a.tab.shared_inter);
+  if (MODE == 2 && a.hbuf_ok && my_tasks > 0) {
+    h_tok = t_begin / (a.H / kDownRows);
+    for (int jj = 0; jj < S; jj++) {
+      int p;
+      int Kj;
+      if (jj < a.k) {
+        p = a.d.inv[h_tok * a.k + jj];
+        Kj = a.tab.inter;
+      } else {
+        p = a.d.offsets[a.tab.n_local] + h_tok;
+        Kj = a.tab.shared_inter;
+      }
+      if (p < 0) continue;
+      const float sc = exp2i(f16_row_exponent(__uint_as_float(a.hmax[p])));
+      const float* src = static_cast<const float*>(a.xin) + static_cast<size_t>(p) * a.x_ld;
+      uint16_t* dst = hbuf + static_cast<size_t>(jj) * kmax;
+      for (int i = threadIdx.x * 8; i < Kj; i += kConsumers * 32 * 8) {
+        const float4 lo = __ldg(reinterpret_cast<const float4*>(src + i));
+        const float4 hi = __ldg(reinterpret_cast<const float4*>(src + i + 4));
+        const float v[8] = {lo.x * sc, lo.y * sc, lo.z * sc, lo.w * sc,
+                            hi.x * sc, hi.y * sc, hi.z * sc, hi.w * sc};
+        uint32_t pk[4];
+#pragma unroll
+        for (int qq = 0; qq < 4; qq++) {
+          __half2 h2 = FMT == kMxfp4 ? __floats2half2_rn(v[2 * qq], v[2 * qq + 1])
+                                     : __floats2half2_rn(v[qq], v[qq + 4]);
+          pk[qq] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(dst + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32));  // consumer warps only
+  }
+
+  // MODE 0 with one token per chunk: the lane's activation blocks stay in registers across
+  // stages (reloaded only when the chunk's token changes).
+  constexpr int XB = 8;  // blocks per lane cached (H <= 8192)
+  uint32_t xc[XB][16];
+  int xc_row = -1;
+  const bool xcache = MODE == 0 && MT == 1 && (a.H / 32) <= 32 * XB;
+
   int q = 0;  // this warp's stage counter
   for (int tk = warp; tk < my_tasks; tk += kConsumers) {
     float comb[NR];  // MODE 2: weighted sum over the task's stages (per-lane partials)
 #pragma unroll
     for (int qq = 0; qq < NR; qq++) comb[qq] = 0.0f;
+    const int t_task = MODE == 2 ? (t_begin + tk) / (a.H / kDownRows) : 0;
     for (int j = 0; j < S; j++, q++) {
       const int slot = 2 * warp + (q & 1);
       if (!mbar_wait_bounded(&full[slot], (q / 2) & 1, a.err_flag, 2u)) return;
@@ -230,34 +278,105 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
 #pragma unroll
         for (int m = 0; m < MT; m++) acc[qq][m] = 0.0f;
       const int nblk = K / 32;
-      // rows in groups of (at most) 4 keep the decoded nibbles in registers
+      if (MODE == 0 && xcache) {
+        // ---- gate/up, one token: x blocks from registers
+        if (rows[0] != xc_row) {
 #pragma unroll
-      for (int g0 = 0; g0 < NR; g0 += 4) {
-        constexpr int G = NR < 4 ? NR : 4;
-        for (int b = lane; b < nblk; b += 32) {
-          uint32_t hw[G][16];
-          float sc[G];
-#pragma unroll
-          for (int qq = 0; qq < G; qq++) {
-            const uint4 w = *reinterpret_cast<const uint4*>(base + (g0 + qq) * rb + b * 16);
-            decode_block<FMT>(w, hw[qq]);
-            sc[qq] = block_scale_smem<FMT>(base + NR * rb + (g0 + qq) * sb, b, a.f);
+          for (int jb = 0; jb < XB; jb++) {
+            const int b = lane + 32 * jb;
+            if (b < nblk) load_x_f16(a.xin, rows[0], a.x_ld, b, xc[jb]);
           }
+          xc_row = rows[0];
+        }
 #pragma unroll
-          for (int m = 0; m < MT; m++) {
-            if (m >= n) break;
+        for (int jb = 0; jb < XB; jb++) {
+          const int b = lane + 32 * jb;
+          if (b >= nblk) break;
+          uint32_t hg[16], hu[16];
+          decode_block<FMT>(*reinterpret_cast<const uint4*>(base + b * 16), hg);
+          decode_block<FMT>(*reinterpret_cast<const uint4*>(base + rb + b * 16), hu);
+          const float sg = block_scale_smem<FMT>(base + 2 * rb, b, a.f);
+          const float su = block_scale_smem<FMT>(base + 2 * rb + sb, b, a.f);
+          uint32_t g0 = 0, g1 = 0, u0 = 0, u1 = 0;
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            g0 = hfma2u(hg[e], xc[jb][e], g0);
+            g1 = hfma2u(hg[e + 1], xc[jb][e + 1], g1);
+            u0 = hfma2u(hu[e], xc[jb][e], u0);
+            u1 = hfma2u(hu[e + 1], xc[jb][e + 1], u1);
+          }
+          acc[0][0] = fmaf(h2sum_f32(g0) + h2sum_f32(g1), sg, acc[0][0]);
+          acc[NR > 1 ? 1 : 0][0] = fmaf(h2sum_f32(u0) + h2sum_f32(u1), su, acc[NR > 1 ? 1 : 0][0]);
+        }
+      } else if (MODE == 2) {
+        // ---- down + combine, one position: h blocks from shared memory (or converted from
+        //      global for a token other than the cached one); each block serves all 8 rows
+        if (n > 0) {
+          const bool from_smem = t_task == h_tok;
+          for (int b = lane; b < nblk; b += 32) {
             uint32_t xv[16];
-            if (MODE == 0) load_x_f16(a.xin, rows[m], a.x_ld, b, xv);
-            else load_x_f32<FMT>(a.xin, rows[m], a.x_ld, b, exp2i(xe[m]), xv);
+            if (from_smem) {
+              const uint4* hp = reinterpret_cast<const uint4*>(hbuf + static_cast<size_t>(j) * kmax + b * 32);
+#pragma unroll
+              for (int qq = 0; qq < 4; qq++) {
+                const uint4 v = hp[qq];
+                xv[4 * qq] = v.x; xv[4 * qq + 1] = v.y; xv[4 * qq + 2] = v.z; xv[4 * qq + 3] = v.w;
+              }
+            } else {
+              load_x_f32<FMT>(a.xin, rows[0], a.x_ld, b, exp2i(xe[0]), xv);
+            }
+#pragma unroll
+            for (int g0 = 0; g0 < NR; g0 += 4) {
+              uint32_t hw[4][16];
+              float sc[4];
+#pragma unroll
+              for (int qq = 0; qq < 4; qq++) {
+                decode_block<FMT>(*reinterpret_cast<const uint4*>(base + (g0 + qq) * rb + b * 16), hw[qq]);
+                sc[qq] = block_scale_smem<FMT>(base + NR * rb + (g0 + qq) * sb, b, a.f);
+              }
+#pragma unroll
+              for (int qq = 0; qq < 4; qq++) {
+                uint32_t a0 = 0, a1 = 0;
+#pragma unroll
+                for (int e = 0; e < 16; e += 2) {
+                  a0 = hfma2u(hw[qq][e], xv[e], a0);
+                  a1 = hfma2u(hw[qq][e + 1], xv[e + 1], a1);
+                }
+                acc[g0 + qq][0] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[qq], acc[g0 + qq][0]);
+              }
+            }
+          }
+        }
+      } else {
+        // ---- general: rows in groups of (at most) 4 keep the decoded nibbles in registers
+#pragma unroll
+        for (int g0 = 0; g0 < NR; g0 += 4) {
+          constexpr int G = NR < 4 ? NR : 4;
+          for (int b = lane; b < nblk; b += 32) {
+            uint32_t hw[G][16];
+            float sc[G];
 #pragma unroll
             for (int qq = 0; qq < G; qq++) {
-              uint32_t a0 = 0, a1 = 0;
+              const uint4 w = *reinterpret_cast<const uint4*>(base + (g0 + qq) * rb + b * 16);
+              decode_block<FMT>(w, hw[qq]);
+              sc[qq] = block_scale_smem<FMT>(base + NR * rb + (g0 + qq) * sb, b, a.f);
+            }
 #pragma unroll
-              for (int e = 0; e < 16; e += 2) {
-                a0 = hfma2u(hw[qq][e], xv[e], a0);
-                a1 = hfma2u(hw[qq][e + 1], xv[e + 1], a1);
+            for (int m = 0; m < MT; m++) {
+              if (m >= n) break;
+              uint32_t xv[16];
+              if (MODE == 0) load_x_f16(a.xin, rows[m], a.x_ld, b, xv);
+              else load_x_f32<FMT>(a.xin, rows[m], a.x_ld, b, exp2i(xe[m]), xv);
+#pragma unroll
+              for (int qq = 0; qq < G; qq++) {
+                uint32_t a0 = 0, a1 = 0;
+#pragma unroll
+                for (int e = 0; e < 16; e += 2) {
+                  a0 = hfma2u(hw[qq][e], xv[e], a0);
+                  a1 = hfma2u(hw[qq][e + 1], xv[e + 1], a1);
+                }
+                acc[g0 + qq][m] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[qq], acc[g0 + qq][m]);
               }
-              acc[g0 + qq][m] = fmaf(h2sum_f32(a0) + h2sum_f32(a1), sc[qq], acc[g0 + qq][m]);
             }
           }
         }
@@ -273,13 +392,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
         if (last) {
 #pragma unroll
           for (int qq = 0; qq < NR; qq++) comb[qq] = warp_sum(comb[qq]);
-          const int t = (t_begin + tk) / (a.H / kDownRows);
           if (lane < NR) {
             float v = comb[0];
 #pragma unroll
             for (int qq = 1; qq < NR; qq++)
               if (lane == qq) v = comb[qq];
-            a.out[static_cast<size_t>(t) * a.out_ld + r * NR + lane] = v;
+            a.out[static_cast<size_t>(t_task) * a.out_ld + r * NR + lane] = v;
           }
         }
         continue;
@@ -294,7 +412,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
           if (m >= n) break;
           if (lane == m) {
             const float unscale = exp2i(-xe[m]);
-            const float g = acc[0][m] * unscale, u = acc[1][m] * unscale;
+            const float g = acc[0][m] * unscale, u = acc[NR > 1 ? 1 : 0][m] * unscale;
             const float hv = __fmul_rn(silu_ref(g), u);
             a.out[static_cast<size_t>(p0 + m) * a.out_ld + r] = hv;
             atomicMax(const_cast<uint32_t*>(a.hmax) + p0 + m, __float_as_uint(fabsf(hv)));
@@ -403,7 +521,13 @@ cudaError_t launch_pipe_down_combine(const ExpertTable& tab, const ExpertFormat&
   a.out = out; a.out_ld = H; a.H = H; a.err_flag = err_flag;
   a.T = T; a.k = k; a.ids = ids; a.e_begin = e_begin;
   a.slot_bytes = down_slot_bytes(tab, f);
-  const size_t smem = pipe_smem(a.slot_bytes);
+  const int kmax = std::max(tab.inter, tab.shared_inter);
+  const size_t hbuf = static_cast<size_t>(k + (tab.shared_inter > 0 ? 1 : 0)) * kmax * 2;
+  size_t smem = pipe_smem(a.slot_bytes);
+  if (smem + hbuf <= 227 * 1024) {
+    a.hbuf_ok = 1;
+    smem += hbuf;
+  }
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (f.fmt == kMxfp4) return launch_pipe_fmt<kMxfp4, 2>(1, a, num_sms(), smem, st);
   return launch_pipe_fmt<kInt4g, 2>(1, a, num_sms(), smem, st);
