@@ -203,6 +203,16 @@ RMOE_API rmoe_status rmoe_moe_forward_host(rmoe_layer* layer, const void* x_host
 RMOE_API rmoe_status rmoe_matmul_mxfp4(float* y, const void* x, int32_t x_dtype, const uint8_t* data,
                               const uint8_t* block_scale, int32_t s, int32_t i, int32_t o,
                               void* stream);
+/* No counterpart in the reference: rmoe_matmul_mxfp4 without any device allocation, for callers
+ * that cannot allocate on the hot path (device memory reserved by their own arena). Scratch is a
+ * fixed device array of RMOE_NOALLOC_SCRATCH_BYTES; shapes needing more (16-bit s*i + 4*s + 256
+ * bytes) are rejected with RMOE_INVALID_ARG. The first call on each device (with that device
+ * current) resolves the array's address; make it before any stream capture. Calls that overlap
+ * in time on one device share the scratch and race: order them on one stream. */
+#define RMOE_NOALLOC_SCRATCH_BYTES ((8u << 20) + 4096u) /* s*i <= 4M at s <= 512, e.g. 512 x 8192 */
+RMOE_API rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_t x_dtype,
+                                      const uint8_t* data, const uint8_t* block_scale, int32_t s,
+                                      int32_t i, int32_t o, void* stream);
 /* kernels::matmul_i4_grouped (src/kernels.rs:276-296) */
 RMOE_API rmoe_status rmoe_matmul_i4_grouped(float* y, const void* x, int32_t x_dtype, const uint8_t* q4,
                                    const void* scale, int32_t scale_dtype, int32_t group_size,

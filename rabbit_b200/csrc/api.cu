@@ -8,6 +8,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -1059,5 +1060,59 @@ extern "C" rmoe_status rmoe_synth_bytes(void* dst, size_t n, uint64_t key, int32
   if (mode != 0 && mode != 1) return fail(RMOE_INVALID_ARG, "rmoe_synth_bytes: mode %d", mode);
   cudaError_t e = launch_synth_bytes(dst, n, key, mode, lo, hi, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rmoe_synth_bytes");
+  return RMOE_OK;
+}
+
+// ------------------------------------------------------------------- no-allocation matmul
+// rmoe_matmul_mxfp4 takes its activation scratch (f16 rows + per-row exponents) from
+// cudaMallocAsync on every call. Some callers cannot allocate at that point: a serving loop
+// that has reserved the device's free memory for its own page arena (so a pool allocation can
+// fail with out-of-memory, or make the driver trim/grow the pool mid-decode), or a caller whose
+// allocator policy forbids device allocations on the hot path. This variant takes the same
+// scratch from a fixed file-scope device array instead, so it never allocates or frees.
+//
+// The scratch holds s*i f16 values + s int32 exponents (+256 bytes of alignment slack):
+// matmul_q_workspace_bytes(s, i) <= RMOE_NOALLOC_SCRATCH_BYTES (8 MiB + 4 KiB): s*i <= 4M
+// elements for s <= 512, e.g. 512 rows at i = 8192. The prep kernel writes every scratch byte the GEMV reads before
+// the GEMV runs, so nothing has to start at zero. Calls that overlap in time on one device
+// (two streams, or two host threads, with no ordering between them) share the array and race;
+// order them on one stream.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[RMOE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+extern "C" rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_t x_dtype,
+                                                 const uint8_t* data, const uint8_t* block_scale,
+                                                 int32_t s, int32_t i, int32_t o, void* stream) {
+  const char* what = "rmoe_matmul_mxfp4_noalloc";
+  if (!y || !x || !data || !block_scale) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  if (s < 0 || i <= 0 || o < 0) return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d o=%d", what, s, i, o);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  const size_t ws = matmul_q_workspace_bytes(s, i);
+  if (ws > RMOE_NOALLOC_SCRATCH_BYTES)
+    return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d needs %zu scratch bytes, above the fixed %zu (split the rows)",
+                what, s, i, ws, static_cast<size_t>(RMOE_NOALLOC_SCRATCH_BYTES));
+  int dev = -1;
+  RMOE_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(RMOE_INVALID_ARG, "%s: device %d", what, dev);
+  void* scratch = nullptr;
+  {
+    // First call on a device (that device current): resolve the array's address once.
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      RMOE_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  cudaError_t e = launch_matmul_q(y, x, x_dtype == RMOE_BF16 ? kBF16 : kF32, data, block_scale,
+                                  ExpertFormat{kMxfp4, 32, kF32}, s, i, o, scratch, ws,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, what);
   return RMOE_OK;
 }

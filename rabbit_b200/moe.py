@@ -242,6 +242,15 @@ def matmul_mxfp4(y, x, data, block_scale, s, i, o, stream=None):
     return y
 
 
+def matmul_mxfp4_noalloc(y, x, data, block_scale, s, i, o, stream=None):
+    """matmul_mxfp4 with its activation scratch in a fixed device array (no allocation; shapes
+    whose scratch exceeds the array raise INVALID_ARG; overlapping calls on one device race)."""
+    _require_cuda(y, x, data, block_scale)
+    check(_lib.load().rmoe_matmul_mxfp4_noalloc(_ptr(y), _ptr(x), _dtype_code(x), _ptr(data),
+                                                _ptr(block_scale), s, i, o, _stream(stream)))
+    return y
+
+
 def matmul_i4_grouped(y, x, q4, scale, group_size, s, i, o, stream=None):
     """kernels::matmul_i4_grouped (src/kernels.rs:276-296); scale f32 or bf16."""
     _require_cuda(y, x, q4, scale)
