@@ -245,8 +245,6 @@ def run_gpu(args):
         flush.zero_()
         step(i)
     torch.cuda.synchronize()
-    layer.set_profiling(True)
-    layer.profile()
     launches0 = layer.stats()["kernel_launches"]
     clocks = ClockSampler(local)
     clocks.start()
@@ -267,9 +265,17 @@ def run_gpu(args):
     clk = clocks.stop()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(step_ms)
+    launches = (layer.stats()["kernel_launches"] - launches0) // args.steps
+    # stage breakdown (and the roofline kernel's duration) from a separate pass over the same
+    # tokens with per-stage events on the launching stream; the timed steps above carry none
+    layer.set_profiling(True)
+    layer.profile()
+    for j in range(args.steps):
+        flush.zero_()
+        step(args.warmup + j)
+    torch.cuda.synchronize()
     prof = layer.profile()
     layer.set_profiling(False)
-    launches = (layer.stats()["kernel_launches"] - launches0) // args.steps
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

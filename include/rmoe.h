@@ -203,6 +203,13 @@ RMOE_API rmoe_status rmoe_moe_forward_host(rmoe_layer* layer, const void* x_host
 RMOE_API rmoe_status rmoe_matmul_mxfp4(float* y, const void* x, int32_t x_dtype, const uint8_t* data,
                               const uint8_t* block_scale, int32_t s, int32_t i, int32_t o,
                               void* stream);
+/* No counterpart in the reference: kernels::matmul_mxfp4 on the tcgen05 tensor cores. The
+ * weights are consumed as stored (E2M1 + E8M0 per 32, kind::mxf4 block32); x becomes a four-term
+ * E2M1 expansion (~11 significant bits), products are exact and accumulated in f32. Needs
+ * i % 32 == 0 (else RMOE_NOT_SUPPORTED). */
+RMOE_API rmoe_status rmoe_matmul_mxfp4_tc(float* y, const void* x, int32_t x_dtype, const uint8_t* data,
+                                 const uint8_t* block_scale, int32_t s, int32_t i, int32_t o,
+                                 void* stream);
 /* No counterpart in the reference: rmoe_matmul_mxfp4 without any device allocation, for callers
  * that cannot allocate on the hot path (device memory reserved by their own arena). Scratch is a
  * fixed device array of RMOE_NOALLOC_SCRATCH_BYTES; shapes needing more (16-bit s*i + 4*s + 256

@@ -2,7 +2,7 @@
 experts, weighted combine with the gated shared expert) behind a C ABI (include/rmoe.h)."""
 from ._lib import RmoeError, load as load_library
 from .moe import (Context, MoeLayer, matmul, matmul_i4_grouped, matmul_mxfp4,
-                  matmul_mxfp4_noalloc, synth_bytes)
+                  matmul_mxfp4_noalloc, matmul_mxfp4_tc, synth_bytes)
 
-__all__ = ["RmoeError", "load_library", "Context", "MoeLayer", "matmul", "matmul_mxfp4", "matmul_mxfp4_noalloc",
+__all__ = ["RmoeError", "load_library", "Context", "MoeLayer", "matmul", "matmul_mxfp4", "matmul_mxfp4_noalloc", "matmul_mxfp4_tc",
            "matmul_i4_grouped", "synth_bytes"]

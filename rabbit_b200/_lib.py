@@ -72,6 +72,7 @@ PROTOTYPES = {
     "rmoe_moe_forward": (C.c_int, [P, P, I32, I32, P, P, P, P]),
     "rmoe_moe_forward_host": (C.c_int, [P, P, I32, I32, P, P, P]),
     "rmoe_matmul_mxfp4": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
+    "rmoe_matmul_mxfp4_tc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_mxfp4_noalloc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_i4_grouped": (C.c_int, [P, P, I32, P, P, I32, I32, I32, I32, I32, P]),
     "rmoe_matmul_f32": (C.c_int, [P, P, I32, P, I32, I32, I32, I32, P]),

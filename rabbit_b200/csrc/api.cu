@@ -1032,6 +1032,30 @@ extern "C" rmoe_status rmoe_matmul_mxfp4(float* y, const void* x, int32_t x_dtyp
                   s, i, o, stream);
 }
 
+extern "C" rmoe_status rmoe_matmul_mxfp4_tc(float* y, const void* x, int32_t x_dtype,
+                                            const uint8_t* data, const uint8_t* block_scale, int32_t s,
+                                            int32_t i, int32_t o, void* stream) {
+  const char* what = "rmoe_matmul_mxfp4_tc";
+  if (!y || !x || !data || !block_scale) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  if (s < 0 || i <= 0 || o < 0) return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d o=%d", what, s, i, o);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  if (s == 0 || o == 0) return RMOE_OK;
+  if (!mxf4_tc_supported(s, i, o)) return fail(RMOE_NOT_SUPPORTED, "%s: i=%d (needs a multiple of 32)", what, i);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t ws = mxf4_tc_workspace_bytes(s, i) + 16;
+  void* buf = nullptr;
+  RMOE_CUDA(cudaMallocAsync(&buf, ws, st), "tc matmul workspace");
+  unsigned* err = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(buf) + ws - 16);
+  cudaError_t e = cudaMemsetAsync(err, 0, 4, st);
+  if (e == cudaSuccess)
+    e = launch_mxf4_tc_matmul(y, x, x_dtype == RMOE_BF16 ? kBF16 : kF32, data, block_scale, s, i, o, buf,
+                              ws - 16, err, st);
+  cudaError_t e2 = cudaFreeAsync(buf, st);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  if (e2 != cudaSuccess) return cuda_fail(e2, what);
+  return RMOE_OK;
+}
+
 extern "C" rmoe_status rmoe_matmul_i4_grouped(float* y, const void* x, int32_t x_dtype,
                                               const uint8_t* q4, const void* scale,
                                               int32_t scale_dtype, int32_t group_size, int32_t s,

@@ -163,6 +163,13 @@ cudaError_t launch_matmul_q(float* y, const void* x, int x_dtype, const uint8_t*
                             void* workspace, size_t ws_bytes, cudaStream_t st);
 size_t matmul_q_workspace_bytes(int s, int i);
 
+// ---- tensor-core MXFP4 GEMM (mxf4_tc.cu) ----
+bool mxf4_tc_supported(int S, int I, int O);
+size_t mxf4_tc_workspace_bytes(int S, int I);
+cudaError_t launch_mxf4_tc_matmul(float* y, const void* x, int x_dtype, const uint8_t* w,
+                                  const uint8_t* w_sf, int S, int I, int O, void* ws, size_t ws_bytes,
+                                  unsigned* err, cudaStream_t st);
+
 // ---- synthetic bytes (synth.cu) ----
 cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,
                                cudaStream_t st);

@@ -117,11 +117,119 @@ __global__ void __launch_bounds__(128) router_certified_kernel(
   }
 }
 
+// One token (decode): a block of 4 warps per expert, 128 slices of c = H/128 elements. Every
+// load of a lane's slice (up to 64 weights and 64 activations) is issued before the chain
+// consumes any, so each warp has a single memory round trip. Same bound as above with the
+// 128-slice scan: each slice sum passes through at most 5 (warp scan) + 4 (cross-warp) roundings,
+// counted as 10 |B_l|.
+// 8 elements of a DT row as raw 16-byte words (bf16: one word, f32: two) and their f32 values.
+template <int DT>
+__device__ __forceinline__ void load_raw8(const void* p, size_t idx, uint4 (&r)[2]) {
+  if (DT == kBF16) {
+    r[0] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + idx));
+  } else {
+    const uint4* f = reinterpret_cast<const uint4*>(static_cast<const float*>(p) + idx);
+    r[0] = __ldg(f);
+    r[1] = __ldg(f + 1);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void expand8(const uint4 (&r)[2], float (&v)[8]) {
+  if (DT == kBF16) {
+    const uint32_t w[4] = {r[0].x, r[0].y, r[0].z, r[0].w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      v[2 * q] = __uint_as_float(w[q] << 16);
+      v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+    }
+  } else {
+    v[0] = __uint_as_float(r[0].x); v[1] = __uint_as_float(r[0].y);
+    v[2] = __uint_as_float(r[0].z); v[3] = __uint_as_float(r[0].w);
+    v[4] = __uint_as_float(r[1].x); v[5] = __uint_as_float(r[1].y);
+    v[6] = __uint_as_float(r[1].z); v[7] = __uint_as_float(r[1].w);
+  }
+}
+
+template <int XD, int WD>
+__global__ void __launch_bounds__(128, 4) router_certified_t1_kernel(
+    const void* __restrict__ x, const void* __restrict__ w, float* __restrict__ mid,
+    float* __restrict__ err, int H) {
+  __shared__ float s_tot[4], s_term[4], s_p[4];
+  const int e = blockIdx.x;
+  const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int c = H / 128;  // multiple of 8
+  const size_t off = static_cast<size_t>(threadIdx.x) * c;
+  const size_t wrow = static_cast<size_t>(e) * H + off;
+  float b = 0.0f, A = 0.0f, P = 0.0f;
+  for (int j0 = 0; j0 < c; j0 += 64) {
+    uint4 wr[8][2], xr[8][2];
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+      if (j0 + 8 * g < c) {
+        load_raw8<WD>(w, wrow + j0 + 8 * g, wr[g]);
+        load_raw8<XD>(x, off + j0 + 8 * g, xr[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+      if (j0 + 8 * g >= c) break;
+      float wv[8], xv[8];
+      expand8<WD>(wr[g], wv);
+      expand8<XD>(xr[g], xv);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float p = __fmul_rn(xv[i], wv[i]);
+        b = __fadd_rn(b, p);
+        A += fabsf(b);
+        P += fabsf(p);
+      }
+    }
+  }
+  float incl = b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  float excl = __shfl_up_sync(kFull, incl, 1);
+  if (lane == 0) excl = 0.0f;
+  if (lane == 31) s_tot[wi] = incl;
+  __syncthreads();
+  float pref = 0.0f;
+  for (int q = 0; q < wi; q++) pref += s_tot[q];
+  const float O = pref + excl;
+  float term = static_cast<float>(c) * fabsf(O) + 2.0f * A + 10.0f * fabsf(b);
+  term = warp_sum(term);
+  P = warp_sum(P);
+  if (lane == 0) {
+    s_term[wi] = term;
+    s_p[wi] = P;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float u = 5.9604645e-08f;  // 2^-24
+    const float n = static_cast<float>(H);
+    const float S = ((s_tot[0] + s_tot[1]) + s_tot[2]) + s_tot[3];
+    const float tt = ((s_term[0] + s_term[1]) + s_term[2]) + s_term[3];
+    const float Pt = ((s_p[0] + s_p[1]) + s_p[2]) + s_p[3];
+    mid[e] = S;
+    err[e] = (1.01f + 2.0f * n * u) * u * (tt + Pt * (1.0f + n * u)) + 1e-37f;
+  }
+}
+
 cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, int w_dtype,
                                     float* mid, float* err, int T, int H, int E,
                                     cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   if (H % 256 != 0 || T > kSmallT) return cudaErrorInvalidValue;
+  if (T == 1 && H % 1024 == 0) {
+    if (x_dtype == kBF16 && w_dtype == kBF16) router_certified_t1_kernel<kBF16, kBF16><<<E, 128, 0, st>>>(x, w, mid, err, H);
+    else if (x_dtype == kBF16) router_certified_t1_kernel<kBF16, kF32><<<E, 128, 0, st>>>(x, w, mid, err, H);
+    else if (w_dtype == kBF16) router_certified_t1_kernel<kF32, kBF16><<<E, 128, 0, st>>>(x, w, mid, err, H);
+    else router_certified_t1_kernel<kF32, kF32><<<E, 128, 0, st>>>(x, w, mid, err, H);
+    return cudaGetLastError();
+  }
   const int blocks = (E + 3) / 4;
   if (T == 1) router_certified_kernel<1><<<blocks, 128, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
   else router_certified_kernel<4><<<blocks, 128, 0, st>>>(x, x_dtype, w, w_dtype, mid, err, T, H, E);
@@ -148,7 +256,7 @@ __device__ __forceinline__ void warp_best(float& v, int& id) {
 // The reference chain for one (token, expert): a = -0.0; a = fl(a + fl(x_k * w_k)), k ascending.
 // The 8192 adds are inherently serial; the loads run 32 elements ahead of the chain so only the
 // add latency remains (~4 cycles per element).
-__device__ float exact_logit(const void* x, int x_dtype, const void* w, int w_dtype, int t, int e,
+__device__ __noinline__ float exact_logit(const void* x, int x_dtype, const void* w, int w_dtype, int t, int e,
                              int H) {
   float a = -0.0f;
   const size_t xo = static_cast<size_t>(t) * H, wo = static_cast<size_t>(e) * H;
@@ -184,6 +292,58 @@ __device__ float exact_logit(const void* x, int x_dtype, const void* w, int w_dt
   return a;
 }
 
+
+// Block-wide selection of the kk best (value, id) pairs (kk <= 32), one pair per thread (threads
+// without an expert hold (-inf, unique id above every expert)). Two levels: each warp ranks its
+// 32 pairs by shuffles and keeps its kk best; every kept candidate then counts the candidates
+// ahead of it. Writes rank-ordered ids/values to out_id/out_v[0..kk). Two independent lists are
+// ranked at once (`v2`/`out2_*`), sharing the barriers. Contains __syncthreads: call from all
+// threads.
+__device__ void block_select2(float v, float v2, int id, int kk, float* cand, int* cand_i,
+                              float* cand2, int* cand2_i, int* out_id, float* out_v,
+                              int* out2_id, float* out2_v) {
+  const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nw = blockDim.x / 32;
+  int r1 = 0, r2 = 0;
+#pragma unroll 8
+  for (int j = 0; j < 32; j++) {
+    const float ov = __shfl_sync(kFull, v, j), ov2 = __shfl_sync(kFull, v2, j);
+    const int oid = __shfl_sync(kFull, id, j);
+    r1 += ahead(ov, oid, v, id);
+    r2 += ahead(ov2, oid, v2, id);
+  }
+  if (r1 < kk) {
+    cand[wi * kk + r1] = v;
+    cand_i[wi * kk + r1] = id;
+  }
+  if (r2 < kk) {
+    cand2[wi * kk + r2] = v2;
+    cand2_i[wi * kk + r2] = id;
+  }
+  __syncthreads();
+  const int C = nw * kk;
+  for (int t = threadIdx.x; t < 2 * C; t += blockDim.x) {
+    const bool second = t >= C;
+    const float* cv = second ? cand2 : cand;
+    const int* ci = second ? cand2_i : cand_i;
+    const int q = second ? t - C : t;
+    const float mv = cv[q];
+    const int mid = ci[q];
+    int r = 0;
+    for (int j = 0; j < C; j++) r += ahead(cv[j], ci[j], mv, mid);
+    if (r < kk) {
+      if (second) {
+        out2_id[r] = mid;
+        out2_v[r] = mv;
+      } else {
+        out_id[r] = mid;
+        out_v[r] = mv;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 constexpr int kMaxPL = 32;  // experts per lane (E <= 1024)
 
 // One block of 512 threads. Warp w routes tokens w, w + 16, ...; then the block builds the dispatch and
@@ -199,8 +359,78 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
   const int T = a.T, E = a.E, k = a.k;
   const int kk = min(k, E);
 
-  // ---------------- 1. route (warp per token)
-  for (int t = wi; t < T; t += blockDim.x / 32) {
+  // ---------------- 1a. route, one or two tokens: the whole block, one expert per thread
+  const bool block_route = T <= 2 && E <= static_cast<int>(blockDim.x);
+  if (block_route) {
+    __shared__ float c1[kSmallT * RMOE_MAX_TOPK_DEV / 2], c2[kSmallT * RMOE_MAX_TOPK_DEV / 2];
+    __shared__ int c1i[kSmallT * RMOE_MAX_TOPK_DEV / 2], c2i[kSmallT * RMOE_MAX_TOPK_DEV / 2];
+    __shared__ int sel_id[RMOE_MAX_TOPK_DEV], lo_id[RMOE_MAX_TOPK_DEV];
+    __shared__ float sel_v[RMOE_MAX_TOPK_DEV], lo_v[RMOE_MAX_TOPK_DEV];
+    __shared__ float s_lo[1024], s_hi[1024];
+    const int e = threadIdx.x;
+    const bool valid = e < E;
+    const int id = valid ? e : 0x40000000 + e;
+    for (int t = 0; t < T; t++) {
+      float lo = -INFINITY, hi = -INFINITY, v = -INFINITY;
+      if (valid) {
+        const float m = a.mid[static_cast<size_t>(t) * E + e];
+        const float r = a.err[static_cast<size_t>(t) * E + e];
+        lo = __fsub_rd(m, r);
+        hi = __fadd_ru(m, r);
+        v = m;
+        if (a.bias) {
+          const float bb = a.bias[e];
+          lo = __fadd_rn(lo, bb);
+          hi = __fadd_rn(hi, bb);
+          v = __fadd_rn(v, bb);
+        }
+        s_lo[e] = lo;
+        s_hi[e] = hi;
+      }
+      // winners by value, and the kk-th largest lower bound
+      block_select2(v, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+      const float Lk = lo_v[kk - 1];
+      const int n_cont = __syncthreads_count(valid && hi >= Lk);
+      const int r = threadIdx.x;
+      const bool pair_ok = r >= kk - 1 || s_lo[sel_id[r]] > s_hi[sel_id[r + 1]];
+      const bool order_ok = __syncthreads_and(pair_ok);
+      const bool set_ok = n_cont == kk;
+      if (!set_ok) {
+        // exact chains for every contender, then the selection on exact values
+        float ex = -INFINITY;
+        if (valid && hi >= Lk) {
+          ex = exact_logit(a.x, a.x_dtype, a.w, a.w_dtype, t, e, a.H);
+          if (a.bias) ex = __fadd_rn(ex, a.bias[e]);
+        }
+        block_select2(ex, ex, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+        if (threadIdx.x == 0) atomicAdd(a.fallback_count, 1u);
+      }
+      if (wi == 0) {
+        if (lane == 0) {
+          const int pend = set_ok && !order_ok ? 1 : 0;
+          a.pending[t] = pend;
+          if (pend) atomicAdd(a.order_pending_count, 1u);
+        }
+        const float sv = lane < kk ? sel_v[lane] : -INFINITY;
+        const float mx = __shfl_sync(kFull, sv, 0);
+        const float exv = lane < kk ? exp_f32(__fsub_rn(sv, mx)) : 0.0f;
+        float sum = 0.0f;
+        for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, exv, j));
+        if (lane < k) {
+          const float wv = lane < kk ? __fdiv_rn(exv, sum) : 0.0f;
+          const int sid = lane < kk ? sel_id[lane] : -1;
+          s_ids[t * k + lane] = sid;
+          s_w[t * k + lane] = wv;
+          a.ids[t * k + lane] = sid;
+          a.rw[t * k + lane] = wv;
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---------------- 1b. route (warp per token)
+  for (int t = wi; t < (block_route ? 0 : T); t += blockDim.x / 32) {
     float lo[PL], hi[PL], v[PL];
 #pragma unroll
     for (int q = 0; q < PL; q++) {
@@ -301,6 +531,7 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
     }
     if (!set_ok) {
       // exact chains for every contender, then select on exact values among them
+#pragma unroll
       for (int q = 0; q < PL; q++) {
         const int e = q * 32 + lane;
         const bool cont = e < E && hi[q] >= Lk;

@@ -242,6 +242,14 @@ def matmul_mxfp4(y, x, data, block_scale, s, i, o, stream=None):
     return y
 
 
+def matmul_mxfp4_tc(y, x, data, block_scale, s, i, o, stream=None):
+    """matmul_mxfp4 on the tcgen05 tensor cores (weights as stored; x as a 4-term E2M1 expansion)."""
+    _require_cuda(y, x, data, block_scale)
+    check(_lib.load().rmoe_matmul_mxfp4_tc(_ptr(y), _ptr(x), _dtype_code(x), _ptr(data),
+                                           _ptr(block_scale), s, i, o, _stream(stream)))
+    return y
+
+
 def matmul_mxfp4_noalloc(y, x, data, block_scale, s, i, o, stream=None):
     """matmul_mxfp4 with its activation scratch in a fixed device array (no allocation; shapes
     whose scratch exceeds the array raise INVALID_ARG; overlapping calls on one device race)."""

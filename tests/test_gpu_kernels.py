@@ -81,6 +81,29 @@ def test_matmul_mxfp4_matches_oracle(cuda_ctx, s, i, o):
     assert rel_l2(y.cpu().numpy(), want) < GEMM_RTOL
 
 
+@pytest.mark.parametrize("s,i,o", [(1, 256, 128), (1, 8192, 256), (3, 512, 100), (8, 1024, 300),
+                                   (33, 2048, 130), (2, 96, 40)])
+@pytest.mark.parametrize("xdt", ["f32", "bf16"])
+def test_matmul_mxfp4_tc_matches_oracle(cuda_ctx, s, i, o, xdt):
+    """tcgen05 kind::mxf4 path: weights as stored, x as a 4-term E2M1 expansion."""
+    import torch
+
+    import rabbit_b200 as rb
+
+    w = random_vec(o * i, 1000 + i) * np.float32(4.0)
+    q, bs = orc.pack_mxfp4(w, o, i)
+    x = random_vec(s * i, 2000 + s).reshape(s, i)
+    if xdt == "bf16":
+        x = synth.round_bf16(x)
+    want = orc.matmul_mxfp4(x, q, bs, s, i, o)
+    y = torch.full((s, o), float("nan"), dtype=torch.float32, device="cuda")
+    xd = _t(x) if xdt == "f32" else _t(x).to(torch.bfloat16)
+    rb.matmul_mxfp4_tc(y, xd, _t(q), _t(bs), s, i, o)
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, want) < GEMM_RTOL
+
+
 @pytest.mark.parametrize("scale_dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("s,i,o,gs", [(1, 256, 64, 32), (4, 512, 48, 64), (9, 128, 16, 128),
                                       (2, 6, 3, 3)])
