@@ -145,6 +145,15 @@ struct rmoe_layer {
   int32_t* ids_host_stage = nullptr;
   float* w_host_stage = nullptr;
   int last_launches = 0;         // kernels launched by the last forward_into
+  // tensor-core expert path (MXFP4)
+  bool use_tc = false;
+  void* tc_plan = nullptr;       // tensor maps (64-byte aligned host copy, passed by value)
+  uint8_t* xt = nullptr;         // [4 P_max + 16][H/2] activation terms per position
+  uint8_t* xsf = nullptr;        // [4 P_max + 16][H/32]
+  uint8_t* ht = nullptr;         // [4 P_max + 16][inter/2] h terms per position
+  uint8_t* hsf = nullptr;        // [4 P_max + 16][inter/32]
+  float* partial = nullptr;      // [SMs][2][32][128] split-tile parts
+  int32_t* tile_cnt = nullptr;   // [max tiles]
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
@@ -155,6 +164,7 @@ struct rmoe_layer {
         if (e) cudaEventDestroy(e);
     }
     if (cap) cudaStreamDestroy(cap);
+    free(tc_plan);
   }
 };
 
@@ -302,17 +312,21 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   } while (0)
 
   const size_t H = D.hidden, I = D.moe_inter, Is = D.shared_inter, E = D.n_experts;
-  // expert table: [gate][up][down][gate sc][up sc][down sc], each region 256-byte aligned
+  // expert table: [gate][up][down][gate sc][up sc][down sc], each region 4096-byte aligned so
+  // that every matrix of every expert is one 2-D tensor view of the whole table (row pitch =
+  // row bytes). A shared expert of the routed width takes the slot after the routed ones.
   const size_t gd = I * (H / 2), dd = H * (I / 2);
   size_t off = 0;
-  const size_t o_gate = off; off = align_up(off + gd, 256);
-  const size_t o_up = off; off = align_up(off + gd, 256);
-  const size_t o_down = off; off = align_up(off + dd, 256);
-  const size_t o_gs = off; off = align_up(off + scale_bytes_for(f, I, H), 256);
-  const size_t o_us = off; off = align_up(off + scale_bytes_for(f, I, H), 256);
-  const size_t o_ds = off; off = align_up(off + scale_bytes_for(f, H, I), 256);
+  const size_t o_gate = off; off = align_up(off + gd, 4096);
+  const size_t o_up = off; off = align_up(off + gd, 4096);
+  const size_t o_down = off; off = align_up(off + dd, 4096);
+  const size_t o_gs = off; off = align_up(off + scale_bytes_for(f, I, H), 4096);
+  const size_t o_us = off; off = align_up(off + scale_bytes_for(f, I, H), 4096);
+  const size_t o_ds = off; off = align_up(off + scale_bytes_for(f, H, I), 4096);
   const size_t stride = off;
-  ALLOC(L->experts, stride * L->n_loc);
+  const bool shared_in_table = L->has_shared && Is == I;
+  const int table_slots = L->n_loc + (shared_in_table ? 1 : 0);
+  ALLOC(L->experts, stride * table_slots);
   L->tab.base = L->experts;
   L->tab.stride = stride;
   L->tab.off_up = o_up - o_gate;
@@ -323,7 +337,11 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   L->tab.n_local = L->n_loc;
   L->tab.inter = static_cast<int>(I);
   L->tab.shared_inter = static_cast<int>(Is);
-  if (L->has_shared) {
+  if (shared_in_table) {
+    uint8_t* b = L->experts + stride * L->n_loc;
+    L->tab.shared = ExpertPtrs{b, b + o_up, b + o_down, b + o_gs, b + o_us, b + o_ds};
+    ALLOC(L->shared_gate_vec, H);
+  } else if (L->has_shared) {
     const size_t sgd = Is * (H / 2), sdd = H * (Is / 2);
     size_t so = 0;
     const size_t s_up = so = align_up(sgd, 256);
@@ -404,6 +422,36 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->hexp, L->P_max);
   ALLOC(L->y, static_cast<size_t>(L->P_max) * H);
   {
+    const char* notc = getenv("RMOE_DISABLE_TC");
+    L->use_tc = moe_tc_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is), f.fmt) &&
+                !(notc && notc[0] == '1') && (!L->has_shared || shared_in_table);
+  }
+  if (L->use_tc) {
+    const size_t rows = static_cast<size_t>(4) * L->P_max + 16;
+    ALLOC(L->xt, rows * (H / 2));
+    ALLOC(L->xsf, rows * (H / 32));
+    ALLOC(L->ht, rows * (I / 2));
+    ALLOC(L->hsf, rows * (I / 32));
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+    ALLOC(L->partial, static_cast<size_t>(std::max(sms, 1)) * 2 * 32 * 128);
+    const size_t max_tiles = static_cast<size_t>(max_chunks) * std::max(I / 64, H / 128);
+    ALLOC(L->tile_cnt, max_tiles);
+    cudaError_t e = cudaMemset(L->tile_cnt, 0, max_tiles * 4);
+    if (e == cudaSuccess) e = cudaMemset(L->xt, 0, rows * (H / 2));
+    if (e == cudaSuccess) e = cudaMemset(L->xsf, 127, rows * (H / 32));
+    if (e == cudaSuccess) e = cudaMemset(L->ht, 0, rows * (I / 2));
+    if (e == cudaSuccess) e = cudaMemset(L->hsf, 127, rows * (I / 32));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset"));
+    const size_t pb = (moe_tc_plan_bytes() + 63) / 64 * 64;
+    L->tc_plan = aligned_alloc(64, pb);
+    if (!L->tc_plan) return cleanup(fail(RMOE_OUT_OF_MEMORY, "rmoe_layer_create: host allocation"));
+    if (!moe_tc_plan(L->tc_plan, L->experts, stride, table_slots, o_gate, o_up, o_down, o_gs, o_us, o_ds,
+                     static_cast<int>(H), static_cast<int>(I), L->xt, L->xsf, L->ht, L->hsf,
+                     static_cast<int>(rows)))
+      return cleanup(fail(RMOE_CUDA_ERROR, "rmoe_layer_create: tensor map encoding failed"));
+  }
+  {
     uint8_t* xd = nullptr;
     ALLOC(xd, static_cast<size_t>(T) * H * 4);
     L->x_dev = xd;
@@ -428,7 +476,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
 #undef ALLOC
   L->stats.local_expert_begin = L->e_begin;
   L->stats.local_expert_end = L->e_end;
-  L->stats.device_bytes = stride * L->n_loc + E * H * 4;
+  L->stats.device_bytes = stride * table_slots + E * H * 4;
   *out = L;
   return RMOE_OK;
 }
@@ -716,7 +764,7 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
   const int H = D.hidden, k = D.topk;
   const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
   const bool gated = L->has_shared && D.shared_gated;
-  const int mt = chunk_tokens(T);
+  const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
   rmoe_status s = RMOE_OK;
   cudaError_t e = cudaSuccess;
   int launches = 10;
@@ -765,8 +813,41 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
     if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st)) != RMOE_OK) return s;
   }
   const int P = T * k + (L->has_shared ? T : 0);
-  RMOE_CUDA(cudaMemsetAsync(L->hmax, 0, static_cast<size_t>(P) * 4, st), "hmax reset");
   const int n_slots = L->n_loc + (L->has_shared ? 1 : 0);
+  if (L->use_tc) {
+    // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
+    // weight folded in), down: one token = combined row directly, else y per position + sum
+    e = launch_terms_by_position(x, xdt, H, L->d.perm_tok, L->d.offsets + n_slots, P, L->xt, L->xsf, st);
+    if (e != cudaSuccess) return cuda_fail(e, "activation terms");
+    marks.mark();
+    e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, L->ht, L->hsf, nullptr,
+                      L->partial, L->tile_cnt, L->dev_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
+    marks.mark();
+    marks.mark();  // (h is quantized inside the gate/up epilogue)
+    if (T == 1) {
+      e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, nullptr, nullptr, out,
+                        L->partial, L->tile_cnt, L->dev_err, st);
+      if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
+      marks.mark();
+      launches = resolved ? 6 : 9;  // router, prologue, order resolve | route, prep, dispatch x3; terms, gate/up, down
+    } else {
+      e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, nullptr, nullptr, L->y,
+                        L->partial, L->tile_cnt, L->dev_err, st);
+      if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
+      marks.mark();
+      e = launch_combine(L->y, L->d, nullptr, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
+      if (e != cudaSuccess) return cuda_fail(e, "combine");
+      launches = resolved ? 7 : 10;
+    }
+    marks.mark();
+    if (resolved) RMOE_CUDA(cudaStreamWaitEvent(st, L->ev_join, 0), "join wait");
+    *ids_src = resolved ? L->ids_final : L->ids;
+    *w_src = resolved ? L->w_final : L->rw;
+    L->last_launches = launches;
+    return RMOE_OK;
+  }
+  RMOE_CUDA(cudaMemsetAsync(L->hmax, 0, static_cast<size_t>(P) * 4, st), "hmax reset");
   const int max_chunks = std::min(T * k, L->n_loc) + (T * k + mt - 1) / mt + (L->has_shared ? (T + mt - 1) / mt : 0);
   const int tasks_gu = max_chunks * (std::max(D.moe_inter, D.shared_inter) / 2);
   const int tasks_dn = max_chunks * (H / 4);

@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   for (int j = 0; j < k; j++) {
     const int p = inv[t * k + j];
     if (p < 0) continue;
-    const float wv = rw[t * k + j];
+    const float wv = rw ? rw[t * k + j] : 1.0f;  // null: weights already inside y
     const float4 v = *reinterpret_cast<const float4*>(y + static_cast<size_t>(p) * H + o);
     acc.x = fmaf(wv, v.x, acc.x);
     acc.y = fmaf(wv, v.y, acc.y);
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   }
   if (has_shared) {
     const int p = *shared_pos0 + t;
-    const float g = perm_w[p];
+    const float g = rw ? perm_w[p] : 1.0f;
     const float4 v = *reinterpret_cast<const float4*>(y + static_cast<size_t>(p) * H + o);
     acc.x = fmaf(g, v.x, acc.x);
     acc.y = fmaf(g, v.y, acc.y);

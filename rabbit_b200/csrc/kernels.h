@@ -170,6 +170,20 @@ cudaError_t launch_mxf4_tc_matmul(float* y, const void* x, int x_dtype, const ui
                                   const uint8_t* w_sf, int S, int I, int O, void* ws, size_t ws_bytes,
                                   unsigned* err, cudaStream_t st);
 
+// ---- tensor-core expert GEMMs of an MXFP4 layer (moe_tc.cu) ----
+bool moe_tc_supported(int H, int I, int Is, int fmt);
+size_t moe_tc_plan_bytes();
+bool moe_tc_plan(void* plan, const uint8_t* arena, size_t stride, int n_slots, size_t off_gate, size_t off_up,
+                 size_t off_down, size_t off_gs, size_t off_us, size_t off_ds, int H, int I, const uint8_t* xt,
+                 const uint8_t* xsf, const uint8_t* ht, const uint8_t* hsf, int term_rows);
+cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const int32_t* perm_tok,
+                                     const int32_t* n_pos, int P_bound, uint8_t* xt, uint8_t* xsf,
+                                     cudaStream_t st);
+// mode 0: gate/up (-> h terms), 1: down (-> y per position), 2: down of one token (-> out row)
+cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
+                          size_t stride, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
+                          int32_t* tile_cnt, unsigned* err, cudaStream_t st);
+
 // ---- synthetic bytes (synth.cu) ----
 cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,
                                cudaStream_t st);

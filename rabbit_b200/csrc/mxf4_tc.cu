@@ -275,6 +275,20 @@ bool make_tmap_sw128(CUtensorMap* m, const void* base, uint64_t row_bytes, uint6
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Byte matrix [rows][row_bytes] as a 2-D tensor, box = box_bytes x box_rows, no swizzle.
+bool make_tmap_rows(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                    uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_bytes, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool mxf4_tc_supported(int S, int I, int O) {
   return S > 0 && O > 0 && I % 32 == 0 && (I / 2) % 16 == 0 && encode_fn() != nullptr;
 }
