@@ -154,6 +154,7 @@ struct rmoe_layer {
   uint8_t* hsf = nullptr;        // [4 P_max + 16][inter/32]
   float* partial = nullptr;      // [SMs][2][32][128] split-tile parts
   int32_t* tile_cnt = nullptr;   // [max tiles]
+  unsigned* front_counter = nullptr;  // one-token front end: finished blocks
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
@@ -437,7 +438,9 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     ALLOC(L->partial, static_cast<size_t>(std::max(sms, 1)) * 2 * 32 * 128);
     const size_t max_tiles = static_cast<size_t>(max_chunks) * std::max(I / 64, H / 128);
     ALLOC(L->tile_cnt, max_tiles);
+    ALLOC(L->front_counter, 1);
     cudaError_t e = cudaMemset(L->tile_cnt, 0, max_tiles * 4);
+    if (e == cudaSuccess) e = cudaMemset(L->front_counter, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(L->xt, 0, rows * (H / 2));
     if (e == cudaSuccess) e = cudaMemset(L->xsf, 127, rows * (H / 32));
     if (e == cudaSuccess) e = cudaMemset(L->ht, 0, rows * (I / 2));
@@ -769,12 +772,17 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
   cudaError_t e = cudaSuccess;
   int launches = 10;
   bool resolved = false;
+  const bool one_front = L->use_tc && T == 1 && small_path(L, T) && H % 4096 == 0 && D.n_experts <= 512;
+  bool terms_done = false;
   if (small_path(L, T)) {
-    // certified router + one-block front end (top-k, dispatch, activation prep)
+    // certified router + one-block front end (top-k, dispatch, activation prep); for one token
+    // on the tensor-core path all of it (and the activation terms) is a single launch
     marks.mark();
-    e = launch_router_certified(x, xdt, L->router, L->router_dtype, L->logits, L->logit_err, T, H,
-                                D.n_experts, st);
-    if (e != cudaSuccess) return cuda_fail(e, "certified router");
+    if (!one_front) {
+      e = launch_router_certified(x, xdt, L->router, L->router_dtype, L->logits, L->logit_err, T, H,
+                                  D.n_experts, st);
+      if (e != cudaSuccess) return cuda_fail(e, "certified router");
+    }
     marks.mark();
     SmallPrologue a{};
     a.T = T; a.E = D.n_experts; a.k = k; a.H = H; a.mt = mt;
@@ -789,8 +797,25 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
     a.fallback_count = L->fallbacks;
     a.order_pending_count = L->order_pending;
     a.pending = L->pending;
-    e = launch_prologue_small(a, L->d, st);
-    if (e != cudaSuccess) return cuda_fail(e, "small-T prologue");
+    if (one_front) {
+      DecodeFront f{};
+      f.x = x; f.x_dtype = xdt; f.w = L->router; f.w_dtype = L->router_dtype;
+      f.bias = a.bias; f.gvec = a.gvec;
+      f.H = H; f.E = D.n_experts; f.k = k;
+      f.e_begin = L->e_begin; f.e_end = L->e_end; f.n_loc = L->n_loc; f.has_shared = a.has_shared;
+      f.mid = L->logits; f.err = L->logit_err; f.gate = L->gate;
+      f.xt = L->xt; f.xsf = L->xsf;
+      f.ids = L->ids; f.rw = L->rw; f.pending = L->pending;
+      f.fallback_count = L->fallbacks; f.order_pending_count = L->order_pending;
+      f.counter = L->front_counter;
+      f.d = L->d;
+      e = launch_decode_front(f, st);
+      if (e != cudaSuccess) return cuda_fail(e, "one-token front end");
+      terms_done = true;
+    } else {
+      e = launch_prologue_small(a, L->d, st);
+      if (e != cudaSuccess) return cuda_fail(e, "small-T prologue");
+    }
     marks.mark();  // top-k, certificate, dispatch and activation prep
     marks.mark();  // (prep and dispatch are folded into the prologue)
     // rank order of near-tied winners: resolved on a side stream, joined before returning
@@ -817,11 +842,14 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
   if (L->use_tc) {
     // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
     // weight folded in), down: one token = combined row directly, else y per position + sum
-    e = launch_terms_by_position(x, xdt, H, L->d.perm_tok, L->d.offsets + n_slots, P, L->xt, L->xsf, st);
-    if (e != cudaSuccess) return cuda_fail(e, "activation terms");
+    if (!terms_done) {
+      e = launch_terms_by_position(x, xdt, H, L->d.perm_tok, L->d.offsets + n_slots, P, L->xt, L->xsf, st);
+      if (e != cudaSuccess) return cuda_fail(e, "activation terms");
+    }
     marks.mark();
+    // one token: every position reads the token's own term rows (0..3)
     e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, L->ht, L->hsf, nullptr,
-                      L->partial, L->tile_cnt, L->dev_err, st);
+                      L->partial, L->tile_cnt, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
     marks.mark();
     marks.mark();  // (h is quantized inside the gate/up epilogue)
@@ -830,7 +858,7 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
                         L->partial, L->tile_cnt, L->dev_err, st);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       marks.mark();
-      launches = resolved ? 6 : 9;  // router, prologue, order resolve | route, prep, dispatch x3; terms, gate/up, down
+      launches = terms_done ? 4 : (resolved ? 6 : 9);  // front (+ order resolve), gate/up, down
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, nullptr, nullptr, L->y,
                         L->partial, L->tile_cnt, L->dev_err, st);

@@ -87,6 +87,32 @@ struct SmallPrologue {
   int32_t* pending;                   // [T] 1 = order to be resolved by launch_resolve_order
 };
 
+// One-token front end of a tensor-core layer (route_small.cu): router logits + certificate,
+// shared gate, activation terms and dispatch in one launch.
+struct DecodeFront {
+  const void* x;
+  int x_dtype;
+  const void* w;                  // router [E][H]
+  int w_dtype;
+  const float* bias;              // logit bias or null
+  const float* gvec;              // shared gate vector or null
+  int H, E, k;
+  int e_begin, e_end, n_loc, has_shared;
+  float* mid;                     // [E]
+  float* err;                     // [E]
+  float* gate;                    // [1]
+  uint8_t* xt;                    // token terms: rows 0..3 of [.][H/2]
+  uint8_t* xsf;                   // [.][H/32]
+  int32_t* ids;                   // [k]
+  float* rw;                      // [k]
+  int32_t* pending;               // [1]
+  unsigned* fallback_count;
+  unsigned* order_pending_count;
+  unsigned* counter;              // finished blocks (zero between launches)
+  DispatchBuffers d;
+};
+cudaError_t launch_decode_front(const DecodeFront& a, cudaStream_t st);
+
 // ---- router (router.cu, route_small.cu) ----
 // Certified logits for T <= 32 tokens (H % 256 == 0): value + rigorous error bound.
 cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, int w_dtype,
@@ -182,7 +208,8 @@ cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const in
 // mode 0: gate/up (-> h terms), 1: down (-> y per position), 2: down of one token (-> out row)
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
                           size_t stride, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
-                          int32_t* tile_cnt, unsigned* err, cudaStream_t st);
+                          int32_t* tile_cnt, unsigned* err, cudaStream_t st,
+                          const int32_t* b_token_rows = nullptr);
 
 // ---- synthetic bytes (synth.cu) ----
 cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,

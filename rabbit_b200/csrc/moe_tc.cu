@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
+#include "terms.cuh"
 
 namespace rmoe {
 
@@ -69,6 +70,7 @@ struct MoeTcArgs {
   float* partial;      // [grid][2][32][128]
   int32_t* tile_cnt;   // parts finished per tile (reset by the finishing CTA)
   unsigned* err;
+  const int32_t* b_tok;  // non-null (one position per chunk): B rows are the token's, 4 * b_tok[p0]
 };
 
 struct StageMeta {
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       tma_prefetch_desc(&maps.a0);
       tma_prefetch_desc(&maps.b);
       long long issued = 0;
-      int cc = -1, ce = 0, cp0 = 0, cn = 0;  // chunk fields of the previous stage
+      int cc = -1, ce = 0, cp0 = 0, cn = 0, cb = 0;  // chunk fields of the previous stage
       for (long long s = s_begin; s < s_end; s++, issued++) {
         const int slot = static_cast<int>(issued % S);
         if (issued >= S && !mbar_wait_bounded(&empty[slot], ((issued / S) - 1) & 1, a.err, 0x100u)) {
@@ -197,6 +199,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           ce = __ldg(a.ch_expert + cc);
           cp0 = __ldg(a.ch_pos + cc);
           cn = __ldg(a.ch_n + cc);
+          if (a.b_tok) cb = __ldg(a.b_tok + cp0);
         }
         m.e = ce;
         m.p0 = cp0;
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           tma_load_2d(ssa + 1024, &maps.s0, ksf, esf + r0 + 64, &full[slot]);
         }
         for (int bx = 0; bx < m.nb; bx++) {
-          const int brow = 4 * m.p0 + 8 * bx;
+          const int brow = 4 * (a.b_tok ? cb : m.p0) + 8 * bx;
           tma_load_2d(sb + bx * 1024, &maps.b, kx, brow, &full[slot]);
           tma_load_2d(sb + bsub + bx * 1024, &maps.b, kx + 128, brow, &full[slot]);
           tma_load_2d(ssb + bx * 128, &maps.bs, ksf, brow, &full[slot]);
@@ -400,34 +403,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
             const int p = m.p0 + t;
             float hv = __fmul_rn(silu_ref(v[t]), ubuf[t * 64 + row]);
             hv *= __ldg(a.perm_w + p);
-            float r = hv;
-            for (int j = 0; j < 4; j++) {
-              const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(r))));
-              int e = 0;
-              if (amax > 0.0f) {
-                const int e0 = ilogbf(amax);
-                e = amax <= 6.0f * exp2i(max(e0 - 2, -149)) ? e0 - 2 : e0 - 1;
-                e = max(-126, min(127, e));
-              }
-              uint32_t nib = 0;
-              if (amax > 0.0f) {
-                const bool neg = r < 0.0f;
-                const float vv = fminf(fabsf(r) * exp2i(-e), 6.0f);
-                const int c = vv < 0.25f ? 0 : vv < 0.75f ? 1 : vv < 1.25f ? 2 : vv < 1.75f ? 3 : vv < 2.5f ? 4 : vv < 3.5f ? 5 : vv < 5.0f ? 6 : 7;
-                const float qv = (c < 4 ? 0.5f * c : static_cast<float>(2 << ((c - 4) >> 1)) * (1.0f + 0.5f * (c & 1))) * exp2i(e);
-                r = neg ? r + qv : r - qv;
-                nib = static_cast<uint32_t>(c) | (neg && c ? 8u : 0u);
-              }
-              const uint32_t sh = nib << (4 * (lane & 7));
-              uint32_t w4[4];
-#pragma unroll
-              for (int g = 0; g < 4; g++) w4[g] = __reduce_or_sync(kFull, (lane >> 3) == g ? sh : 0u);
-              if (lane == 0) {
-                const size_t trow = static_cast<size_t>(4 * p + j);
-                *reinterpret_cast<uint4*>(a.ht + trow * (a.inter / 2) + i0 / 2) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                a.hsf[trow * (a.inter / 32) + i0 / 32] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
-              }
-            }
+            const size_t trow = static_cast<size_t>(4 * p);
+            warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2,
+                        a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32);
           }
         }
       } else if (MODE == kModeDown) {
@@ -447,66 +425,19 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------- activation terms per position
-// xt rows 4p..4p+3 = terms of x[perm_tok[p]]; one thread per (position, 32-block).
+// xt rows 4p..4p+3 = terms of x[perm_tok[p]]; one warp per (position, 32-block).
 __global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __restrict__ x, int x_dtype, int H,
                                                                 const int32_t* __restrict__ perm_tok,
                                                                 const int32_t* __restrict__ n_pos, int P_bound,
                                                                 uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
   const int nb = H / 32;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= P_bound * nb) return;
-  const int p = idx / nb, b = idx % nb;
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (wid >= P_bound * nb) return;
+  const int p = wid / nb, b = wid % nb;
   if (p >= *n_pos) return;
   const int tok = perm_tok[p];
-  float r[32];
-  if (x_dtype == kBF16) {
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + static_cast<size_t>(tok) * H + b * 32);
-#pragma unroll
-    for (int qq = 0; qq < 4; qq++) {
-      const uint4 w = __ldg(src + qq);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        r[8 * qq + 2 * i] = __uint_as_float(ww[i] << 16);
-        r[8 * qq + 2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
-      }
-    }
-  } else {
-    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<size_t>(tok) * H + b * 32);
-#pragma unroll
-    for (int qq = 0; qq < 8; qq++) {
-      const float4 w = __ldg(src + qq);
-      r[4 * qq] = w.x; r[4 * qq + 1] = w.y; r[4 * qq + 2] = w.z; r[4 * qq + 3] = w.w;
-    }
-  }
-#pragma unroll 1
-  for (int j = 0; j < 4; j++) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(r[i]));
-    int e = 0;
-    if (amax > 0.0f) {
-      const int e0 = ilogbf(amax);
-      e = amax <= 6.0f * exp2i(max(e0 - 2, -149)) ? e0 - 2 : e0 - 1;
-      e = max(-126, min(127, e));
-    }
-    uint32_t packed[4] = {0, 0, 0, 0};
-    if (amax > 0.0f) {
-      const float inv = exp2i(-e), sc = exp2i(e);
-#pragma unroll
-      for (int i = 0; i < 32; i++) {
-        const bool neg = r[i] < 0.0f;
-        const float vv = fminf(fabsf(r[i]) * inv, 6.0f);
-        const int c = vv < 0.25f ? 0 : vv < 0.75f ? 1 : vv < 1.25f ? 2 : vv < 1.75f ? 3 : vv < 2.5f ? 4 : vv < 3.5f ? 5 : vv < 5.0f ? 6 : 7;
-        const float qv = (c < 4 ? 0.5f * c : static_cast<float>(2 << ((c - 4) >> 1)) * (1.0f + 0.5f * (c & 1))) * sc;
-        r[i] = neg ? r[i] + qv : r[i] - qv;
-        packed[i / 8] |= (static_cast<uint32_t>(c) | (neg && c ? 8u : 0u)) << (4 * (i % 8));
-      }
-    }
-    const size_t row = static_cast<size_t>(4 * p + j);
-    *reinterpret_cast<uint4*>(xt + row * (H / 2) + b * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    xsf[row * nb + b] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
-  }
+  const float r = load_elem(x, x_dtype, static_cast<size_t>(tok) * H + b * 32 + lane);
+  warp_terms4(r, xt + static_cast<size_t>(4 * p) * (H / 2) + b * 16, H / 2, xsf + static_cast<size_t>(4 * p) * nb + b, nb);
 }
 
 // ---------------------------------------------------------------------- host side
@@ -562,7 +493,7 @@ cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const in
                                      const int32_t* n_pos, int P_bound, uint8_t* xt, uint8_t* xsf,
                                      cudaStream_t st) {
   if (P_bound <= 0) return cudaSuccess;
-  const int n = P_bound * (H / 32);
+  const int n = P_bound * (H / 32) * 32;
   terms_by_position_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, x_dtype, H, perm_tok, n_pos, P_bound, xt, xsf);
   return cudaGetLastError();
 }
@@ -574,7 +505,7 @@ static size_t moe_tc_smem(int stages, int b_boxes) {
 // mode: 0 gate/up, 1 down, 2 down for one token. mt = positions per chunk (<= 32).
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
                           size_t stride, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
-                          int32_t* tile_cnt, unsigned* err, cudaStream_t st) {
+                          int32_t* tile_cnt, unsigned* err, cudaStream_t st, const int32_t* b_token_rows) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   MoeTcArgs a{};
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.ch_n = d.ch_n; a.n_chunks = d.n_chunks;
@@ -587,6 +518,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   a.ht = ht; a.hsf = hsf; a.inter = I;
   a.y = y; a.hidden = H;
   a.partial = partial; a.tile_cnt = tile_cnt; a.err = err;
+  a.b_tok = b_token_rows;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, a.b_boxes) > 227 * 1024) stages--;
   a.stages = stages;

@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "terms.cuh"
 
 namespace rmoe {
 
@@ -703,6 +704,237 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
     }
     __syncthreads();
   }
+}
+
+
+// ---------------------------------------------------------------------------------------
+// One token, one launch: blocks [0, E/2) compute the certified router logits of two experts each
+// (16 warps, 512 slices of H/512 elements, the loads of both experts issued before either chain;
+// each slice sum passes through at most 5 + 15 + 1 roundings in the scan, counted as 22 |B_l|);
+// the next block the shared-expert gate
+// sigmoid(x . g); blocks after it the four-term E2M1 expansion of x (one warp per 32-block).
+// The block that finishes last (a device counter, reset by it) runs the top-k with its
+// certificate and the dispatch of the single token.
+template <int XD, int WD>
+__global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
+  __shared__ float s_tot[2][16], s_term[2][16], s_p[2][16];
+  __shared__ int s_last;
+  const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int E = a.E, H = a.H;
+  const int nrb = (E + 1) / 2;  // router blocks: experts 2b, 2b + 1
+  const int b = blockIdx.x;
+  if (b < nrb) {
+    const int c = H / 512;  // multiple of 8
+    const size_t off = static_cast<size_t>(threadIdx.x) * c;
+    float bs[2] = {0.0f, 0.0f}, A[2] = {0.0f, 0.0f}, P[2] = {0.0f, 0.0f};
+    for (int j0 = 0; j0 < c; j0 += 16) {
+      uint4 wr[2][2][2], xr[2][2];
+#pragma unroll
+      for (int g = 0; g < 2; g++) {
+        if (j0 + 8 * g < c) {
+          load_raw8<XD>(a.x, off + j0 + 8 * g, xr[g]);
+#pragma unroll
+          for (int q = 0; q < 2; q++) {
+            const int e = min(2 * b + q, E - 1);
+            load_raw8<WD>(a.w, static_cast<size_t>(e) * H + off + j0 + 8 * g, wr[q][g]);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < 2; g++) {
+        if (j0 + 8 * g >= c) break;
+        float xv[8];
+        expand8<XD>(xr[g], xv);
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          float wv[8];
+          expand8<WD>(wr[q][g], wv);
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float pp = __fmul_rn(xv[i], wv[i]);
+            bs[q] = __fadd_rn(bs[q], pp);
+            A[q] += fabsf(bs[q]);
+            P[q] += fabsf(pp);
+          }
+        }
+      }
+    }
+    float excl[2];
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      float incl = bs[q];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      excl[q] = __shfl_up_sync(kFull, incl, 1);
+      if (lane == 0) excl[q] = 0.0f;
+      if (lane == 31) s_tot[q][wi] = incl;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      float pref = 0.0f;
+      for (int w = 0; w < wi; w++) pref += s_tot[q][w];
+      const float O = pref + excl[q];
+      float term = static_cast<float>(c) * fabsf(O) + 2.0f * A[q] + 22.0f * fabsf(bs[q]);
+      term = warp_sum(term);
+      const float Pw = warp_sum(P[q]);
+      if (lane == 0) {
+        s_term[q][wi] = term;
+        s_p[q][wi] = Pw;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 && 2 * b + static_cast<int>(threadIdx.x) < E) {
+      const int q = threadIdx.x;
+      const float u = 5.9604645e-08f;  // 2^-24
+      const float n = static_cast<float>(H);
+      float S = 0.0f, tt = 0.0f, Pt = 0.0f;
+      for (int w = 0; w < 16; w++) {
+        S += s_tot[q][w];
+        tt += s_term[q][w];
+        Pt += s_p[q][w];
+      }
+      a.mid[2 * b + q] = S;
+      a.err[2 * b + q] = (1.01f + 2.0f * n * u) * u * (tt + Pt * (1.0f + n * u)) + 1e-37f;
+    }
+  } else if (b == nrb) {
+    if (a.gvec) {
+      float dot = 0.0f;
+      for (int i = threadIdx.x * 8; i < H; i += 512 * 8) {
+        float xv[8];
+        load8(a.x, XD, i, xv);
+#pragma unroll
+        for (int q = 0; q < 8; q++) dot = fmaf(xv[q], a.gvec[i + q], dot);
+      }
+      dot = warp_sum(dot);
+      if (lane == 0) s_tot[0][wi] = dot;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float d = 0.0f;
+        for (int q = 0; q < 16; q++) d += s_tot[0][q];
+        a.gate[0] = sigmoid_ref(d);
+      }
+    } else if (threadIdx.x == 0) {
+      a.gate[0] = 1.0f;
+    }
+  } else {
+    const int blk = (b - nrb - 1) * 16 + wi;  // 32-block of x
+    if (blk < H / 32) {
+      const float r = load_elem(a.x, XD, static_cast<size_t>(blk) * 32 + lane);
+      warp_terms4(r, a.xt + blk * 16, H / 2, a.xsf + blk, H / 32);
+    }
+  }
+  // ---- the last block to finish runs the front end
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(a.counter, 1u);
+    s_last = old == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ float c1[16 * RMOE_MAX_TOPK_DEV], c2[16 * RMOE_MAX_TOPK_DEV];
+  __shared__ int c1i[16 * RMOE_MAX_TOPK_DEV], c2i[16 * RMOE_MAX_TOPK_DEV];
+  __shared__ int sel_id[RMOE_MAX_TOPK_DEV], lo_id[RMOE_MAX_TOPK_DEV];
+  __shared__ float sel_v[RMOE_MAX_TOPK_DEV], lo_v[RMOE_MAX_TOPK_DEV];
+  __shared__ float s_lo[512], s_hi[512];
+  const int k = a.k, kk = min(k, E);
+  const int e = threadIdx.x;
+  const bool valid = e < E;
+  const int id = valid ? e : 0x40000000 + e;
+  float lo = -INFINITY, hi = -INFINITY, v = -INFINITY;
+  if (valid) {
+    const float m = __ldcg(a.mid + e);
+    const float r = __ldcg(a.err + e);
+    lo = __fsub_rd(m, r);
+    hi = __fadd_ru(m, r);
+    v = m;
+    if (a.bias) {
+      const float bb = a.bias[e];
+      lo = __fadd_rn(lo, bb);
+      hi = __fadd_rn(hi, bb);
+      v = __fadd_rn(v, bb);
+    }
+    s_lo[e] = lo;
+    s_hi[e] = hi;
+  }
+  block_select2(v, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  const float Lk = lo_v[kk - 1];
+  const int n_cont = __syncthreads_count(valid && hi >= Lk);
+  const int rr = threadIdx.x;
+  const bool pair_ok = rr >= kk - 1 || s_lo[sel_id[rr]] > s_hi[sel_id[rr + 1]];
+  const bool order_ok = __syncthreads_and(pair_ok);
+  const bool set_ok = n_cont == kk;
+  if (!set_ok) {
+    float ex = -INFINITY;
+    if (valid && hi >= Lk) {
+      ex = exact_logit(a.x, XD, a.w, WD, 0, e, H);
+      if (a.bias) ex = __fadd_rn(ex, a.bias[e]);
+    }
+    block_select2(ex, ex, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+    if (threadIdx.x == 0) atomicAdd(a.fallback_count, 1u);
+  }
+  if (wi == 0) {
+    if (lane == 0) {
+      const int pend = set_ok && !order_ok ? 1 : 0;
+      a.pending[0] = pend;
+      if (pend) atomicAdd(a.order_pending_count, 1u);
+    }
+    const float sv = lane < kk ? sel_v[lane] : -INFINITY;
+    const float mx = __shfl_sync(kFull, sv, 0);
+    const float exv = lane < kk ? exp_f32(__fsub_rn(sv, mx)) : 0.0f;
+    float sum = 0.0f;
+    for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, exv, j));
+    const float wv = lane < kk ? __fdiv_rn(exv, sum) : 0.0f;
+    const int sid = lane < kk ? sel_id[lane] : -1;
+    if (lane < k) {
+      a.ids[lane] = sid;
+      a.rw[lane] = wv;
+    }
+    // dispatch of the one token: positions by ascending expert id, one chunk per position
+    const bool local = lane < kk && sid >= a.e_begin && sid < a.e_end;
+    int pos = 0;
+    for (int j = 0; j < kk; j++) {
+      const int o = __shfl_sync(kFull, sid, j);
+      pos += (o >= a.e_begin && o < a.e_end && o < sid) ? 1 : 0;
+    }
+    const int n_routed = __popc(__ballot_sync(kFull, local));
+    if (lane < k) a.d.inv[lane] = local ? pos : -1;
+    if (local) {
+      a.d.ch_expert[pos] = sid - a.e_begin;
+      a.d.ch_pos[pos] = pos;
+      a.d.ch_n[pos] = 1;
+      a.d.perm_tok[pos] = 0;
+      a.d.perm_w[pos] = wv;
+    }
+    if (lane == 0) {
+      if (a.has_shared) {
+        a.d.ch_expert[n_routed] = a.n_loc;
+        a.d.ch_pos[n_routed] = n_routed;
+        a.d.ch_n[n_routed] = 1;
+        a.d.perm_tok[n_routed] = 0;
+        a.d.perm_w[n_routed] = __ldcg(a.gate);
+      }
+      a.d.n_chunks[0] = n_routed + a.has_shared;
+      a.d.offsets[a.n_loc] = n_routed;
+      a.d.offsets[a.n_loc + a.has_shared] = n_routed + a.has_shared;
+      *a.counter = 0;
+    }
+  }
+}
+
+cudaError_t launch_decode_front(const DecodeFront& a, cudaStream_t st) {
+  if (a.H % 4096 != 0 || a.E > 512 || a.k > RMOE_MAX_TOPK_DEV) return cudaErrorInvalidValue;
+  const int blocks = (a.E + 1) / 2 + 1 + (a.H / 32 + 15) / 16;
+  if (a.x_dtype == kBF16 && a.w_dtype == kBF16) decode_front_kernel<kBF16, kBF16><<<blocks, 512, 0, st>>>(a);
+  else if (a.x_dtype == kBF16) decode_front_kernel<kBF16, kF32><<<blocks, 512, 0, st>>>(a);
+  else if (a.w_dtype == kBF16) decode_front_kernel<kF32, kBF16><<<blocks, 512, 0, st>>>(a);
+  else decode_front_kernel<kF32, kF32><<<blocks, 512, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 // Final routing in the reference's rank order. Tokens whose order certificate failed get exact
