@@ -152,9 +152,14 @@ struct rmoe_layer {
   uint8_t* xsf = nullptr;        // [4 P_max + 16][H/32]
   uint8_t* ht = nullptr;         // [4 P_max + 16][inter/2] h terms per position
   uint8_t* hsf = nullptr;        // [4 P_max + 16][inter/32]
-  float* partial = nullptr;      // [SMs][2][32][128] split-tile parts
+  float* partial = nullptr;      // gate/up unit parts of split tiles
+  float* partial2 = nullptr;     // down unit parts of split tiles
   int32_t* tile_cnt = nullptr;   // [max tiles]
   unsigned* front_counter = nullptr;  // one-token front end: finished blocks
+  int* tc_work = nullptr;        // [2] claimed units / finished CTAs of the running expert kernel
+  size_t tc_off_down = 0;        // tile-major down region inside an expert slot
+  uint8_t* tc_stage = nullptr;   // one expert in the reference layout, before retiling
+  unsigned long long* tc_trace = nullptr;  // RMOE_TC_TRACE=1: gate/up stage timestamps of CTA 0
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
@@ -324,8 +329,18 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   const size_t o_gs = off; off = align_up(off + scale_bytes_for(f, I, H), 4096);
   const size_t o_us = off; off = align_up(off + scale_bytes_for(f, I, H), 4096);
   const size_t o_ds = off; off = align_up(off + scale_bytes_for(f, H, I), 4096);
-  const size_t stride = off;
   const bool shared_in_table = L->has_shared && Is == I;
+  {
+    const char* notc = getenv("RMOE_DISABLE_TC");
+    L->use_tc = moe_tc_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is), f.fmt) &&
+                !(notc && notc[0] == '1') && (!L->has_shared || shared_in_table);
+  }
+  if (L->use_tc) {
+    // tensor-core layers keep their weights tile-major (moe_tc.cu): [gate/up tiles][down tiles]
+    L->tc_off_down = align_up(moe_tc_region_bytes(static_cast<int>(H), static_cast<int>(I), 0), 4096);
+    off = align_up(L->tc_off_down + moe_tc_region_bytes(static_cast<int>(H), static_cast<int>(I), 1), 4096);
+  }
+  const size_t stride = off;
   const int table_slots = L->n_loc + (shared_in_table ? 1 : 0);
   ALLOC(L->experts, stride * table_slots);
   L->tab.base = L->experts;
@@ -422,25 +437,28 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->hq, static_cast<size_t>(L->P_max) * L->h_ld);
   ALLOC(L->hexp, L->P_max);
   ALLOC(L->y, static_cast<size_t>(L->P_max) * H);
-  {
-    const char* notc = getenv("RMOE_DISABLE_TC");
-    L->use_tc = moe_tc_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is), f.fmt) &&
-                !(notc && notc[0] == '1') && (!L->has_shared || shared_in_table);
-  }
   if (L->use_tc) {
     const size_t rows = static_cast<size_t>(4) * L->P_max + 16;
+    ALLOC(L->tc_stage, 2 * gd + dd + 2 * (I * H / 32) + H * I / 32);  // one expert as uploaded
     ALLOC(L->xt, rows * (H / 2));
     ALLOC(L->xsf, rows * (H / 32));
     ALLOC(L->ht, rows * (I / 2));
     ALLOC(L->hsf, rows * (I / 32));
-    int sms = 0;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
-    ALLOC(L->partial, static_cast<size_t>(std::max(sms, 1)) * 2 * 32 * 128);
+    ALLOC(L->partial, moe_tc_partial_floats(static_cast<int>(H), static_cast<int>(I), k, n_slots));
+    ALLOC(L->partial2, moe_tc_partial_floats(static_cast<int>(H), static_cast<int>(I), k, n_slots));
+    ALLOC(L->tc_work, 4);
     const size_t max_tiles = static_cast<size_t>(max_chunks) * std::max(I / 64, H / 128);
     ALLOC(L->tile_cnt, max_tiles);
     ALLOC(L->front_counter, 1);
+    if (const char* tr = getenv("RMOE_TC_TRACE")) {
+      if (tr[0] == '1') {
+        ALLOC(L->tc_trace, 8192);
+        if (cudaMemset(L->tc_trace, 0, 8192 * 8) != cudaSuccess) return cleanup(fail(RMOE_CUDA_ERROR, "trace"));
+      }
+    }
     cudaError_t e = cudaMemset(L->tile_cnt, 0, max_tiles * 4);
     if (e == cudaSuccess) e = cudaMemset(L->front_counter, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(L->tc_work, 0, 16);
     if (e == cudaSuccess) e = cudaMemset(L->xt, 0, rows * (H / 2));
     if (e == cudaSuccess) e = cudaMemset(L->xsf, 127, rows * (H / 32));
     if (e == cudaSuccess) e = cudaMemset(L->ht, 0, rows * (I / 2));
@@ -449,8 +467,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     const size_t pb = (moe_tc_plan_bytes() + 63) / 64 * 64;
     L->tc_plan = aligned_alloc(64, pb);
     if (!L->tc_plan) return cleanup(fail(RMOE_OUT_OF_MEMORY, "rmoe_layer_create: host allocation"));
-    if (!moe_tc_plan(L->tc_plan, L->experts, stride, table_slots, o_gate, o_up, o_down, o_gs, o_us, o_ds,
-                     static_cast<int>(H), static_cast<int>(I), L->xt, L->xsf, L->ht, L->hsf,
+    if (!moe_tc_plan(L->tc_plan, static_cast<int>(H), static_cast<int>(I), L->xt, L->xsf, L->ht, L->hsf,
                      static_cast<int>(rows)))
       return cleanup(fail(RMOE_CUDA_ERROR, "rmoe_layer_create: tensor map encoding failed"));
   }
@@ -593,6 +610,33 @@ static rmoe_status put_matrix(const rmoe_layer* L, const char* what, size_t rows
   return RMOE_OK;
 }
 
+// Tensor-core layers: the three matrices go through a staging copy in the reference layout and
+// are retiled into the expert's slot (gate/up tiles, then down tiles).
+static rmoe_status put_tiled(rmoe_layer* L, const char* what, const void* gate, size_t gate_bytes,
+                             const void* gate_scale, size_t gate_scale_bytes, const void* up, size_t up_bytes,
+                             const void* up_scale, size_t up_scale_bytes, const void* down, size_t down_bytes,
+                             const void* down_scale, size_t down_scale_bytes, uint8_t* slot) {
+  const size_t H = L->desc.hidden, I = L->desc.moe_inter;
+  const size_t gd = I * (H / 2), dd = H * (I / 2), gs = I * (H / 32), ds = H * (I / 32);
+  uint8_t* g = L->tc_stage;
+  uint8_t* u = g + gd;
+  uint8_t* dn = u + gd;
+  uint8_t* gsc = dn + dd;
+  uint8_t* usc = gsc + gs;
+  uint8_t* dsc = usc + gs;
+  rmoe_status s;
+  if ((s = put_matrix(L, what, I, H, gate, gate_bytes, gate_scale, gate_scale_bytes, g, gsc)) != RMOE_OK) return s;
+  if ((s = put_matrix(L, what, I, H, up, up_bytes, up_scale, up_scale_bytes, u, usc)) != RMOE_OK) return s;
+  if ((s = put_matrix(L, what, H, I, down, down_bytes, down_scale, down_scale_bytes, dn, dsc)) != RMOE_OK) return s;
+  cudaError_t e = launch_tc_relayout(0, g, u, gsc, usc, static_cast<int>(H), static_cast<int>(I), slot, 0);
+  if (e == cudaSuccess)
+    e = launch_tc_relayout(1, dn, nullptr, dsc, nullptr, static_cast<int>(H), static_cast<int>(I),
+                           slot + L->tc_off_down, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return RMOE_OK;
+}
+
 static rmoe_status local_slot(const rmoe_layer* L, int32_t eid, const char* what, int* slot) {
   if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
   if (eid < 0 || eid >= L->desc.n_experts)
@@ -616,6 +660,13 @@ extern "C" rmoe_status rmoe_upload_expert(rmoe_layer* L, int32_t eid, const void
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   const size_t H = L->desc.hidden, I = L->desc.moe_inter;
   uint8_t* b = L->experts + L->tab.stride * slot;
+  if (L->use_tc) {
+    if ((s = put_tiled(L, "rmoe_upload_expert", gate, gate_bytes, gate_scale, gate_scale_bytes, up, up_bytes,
+                       up_scale, up_scale_bytes, down, down_bytes, down_scale, down_scale_bytes, b)) != RMOE_OK)
+      return s;
+    L->uploaded[slot] = 1;
+    return RMOE_OK;
+  }
   if ((s = put_matrix(L, "rmoe_upload_expert gate", I, H, gate, gate_bytes, gate_scale,
                       gate_scale_bytes, b, b + L->tab.off_gs)) != RMOE_OK)
     return s;
@@ -661,6 +712,16 @@ extern "C" rmoe_status rmoe_upload_shared(rmoe_layer* L, const void* gate, size_
   const size_t H = L->desc.hidden, Is = L->desc.shared_inter;
   const ExpertPtrs& p = L->tab.shared;
   rmoe_status s;
+  if (L->use_tc) {
+    if ((s = put_tiled(L, "rmoe_upload_shared", gate, gate_bytes, gate_scale, gate_scale_bytes, up, up_bytes,
+                       up_scale, up_scale_bytes, down, down_bytes, down_scale, down_scale_bytes,
+                       L->experts + L->tab.stride * L->n_loc)) != RMOE_OK)
+      return s;
+    if (shared_gate && L->desc.shared_gated)
+      RMOE_CUDA(cudaMemcpy(L->shared_gate_vec, shared_gate, H * 4, cudaMemcpyDefault), "rmoe_upload_shared gate vector");
+    L->has_shared_w = true;
+    return RMOE_OK;
+  }
   if ((s = put_matrix(L, "rmoe_upload_shared gate", Is, H, gate, gate_bytes, gate_scale, gate_scale_bytes,
                       const_cast<uint8_t*>(p.gate), (uint8_t*)p.gate_scale)) != RMOE_OK)
     return s;
@@ -758,6 +819,45 @@ extern "C" rmoe_status rmoe_dispatch(rmoe_layer* L, const int32_t* ids, int32_t 
   return RMOE_OK;
 }
 
+// Diagnostics (RMOE_TC_TRACE=1, direct launches only): CTA 0's stage timeline and every CTA's
+// entry / exit of the last tensor-core kernel, to stderr.
+static rmoe_status print_tc_trace(rmoe_layer* L, cudaStream_t st, const char* what, size_t off) {
+  fprintf(stderr, "== %s\n", what);
+  {
+    unsigned long long t0h = 0;
+    RMOE_CUDA(cudaMemcpy(&t0h, L->tc_trace + off, 8, cudaMemcpyDeviceToHost), "trace t0");
+    fprintf(stderr, "   t0 (first issue, globaltimer) = %llu ns\n", t0h);
+  }
+      static unsigned long long tr[4096];
+      RMOE_CUDA(cudaStreamSynchronize(st), "trace sync");
+      RMOE_CUDA(cudaMemcpy(tr, L->tc_trace + off, sizeof(tr), cudaMemcpyDeviceToHost), "trace read");
+      const unsigned long long t0 = tr[0];
+      unsigned long long s0 = ~0ull, s1 = 0, e0 = ~0ull, e1 = 0;
+      for (int c = 0; c < 256 && tr[1024 + 4 * c]; c++) {
+        s0 = std::min(s0, tr[1024 + 4 * c]); s1 = std::max(s1, tr[1024 + 4 * c]);
+        e0 = std::min(e0, tr[1024 + 4 * c + 3]); e1 = std::max(e1, tr[1024 + 4 * c + 3]);
+      }
+      fprintf(stderr, "cta entry %.2f..%.2f  exit %.2f..%.2f us (rel. cta0 first issue); cta0 setup done %.2f epi done %.2f exit %.2f\n",
+              (double)(long long)(s0 - t0) * 1e-3, (double)(long long)(s1 - t0) * 1e-3, (double)(long long)(e0 - t0) * 1e-3,
+              (double)(long long)(e1 - t0) * 1e-3, (double)(long long)(tr[1025] - t0) * 1e-3,
+              (double)(long long)(tr[1026] - t0) * 1e-3, (double)(long long)(tr[1027] - t0) * 1e-3);
+      for (int c = 0; c < 148 && tr[1024 + 4 * c]; c += 16)
+        fprintf(stderr, "  cta %3d entry %.2f exit %.2f\n", c, (double)(long long)(tr[1024 + 4 * c] - t0) * 1e-3,
+                (double)(long long)(tr[1024 + 4 * c + 3] - t0) * 1e-3);
+      for (int i = 0; i < 32 && tr[3072 + i * 4]; i++)
+        fprintf(stderr, "  epi part %2d (tile*16+unit %4llu): wait from %7.2f got %7.2f done %7.2f us\n", i, tr[3072 + i * 4 + 3],
+                (double)(long long)(tr[3072 + i * 4] - t0) * 1e-3, (double)(long long)(tr[3072 + i * 4 + 1] - t0) * 1e-3,
+                (double)(long long)(tr[3072 + i * 4 + 2] - t0) * 1e-3);
+      for (int i = 0; i < 64 && tr[i * 4]; i++)
+        fprintf(stderr, "  mma %2d cycles: sfa wait %5llu sfb wait %5llu mma issue %5llu commit %5llu\n", i, tr[2048 + i * 4],
+                tr[2048 + i * 4 + 1], tr[2048 + i * 4 + 2], tr[2048 + i * 4 + 3]);
+      for (int i = 0; i < 64 && tr[i * 4]; i++)
+        fprintf(stderr, "stage %2d issue %7.2f full %7.2f sf %7.2f mma %7.2f us\n", i, (tr[i * 4] - t0) * 1e-3,
+                (tr[i * 4 + 1] - t0) * 1e-3, (tr[i * 4 + 2] - t0) * 1e-3, (tr[i * 4 + 3] - t0) * 1e-3);
+      RMOE_CUDA(cudaMemset(L->tc_trace + off, 0, sizeof(tr)), "trace reset");
+      return RMOE_OK;
+}
+
 // Enqueues one forward on `st` (stream-ordered, capturable): x -> out, routing left in
 // *ids_src / *w_src (reference rank order). L->last_launches = kernels it launched.
 static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, int T, float* out,
@@ -797,6 +897,7 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
     a.fallback_count = L->fallbacks;
     a.order_pending_count = L->order_pending;
     a.pending = L->pending;
+    a.errflag = L->dev_err;
     if (one_front) {
       DecodeFront f{};
       f.x = x; f.x_dtype = xdt; f.w = L->router; f.w_dtype = L->router_dtype;
@@ -848,20 +949,27 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
     }
     marks.mark();
     // one token: every position reads the token's own term rows (0..3)
-    e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, L->ht, L->hsf, nullptr,
-                      L->partial, L->tile_cnt, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr);
+    e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
+                      L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
+                      L->tc_trace);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
+
     marks.mark();
     marks.mark();  // (h is quantized inside the gate/up epilogue)
     if (T == 1) {
-      e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, nullptr, nullptr, out,
-                        L->partial, L->tile_cnt, L->dev_err, st);
+      e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
+                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr,
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
+      if (L->tc_trace) {
+        if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
+        if ((s = print_tc_trace(L, st, "down (one token)", 4096)) != RMOE_OK) return s;
+      }
       marks.mark();
       launches = terms_done ? 4 : (resolved ? 6 : 9);  // front (+ order resolve), gate/up, down
     } else {
-      e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->tab.stride, nullptr, nullptr, L->y,
-                        L->partial, L->tile_cnt, L->dev_err, st);
+      e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
+                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr, nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       marks.mark();
       e = launch_combine(L->y, L->d, nullptr, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);

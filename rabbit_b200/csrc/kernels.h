@@ -85,6 +85,7 @@ struct SmallPrologue {
   unsigned* fallback_count;           // tokens whose expert set was uncertain (exact recompute)
   unsigned* order_pending_count;      // tokens whose rank order was resolved off the critical path
   int32_t* pending;                   // [T] 1 = order to be resolved by launch_resolve_order
+  unsigned* errflag;                  // bounded-wait failures
 };
 
 // One-token front end of a tensor-core layer (route_small.cu): router logits + certificate,
@@ -199,17 +200,22 @@ cudaError_t launch_mxf4_tc_matmul(float* y, const void* x, int x_dtype, const ui
 // ---- tensor-core expert GEMMs of an MXFP4 layer (moe_tc.cu) ----
 bool moe_tc_supported(int H, int I, int Is, int fmt);
 size_t moe_tc_plan_bytes();
-bool moe_tc_plan(void* plan, const uint8_t* arena, size_t stride, int n_slots, size_t off_gate, size_t off_up,
-                 size_t off_down, size_t off_gs, size_t off_us, size_t off_ds, int H, int I, const uint8_t* xt,
-                 const uint8_t* xsf, const uint8_t* ht, const uint8_t* hsf, int term_rows);
+bool moe_tc_plan(void* plan, int H, int I, const uint8_t* xt, const uint8_t* xsf, const uint8_t* ht,
+                 const uint8_t* hsf, int term_rows);
+size_t moe_tc_region_bytes(int H, int I, int down);
+cudaError_t launch_tc_relayout(int down, const uint8_t* m0, const uint8_t* m1, const uint8_t* s0,
+                               const uint8_t* s1, int H, int I, uint8_t* dst, cudaStream_t st);
 cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const int32_t* perm_tok,
                                      const int32_t* n_pos, int P_bound, uint8_t* xt, uint8_t* xsf,
                                      cudaStream_t st);
 // mode 0: gate/up (-> h terms), 1: down (-> y per position), 2: down of one token (-> out row)
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
-                          size_t stride, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
-                          int32_t* tile_cnt, unsigned* err, cudaStream_t st,
-                          const int32_t* b_token_rows = nullptr);
+                          const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
+                          int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st,
+                          const int32_t* b_token_rows = nullptr, unsigned long long* trace = nullptr,
+                          const float* partial_in = nullptr);
+// Unit parts of split tiles (floats) a layer must provide for batches of up to 8 tokens.
+size_t moe_tc_partial_floats(int H, int I, int k, int n_slots);
 
 // ---- synthetic bytes (synth.cu) ----
 cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,

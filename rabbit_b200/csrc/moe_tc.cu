@@ -32,7 +32,7 @@
 
 namespace rmoe {
 
-constexpr int kMtThreads = 320;
+constexpr int kMtThreads = 352;
 constexpr int kMtKStage = 512;            // K elements per stage (two 128-byte swizzle columns)
 constexpr int kMtMaxStages = 6;
 constexpr int kMtAccCols = 128;           // one accumulator: N <= 128 (32 positions x 4 terms)
@@ -42,13 +42,19 @@ constexpr uint32_t kMtTmemCols = 512;
 enum { kModeGateUp = 0, kModeDown = 1, kModeDownOne = 2 };
 
 struct MoeTcMaps {
-  CUtensorMap a0;   // GATE_UP: gate data rows; DOWN: down data rows   (box 128 B x 64 rows, SW128)
-  CUtensorMap a1;   // GATE_UP: up data rows;   DOWN: unused
-  CUtensorMap s0;   // scale rows of a0 (box 16 B x 64 rows)
-  CUtensorMap s1;   // scale rows of a1
   CUtensorMap b;    // activation terms (box 128 B x 8 rows, SW128)
   CUtensorMap bs;   // their scale rows (box 16 B x 8 rows)
 };
+
+// Expert weights of a tensor-core layer are stored tile-major: for each 128-row tile m and
+// 512-column stage ks one block of kTileBlock bytes =
+//   [2 x 16 KB: 128 rows x 128 B of E2M1 for columns 256 h .. 256 h + 255 of the stage, each row's
+//    16-byte chunk c at chunk position c ^ (row & 7) (the 128-byte swizzle image)]
+//   [2 KB of E8M0 words: word (g * 128 + L * 4 + j) = scales of k-blocks 4g..4g+3 of row L + 32 j,
+//    i.e. per k-group g a 32 x 16-byte block that one tcgen05.cp places in TMEM as the MMA reads it]
+// GATE_UP tiles hold gate rows 64m..64m+63 then the same up rows; DOWN tiles down rows 128m...
+// A stage is then one contiguous bulk copy, already in the shape the MMA and TMEM want.
+constexpr int kTileBlock = 32768 + 2048;
 
 struct MoeTcArgs {
   const int32_t* ch_expert;
@@ -58,8 +64,8 @@ struct MoeTcArgs {
   const float* perm_w;
   int K;               // reduction length of one expert (GATE_UP: hidden, DOWN: inter)
   int out_rows;        // GATE_UP: inter; DOWN: hidden
-  int rows_per_expert_data;  // row offset between experts in the a0/a1 views
-  int rows_per_expert_sf;    // row offset between experts in the s0/s1 views
+  const uint8_t* wbase; // tile blocks of expert slot 0 for this projection
+  size_t wstride;       // bytes between expert slots
   int b_boxes;         // activation boxes (8 rows) reserved per stage
   int stages;          // ring depth
   uint8_t* ht;         // GATE_UP out: h terms [4P][inter/2]
@@ -67,30 +73,61 @@ struct MoeTcArgs {
   int inter;           // GATE_UP: row pitch source of ht / hsf
   float* y;            // DOWN: [P][hidden]; DOWN_ONE: [hidden]
   int hidden;
-  float* partial;      // [grid][2][32][128]
+  float* partial;      // [units][8][128] unit parts of split tiles
   int32_t* tile_cnt;   // parts finished per tile (reset by the finishing CTA)
   unsigned* err;
   const int32_t* b_tok;  // non-null (one position per chunk): B rows are the token's, 4 * b_tok[p0]
+  unsigned long long* trace;  // optional: CTA 0's per-stage timestamps [stage][4] (ns)
+  int* work;           // [4] units claimed, CTAs finished, h slices ready, parts stored (zero between launches)
+  int unit_stages;     // stages per claimed unit (split tiles when smaller than a tile)
+  // down kernels after a split gate/up pass: the gate/up unit parts, summed here into h terms
+  const float* partial_in;
+  int gu_split;        // 1: gate/up left unit parts (sum them in the prologue)
+  int upt_gu;          // gate/up units per tile
+  int ntm_gu;          // gate/up tiles per chunk (inter / 64)
 };
 
 struct StageMeta {
-  int tile, u, c, m, ks, e, p0, n, nb, first, last, pad;
+  int nb, pad0, pad1, pad2;
 };
+
+// One unit of work as handed from the weight producer to the other roles.
+struct PartRec {
+  int tile;   // -1: no more work
+  int uit;    // unit index inside the tile
+  int unit;   // global unit id
+  int e;      // expert slot of the unit's first stage
+  int p0;     // first position of the tile's chunk
+  int n;      // positions in the chunk
+  int brow;   // first activation row of the chunk (4 * token or 4 * position)
+  int pad;
+};
+constexpr int kRecRing = 4;
+
+constexpr int kBOff = (kTileBlock + 1023) & ~1023;
 
 // Shared-memory carve-up (offsets from the 1024-aligned base).
 struct MtLayout {
-  int stage_pitch, off_bar, off_meta, off_misc, off_ubuf, total;
+  int stage_pitch, off_bar, off_meta, off_rec, off_misc, off_ubuf, total;
 };
 __host__ __device__ inline MtLayout mt_layout(int stages, int b_boxes) {
   MtLayout l;
-  const int sb = 32768 + 2 * b_boxes * 1024 + 2048 + b_boxes * 128;
+  // [A tile + its scales: kTileBlock][pad to 1 KB][B: 2 x b_boxes KB][B scales: b_boxes x 128 B]
+  const int sb = kBOff + 2 * b_boxes * 1024 + b_boxes * 128;
   l.stage_pitch = (sb + 1023) & ~1023;
-  l.off_bar = stages * l.stage_pitch;                          // 3 * stages + 4 mbarriers
-  l.off_meta = l.off_bar + (3 * stages + 4) * 8;
-  l.off_misc = l.off_meta + stages * static_cast<int>(sizeof(StageMeta));
-  l.off_ubuf = (l.off_misc + 16 + 15) & ~15;                   // tmem slot, abort, last flag
+  l.off_bar = stages * l.stage_pitch;  // 5 * stages + 8 + 2 * kRecRing mbarriers
+  l.off_meta = l.off_bar + (5 * stages + 8 + 2 * kRecRing) * 8;
+  l.off_rec = l.off_meta + stages * static_cast<int>(sizeof(StageMeta));
+  l.off_misc = l.off_rec + kRecRing * static_cast<int>(sizeof(PartRec));
+  l.off_ubuf = (l.off_misc + 16 + 15) & ~15;  // tmem slot, abort, last flag
   l.total = l.off_ubuf + 32 * 64 * 4;
   return l;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // True on every epilogue thread iff p holds on all 128 of them (named barrier 1 with an AND
@@ -108,26 +145,40 @@ __device__ __forceinline__ bool epi_all(bool p) {
   return r != 0;
 }
 
-__device__ __forceinline__ int cta_of(long long s, long long total, int grid) {
-  return static_cast<int>(((s + 1) * grid + total - 1) / total) - 1;
-}
-
-// Tile / chunk / K-stage of flat stage s of the work list.
+// Walks consecutive stages of the flat list (tile-major, L stages per tile) from stage s.
 template <int MODE>
-__device__ __forceinline__ void decode_stage(long long s, int L, int ntm, int kst, StageMeta& m) {
-  m.tile = static_cast<int>(s / L);
-  m.u = static_cast<int>(s % L);
-  if (MODE == kModeDownOne) {
-    m.m = m.tile;
-    m.c = m.u / kst;
-    m.ks = m.u % kst;
-  } else {
-    m.c = m.tile / ntm;
-    m.m = m.tile % ntm;
-    m.ks = m.u;
+struct StageWalker {
+  int u, c, m, ks, L, ntm, kst;
+  __device__ __forceinline__ void init(int s, int L_, int ntm_, int kst_) {
+    L = L_; ntm = ntm_; kst = kst_;
+    const int tile = s / L;
+    u = s % L;
+    if (MODE == kModeDownOne) {
+      m = tile;
+      c = u / kst;
+      ks = u % kst;
+    } else {
+      c = tile / ntm;
+      m = tile % ntm;
+      ks = u;
+    }
   }
-}
+  __device__ __forceinline__ void next() {
+    u++;
+    if (MODE == kModeDownOne) {
+      if (++ks == kst) { ks = 0; c++; }
+      if (u == L) { u = 0; ks = 0; c = 0; m++; }
+    } else {
+      ks = u;
+      if (u == L) { u = 0; ks = 0; if (++m == ntm) { m = 0; c++; } }
+    }
+  }
+};
 
+// Work is claimed dynamically: unit = U consecutive stages of one tile (U divides L), claimed in
+// increasing order from a device counter, so SMs that stream faster take more units. A tile cut
+// into several units is accumulated per unit; the CTA finishing the tile's last unit adds the
+// unit parts in K order (deterministic). The last CTA to exit resets the counters.
 template <int MODE>
 __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_constant__ MoeTcMaps maps,
                                                              MoeTcArgs a) {
@@ -140,33 +191,45 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.off_bar);
   uint64_t* sf_full = full + S;
   uint64_t* empty = sf_full + S;
-  uint64_t* acc_full = empty + S;       // [2]
-  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* bfull = empty + S;          // activation operand of the stage landed
+  uint64_t* acc_full = bfull + S;       // [4]
+  uint64_t* acc_empty = acc_full + 4;   // [4]
+  uint64_t* rec_full = acc_empty + 4;   // [kRecRing]
+  uint64_t* rec_empty = rec_full + kRecRing;
+  uint64_t* sfa_done = rec_empty + kRecRing;  // [S] A's scale factors copied into TMEM
   StageMeta* meta = reinterpret_cast<StageMeta*>(smem + lay.off_meta);
+  PartRec* recs = reinterpret_cast<PartRec*>(smem + lay.off_rec);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + lay.off_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;
   float* ubuf = reinterpret_cast<float*>(smem + lay.off_ubuf);  // [32][64] up values (GATE_UP)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (a.trace && threadIdx.x == 0) a.trace[1024 + 4 * blockIdx.x] = global_ns();
   const int nch = *a.n_chunks;
   const int kst = a.K / kMtKStage;
   const int ntm = MODE == kModeGateUp ? a.out_rows / 64 : a.out_rows / 128;
   const int L = MODE == kModeDownOne ? max(1, nch * kst) : kst;
-  const long long ntiles = MODE == kModeDownOne ? ntm : static_cast<long long>(nch) * ntm;
-  const long long total = ntiles * L;
-  const int grid = gridDim.x;
-  const long long s_begin = total * blockIdx.x / grid, s_end = total * (blockIdx.x + 1) / grid;
+  const int U = a.unit_stages < L && L % a.unit_stages == 0 ? a.unit_stages : L;
+  const int upt = L / U;  // units per tile
+  const int ntiles = MODE == kModeDownOne ? ntm : nch * ntm;
+  const int total_units = ntiles * upt;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
       mbar_init(&full[i], 1);
       mbar_init(&sf_full[i], 128);
       mbar_init(&empty[i], 1);
+      mbar_init(&bfull[i], 1);
+      mbar_init(&sfa_done[i], 1);
     }
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < 4; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
+    }
+    for (int i = 0; i < kRecRing; i++) {
+      mbar_init(&rec_full[i], 1);
+      mbar_init(&rec_empty[i], 2 + 128 + 128);  // activation producer, MMA issuer, epilogue, scale warps
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -176,156 +239,266 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t sf_base = tbase + 2 * kMtAccCols;
+  // accumulators: N <= 8 * b_boxes columns each; four when they fit in 256 columns
+  const int acc_cols = ((8 * a.b_boxes + 31) / 32) * 32;
+  const int nacc = acc_cols <= 64 ? 4 : 2;
+  const uint32_t sf_base = tbase + 256;
+  if (a.trace && threadIdx.x == 0) a.trace[1024 + 4 * blockIdx.x + 1] = global_ns();
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0 && s_begin < s_end) {
-      tma_prefetch_desc(&maps.a0);
-      tma_prefetch_desc(&maps.b);
-      long long issued = 0;
-      int cc = -1, ce = 0, cp0 = 0, cn = 0, cb = 0;  // chunk fields of the previous stage
-      for (long long s = s_begin; s < s_end; s++, issued++) {
-        const int slot = static_cast<int>(issued % S);
-        if (issued >= S && !mbar_wait_bounded(&empty[slot], ((issued / S) - 1) & 1, a.err, 0x100u)) {
+    // ------------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
+      int cc = -1, ce = 0, cn = 0;  // chunk fields of the current stage
+      // claim the first unit and load its chunk fields
+      int unit = atomicAdd(a.work, 1);
+      int ue = 0, up0 = 0, un = 0, ubr = 0;
+      auto chunk_of = [&](int u, int& c) {  // chunk of the unit's first stage
+        const int t = u / upt;
+        c = MODE == kModeDownOne ? ((u % upt) * U) / kst : t / ntm;
+      };
+      auto load_unit = [&](int u) {
+        if (u >= total_units) return;
+        int c;
+        chunk_of(u, c);
+        ue = __ldg(a.ch_expert + c);
+        up0 = __ldg(a.ch_pos + c);  // (one token: the position the unit's K run starts on)
+        un = MODE == kModeDownOne ? 1 : __ldg(a.ch_n + c);
+        ubr = 4 * (a.b_tok ? __ldg(a.b_tok + up0) : up0);
+      };
+      load_unit(unit);
+      for (int part = 0;; part++) {
+        const bool stop = unit >= total_units || *abort_flag;
+        const int nxt = stop ? unit : atomicAdd(a.work, 1);  // next claim; used after this unit
+        if (part >= kRecRing && !mbar_wait_bounded(&rec_empty[rslot], rph ^ 1, a.err, 0x10u)) {
           *abort_flag = 1;
           break;
         }
+        PartRec& r = recs[rslot];
+        r.tile = stop ? -1 : unit / upt;
+        r.uit = stop ? 0 : unit % upt;
+        r.unit = unit;
+        r.e = ue;
+        r.p0 = up0;
+        r.n = un;
+        r.brow = ubr;
+        mbar_arrive(&rec_full[rslot]);
+        if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+        if (stop) break;
+        StageWalker<MODE> w;
+        w.init((unit / upt) * L + (unit % upt) * U, L, ntm, kst);
+        cc = w.c;
+        ce = ue;
+        cn = un;
+        for (int j = 0; j < U; j++, w.next(), issued++) {
+          if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (w.c != cc) {  // (one token: the K run crosses experts inside a tile)
+            cc = w.c;
+            ce = __ldg(a.ch_expert + cc);
+          }
+          meta[slot].nb = MODE == kModeDownOne ? 1 : (4 * cn + 7) / 8;
+          uint8_t* st = smem + slot * stage_pitch;
+          if (a.trace && blockIdx.x == 0 && issued < 256) a.trace[issued * 4 + 0] = global_ns();
+          mbar_arrive_expect_tx(&full[slot], kTileBlock);
+          const uint8_t* blk = a.wbase + static_cast<size_t>(ce) * a.wstride +
+                               (static_cast<size_t>(w.m) * kst + w.ks) * kTileBlock;
+          bulk_g2s(st, blk, kTileBlock, &full[slot]);
+          if (++slot == S) { slot = 0; ph ^= 1; }
+          if (j == 0) load_unit(nxt);  // next unit's fields load while this one streams
+        }
+        unit = nxt;
         if (*abort_flag) break;
-        StageMeta m;
-        decode_stage<MODE>(s, L, ntm, kst, m);
-        if (m.c != cc) {
-          cc = m.c;
-          ce = __ldg(a.ch_expert + cc);
-          cp0 = __ldg(a.ch_pos + cc);
-          cn = __ldg(a.ch_n + cc);
-          if (a.b_tok) cb = __ldg(a.b_tok + cp0);
-        }
-        m.e = ce;
-        m.p0 = cp0;
-        m.n = cn;
-        m.nb = (4 * cn + 7) / 8;
-        m.first = (m.u == 0 || s == s_begin) ? 1 : 0;
-        m.last = (m.u == L - 1 || s == s_end - 1) ? 1 : 0;
-        meta[slot] = m;
-        uint8_t* st = smem + slot * stage_pitch;
-        uint8_t* sb = st + 32768;
-        uint8_t* ssa = sb + 2 * bsub;
-        uint8_t* ssb = ssa + 2048;
-        const uint32_t bytes = 32768 + 2048 + m.nb * (2 * 1024 + 128);
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        const int kx = m.ks * (kMtKStage / 2);       // byte column of this stage in a row
-        const int ksf = m.ks * (kMtKStage / 32);     // scale byte column
-        const int erow = m.e * a.rows_per_expert_data;
-        const int esf = m.e * a.rows_per_expert_sf;
-        if (MODE == kModeGateUp) {
-          const int r0 = m.m * 64;
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            tma_load_2d(st + h * 16384, &maps.a0, kx + 128 * h, erow + r0, &full[slot]);
-            tma_load_2d(st + h * 16384 + 8192, &maps.a1, kx + 128 * h, erow + r0, &full[slot]);
-          }
-          tma_load_2d(ssa, &maps.s0, ksf, esf + r0, &full[slot]);
-          tma_load_2d(ssa + 1024, &maps.s1, ksf, esf + r0, &full[slot]);
-        } else {
-          const int r0 = m.m * 128;
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            tma_load_2d(st + h * 16384, &maps.a0, kx + 128 * h, erow + r0, &full[slot]);
-            tma_load_2d(st + h * 16384 + 8192, &maps.a0, kx + 128 * h, erow + r0 + 64, &full[slot]);
-          }
-          tma_load_2d(ssa, &maps.s0, ksf, esf + r0, &full[slot]);
-          tma_load_2d(ssa + 1024, &maps.s0, ksf, esf + r0 + 64, &full[slot]);
-        }
-        for (int bx = 0; bx < m.nb; bx++) {
-          const int brow = 4 * (a.b_tok ? cb : m.p0) + 8 * bx;
-          tma_load_2d(sb + bx * 1024, &maps.b, kx, brow, &full[slot]);
-          tma_load_2d(sb + bsub + bx * 1024, &maps.b, kx + 128, brow, &full[slot]);
-          tma_load_2d(ssb + bx * 128, &maps.bs, ksf, brow, &full[slot]);
+      }
+      if (*abort_flag) {
+        // unblock the roles waiting for a record: an end record in every ring slot they may read
+        for (int i = 0; i < kRecRing; i++) {
+          recs[i].tile = -1;
         }
       }
       // copies still landing (only after an abort) finish before the CTA exits
-      for (long long i = (issued > S ? issued - S : 0); i < issued; i++)
+      for (int i = (issued > S ? issued - S : 0); i < issued; i++)
         mbar_wait_bounded(&full[i % S], (i / S) & 1, a.err, 0x200u);
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------------ activation producer
+    if (lane == 0) {
+      tma_prefetch_desc(&maps.b);
+      tma_prefetch_desc(&maps.bs);
+      int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
+      if (MODE != kModeGateUp && a.gu_split) {
+        // the activation operand is h: wait until every CTA has written its h slices
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_gpu(a.work + 2) < static_cast<int>(gridDim.x)) {
+          if (global_ns() - t0 > 2000000000ull) {
+            atomicOr(a.err, 0x40000u);
+            *abort_flag = 1;
+            break;
+          }
+          __nanosleep(32);
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");  // h was written by plain stores
+      }
+      for (;;) {
+        if (!mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x20u)) break;
+        const PartRec r = recs[rslot];
+        mbar_arrive(&rec_empty[rslot]);
+        if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+        if (r.tile < 0 || *abort_flag) break;
+        StageWalker<MODE> w;
+        w.init(r.tile * L + r.uit * U, L, ntm, kst);
+        const int nb = MODE == kModeDownOne ? 1 : (4 * r.n + 7) / 8;
+        int brow0 = r.brow, cc = w.c;
+        bool ok = true;
+        for (int j = 0; j < U; j++, w.next(), issued++) {
+          if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
+            ok = false;
+            break;
+          }
+          if (MODE == kModeDownOne && w.c != cc) {  // the K run moved to the next position
+            cc = w.c;
+            const int p = __ldg(a.ch_pos + cc);
+            brow0 = 4 * (a.b_tok ? __ldg(a.b_tok + p) : p);
+          }
+          uint8_t* sb = smem + slot * stage_pitch + kBOff;
+          uint8_t* ssb = sb + 2 * bsub;
+          mbar_arrive_expect_tx(&bfull[slot], nb * (2 * 1024 + 128));
+          const int kx = w.ks * (kMtKStage / 2);       // byte column of this stage in a B row
+          const int ksf = w.ks * (kMtKStage / 32);     // scale byte column
+          for (int bx = 0; bx < nb; bx++) {
+            const int brow = brow0 + 8 * bx;
+            tma_load_2d(sb + bx * 1024, &maps.b, kx, brow, &bfull[slot]);
+            tma_load_2d(sb + bsub + bx * 1024, &maps.b, kx + 128, brow, &bfull[slot]);
+            tma_load_2d(ssb + bx * 128, &maps.bs, ksf, brow, &bfull[slot]);
+          }
+          if (++slot == S) { slot = 0; ph ^= 1; }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+      for (int i = (issued > S ? issued - S : 0); i < issued; i++)
+        mbar_wait_bounded(&bfull[i % S], (i / S) & 1, a.err, 0x200u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0 && s_begin < s_end) {
-      long long i = 0;
-      int buf = 0, tiles_done = 0;
+    if (lane == 0) {
+      int i = 0, buf = 0, parts = 0, rslot = 0, rph = 0;
       bool ok = true;
-      for (long long s = s_begin; s < s_end && ok; s++, i++) {
-        const int slot = static_cast<int>(i % S);
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait_bounded(&full[slot], ph, a.err, 0x400u) ||
-            !mbar_wait_bounded(&sf_full[slot], ph, a.err, 0x800u)) {
-          ok = false;
-          break;
-        }
-        const StageMeta m = meta[slot];
-        if (m.first && tiles_done >= 2 &&
-            !mbar_wait_bounded(&acc_empty[buf], ((tiles_done / 2) - 1) & 1, a.err, 0x1000u)) {
+      const uint64_t da0 = sw128_desc(smem), db0 = sw128_desc(smem + kBOff);  // slot 0
+      for (;;) {
+        if (!mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x20u)) break;
+        const int tile = recs[rslot].tile;
+        mbar_arrive(&rec_empty[rslot]);
+        if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+        if (tile < 0 || *abort_flag) break;
+        if (parts >= nacc && !mbar_wait_bounded(&acc_empty[buf], ((parts / nacc) - 1) & 1, a.err, 0x1000u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint8_t* st = smem + slot * stage_pitch;
-        const uint64_t da = sw128_desc(st), db = sw128_desc(st + 32768);
-        const uint32_t idesc = mxf4_idesc(8 * m.nb);
-        const uint32_t sfa = sf_base + slot * kMtSfCols, sfb = sfa + 16;
-        const uint32_t dacc = tbase + buf * kMtAccCols;
+        const uint32_t dacc = tbase + buf * acc_cols;
+        for (int j = 0; j < U && ok; j++, i++) {
+          const int slot = i % S;
+          const uint32_t ph = (i / S) & 1;
+          if (a.trace && blockIdx.x == 0 && i < 256) a.trace[i * 4 + 2] = global_ns();
+          // both operands' scale factors in TMEM: A's copies committed to sfa_done (issued
+          // once the stage's data landed), B's stores behind sf_full (after the B operand landed)
+          if (!mbar_wait_bounded(&sfa_done[slot], ph, a.err, 0x800u) ||
+              !mbar_wait_bounded(&sf_full[slot], ph, a.err, 0x800u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // operands of the stage's 8 MMAs computed first, then issued back to back
+          const uint64_t da = da0 + static_cast<uint64_t>((slot * stage_pitch) >> 4);
+          const uint64_t db = db0 + static_cast<uint64_t>((slot * stage_pitch) >> 4);
+          const uint32_t idesc = mxf4_idesc(8 * meta[slot].nb);
+          const uint32_t sfa = sf_base + slot * kMtSfCols, sfb = sfa + 16;
+          uint64_t dak[8], dbk[8];
+          uint32_t idk[8], sak[8], sbk[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-          const int h = k >> 2, w = k & 3;  // swizzle column, 32-byte step inside it
-          const uint64_t adv = static_cast<uint64_t>((32 * w) >> 4);
-          const uint64_t da_k = da + static_cast<uint64_t>((h * 16384) >> 4) + adv;
-          const uint64_t db_k = db + static_cast<uint64_t>((h * bsub) >> 4) + adv;
-          const uint32_t byte = static_cast<uint32_t>(2 * (k & 1)) << 30;
-          mma_mxf4(dacc, da_k, db_k, idesc, (sfa + 4 * (k >> 1)) | byte, (sfb + 4 * (k >> 1)) | byte,
-                   (m.first && k == 0) ? 0u : 1u);
+          for (int k = 0; k < 8; k++) {
+            const uint32_t adv = (32 * (k & 3)) >> 4;
+            dak[k] = da + ((k >> 2) * (16384 >> 4) + adv);
+            dbk[k] = db + ((k >> 2) * (bsub >> 4) + adv);
+            const uint32_t sid = static_cast<uint32_t>(2 * (k & 1));
+            sak[k] = (sfa + 4 * (k >> 1)) | (sid << 30);
+            sbk[k] = (sfb + 4 * (k >> 1)) | (sid << 30);
+            idk[k] = idesc | (sid << 29) | (sid << 4);
+          }
+          const uint32_t acc0 = j == 0 ? 0u : 1u;
+#pragma unroll
+          for (int k = 0; k < 8; k++) mma_mxf4_run(dacc, dak[k], dbk[k], idk[k], sak[k], sbk[k], k == 0 ? acc0 : 1u);
+          tc_commit(&empty[slot]);
+          if (a.trace && blockIdx.x == 0 && i < 256) a.trace[i * 4 + 3] = global_ns();
         }
-        tc_commit(&empty[slot]);
-        if (m.last) {
-          tc_commit(&acc_full[buf]);
-          buf ^= 1;
-          tiles_done++;
-        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+        if (++buf == nacc) buf = 0;
+        parts++;
       }
       if (!ok) *abort_flag = 1;
     }
   } else if (warp < 6) {
-    // ------------------------------------------------------------------ scale factors -> TMEM
+    // ------------------------------------------------------------------ B scale factors -> TMEM
     const int q = warp & 3;
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
-    long long i = 0;
-    for (long long s = s_begin; s < s_end; s++, i++) {
-      const int slot = static_cast<int>(i % S);
-      if (!mbar_wait_bounded(&full[slot], (i / S) & 1, a.err, 0x4000u)) break;
-      if (*abort_flag) break;
-      const uint8_t* st = smem + slot * stage_pitch;
-      const uint8_t* ssa = st + 32768 + 2 * bsub;
-      const uint8_t* ssb = ssa + 2048;
-      const int nrows_b = 8 * meta[slot].nb;
-      const uint32_t sfa = sf_base + slot * kMtSfCols, sfb = sfa + 16;
-      // row (lane + 32 j) of A / B: 16 scale bytes = 4 words (k-groups g = 0..3)
-      uint4 ra[4], rb[4];
+    int i = 0, rslot = 0, rph = 0;
+    bool ok = true;
+    while (ok) {
+      if (!__all_sync(kFull, mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u))) break;
+      const int tile = recs[rslot].tile;
+      mbar_arrive(&rec_empty[rslot]);
+      if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+      if (tile < 0) break;
+      for (int j = 0; j < U; j++, i++) {
+        const int slot = i % S;
+        // (every exit below is decided warp-wide: the TMEM stores are .sync.aligned)
+        if (q == 2) {
+          // A's scale factors: each k-group's 32 x 16-byte block straight into TMEM
+          bool got = lane != 0 || mbar_wait_bounded(&full[slot], (i / S) & 1, a.err, 0x4000u);
+          got = __shfl_sync(kFull, got, 0);
+          if (!got) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            tc_fence_after();
+            const uint8_t* ssa = smem + slot * stage_pitch + 32768;
+            const uint32_t sfa = sf_base + slot * kMtSfCols;
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        ra[j] = *reinterpret_cast<const uint4*>(ssa + (lane + 32 * j) * 16);
-        const int n = lane + 32 * j;
-        rb[j] = n < nrows_b ? *reinterpret_cast<const uint4*>(ssb + n * 16) : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+            for (int g = 0; g < 4; g++) tmem_cp_rows16_x4(sfa + 4 * g, rows16_desc(ssa + g * 512));
+            tc_commit(&sfa_done[slot]);  // the MMA issuer waits for it; this warp runs ahead
+          }
+          __syncwarp();
+        }
+        const bool gotb = mbar_wait_bounded(&bfull[slot], (i / S) & 1, a.err, 0x4000u) && !*abort_flag;
+        if (!__all_sync(kFull, gotb)) {
+          ok = false;
+          break;
+        }
+        if (a.trace && blockIdx.x == 0 && i < 256 && q == 0 && lane == 0) a.trace[i * 4 + 1] = global_ns();
+        const uint8_t* ssb = smem + slot * stage_pitch + kBOff + 2 * bsub;
+        const int nrows_b = 8 * meta[slot].nb;
+        const uint32_t sfb = sf_base + slot * kMtSfCols + 16;
+        uint4 rb[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const int n = lane + 32 * jj;
+          rb[jj] = n < nrows_b ? *reinterpret_cast<const uint4*>(ssb + n * 16) : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+        }
+        tmem_st4(lane_addr | (sfb + 0), rb[0].x, rb[1].x, rb[2].x, rb[3].x);
+        tmem_st4(lane_addr | (sfb + 4), rb[0].y, rb[1].y, rb[2].y, rb[3].y);
+        tmem_st4(lane_addr | (sfb + 8), rb[0].z, rb[1].z, rb[2].z, rb[3].z);
+        tmem_st4(lane_addr | (sfb + 12), rb[0].w, rb[1].w, rb[2].w, rb[3].w);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sf_full[slot]);
       }
-      tmem_st4(lane_addr | (sfa + 0), ra[0].x, ra[1].x, ra[2].x, ra[3].x);
-      tmem_st4(lane_addr | (sfa + 4), ra[0].y, ra[1].y, ra[2].y, ra[3].y);
-      tmem_st4(lane_addr | (sfa + 8), ra[0].z, ra[1].z, ra[2].z, ra[3].z);
-      tmem_st4(lane_addr | (sfa + 12), ra[0].w, ra[1].w, ra[2].w, ra[3].w);
-      tmem_st4(lane_addr | (sfb + 0), rb[0].x, rb[1].x, rb[2].x, rb[3].x);
-      tmem_st4(lane_addr | (sfb + 4), rb[0].y, rb[1].y, rb[2].y, rb[3].y);
-      tmem_st4(lane_addr | (sfb + 8), rb[0].z, rb[1].z, rb[2].z, rb[3].z);
-      tmem_st4(lane_addr | (sfb + 12), rb[0].w, rb[1].w, rb[2].w, rb[3].w);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sf_full[slot]);
     }
   } else {
     // ------------------------------------------------------------------ epilogue
@@ -333,74 +506,89 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     const int et = threadIdx.x - 192;   // 0..127 within the epilogue warps
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
     const int row = 32 * q + lane;      // accumulator row (A-tile row)
-    const long long first_tile = s_begin / L;
-    const long long last_tile = s_begin < s_end ? (s_end - 1) / L : first_tile - 1;
-    int buf = 0, seen = 0;
-    for (long long tile = first_tile; tile <= last_tile; tile++) {
-      const bool got = mbar_wait_bounded(&acc_full[buf], (seen / 2) & 1, a.err, 0x8000u);
-      if (!epi_all(got && !*abort_flag)) break;
-      tc_fence_after();
-      StageMeta m;
-      decode_stage<MODE>(tile * L, L, ntm, kst, m);
-      m.e = __ldg(a.ch_expert + m.c);
-      m.p0 = __ldg(a.ch_pos + m.c);
-      m.n = __ldg(a.ch_n + m.c);
-      m.nb = (4 * m.n + 7) / 8;
-      if (MODE == kModeDownOne) {  // K runs over every chunk; the output is the one token
-        m.n = 1;
-        m.nb = 1;
+    if (MODE != kModeGateUp && a.gu_split) {
+      // h of every position from the gate/up unit parts: one warp per (gate/up tile, 32 inter
+      // rows), parts added in K order, h = silu(g) u w, written as the four-term operand
+      const int ew = et / 32;
+      const int items = 2 * nch * a.ntm_gu;
+      for (int it = blockIdx.x * 4 + ew; it < items; it += gridDim.x * 4) {
+        const int tile = it / 2, hf = it % 2;
+        const int c = tile / a.ntm_gu, m = tile % a.ntm_gu;
+        const int p0 = __ldg(a.ch_pos + c), n = __ldg(a.ch_n + c);
+        const int i0 = m * 64 + hf * 32;
+        for (int t = 0; t < n; t++) {
+          float g = 0.0f, u = 0.0f;
+          for (int j = 0; j < a.upt_gu; j++) {
+            const float* qp = a.partial_in + static_cast<size_t>(tile * a.upt_gu + j) * 8 * 128 + t * 128;
+            g += __ldcg(qp + hf * 32 + lane);
+            u += __ldcg(qp + 64 + hf * 32 + lane);
+          }
+          const int p = p0 + t;
+          const float hv = __fmul_rn(silu_ref(g), u) * __ldg(a.perm_w + p);
+          const size_t trow = static_cast<size_t>(4 * p);
+          warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2,
+                      a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32);
+        }
       }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (et == 0) {
+        __threadfence();
+        atomicAdd(a.work + 2, 1);  // this CTA's h slices are written
+      }
+    }
+    int buf = 0, seen = 0, rslot = 0, rph = 0;
+    for (;;) {
+      const bool gotr = mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u);
+      if (!epi_all(gotr)) break;
+      const PartRec r = recs[rslot];
+      mbar_arrive(&rec_empty[rslot]);
+      if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+      if (r.tile < 0) break;
+      const unsigned long long e0 = a.trace && blockIdx.x == 0 ? global_ns() : 0;
+      const bool got = mbar_wait_bounded(&acc_full[buf], (seen / nacc) & 1, a.err, 0x8000u);
+      if (!epi_all(got && !*abort_flag)) break;
+      if (a.trace && blockIdx.x == 0 && et == 0 && seen < 128) {
+        a.trace[3072 + seen * 4 + 0] = e0;
+        a.trace[3072 + seen * 4 + 1] = global_ns();
+        a.trace[3072 + seen * 4 + 3] = r.tile * 16 + r.uit;
+      }
+      tc_fence_after();
+      const int mm = MODE == kModeDownOne ? r.tile : r.tile % ntm;
+      const int p0 = r.p0;
+      const int n = r.n;
+      const int nb = (4 * n + 7) / 8;
       float v[32];
-      const uint32_t dacc = tbase + buf * kMtAccCols;
-      for (int c0 = 0; c0 < 8 * m.nb; c0 += 8) {
-        float r[8];
-        tmem_ld8(dacc + lane_addr + c0, r);
-        v[c0 / 4] = ((r[0] + r[1]) + r[2]) + r[3];
-        v[c0 / 4 + 1] = ((r[4] + r[5]) + r[6]) + r[7];
+      const uint32_t dacc = tbase + buf * acc_cols;
+      for (int c0 = 0; c0 < 8 * nb; c0 += 8) {
+        float rr[8];
+        tmem_ld8(dacc + lane_addr + c0, rr);
+        v[c0 / 4] = ((rr[0] + rr[1]) + rr[2]) + rr[3];
+        v[c0 / 4 + 1] = ((rr[4] + rr[5]) + rr[6]) + rr[7];
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
-      buf ^= 1;
+      if (++buf == nacc) buf = 0;
       seen++;
-      // ---- whole tile here, or the last of its parts?
-      const long long ts = static_cast<long long>(m.tile) * L, te = ts + L;
-      const bool whole = ts >= s_begin && te <= s_end;
-      (void)et;
-      if (!whole) {
-        const int slot2 = (m.tile == first_tile) ? 0 : 1;
-        float* pp = a.partial + (static_cast<size_t>(blockIdx.x) * 2 + slot2) * 32 * 128;
-        for (int t = 0; t < m.n; t++) pp[t * 128 + row] = v[t];
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (et == 0) {
-          const int c0 = cta_of(ts, total, grid), c1 = cta_of(te - 1, total, grid);
-          const int old = atomicAdd(a.tile_cnt + m.tile, 1);
-          *last_flag = old == c1 - c0;
-          if (old == c1 - c0) a.tile_cnt[m.tile] = 0;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (!*last_flag) continue;
-        __threadfence();
-        const int c0 = cta_of(ts, total, grid), c1 = cta_of(te - 1, total, grid);
-        for (int t = 0; t < m.n; t++) v[t] = 0.0f;
-        for (int cc = c0; cc <= c1; cc++) {
-          const long long fb = total * cc / grid;
-          const int sl = (m.tile == fb / L) ? 0 : 1;
-          const float* qp = a.partial + (static_cast<size_t>(cc) * 2 + sl) * 32 * 128;
-          for (int t = 0; t < m.n; t++) v[t] += __ldcg(qp + t * 128 + row);
-        }
+      if (upt > 1) {
+        // one unit of a split tile: store its part; the parts are added in K order by the pass
+        // that needs the tile (the down kernel's prologue for gate/up, the end of this kernel
+        // for the one-token down projection)
+        float* pp = a.partial + static_cast<size_t>(r.unit) * 8 * 128;
+        for (int t = 0; t < n; t++) pp[t * 128 + row] = v[t];
+        if (a.trace && blockIdx.x == 0 && et == 0 && seen <= 128) a.trace[3072 + (seen - 1) * 4 + 2] = global_ns();
+        continue;
       }
       // ---- finalize
       if (MODE == kModeGateUp) {
-        // rows 0..63 gate, 64..127 up (of inter rows m*64 ..): h = silu(g) u w
+        // rows 0..63 gate, 64..127 up (of inter rows mm*64 ..): h = silu(g) u w
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (q >= 2)
-          for (int t = 0; t < m.n; t++) ubuf[t * 64 + (row - 64)] = v[t];
+          for (int t = 0; t < n; t++) ubuf[t * 64 + (row - 64)] = v[t];
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (q < 2) {
-          const int i0 = m.m * 64 + 32 * q;  // first inter index of this warp's 32-block
-          for (int t = 0; t < m.n; t++) {
-            const int p = m.p0 + t;
+          const int i0 = mm * 64 + 32 * q;  // first inter index of this warp's 32-block
+          for (int t = 0; t < n; t++) {
+            const int p = p0 + t;
             float hv = __fmul_rn(silu_ref(v[t]), ubuf[t * 64 + row]);
             hv *= __ldg(a.perm_w + p);
             const size_t trow = static_cast<size_t>(4 * p);
@@ -409,19 +597,60 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           }
         }
       } else if (MODE == kModeDown) {
-        const int orow = m.m * 128 + row;
-        for (int t = 0; t < m.n; t++) a.y[static_cast<size_t>(m.p0 + t) * a.hidden + orow] = v[t];
+        const int orow = mm * 128 + row;
+        for (int t = 0; t < n; t++) a.y[static_cast<size_t>(p0 + t) * a.hidden + orow] = v[t];
       } else {
-        a.y[m.m * 128 + row] = v[0];
+        a.y[mm * 128 + row] = v[0];
+      }
+      if (a.trace && blockIdx.x == 0 && et == 0 && seen <= 128) a.trace[3072 + (seen - 1) * 4 + 2] = global_ns();
+    }
+  }
+  if (MODE == kModeDownOne && upt > 1 && warp >= 6 && warp < 10) {
+    // every CTA's parts stored -> each CTA adds the parts of its share of output rows in K order
+    const int et = threadIdx.x - 192;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (et == 0) {
+      __threadfence();
+      atomicAdd(a.work + 3, 1);
+      const uint64_t t0 = global_ns();
+      while (ld_acquire_gpu(a.work + 3) < static_cast<int>(gridDim.x)) {
+        if (global_ns() - t0 > 2000000000ull) {
+          atomicOr(a.err, 0x20000u);
+          *abort_flag = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (!*abort_flag) {
+      for (int orow = blockIdx.x * 128 + et; orow < a.hidden; orow += gridDim.x * 128) {
+        const int tile = orow / 128, rr = orow % 128;
+        float v = 0.0f;
+        for (int j = 0; j < upt; j++) v += __ldcg(a.partial + static_cast<size_t>(tile * upt + j) * 8 * 128 + rr);
+        a.y[orow] = v;
       }
     }
   }
+  if (a.trace && warp == 6 && lane == 0) a.trace[1024 + 4 * blockIdx.x + 2] = global_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, kMtTmemCols);
   }
+  if (threadIdx.x == 0) {
+    // the last CTA out resets the work counters for the next launch
+    __threadfence();
+    const int old = atomicAdd(a.work + 1, 1);
+    if (old == static_cast<int>(gridDim.x) - 1) {
+      a.work[0] = 0;
+      a.work[1] = 0;
+      a.work[2] = 0;
+      a.work[3] = 0;
+    }
+  }
+  if (a.trace && threadIdx.x == 32) a.trace[1024 + 4 * blockIdx.x + 3] = global_ns();
 }
 
 // ---------------------------------------------------------------------- activation terms per position
@@ -460,6 +689,13 @@ static int sm_count() {
   return n;
 }
 
+size_t moe_tc_partial_floats(int H, int I, int k, int n_slots) {
+  const size_t chunks = static_cast<size_t>(8) * k + 8 + n_slots;  // at most, with <= 8 tokens
+  const size_t gu = chunks * (I / 64) * ((H / kMtKStage + 3) / 4);
+  const size_t dn = chunks * (H / 128) * ((I / kMtKStage + 3) / 4);
+  return (std::max(gu, dn) + 64) * 8 * 128;
+}
+
 bool moe_tc_supported(int H, int I, int Is, int fmt) {
   return fmt == kMxfp4 && H % kMtKStage == 0 && H % 128 == 0 && I % kMtKStage == 0 && I % 64 == 0 &&
          (Is == 0 || Is == I);
@@ -468,25 +704,59 @@ bool moe_tc_supported(int H, int I, int Is, int fmt) {
 size_t moe_tc_plan_bytes() { return sizeof(MoeTcPlanImpl); }
 
 // Tensor maps of one layer (built once: every pointer is fixed at layer creation).
-bool moe_tc_plan(void* plan, const uint8_t* arena, size_t stride, int n_slots, size_t off_gate, size_t off_up,
-                 size_t off_down, size_t off_gs, size_t off_us, size_t off_ds, int H, int I, const uint8_t* xt,
-                 const uint8_t* xsf, const uint8_t* ht, const uint8_t* hsf, int term_rows) {
+bool moe_tc_plan(void* plan, int H, int I, const uint8_t* xt, const uint8_t* xsf, const uint8_t* ht,
+                 const uint8_t* hsf, int term_rows) {
   MoeTcPlanImpl* p = static_cast<MoeTcPlanImpl*>(plan);
-  const uint64_t bytes = stride * static_cast<uint64_t>(n_slots);
   bool ok = true;
-  ok = ok && make_tmap_sw128(&p->gu.a0, arena + off_gate, H / 2, (bytes - off_gate) / (H / 2), 64);
-  ok = ok && make_tmap_sw128(&p->gu.a1, arena + off_up, H / 2, (bytes - off_up) / (H / 2), 64);
-  ok = ok && make_tmap_rows(&p->gu.s0, arena + off_gs, H / 32, (bytes - off_gs) / (H / 32), 16, 64);
-  ok = ok && make_tmap_rows(&p->gu.s1, arena + off_us, H / 32, (bytes - off_us) / (H / 32), 16, 64);
   ok = ok && make_tmap_sw128(&p->gu.b, xt, H / 2, term_rows, 8);
   ok = ok && make_tmap_rows(&p->gu.bs, xsf, H / 32, term_rows, 16, 8);
-  ok = ok && make_tmap_sw128(&p->dn.a0, arena + off_down, I / 2, (bytes - off_down) / (I / 2), 64);
-  p->dn.a1 = p->dn.a0;
-  ok = ok && make_tmap_rows(&p->dn.s0, arena + off_ds, I / 32, (bytes - off_ds) / (I / 32), 16, 64);
-  p->dn.s1 = p->dn.s0;
   ok = ok && make_tmap_sw128(&p->dn.b, ht, I / 2, term_rows, 8);
   ok = ok && make_tmap_rows(&p->dn.bs, hsf, I / 32, term_rows, 16, 8);
   return ok;
+}
+
+// Bytes of one expert's tile-major gate/up and down regions.
+size_t moe_tc_region_bytes(int H, int I, int down) {
+  return down ? static_cast<size_t>(H / 128) * (I / kMtKStage) * kTileBlock
+              : static_cast<size_t>(I / 64) * (H / kMtKStage) * kTileBlock;
+}
+
+// Reference row-major matrices (E2M1 rows of K/2 bytes, E8M0 rows of K/32 bytes) -> tile blocks.
+// Tile row r is row m * half + r of m0 (r < half) or row m * half + r - half of m1.
+__global__ void tc_relayout_kernel(const uint8_t* __restrict__ m0, const uint8_t* __restrict__ m1,
+                                   const uint8_t* __restrict__ s0, const uint8_t* __restrict__ s1, int K,
+                                   int half, int ntiles, uint8_t* __restrict__ dst) {
+  const int KS = K / kMtKStage;
+  const size_t nchunk = static_cast<size_t>(ntiles) * KS * 2 * 128 * 8;
+  const size_t nword = static_cast<size_t>(ntiles) * KS * 512;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nchunk; i += stride) {
+    const int c = i & 7, r = (i >> 3) & 127, h = (i >> 10) & 1;
+    const size_t blk = i >> 11;
+    const int m = static_cast<int>(blk / KS), ks = static_cast<int>(blk % KS);
+    const uint8_t* row = r < half ? m0 + static_cast<size_t>(m * half + r) * (K / 2)
+                                  : m1 + static_cast<size_t>(m * half + r - half) * (K / 2);
+    const uint4 v = *reinterpret_cast<const uint4*>(row + 256 * ks + 128 * h + 16 * c);
+    *reinterpret_cast<uint4*>(dst + blk * kTileBlock + h * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+  }
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nword; i += stride) {
+    const int j = i & 3, g = (i >> 2) & 3, L = (i >> 4) & 31;
+    const size_t blk = i >> 9;
+    const int m = static_cast<int>(blk / KS), ks = static_cast<int>(blk % KS);
+    const int r = L + 32 * j;
+    const uint8_t* row = r < half ? s0 + static_cast<size_t>(m * half + r) * (K / 32)
+                                  : s1 + static_cast<size_t>(m * half + r - half) * (K / 32);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + 16 * ks + 4 * g);
+    *reinterpret_cast<uint32_t*>(dst + blk * kTileBlock + 32768 + ((g * 128 + L * 4 + j) << 2)) = w;
+  }
+}
+
+// gate/up: m0 = gate, m1 = up (K = hidden); down: m0 = down (K = inter), m1 unused.
+cudaError_t launch_tc_relayout(int down, const uint8_t* m0, const uint8_t* m1, const uint8_t* s0,
+                               const uint8_t* s1, int H, int I, uint8_t* dst, cudaStream_t st) {
+  const int K = down ? I : H, half = down ? 128 : 64, ntiles = down ? H / 128 : I / 64;
+  tc_relayout_kernel<<<1184, 256, 0, st>>>(m0, down ? m0 : m1, s0, down ? s0 : s1, K, half, ntiles, dst);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const int32_t* perm_tok,
@@ -504,21 +774,32 @@ static size_t moe_tc_smem(int stages, int b_boxes) {
 
 // mode: 0 gate/up, 1 down, 2 down for one token. mt = positions per chunk (<= 32).
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
-                          size_t stride, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
-                          int32_t* tile_cnt, unsigned* err, cudaStream_t st, const int32_t* b_token_rows) {
+                          const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
+                          int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st, const int32_t* b_token_rows,
+                          unsigned long long* trace, const float* partial_in) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   MoeTcArgs a{};
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.ch_n = d.ch_n; a.n_chunks = d.n_chunks;
   a.perm_w = d.perm_w;
   a.K = mode == 0 ? H : I;
   a.out_rows = mode == 0 ? I : H;
-  a.rows_per_expert_data = static_cast<int>(stride / (a.K / 2));
-  a.rows_per_expert_sf = static_cast<int>(stride / (a.K / 32));
+  a.wbase = arena + (mode == 0 ? 0 : off_down);
+  a.wstride = stride;
   a.b_boxes = (4 * mt + 7) / 8;
   a.ht = ht; a.hsf = hsf; a.inter = I;
   a.y = y; a.hidden = H;
   a.partial = partial; a.tile_cnt = tile_cnt; a.err = err;
   a.b_tok = b_token_rows;
+  a.trace = trace;
+  a.work = work;
+  a.unit_stages = mt <= 8 ? 4 : 1 << 30;  // small batches: split tiles into 4-stage units
+  {
+    const int kst_gu = H / kMtKStage;  // the gate/up pass split its tiles exactly when this holds
+    a.gu_split = (mode != 0 && mt <= 8 && kst_gu > 4 && kst_gu % 4 == 0) ? 1 : 0;
+    a.upt_gu = kst_gu / 4;
+  }
+  a.ntm_gu = I / 64;
+  a.partial_in = partial_in;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, a.b_boxes) > 227 * 1024) stages--;
   a.stages = stages;
@@ -526,24 +807,28 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const MoeTcMaps& maps = mode == 0 ? p->gu : p->dn;
   const int grid = sm_count();
-  cudaError_t e;
-  switch (mode) {
-    case 0:
-      e = cudaFuncSetAttribute(moe_tc_kernel<kModeGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      moe_tc_kernel<kModeGateUp><<<grid, kMtThreads, smem, st>>>(maps, a);
-      break;
-    case 1:
-      e = cudaFuncSetAttribute(moe_tc_kernel<kModeDown>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      moe_tc_kernel<kModeDown><<<grid, kMtThreads, smem, st>>>(maps, a);
-      break;
-    default:
-      e = cudaFuncSetAttribute(moe_tc_kernel<kModeDownOne>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      moe_tc_kernel<kModeDownOne><<<grid, kMtThreads, smem, st>>>(maps, a);
-      break;
-  }
+  // Down kernels whose CTAs wait on each other (h slices, the one-token output sum) rely on all
+  // CTAs being resident together: the grid is one CTA per SM and a CTA needs most of an SM's
+  // shared memory, so no two of them share an SM; the waits are bounded either way. (A
+  // cooperative launch would also guarantee residency, but inside a CUDA graph it waits for the
+  // order-resolving kernel running beside it.)
+  const bool coop = false;
+  void (*kern)(const MoeTcMaps, MoeTcArgs) = mode == 0 ? moe_tc_kernel<kModeGateUp>
+                                             : mode == 1 ? moe_tc_kernel<kModeDown> : moe_tc_kernel<kModeDownOne>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMtThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = coop ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, maps, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "pipe.cuh"
 #include "terms.cuh"
 
 namespace rmoe {
@@ -937,11 +938,48 @@ cudaError_t launch_decode_front(const DecodeFront& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// The reference chain for one (token, expert) with the token's activations and the expert's
+// router row both staged in shared memory: a = -0.0; a = fl(a + fl(x_k * w_k)), k ascending.
+// Two 8-element chunks are read ahead, so only the add latency (~4 cycles per element) remains.
+template <int XD, int WD>
+__device__ __forceinline__ float exact_chain_smem(const uint8_t* xs, const uint8_t* ws, int H) {
+  constexpr int XB = XD == kBF16 ? 16 : 32, WB = WD == kBF16 ? 16 : 32;  // bytes per 8 elements
+  auto ld = [](const uint8_t* p, int dt, uint4 (&r)[2]) {
+    r[0] = *reinterpret_cast<const uint4*>(p);
+    if (dt == kF32) r[1] = *reinterpret_cast<const uint4*>(p + 16);
+  };
+  const int nch = H / 8;
+  uint4 xr[2][2], wr[2][2];
+  ld(xs, XD, xr[0]);
+  ld(ws, WD, wr[0]);
+  float acc = -0.0f;
+  for (int c = 0; c < nch; c += 2) {
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      if (c + j >= nch) break;
+      if (c + j + 1 < nch) {
+        ld(xs + (c + j + 1) * XB, XD, xr[(j + 1) & 1]);
+        ld(ws + (c + j + 1) * WB, WD, wr[(j + 1) & 1]);
+      }
+      float xv[8], wv[8];
+      expand8<XD>(xr[j], xv);
+      expand8<WD>(wr[j], wv);
+#pragma unroll
+      for (int i = 0; i < 8; i++) acc = __fadd_rn(acc, __fmul_rn(xv[i], wv[i]));
+    }
+  }
+  return acc;
+}
+
 // Final routing in the reference's rank order. Tokens whose order certificate failed get exact
-// chains for their k winners (the set is already certain) and are re-ranked on those values;
-// the others are copied. Runs beside the expert GEMVs.
+// chains for their k winners (the set is already certain), one lane per winner, on the token's
+// activations and the winners' router rows bulk-copied into shared memory; they are re-ranked on
+// those values. Other tokens are copied. Runs beside the expert GEMMs.
+template <int XD, int WD>
 __global__ void __launch_bounds__(32) resolve_order_kernel(SmallPrologue a, int32_t* ids_final,
                                                            float* w_final) {
+  extern __shared__ __align__(128) uint8_t rs_smem[];
+  __shared__ uint64_t bar;
   const int t = blockIdx.x, lane = threadIdx.x;
   const int k = a.k, kk = min(a.k, a.E);
   if (!a.pending[t]) {
@@ -951,10 +989,26 @@ __global__ void __launch_bounds__(32) resolve_order_kernel(SmallPrologue a, int3
     }
     return;
   }
+  const uint32_t xbytes = static_cast<uint32_t>(a.H) * (XD == kBF16 ? 2 : 4);
+  const uint32_t wbytes = static_cast<uint32_t>(a.H) * (WD == kBF16 ? 2 : 4);
   const int e = lane < kk ? a.ids[t * k + lane] : -1;
+  if (lane == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(&bar, xbytes + kk * wbytes);
+    bulk_g2s(rs_smem, static_cast<const uint8_t*>(a.x) + static_cast<size_t>(t) * xbytes, xbytes, &bar);
+  }
+  __syncwarp();
+  for (int j = 0; j < kk; j++) {
+    const int ej = __shfl_sync(kFull, e, j);
+    if (lane == 0)
+      bulk_g2s(rs_smem + xbytes + j * wbytes, static_cast<const uint8_t*>(a.w) + static_cast<size_t>(ej) * wbytes,
+               wbytes, &bar);
+  }
+  const bool got = mbar_wait_bounded(&bar, 0, a.errflag, 0x100000u);
   float v = -INFINITY;
-  if (e >= 0) {
-    v = exact_logit(a.x, a.x_dtype, a.w, a.w_dtype, t, e, a.H);
+  if (got && e >= 0) {
+    v = exact_chain_smem<XD, WD>(rs_smem, rs_smem + xbytes + lane * wbytes, a.H);
     if (a.bias) v = __fadd_rn(v, a.bias[e]);
   }
   unsigned tk = 0;
@@ -983,8 +1037,19 @@ __global__ void __launch_bounds__(32) resolve_order_kernel(SmallPrologue a, int3
 cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final,
                                  cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
-  resolve_order_kernel<<<a.T, 32, 0, st>>>(a, ids_final, w_final);
-  return cudaGetLastError();
+  const int xs = a.x_dtype == kBF16 ? 2 : 4, ws = a.w_dtype == kBF16 ? 2 : 4;
+  const size_t smem = static_cast<size_t>(a.H) * xs + static_cast<size_t>(min(a.k, a.E)) * a.H * ws;
+  if (a.H % 16 != 0 || smem > 220 * 1024) return cudaErrorInvalidValue;
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kern<<<a.T, 32, smem, st>>>(a, ids_final, w_final);
+    return cudaGetLastError();
+  };
+  if (a.x_dtype == kBF16 && a.w_dtype == kBF16) return go(resolve_order_kernel<kBF16, kBF16>);
+  if (a.x_dtype == kBF16) return go(resolve_order_kernel<kBF16, kF32>);
+  if (a.w_dtype == kBF16) return go(resolve_order_kernel<kF32, kBF16>);
+  return go(resolve_order_kernel<kF32, kF32>);
 }
 
 cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers& d,

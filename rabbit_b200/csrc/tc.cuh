@@ -68,6 +68,19 @@ __host__ __device__ constexpr uint32_t mxf4_idesc(int n) {
          | (static_cast<uint32_t>(128 >> 4) << 24);  // M / 16
 }
 
+// Same, with the instruction descriptor already carrying the scale-factor byte ids and no
+// compiler memory barrier, so a run of MMAs issues back to back (the issuing thread's own
+// instruction latency, not the tensor core, otherwise bounds the issue rate). Ordering with
+// later memory operations comes from the tcgen05.commit that follows the run.
+__device__ __forceinline__ void mma_mxf4_run(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t id,
+                                             uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(id), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+}
+
 // D[tmem_d] (+)= A[desc_a] . B[desc_b]^T with per-32 scales from TMEM (block32 = 2 scales per
 // row per K = 64 step).
 __device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
@@ -80,6 +93,18 @@ __device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t desc_a, uint6
       "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
       ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(id), "r"(accumulate), "r"(tsfa), "r"(tsfb)
       : "memory");
+}
+
+// ---- shared memory -> TMEM copies (asynchronous, in issue order with this thread's MMAs) ----
+// Source: 32 rows x 16 bytes, rows contiguous (8-row core matrices 128 B apart, no swizzle).
+__device__ __forceinline__ uint64_t rows16_desc(const void* src) {
+  const uint64_t addr = smem_u32(src);
+  return ((addr >> 4) & 0x3FFFull) | ((128ull >> 4) << 32) | (1ull << 46);
+}
+// Row r of the source lands in TMEM lane r of every sub-partition (r, r + 32, r + 64, r + 96),
+// its four 32-bit words in columns taddr .. taddr + 3.
+__device__ __forceinline__ void tmem_cp_rows16_x4(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
 }
 
 // ---- TMEM <-> registers (a warp accesses the 32 lanes of its sub-partition) ----
