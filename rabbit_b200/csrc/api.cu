@@ -944,7 +944,8 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
     // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
     // weight folded in), down: one token = combined row directly, else y per position + sum
     if (!terms_done) {
-      e = launch_terms_by_position(x, xdt, H, L->d.perm_tok, L->d.offsets + n_slots, P, L->xt, L->xsf, st);
+      e = launch_terms_by_position(x, xdt, H, T, k, L->d.inv, L->has_shared ? L->d.offsets + L->n_loc : nullptr,
+                                   L->xt, L->xsf, st);
       if (e != cudaSuccess) return cuda_fail(e, "activation terms");
     }
     marks.mark();

@@ -205,9 +205,8 @@ bool moe_tc_plan(void* plan, int H, int I, const uint8_t* xt, const uint8_t* xsf
 size_t moe_tc_region_bytes(int H, int I, int down);
 cudaError_t launch_tc_relayout(int down, const uint8_t* m0, const uint8_t* m1, const uint8_t* s0,
                                const uint8_t* s1, int H, int I, uint8_t* dst, cudaStream_t st);
-cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const int32_t* perm_tok,
-                                     const int32_t* n_pos, int P_bound, uint8_t* xt, uint8_t* xsf,
-                                     cudaStream_t st);
+cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, int T, int k, const int32_t* inv,
+                                     const int32_t* shared_pos0, uint8_t* xt, uint8_t* xsf, cudaStream_t st);
 // mode 0: gate/up (-> h terms), 1: down (-> y per position), 2: down of one token (-> out row)
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,

@@ -42,8 +42,10 @@ constexpr uint32_t kMtTmemCols = 512;
 enum { kModeGateUp = 0, kModeDown = 1, kModeDownOne = 2 };
 
 struct MoeTcMaps {
-  CUtensorMap b;    // activation terms (box 128 B x 8 rows, SW128)
-  CUtensorMap bs;   // their scale rows (box 16 B x 8 rows)
+  CUtensorMap b;     // activation terms (box 128 B x 8 rows, SW128)
+  CUtensorMap bs;    // their scale rows (box 16 B x 8 rows)
+  CUtensorMap b128;  // the same with 128-row boxes (chunks of up to 32 positions)
+  CUtensorMap bs128;
 };
 
 // Expert weights of a tensor-core layer are stored tile-major: for each 128-row tile m and
@@ -120,7 +122,7 @@ __host__ __device__ inline MtLayout mt_layout(int stages, int b_boxes) {
   l.off_rec = l.off_meta + stages * static_cast<int>(sizeof(StageMeta));
   l.off_misc = l.off_rec + kRecRing * static_cast<int>(sizeof(PartRec));
   l.off_ubuf = (l.off_misc + 16 + 15) & ~15;  // tmem slot, abort, last flag
-  l.total = l.off_ubuf + 32 * 64 * 4;
+  l.total = l.off_ubuf + 128 * 33 * 4;  // [128 tile rows][32 positions] (+1 pad)
   return l;
 }
 
@@ -364,14 +366,22 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           }
           uint8_t* sb = smem + slot * stage_pitch + kBOff;
           uint8_t* ssb = sb + 2 * bsub;
-          mbar_arrive_expect_tx(&bfull[slot], nb * (2 * 1024 + 128));
           const int kx = w.ks * (kMtKStage / 2);       // byte column of this stage in a B row
           const int ksf = w.ks * (kMtKStage / 32);     // scale byte column
-          for (int bx = 0; bx < nb; bx++) {
-            const int brow = brow0 + 8 * bx;
-            tma_load_2d(sb + bx * 1024, &maps.b, kx, brow, &bfull[slot]);
-            tma_load_2d(sb + bsub + bx * 1024, &maps.b, kx + 128, brow, &bfull[slot]);
-            tma_load_2d(ssb + bx * 128, &maps.bs, ksf, brow, &bfull[slot]);
+          if (a.b_boxes == 16) {
+            // up to 32 positions: one 128-row box per column (rows past the chunk are not used)
+            mbar_arrive_expect_tx(&bfull[slot], 2 * 16384 + 2048);
+            tma_load_2d(sb, &maps.b128, kx, brow0, &bfull[slot]);
+            tma_load_2d(sb + bsub, &maps.b128, kx + 128, brow0, &bfull[slot]);
+            tma_load_2d(ssb, &maps.bs128, ksf, brow0, &bfull[slot]);
+          } else {
+            mbar_arrive_expect_tx(&bfull[slot], nb * (2 * 1024 + 128));
+            for (int bx = 0; bx < nb; bx++) {
+              const int brow = brow0 + 8 * bx;
+              tma_load_2d(sb + bx * 1024, &maps.b, kx, brow, &bfull[slot]);
+              tma_load_2d(sb + bsub + bx * 1024, &maps.b, kx + 128, brow, &bfull[slot]);
+              tma_load_2d(ssb + bx * 128, &maps.bs, ksf, brow, &bfull[slot]);
+            }
           }
           if (++slot == S) { slot = 0; ph ^= 1; }
         }
@@ -483,7 +493,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         }
         if (a.trace && blockIdx.x == 0 && i < 256 && q == 0 && lane == 0) a.trace[i * 4 + 1] = global_ns();
         const uint8_t* ssb = smem + slot * stage_pitch + kBOff + 2 * bsub;
-        const int nrows_b = 8 * meta[slot].nb;
+        // every row the stage buffer holds (rows past the chunk's are never read by the MMA);
+        // meta[] is not read here: only the weight producer's barrier orders its writes
+        const int nrows_b = 8 * a.b_boxes;
         const uint32_t sfb = sf_base + slot * kMtSfCols + 16;
         uint4 rb[4];
 #pragma unroll
@@ -580,21 +592,26 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       }
       // ---- finalize
       if (MODE == kModeGateUp) {
-        // rows 0..63 gate, 64..127 up (of inter rows mm*64 ..): h = silu(g) u w
+        // rows 0..63 gate, 64..127 up (inter rows mm*64 ..): the tile goes through shared memory
+        // as [row][position]; thread (position t, 32-row block hb) then forms h = silu(g) u w
+        // for its 32 inter rows and expands them into the four-term operand on its own
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (q >= 2)
-          for (int t = 0; t < n; t++) ubuf[t * 64 + (row - 64)] = v[t];
+        for (int t = 0; t < n; t++) ubuf[row * 33 + t] = v[t];
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (q < 2) {
-          const int i0 = mm * 64 + 32 * q;  // first inter index of this warp's 32-block
-          for (int t = 0; t < n; t++) {
-            const int p = p0 + t;
-            float hv = __fmul_rn(silu_ref(v[t]), ubuf[t * 64 + row]);
-            hv *= __ldg(a.perm_w + p);
-            const size_t trow = static_cast<size_t>(4 * p);
-            warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2,
-                        a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32);
+        if (et < 2 * n) {
+          const int t = et >> 1, hb = et & 1;
+          const int p = p0 + t;
+          const float wp = __ldg(a.perm_w + p);
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const float g = ubuf[(hb * 32 + i) * 33 + t], u = ubuf[(64 + hb * 32 + i) * 33 + t];
+            h[i] = __fmul_rn(silu_ref(g), u) * wp;
           }
+          const int i0 = mm * 64 + hb * 32;
+          const size_t trow = static_cast<size_t>(4 * p);
+          thread_terms4(h, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2,
+                        a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32);
         }
       } else if (MODE == kModeDown) {
         const int orow = mm * 128 + row;
@@ -654,19 +671,51 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------- activation terms per position
-// xt rows 4p..4p+3 = terms of x[perm_tok[p]]; one warp per (position, 32-block).
-__global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __restrict__ x, int x_dtype, int H,
-                                                                const int32_t* __restrict__ perm_tok,
-                                                                const int32_t* __restrict__ n_pos, int P_bound,
+// xt rows 4p..4p+3 = terms of the token of position p. One warp per (token, 32-block): the terms
+// are computed once and stored at each of the token's routed positions (inv) and its shared one.
+__global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __restrict__ x, int x_dtype, int H, int T,
+                                                                int k, const int32_t* __restrict__ inv,
+                                                                const int32_t* __restrict__ shared_pos0,
                                                                 uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
   const int nb = H / 32;
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  if (wid >= P_bound * nb) return;
-  const int p = wid / nb, b = wid % nb;
-  if (p >= *n_pos) return;
-  const int tok = perm_tok[p];
-  const float r = load_elem(x, x_dtype, static_cast<size_t>(tok) * H + b * 32 + lane);
-  warp_terms4(r, xt + static_cast<size_t>(4 * p) * (H / 2) + b * 16, H / 2, xsf + static_cast<size_t>(4 * p) * nb + b, nb);
+  if (wid >= T * nb) return;
+  const int t = wid / nb, b = wid % nb;
+  float r = load_elem(x, x_dtype, static_cast<size_t>(t) * H + b * 32 + lane);
+  // the token's positions: k routed slots (-1 when not local) and the shared one
+  int pos = -1;
+  if (lane < k) pos = __ldg(inv + t * k + lane);
+  else if (lane == k && shared_pos0) pos = __ldg(shared_pos0) + t;
+  uint32_t packed_w[4][4];
+  uint8_t sfb[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(r))));
+    int e = 0;
+    uint32_t nib = 0;
+    if (amax > 0.0f) {
+      e = e2m1_block_exponent(amax);
+      const bool neg = r < 0.0f;
+      const int c = e2m1_nearest(fminf(fabsf(r) * exp2i(-e), 6.0f));
+      const float q = e2m1_magnitude(c) * exp2i(e);
+      r = neg ? r + q : r - q;
+      nib = static_cast<uint32_t>(c) | (neg && c ? 8u : 0u);
+    }
+    const uint32_t sh = nib << (4 * (lane & 7));
+#pragma unroll
+    for (int g = 0; g < 4; g++) packed_w[j][g] = __reduce_or_sync(kFull, (lane >> 3) == g ? sh : 0u);
+    sfb[j] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+  }
+  // lanes holding a position each store the 4 term rows' 16 bytes + scale bytes there
+  if (pos >= 0) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const size_t row = static_cast<size_t>(4 * pos + j);
+      *reinterpret_cast<uint4*>(xt + row * (H / 2) + b * 16) =
+          make_uint4(packed_w[j][0], packed_w[j][1], packed_w[j][2], packed_w[j][3]);
+      xsf[row * nb + b] = sfb[j];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------- host side
@@ -712,6 +761,10 @@ bool moe_tc_plan(void* plan, int H, int I, const uint8_t* xt, const uint8_t* xsf
   ok = ok && make_tmap_rows(&p->gu.bs, xsf, H / 32, term_rows, 16, 8);
   ok = ok && make_tmap_sw128(&p->dn.b, ht, I / 2, term_rows, 8);
   ok = ok && make_tmap_rows(&p->dn.bs, hsf, I / 32, term_rows, 16, 8);
+  ok = ok && make_tmap_sw128(&p->gu.b128, xt, H / 2, term_rows, 128);
+  ok = ok && make_tmap_rows(&p->gu.bs128, xsf, H / 32, term_rows, 16, 128);
+  ok = ok && make_tmap_sw128(&p->dn.b128, ht, I / 2, term_rows, 128);
+  ok = ok && make_tmap_rows(&p->dn.bs128, hsf, I / 32, term_rows, 16, 128);
   return ok;
 }
 
@@ -759,12 +812,13 @@ cudaError_t launch_tc_relayout(int down, const uint8_t* m0, const uint8_t* m1, c
   return cudaGetLastError();
 }
 
-cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, const int32_t* perm_tok,
-                                     const int32_t* n_pos, int P_bound, uint8_t* xt, uint8_t* xsf,
-                                     cudaStream_t st) {
-  if (P_bound <= 0) return cudaSuccess;
-  const int n = P_bound * (H / 32) * 32;
-  terms_by_position_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, x_dtype, H, perm_tok, n_pos, P_bound, xt, xsf);
+cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, int T, int k, const int32_t* inv,
+                                     const int32_t* shared_pos0, uint8_t* xt, uint8_t* xsf, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (k > 31) return cudaErrorInvalidValue;
+  const long long n = static_cast<long long>(T) * (H / 32) * 32;
+  terms_by_position_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(x, x_dtype, H, T, k, inv, shared_pos0,
+                                                                                  xt, xsf);
   return cudaGetLastError();
 }
 

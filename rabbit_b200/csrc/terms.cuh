@@ -53,4 +53,33 @@ __device__ __forceinline__ void warp_terms4(float r, uint8_t* rows, size_t pitch
   }
 }
 
+// One thread, one 32-block held in registers: the same four-term expansion as warp_terms4,
+// serially over the 32 values; writes term j's 16 bytes to rows + j * pitch and its scale byte
+// to sf + j * sf_pitch.
+__device__ __forceinline__ void thread_terms4(float (&r)[32], uint8_t* rows, size_t pitch, uint8_t* sf,
+                                              size_t sf_pitch) {
+#pragma unroll 1
+  for (int j = 0; j < 4; j++) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(r[i]));
+    uint32_t w[4] = {0, 0, 0, 0};
+    int e = 0;
+    if (amax > 0.0f) {
+      e = e2m1_block_exponent(amax);
+      const float inv = exp2i(-e), sc = exp2i(e);
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        const bool neg = r[i] < 0.0f;
+        const int c = e2m1_nearest(fminf(fabsf(r[i]) * inv, 6.0f));
+        const float q = e2m1_magnitude(c) * sc;
+        r[i] = neg ? r[i] + q : r[i] - q;
+        w[i / 8] |= (static_cast<uint32_t>(c) | (neg && c ? 8u : 0u)) << (4 * (i % 8));
+      }
+    }
+    *reinterpret_cast<uint4*>(rows + j * pitch) = make_uint4(w[0], w[1], w[2], w[3]);
+    sf[j * sf_pitch] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+  }
+}
+
 }  // namespace rmoe
