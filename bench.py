@@ -195,6 +195,15 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------ GPU path
+def ncu_traffic(key):
+    """DRAM bytes per launch of a kernel from the committed ncu capture (profiles/), or None."""
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "ncu_traffic.json")) as f:
+            return json.load(f).get(key)
+    except (OSError, ValueError):
+        return None
+
+
 def expert_touch_bytes(cfg, ids_np, with_shared=True):
     """Algorithmic bytes of one forward: distinct touched experts (+ shared) + router + x + out."""
     distinct = len(np.unique(ids_np[ids_np >= 0]))
@@ -365,18 +374,20 @@ def run_gpu(args):
         "metric": "moe_layer_decode_us_per_token", "value": us_per_token, "unit": "us/token",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-        "dtype": "mxfp4 weights x f16 activations, f32 accumulate", "data": "synthetic",
+        "dtype": "mxfp4 weights x 4-term e2m1 activations (tcgen05 kind::mxf4), f32 accumulate", "data": "synthetic",
         "config": {"workload": DECODE_CFG, "tokens_per_step_per_gpu": 1, "hidden": cfg.hidden,
                    "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
                    "shared_inter": cfg.shared_inter, "weights": "mxfp4 (E2M1 + E8M0/32)",
                    "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
                    "l2": "flushed between timed steps (256 MiB write, then a 256 MiB read that drains the write-backs)",
                    "layer_algorithmic_bytes": layer_bytes},
-        "roofline": {"bound": "hbm", "kernel": "gemv_gate_up (fused gate/up + SwiGLU)",
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<gate_up> (tcgen05 kind::mxf4, SwiGLU epilogue)",
                      "achieved": gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None,
                      "peak": hbm_peak, "unit": "GB/s", "peak_kind": peak_kind,
                      "frac": (gu_bytes / (gu_ms / 1e3) / 1e9 / hbm_peak) if gu_ms > 0 else None,
-                     "traffic": None, "kernel_us": gu_ms * 1e3, "kernel_bytes": gu_bytes,
+                     "traffic": ncu_traffic("moe_tc_kernel_gate_up_decode_bytes"),
+                     "traffic_source": "profiles/moe_tc_kernel_decode_small.md (ncu, per launch)",
+                     "kernel_us": gu_ms * 1e3, "kernel_bytes": gu_bytes,
                      "layer_achieved_gbs": layer_bytes / (ms_per_step / 1e3) / 1e9,
                      "layer_frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / hbm_peak,
                      "down_us": dn_ms * 1e3},
