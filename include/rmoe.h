@@ -190,6 +190,15 @@ RMOE_API rmoe_status rmoe_dispatch(rmoe_layer* layer, const int32_t* ids, int32_
 RMOE_API rmoe_status rmoe_moe_forward(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                              float* out, int32_t* ids_out, float* w_out, void* stream);
 
+/* The expert loop with routing given (glm52::moe::moe's loop over Routing via apply_single_expert,
+ * src/glm52/moe.rs:463-513): out[t] = sum_j weights[t][j] * expert_{ids[t][j]}(x[t]), plus the
+ * (gated) shared expert when with_shared != 0. ids/weights [T][k] (device or host pointers); slots
+ * with id -1 or an expert not resident on this layer's EP rank contribute nothing (the building
+ * block of expert parallelism: each rank runs it on the token rows it receives). */
+RMOE_API rmoe_status rmoe_moe_forward_routed(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                                    const int32_t* ids, const float* weights, int32_t with_shared,
+                                    float* out, void* stream);
+
 /* Same, with HOST buffers as the Rust call sites hold them (x: &[f32] / bf16 bits, out:
  * &mut [f32]): copies in, runs, copies out and synchronizes. The drop-in for moe_forward's
  * signature. */

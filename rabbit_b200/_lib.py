@@ -70,6 +70,7 @@ PROTOTYPES = {
     "rmoe_route": (C.c_int, [P, P, I32, I32, P, P, P]),
     "rmoe_dispatch": (C.c_int, [P, P, I32, P, P, P, P, P, P]),
     "rmoe_moe_forward": (C.c_int, [P, P, I32, I32, P, P, P, P]),
+    "rmoe_moe_forward_routed": (C.c_int, [P, P, I32, I32, P, P, I32, P, P]),
     "rmoe_moe_forward_host": (C.c_int, [P, P, I32, I32, P, P, P]),
     "rmoe_matmul_mxfp4": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_mxfp4_tc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),

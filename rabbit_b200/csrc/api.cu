@@ -789,10 +789,11 @@ static bool small_path(const rmoe_layer* L, int T) {
 
 static int chunk_tokens(int T) { return T >= 8 ? 8 : (T >= 4 ? 4 : (T >= 2 ? 2 : 1)); }
 
-static rmoe_status dispatch_into(rmoe_layer* L, int T, int mt, const float* gate, cudaStream_t st) {
+static rmoe_status dispatch_into(rmoe_layer* L, int T, int mt, const float* gate, cudaStream_t st,
+                                 bool hs) {
   const rmoe_layer_desc& D = L->desc;
   cudaError_t e = launch_dispatch(L->ids, L->rw, T, D.topk, L->e_begin, L->e_end, mt,
-                                  L->has_shared ? 1 : 0, gate, D.moe_inter, D.shared_inter,
+                                  hs ? 1 : 0, gate, D.moe_inter, D.shared_inter,
                                   D.hidden, L->rpt_gu, L->rpt_dn, L->d, st);
   if (e != cudaSuccess) return cuda_fail(e, "dispatch");
   return RMOE_OK;
@@ -808,7 +809,7 @@ extern "C" rmoe_status rmoe_dispatch(rmoe_layer* L, const int32_t* ids, int32_t 
   const size_t n = static_cast<size_t>(T) * L->desc.topk;
   RMOE_CUDA(cudaMemcpyAsync(L->ids, ids, n * 4, cudaMemcpyDeviceToDevice, st), "rmoe_dispatch ids");
   RMOE_CUDA(cudaMemsetAsync(L->rw, 0, n * 4, st), "rmoe_dispatch weights");
-  rmoe_status s = dispatch_into(L, T, chunk_tokens(T), nullptr, st);
+  rmoe_status s = dispatch_into(L, T, chunk_tokens(T), nullptr, st, L->has_shared);
   if (s != RMOE_OK) return s;
   const int E = L->n_loc;
   if (counts) RMOE_CUDA(cudaMemcpyAsync(counts, L->d.counts, E * 4, cudaMemcpyDeviceToDevice, st), "counts");
@@ -857,6 +858,103 @@ static rmoe_status print_tc_trace(rmoe_layer* L, cudaStream_t st, const char* wh
       RMOE_CUDA(cudaMemset(L->tc_trace + off, 0, sizeof(tr)), "trace reset");
       return RMOE_OK;
 }
+
+// The expert part of a forward once routing and dispatch are on the device: activation operands,
+// gate/up, down and the combine into `out`. hs: the shared expert takes part (its positions are
+// in the dispatch); terms_done: the front end already wrote the token's activation terms;
+// fused_ok: the small-batch front end ran (one-token / fused down+combine paths allowed).
+static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T, int mt, bool hs, bool terms_done,
+                                   bool fused_ok, float* out, cudaStream_t st, StageMarks& marks, int* launches_io) {
+  const rmoe_layer_desc& D = L->desc;
+  const int H = D.hidden, k = D.topk;
+  cudaError_t e = cudaSuccess;
+  rmoe_status s = RMOE_OK;
+  int& launches = *launches_io;
+  const int P = T * k + (hs ? T : 0);
+  const int n_slots = L->n_loc + (hs ? 1 : 0);
+  if (L->use_tc) {
+    // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
+    // weight folded in), down: one token = combined row directly, else y per position + sum
+    if (!terms_done) {
+      e = launch_terms_by_position(x, xdt, H, T, k, L->d.inv, hs ? L->d.offsets + L->n_loc : nullptr,
+                                   L->xt, L->xsf, st);
+      if (e != cudaSuccess) return cuda_fail(e, "activation terms");
+    }
+    marks.mark();
+    // one token: every position reads the token's own term rows (0..3)
+    e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
+                      L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
+                      L->tc_trace);
+    if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
+
+    marks.mark();
+    marks.mark();  // (h is quantized inside the gate/up epilogue)
+    if (T == 1) {
+      e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
+                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr,
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
+      if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
+      if (L->tc_trace) {
+        if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
+        if ((s = print_tc_trace(L, st, "down (one token)", 4096)) != RMOE_OK) return s;
+      }
+      marks.mark();
+      launches = terms_done ? 4 : (fused_ok ? 6 : 9);  // front (+ order resolve), gate/up, down
+    } else {
+      e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
+                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr, nullptr, L->partial);
+      if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
+      marks.mark();
+      e = launch_combine(L->y, L->d, nullptr, T, k, H, L->n_loc, hs ? 1 : 0, out, st);
+      if (e != cudaSuccess) return cuda_fail(e, "combine");
+      launches = fused_ok ? 7 : 10;
+    }
+    marks.mark();
+    return RMOE_OK;
+  }
+  RMOE_CUDA(cudaMemsetAsync(L->hmax, 0, static_cast<size_t>(P) * 4, st), "hmax reset");
+  const int max_chunks = std::min(T * k, L->n_loc) + (T * k + mt - 1) / mt + (hs ? (T + mt - 1) / mt : 0);
+  const int tasks_gu = max_chunks * (std::max(D.moe_inter, D.shared_inter) / 2);
+  const int tasks_dn = max_chunks * (H / 4);
+  marks.mark();
+  if (L->use_pipe)
+    e = launch_pipe_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, L->h, L->hmax, L->h_ld,
+                            L->dev_err, st);
+  else
+    e = launch_gemv_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, tasks_gu, L->h, L->hmax,
+                            L->h_ld, st);
+  if (e != cudaSuccess) return cuda_fail(e, "gate/up");
+  marks.mark();
+  if (L->use_pipe && fused_ok && hs == L->has_shared) {
+    // down projection + weighted combine + gated shared expert in one kernel
+    marks.mark();  // (h quantization happens inside the down kernel)
+    e = launch_pipe_down_combine(L->tab, L->fmt, L->d, L->h, L->hmax, L->ids, T, k, L->e_begin,
+                                 H, L->h_ld, out, L->dev_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "down + combine");
+    marks.mark();
+    launches -= 2;
+  } else if (L->use_pipe) {
+    marks.mark();  // (h quantization happens inside the down kernel)
+    e = launch_pipe_down(L->tab, L->fmt, L->d, L->h, L->hmax, H, mt, L->h_ld, L->y, L->dev_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "down");
+    marks.mark();
+    e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, hs ? 1 : 0, out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "combine");
+    launches -= 1;
+  } else {
+    e = launch_quant_h(L->h, L->hmax, L->d.offsets + n_slots, P, L->h_ld, L->fmt.fmt, L->hq, L->hexp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "h quantize");
+    marks.mark();
+    e = launch_gemv_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, tasks_dn, L->h_ld, L->y, st);
+    if (e != cudaSuccess) return cuda_fail(e, "down");
+    marks.mark();
+    e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, hs ? 1 : 0, out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "combine");
+  }
+  marks.mark();
+  return RMOE_OK;
+}
+
 
 // Enqueues one forward on `st` (stream-ordered, capturable): x -> out, routing left in
 // *ids_src / *w_src (reference rank order). L->last_launches = kernels it launched.
@@ -936,94 +1034,11 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
                            L->xq, L->xexp, L->gate, st);
     if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
     marks.mark();
-    if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st)) != RMOE_OK) return s;
+    if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, L->has_shared)) != RMOE_OK) return s;
   }
-  const int P = T * k + (L->has_shared ? T : 0);
-  const int n_slots = L->n_loc + (L->has_shared ? 1 : 0);
-  if (L->use_tc) {
-    // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
-    // weight folded in), down: one token = combined row directly, else y per position + sum
-    if (!terms_done) {
-      e = launch_terms_by_position(x, xdt, H, T, k, L->d.inv, L->has_shared ? L->d.offsets + L->n_loc : nullptr,
-                                   L->xt, L->xsf, st);
-      if (e != cudaSuccess) return cuda_fail(e, "activation terms");
-    }
-    marks.mark();
-    // one token: every position reads the token's own term rows (0..3)
-    e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
-                      L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
-                      L->tc_trace);
-    if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
-
-    marks.mark();
-    marks.mark();  // (h is quantized inside the gate/up epilogue)
-    if (T == 1) {
-      e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
-                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
-      if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
-      if (L->tc_trace) {
-        if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
-        if ((s = print_tc_trace(L, st, "down (one token)", 4096)) != RMOE_OK) return s;
-      }
-      marks.mark();
-      launches = terms_done ? 4 : (resolved ? 6 : 9);  // front (+ order resolve), gate/up, down
-    } else {
-      e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
-                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr, nullptr, L->partial);
-      if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
-      marks.mark();
-      e = launch_combine(L->y, L->d, nullptr, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
-      if (e != cudaSuccess) return cuda_fail(e, "combine");
-      launches = resolved ? 7 : 10;
-    }
-    marks.mark();
-    if (resolved) RMOE_CUDA(cudaStreamWaitEvent(st, L->ev_join, 0), "join wait");
-    *ids_src = resolved ? L->ids_final : L->ids;
-    *w_src = resolved ? L->w_final : L->rw;
-    L->last_launches = launches;
-    return RMOE_OK;
-  }
-  RMOE_CUDA(cudaMemsetAsync(L->hmax, 0, static_cast<size_t>(P) * 4, st), "hmax reset");
-  const int max_chunks = std::min(T * k, L->n_loc) + (T * k + mt - 1) / mt + (L->has_shared ? (T + mt - 1) / mt : 0);
-  const int tasks_gu = max_chunks * (std::max(D.moe_inter, D.shared_inter) / 2);
-  const int tasks_dn = max_chunks * (H / 4);
-  marks.mark();
-  if (L->use_pipe)
-    e = launch_pipe_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, L->h, L->hmax, L->h_ld,
-                            L->dev_err, st);
-  else
-    e = launch_gemv_gate_up(L->tab, L->fmt, L->d, L->xq, L->xexp, H, mt, tasks_gu, L->h, L->hmax,
-                            L->h_ld, st);
-  if (e != cudaSuccess) return cuda_fail(e, "gate/up");
-  marks.mark();
-  if (L->use_pipe && small_path(L, T)) {
-    // down projection + weighted combine + gated shared expert in one kernel
-    marks.mark();  // (h quantization happens inside the down kernel)
-    e = launch_pipe_down_combine(L->tab, L->fmt, L->d, L->h, L->hmax, L->ids, T, k, L->e_begin,
-                                 H, L->h_ld, out, L->dev_err, st);
-    if (e != cudaSuccess) return cuda_fail(e, "down + combine");
-    marks.mark();
-    launches -= 2;
-  } else if (L->use_pipe) {
-    marks.mark();  // (h quantization happens inside the down kernel)
-    e = launch_pipe_down(L->tab, L->fmt, L->d, L->h, L->hmax, H, mt, L->h_ld, L->y, L->dev_err, st);
-    if (e != cudaSuccess) return cuda_fail(e, "down");
-    marks.mark();
-    e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
-    if (e != cudaSuccess) return cuda_fail(e, "combine");
-    launches -= 1;
-  } else {
-    e = launch_quant_h(L->h, L->hmax, L->d.offsets + n_slots, P, L->h_ld, L->fmt.fmt, L->hq, L->hexp, st);
-    if (e != cudaSuccess) return cuda_fail(e, "h quantize");
-    marks.mark();
-    e = launch_gemv_down(L->tab, L->fmt, L->d, L->hq, L->hexp, H, mt, tasks_dn, L->h_ld, L->y, st);
-    if (e != cudaSuccess) return cuda_fail(e, "down");
-    marks.mark();
-    e = launch_combine(L->y, L->d, L->rw, T, k, H, L->n_loc, L->has_shared ? 1 : 0, out, st);
-    if (e != cudaSuccess) return cuda_fail(e, "combine");
-  }
-  marks.mark();
+  if ((s = enqueue_experts(L, x, xdt, T, mt, L->has_shared, terms_done, small_path(L, T), out, st, marks,
+                            &launches)) != RMOE_OK)
+    return s;
   // the rank-order resolver joins back before the forward counts as done
   if (resolved) RMOE_CUDA(cudaStreamWaitEvent(st, L->ev_join, 0), "join wait");
   *ids_src = resolved ? L->ids_final : L->ids;
@@ -1199,6 +1214,50 @@ extern "C" rmoe_status rmoe_moe_forward(rmoe_layer* L, const void* x, int32_t x_
   if (!x || !out) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: null x/out");
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   return forward_into(L, x, x_dtype, T, out, ids_out, w_out, static_cast<cudaStream_t>(stream));
+}
+
+// out[t] = sum_j w[t][j] * expert_{ids[t][j]}(x[t]) (+ the gated shared expert), given routing:
+// the expert loop of glm52::moe::moe with its Routing (apply_single_expert, src/glm52/moe.rs:463-513).
+// Slots naming an expert that is not resident here (or -1) contribute nothing, so expert-parallel
+// ranks run it on the token rows they receive.
+extern "C" rmoe_status rmoe_moe_forward_routed(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T,
+                                               const int32_t* ids, const float* weights, int32_t with_shared,
+                                               float* out, void* stream) {
+  const char* what = "rmoe_moe_forward_routed";
+  if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
+  if (T < 0 || T > L->max_tokens)
+    return fail(RMOE_INVALID_ARG, "%s: T = %d outside [0, max_tokens = %d]", what, T, L->max_tokens);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  if (T == 0) return RMOE_OK;
+  if (!x || !ids || !weights || !out) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  rmoe_status s = check_uploaded(L);
+  if (s != RMOE_OK) return s;
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const rmoe_layer_desc& D = L->desc;
+  const int H = D.hidden, k = D.topk;
+  const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
+  const bool hs = with_shared && L->has_shared;
+  const bool gated = hs && D.shared_gated;
+  const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
+  const size_t n = static_cast<size_t>(T) * k;
+  RMOE_CUDA(cudaMemcpyAsync(L->ids, ids, n * 4, cudaMemcpyDefault, st), "routed ids");
+  RMOE_CUDA(cudaMemcpyAsync(L->rw, weights, n * 4, cudaMemcpyDefault, st), "routed weights");
+  cudaError_t e = launch_prep_tokens(x, xdt, T, H, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr, L->xq,
+                                     L->xexp, L->gate, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
+  if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs)) != RMOE_OK) return s;
+  StageMarks marks(L, st);
+  const bool prof = L->profiling;
+  L->profiling = false;  // (stage events cover rmoe_moe_forward only)
+  int launches = 0;
+  s = enqueue_experts(L, x, xdt, T, mt, hs, false, false, out, st, marks, &launches);
+  L->profiling = prof;
+  if (s != RMOE_OK) return s;
+  L->stats.kernel_launches += launches;
+  L->stats.forward_calls++;
+  L->stats.tokens_routed += T;
+  return RMOE_OK;
 }
 
 extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, int32_t x_dtype,

@@ -222,6 +222,18 @@ class MoeLayer:
                                         _ptr(ids), _ptr(w), _stream(stream)))
         return (out, ids, w) if return_routing else out
 
+    def forward_routed(self, x, ids, weights, with_shared=True, out=None, stream=None):
+        """The expert loop with given routing (apply_single_expert over a Routing,
+        src/glm52/moe.rs:463-513): out[t] = sum_j w[t][j] * expert_{ids[t][j]}(x[t]) (+ shared).
+        Slots with id -1 or a non-resident expert contribute nothing."""
+        _require_cuda(x, ids, weights)
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
+        check(self.lib.rmoe_moe_forward_routed(self.handle, _ptr(x), _dtype_code(x), T, _ptr(ids), _ptr(weights),
+                                               1 if with_shared else 0, _ptr(out), _stream(stream)))
+        return out
+
     def moe_forward_host(self, x, out=None):
         """Host buffers in and out (x: f32 or bf16 bits as uint16; pinned torch tensors work
         too): the signature rabbit's moe_forward call sites have."""
