@@ -14,8 +14,9 @@ reference path restated in C (AVX-512 tier, oracle/) timed on this host's cores.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rmoe|reference]
 
 With N > 1 (torchrun, one process per GPU) every rank runs its own replica of the layer on its
-own tokens (weak scaling; the expert-parallel path is separate): value = max-over-ranks time /
-all tokens processed.
+own tokens (weak scaling): value = max-over-ranks time / all tokens processed. The line's "ep"
+object is config 3 at the same N: a 4-layer stack, 4096 tokens per step, experts sharded 512 / N
+per GPU with NCCL all-to-all dispatch and combine (strong scaling: total work fixed).
 """
 from __future__ import annotations
 
@@ -215,6 +216,95 @@ def expert_touch_bytes(cfg, ids_np, with_shared=True):
     return total, gu, distinct
 
 
+EP_CFG = "c3_qwen_ep"
+
+
+def run_ep(args, ctx, dev, rank, world, flush):
+    """Config 3: a stack of 4 MoE layers, 4096 tokens per step over the whole job, experts sharded
+    512 / N per GPU (expert e on rank e // (512 / N)), tokens split 4096 / N per GPU, NCCL
+    all-to-all dispatch and combine (rabbit_b200.ep). Layer l + 1 reads layer l's output (bf16).
+    Returns the sub-object of the JSON line (value = tokens/s over the job, max-over-ranks time)."""
+    import torch
+    import torch.distributed as dist
+
+    from rabbit_b200.ep import ExpertParallelMoe
+    from rabbit_b200.synth import build_layer, x_device
+
+    cfg = synth.CONFIGS[EP_CFG]
+    t_local = cfg.tokens // world
+    t_build = time.perf_counter()
+    layers = [build_layer(ctx, cfg, max_tokens=cfg.tokens, layer=l, ep_rank=rank, ep_size=world)
+              for l in range(cfg.n_layers)]
+    build_s = time.perf_counter() - t_build
+    eps = [ExpertParallelMoe(L) for L in layers]
+    x0 = x_device(cfg, synth.activations(cfg, tokens=t_local, token_offset=rank * t_local))
+    stream = torch.cuda.current_stream()
+
+    def step():
+        x, ids_l = x0, []
+        for ep in eps:
+            out, ids, _ = ep.forward(x)
+            ids_l.append(ids)
+            x = out.to(torch.bfloat16)
+        return x, ids_l
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = []
+    xbytes = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for _ in range(args.ep_steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        _, ids_l = step()
+        b.record(stream)
+        ev.append((a, b))
+        xbytes.append(sum(ep.last_exchange_bytes for ep in eps))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.ep_steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # algorithmic bytes on this rank: its distinct touched experts per layer (+ shared, router, x, out)
+    per = cfg.n_experts // world
+    lo, hi = rank * per, (rank + 1) * per
+    rbytes = 0.0
+    for ids in ids_l:
+        if world > 1:
+            g = torch.empty((world,) + tuple(ids.shape), dtype=ids.dtype, device=dev)
+            dist.all_gather_into_tensor(g, ids.contiguous())
+            ids = g.reshape(-1, cfg.topk)
+        a = ids.cpu().numpy()
+        distinct = len(np.unique(a[(a >= lo) & (a < hi)]))
+        rbytes += (distinct + 1) * cfg.expert_bytes() + cfg.n_experts * cfg.hidden * 2 + \
+            t_local * cfg.hidden * (2 + 4)
+    rb_t = torch.tensor([rbytes, float(np.mean(xbytes))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(rb_t, op=dist.ReduceOp.MAX)
+    max_bytes, max_x = (float(v) for v in rb_t.tolist())
+    hbm_peak, _, peak_kind = peaks()
+    res = {"metric": "moe_ep_stack_tokens_per_s", "value": cfg.tokens / (ms / 1e3), "unit": "tokens/s",
+           "ms_per_step": ms, "steps": args.ep_steps, "warmup": args.warmup,
+           "config": {"workload": EP_CFG, "layers": cfg.n_layers, "tokens_per_step": cfg.tokens,
+                      "tokens_per_gpu": t_local, "experts_per_gpu": per,
+                      "parallelism": f"ep{world}" if world > 1 else "single gpu (all experts local)",
+                      "l2": "inputs larger than L2 (GBs of expert weights per step) and flushed between steps"},
+           "max_rank_algorithmic_bytes": max_bytes,
+           "achieved_gbs_per_gpu": max_bytes / (ms / 1e3) / 1e9,
+           "hbm_frac_per_gpu": max_bytes / (ms / 1e3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
+           "remote_bytes_per_gpu_per_step": max_x, "build_s": build_s}
+    for L in layers:
+        L.close()
+    return res
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -402,6 +492,11 @@ def run_gpu(args):
         "clocks": clk,
         "prefill": pre,
     }
+    if not args.no_ep:
+        layer.close()
+        layer = None
+        torch.cuda.empty_cache()
+        line["ep"] = run_ep(args, ctx, dev, rank, world, flush)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, n, used = cpu_decode_time(dcfg, budget_s=args.cpu_budget, threads=physical_cores())
         line["cpu_baseline"] = {
@@ -411,7 +506,8 @@ def run_gpu(args):
                       "C restatement of rabbit's AVX-512 MXFP4 tier + f32 router, OpenMP over rows"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    layer.close()
+    if layer is not None:
+        layer.close()
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
@@ -426,6 +522,8 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=3)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel stack (config 3)")
+    ap.add_argument("--ep-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--small-experts", type=int, default=0,
                     help="profiling only: resident experts (same shapes); not a bench config")

@@ -5,14 +5,16 @@ expert replicated.
 One forward on every rank:
 
 1. route the rank's own tokens with the replicated router (bit-exact, same kernel as one GPU);
-2. exchange counts, then token rows and their (expert, weight) slots with ``all_to_all_single``
-   (variable splits), each slot sent to the rank owning its expert;
+2. exchange counts, then token rows with ``all_to_all_single`` (variable splits): a token goes
+   once to every rank owning at least one of its k experts, with its [k] ids and weights (slots
+   of other ranks set to -1 / 0);
 3. run the received rows through the local experts with the routing weights folded in
-   (``forward_routed``: rabbit's ``apply_single_expert`` loop, src/glm52/moe.rs:463-513);
-4. send the weighted expert outputs back the same way;
-5. on the token's owner: ``out[t] = ((y_0 + y_1) + ... + y_{k-1}) + shared(x_t)`` in routing rank
-   order with the gated shared expert last (qwen38/generate.rs:324-349), a fixed order on every
-   world size.
+   (``forward_routed``: rabbit's ``apply_single_expert`` loop, src/glm52/moe.rs:463-513), which
+   sums each row's local slots in slot order;
+4. send those per-(token, rank) partial sums back the same way;
+5. on the token's owner: ``out[t] = ((p_0 + p_1) + ... + p_{N-1}) + shared(x_t)`` over the ranks in
+   order, the gated shared expert last (qwen38/generate.rs:324-349). The order is fixed for a
+   world size; against one GPU the slot sums are only regrouped (f32 rounding).
 
 There is no all-reduce: the only collectives are the two data exchanges (and the counts), which
 the reference has no counterpart for (it runs on one host). The compute side is any object with
@@ -29,8 +31,10 @@ class ExpertParallelMoe:
     def __init__(self, layer, group=None, max_rows=None):
         self.layer = layer
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        solo = group is None and not dist.is_initialized()
+        self.world = 1 if solo else dist.get_world_size(group)
+        self.rank = 0 if solo else dist.get_rank(group)
+        self.last_exchange_bytes = 0  # bytes this rank sent in the last forward (both exchanges)
         if layer.n_experts % self.world:
             raise ValueError(f"{layer.n_experts} experts do not split over {self.world} ranks")
         self.per_rank = layer.n_experts // self.world
@@ -45,46 +49,42 @@ class ExpertParallelMoe:
         return out
 
     def forward(self, x):
-        """x [T_local, H] on this rank's device -> out [T_local, H] f32."""
+        """x [T_local, H] on this rank's device -> (out [T_local, H] f32, ids, weights)."""
         lay = self.layer
-        T, k, H = x.shape[0], lay.topk, lay.hidden
+        T, k, H, N = x.shape[0], lay.topk, lay.hidden, self.world
         dev = x.device
         ids, w = lay.route(x)                                   # [T, k] rank order, bit-exact
-        flat_ids = ids.reshape(-1).long()
-        valid = flat_ids >= 0
-        dest = torch.where(valid, flat_ids // self.per_rank, torch.full_like(flat_ids, self.world))
-        order = torch.argsort(dest * (T * k) + torch.arange(T * k, device=dev), stable=True)
-        order = order[: int(valid.sum())]                       # slots grouped by rank, (t, j) inside
-        send_counts = torch.bincount(dest[order], minlength=self.world)[: self.world]
+        if N == 1:  # every expert local: the one-device layer
+            return lay.forward_routed(x, ids, w, with_shared=True), ids, w
+        dest = torch.where(ids >= 0, ids.long() // self.per_rank, torch.full_like(ids, -1, dtype=torch.long))
+        # one row per (destination rank, token) that has a slot there, rank-major, token order
+        hit = (dest.unsqueeze(2) == torch.arange(N, device=dev)).any(dim=1)      # [T, N]
+        r_idx, t_idx = hit.t().nonzero(as_tuple=True)
+        send_counts = torch.bincount(r_idx, minlength=N)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         sc, rc = send_counts.tolist(), recv_counts.tolist()
-        tok = order // k
-        send_x = x[tok]
-        send_meta = torch.stack([flat_ids[order].to(torch.float32), w.reshape(-1)[order]], dim=1)
-        recv_x = self._exchange(send_x, sc, rc)
-        recv_meta = self._exchange(send_meta, sc, rc)
-        # the local experts: one slot per received row (the other k-1 slots empty)
+        mine = dest[t_idx] == r_idx.unsqueeze(1)                                  # slots on that rank
+        send_ids = torch.where(mine, ids[t_idx], torch.full_like(ids[t_idx], -1))
+        send_w = torch.where(mine, w[t_idx], torch.zeros_like(w[t_idx]))
+        recv_x = self._exchange(x[t_idx], sc, rc)
+        recv_ids = self._exchange(send_ids, sc, rc)
+        recv_w = self._exchange(send_w, sc, rc)
+        # the local experts over every received row (up to k slots each, weights folded in)
         R = recv_x.shape[0]
         y = torch.empty((R, H), dtype=torch.float32, device=dev)
-        if R:
-            rid = torch.full((R, k), -1, dtype=torch.int32, device=dev)
-            rw = torch.zeros((R, k), dtype=torch.float32, device=dev)
-            rid[:, 0] = recv_meta[:, 0].round().to(torch.int32)
-            rw[:, 0] = recv_meta[:, 1]
-            step = self.max_rows or R
-            for r0 in range(0, R, step):
-                r1 = min(R, r0 + step)
-                y[r0:r1] = lay.forward_routed(recv_x[r0:r1], rid[r0:r1].contiguous(), rw[r0:r1].contiguous(),
-                                              with_shared=False)
-        back = self._exchange(y, rc, sc)                        # rows in send order
-        ys = torch.zeros((T * k, H), dtype=torch.float32, device=dev)
-        ys[order] = back
-        ys = ys.reshape(T, k, H)
-        none_ids = torch.full((T, k), -1, dtype=torch.int32, device=dev)
-        shared = lay.forward_routed(x, none_ids, torch.zeros((T, k), dtype=torch.float32, device=dev),
-                                    with_shared=True)
-        out = ys[:, 0].clone()
-        for j in range(1, k):
-            out = out + ys[:, j]
+        step = self.max_rows or max(R, 1)
+        for r0 in range(0, R, step):
+            r1 = min(R, r0 + step)
+            lay.forward_routed(recv_x[r0:r1], recv_ids[r0:r1], recv_w[r0:r1], with_shared=False, out=y[r0:r1])
+        back = self._exchange(y, rc, sc)                        # partial sums, in send order
+        self.last_exchange_bytes = (t_idx.numel() * (H * x.element_size() + k * 8)
+                                    + R * H * 4) - (sc[self.rank] * (H * x.element_size() + k * 8)
+                                                    + rc[self.rank] * H * 4)
+        parts = torch.zeros((N, T, H), dtype=torch.float32, device=dev)
+        parts[r_idx, t_idx] = back
+        shared = lay.forward_routed(x, torch.full_like(ids, -1), torch.zeros_like(w), with_shared=True)
+        out = parts[0].clone()
+        for r in range(1, N):
+            out += parts[r]
         return out + shared, ids, w

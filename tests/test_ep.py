@@ -52,7 +52,8 @@ class OracleLayer:
             w[t] = [v for _, v in r]
         return torch.from_numpy(ids), torch.from_numpy(w)
 
-    def forward_routed(self, x, ids, w, with_shared=True):
+    def forward_routed(self, x, ids, w, with_shared=True, out=None):
+        dst = out
         xn = x.numpy().astype(np.float32)
         out = np.zeros((xn.shape[0], self.hidden), np.float32)
         for t in range(xn.shape[0]):
@@ -63,6 +64,9 @@ class OracleLayer:
             if with_shared and self.cfg.shared_inter:
                 gate = np.float32(1.0 / (1.0 + np.exp(-np.float32(np.dot(xn[t], self.gvec)))))
                 out[t] += gate * self._ffn(xn[t:t + 1], self.shared, self.cfg.shared_inter)[0]
+        if dst is not None:
+            dst.copy_(torch.from_numpy(out))
+            return dst
         return torch.from_numpy(out)
 
 
