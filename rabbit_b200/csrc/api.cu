@@ -849,6 +849,10 @@ static rmoe_status print_tc_trace(rmoe_layer* L, cudaStream_t st, const char* wh
         fprintf(stderr, "  epi part %2d (tile*16+unit %4llu): wait from %7.2f got %7.2f done %7.2f us\n", i, tr[3072 + i * 4 + 3],
                 (double)(long long)(tr[3072 + i * 4] - t0) * 1e-3, (double)(long long)(tr[3072 + i * 4 + 1] - t0) * 1e-3,
                 (double)(long long)(tr[3072 + i * 4 + 2] - t0) * 1e-3);
+      for (int i = 0; i < 32 && tr[3584 + i * 4]; i++)
+        fprintf(stderr, "  epi(q0) %2d: got %7.2f ld %7.2f ubuf %7.2f done %7.2f us\n", i,
+                (double)(long long)(tr[3584 + i * 4] - t0) * 1e-3, (double)(long long)(tr[3584 + i * 4 + 1] - t0) * 1e-3,
+                (double)(long long)(tr[3584 + i * 4 + 2] - t0) * 1e-3, (double)(long long)(tr[3584 + i * 4 + 3] - t0) * 1e-3);
       for (int i = 0; i < 64 && tr[i * 4]; i++)
         fprintf(stderr, "  mma %2d cycles: sfa wait %5llu sfb wait %5llu mma issue %5llu commit %5llu\n", i, tr[2048 + i * 4],
                 tr[2048 + i * 4 + 1], tr[2048 + i * 4 + 2], tr[2048 + i * 4 + 3]);
@@ -902,8 +906,13 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       launches = terms_done ? 4 : (fused_ok ? 6 : 9);  // front (+ order resolve), gate/up, down
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
-                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr, nullptr, L->partial);
+                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr,
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
+      if (L->tc_trace) {
+        if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
+        if ((s = print_tc_trace(L, st, "down", 4096)) != RMOE_OK) return s;
+      }
       marks.mark();
       e = launch_combine(L->y, L->d, nullptr, T, k, H, L->n_loc, hs ? 1 : 0, out, st);
       if (e != cudaSuccess) return cuda_fail(e, "combine");

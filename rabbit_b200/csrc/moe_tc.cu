@@ -570,12 +570,14 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       const int n = r.n;
       const int nb = (4 * n + 7) / 8;
       float v[32];
+      const bool tr2 = MODE == kModeGateUp && a.trace && blockIdx.x == 0 && et == 64 && seen < 128;
+      if (tr2) a.trace[3584 + seen * 4 + 0] = global_ns();
       const uint32_t dacc = tbase + buf * acc_cols;
-      for (int c0 = 0; c0 < 8 * nb; c0 += 8) {
-        float rr[8];
-        tmem_ld8(dacc + lane_addr + c0, rr);
-        v[c0 / 4] = ((rr[0] + rr[1]) + rr[2]) + rr[3];
-        v[c0 / 4 + 1] = ((rr[4] + rr[5]) + rr[6]) + rr[7];
+      for (int c0 = 0; c0 < 8 * nb; c0 += 32) {  // (columns past 8 * nb are read, never used)
+        float rr[32];
+        tmem_ld32(dacc + lane_addr + c0, rr);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[c0 / 4 + i] = ((rr[4 * i] + rr[4 * i + 1]) + rr[4 * i + 2]) + rr[4 * i + 3];
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
@@ -593,26 +595,33 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       // ---- finalize
       if (MODE == kModeGateUp) {
         // rows 0..63 gate, 64..127 up (inter rows mm*64 ..): the tile goes through shared memory
-        // as [row][position]; thread (position t, 32-row block hb) then forms h = silu(g) u w
-        // for its 32 inter rows and expands them into the four-term operand on its own
+        // as [row][position]; then four threads per (position t, 32-row block hb), 8 inter rows
+        // each, form h = silu(g) u w and expand it into the four-term operand together
+        if (tr2) a.trace[3584 + (seen - 1) * 4 + 1] = global_ns();
         asm volatile("bar.sync 1, 128;" ::: "memory");
         for (int t = 0; t < n; t++) ubuf[row * 33 + t] = v[t];
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (et < 2 * n) {
-          const int t = et >> 1, hb = et & 1;
+        if (tr2) a.trace[3584 + (seen - 1) * 4 + 2] = global_ns();
+        for (int item0 = 32 * q; item0 < 8 * n; item0 += 128) {  // warp-uniform trip count
+          const int item = item0 + lane;
+          const bool valid = item < 8 * n;  // whole quads: 8 n is a multiple of 4
+          const int jb = item >> 2, s4 = item & 3;
+          const int hb = valid ? jb / n : 0, t = valid ? jb - hb * n : 0;
           const int p = p0 + t;
-          const float wp = __ldg(a.perm_w + p);
-          float h[32];
+          const float wp = valid ? __ldg(a.perm_w + p) : 0.0f;
+          float h[8];
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const float g = ubuf[(hb * 32 + i) * 33 + t], u = ubuf[(64 + hb * 32 + i) * 33 + t];
-            h[i] = __fmul_rn(silu_ref(g), u) * wp;
+          for (int i = 0; i < 8; i++) {
+            const int rr = hb * 32 + 8 * s4 + i;
+            const float g = ubuf[rr * 33 + t], u = ubuf[(64 + rr) * 33 + t];
+            h[i] = valid ? __fmul_rn(silu_ref(g), u) * wp : 0.0f;
           }
           const int i0 = mm * 64 + hb * 32;
           const size_t trow = static_cast<size_t>(4 * p);
-          thread_terms4(h, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2,
-                        a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32);
+          quad_terms4(h, a.ht + trow * (a.inter / 2) + i0 / 2 + 4 * s4, a.inter / 2,
+                      a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32, s4 == 0, valid);
         }
+        if (tr2) a.trace[3584 + (seen - 1) * 4 + 3] = global_ns();
       } else if (MODE == kModeDown) {
         const int orow = mm * 128 + row;
         for (int t = 0; t < n; t++) a.y[static_cast<size_t>(p0 + t) * a.hidden + orow] = v[t];

@@ -11,17 +11,29 @@
 
 namespace rmoe {
 
+// Branch-free (lanes of a warp take different codes): code = number of rounding boundaries at or
+// below v, i.e. ties round up.
 __device__ __forceinline__ int e2m1_nearest(float v) {  // 0 <= v <= 6
-  return v < 0.25f ? 0 : v < 0.75f ? 1 : v < 1.25f ? 2 : v < 1.75f ? 3 : v < 2.5f ? 4 : v < 3.5f ? 5 : v < 5.0f ? 6 : 7;
+  return (v >= 0.25f) + (v >= 0.75f) + (v >= 1.25f) + (v >= 1.75f) + (v >= 2.5f) + (v >= 3.5f) + (v >= 5.0f);
 }
+// |value| of code c: 0, .5, 1, 1.5, 2, 3, 4, 6 (c >= 2: 2^((c >> 1) - 1) * (1 + (c & 1) / 2)).
 __device__ __forceinline__ float e2m1_magnitude(int c) {
-  return c < 4 ? 0.5f * c : static_cast<float>(2 << ((c - 4) >> 1)) * (1.0f + 0.5f * (c & 1));
+  const uint32_t hi = (static_cast<uint32_t>((c >> 1) + 126) << 23) | (static_cast<uint32_t>(c & 1) << 22);
+  return __uint_as_float(c >= 2 ? hi : (c ? 0x3F000000u : 0u));
 }
 
-// Smallest e with amax <= 6 * 2^e (amax > 0), clamped to the normal range.
+// Smallest e with amax <= 6 * 2^e (amax > 0), clamped to the normal range. For a normal amax =
+// 2^e0 * (1 + f): amax <= 6 * 2^(e0 - 2) = 1.5 * 2^e0 iff f <= 1/2.
 __device__ __forceinline__ int e2m1_block_exponent(float amax) {
-  const int e0 = ilogbf(amax);  // amax in [2^e0, 2^(e0+1))
-  const int e = amax <= 6.0f * exp2i(max(e0 - 2, -149)) ? e0 - 2 : e0 - 1;
+  const uint32_t b = __float_as_uint(amax);
+  int e;
+  if (b >= 0x00800000u) {
+    const int e0 = static_cast<int>(b >> 23) - 127;
+    e = (b & 0x7FFFFFu) <= 0x400000u ? e0 - 2 : e0 - 1;
+  } else {  // subnormal
+    const int e0 = ilogbf(amax);
+    e = amax <= 6.0f * exp2i(max(e0 - 2, -149)) ? e0 - 2 : e0 - 1;
+  }
   return max(-126, min(127, e));
 }
 
@@ -79,6 +91,41 @@ __device__ __forceinline__ void thread_terms4(float (&r)[32], uint8_t* rows, siz
     }
     *reinterpret_cast<uint4*>(rows + j * pitch) = make_uint4(w[0], w[1], w[2], w[3]);
     sf[j * sf_pitch] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+  }
+}
+
+// Four lanes, one 32-block: lane s (= lane % 4 within its aligned quad) holds elements
+// 8s .. 8s + 7. The same expansion as warp_terms4 (amax over the quad by two shuffles); each lane
+// writes its own 32-bit word of term j's 16 bytes to rows + j * pitch (rows already offset by 4s)
+// and the quad's lane 0 the scale byte. All 32 lanes of the warp must call (quads independent);
+// `store` gates the memory writes only.
+__device__ __forceinline__ void quad_terms4(float (&r)[8], uint8_t* rows, size_t pitch, uint8_t* sf,
+                                            size_t sf_pitch, bool lead, bool store) {
+#pragma unroll 1
+  for (int j = 0; j < 4; j++) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(r[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+    uint32_t w = 0;
+    int e = 0;
+    if (amax > 0.0f) {
+      e = e2m1_block_exponent(amax);
+      const float inv = exp2i(-e), sc = exp2i(e);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const bool neg = r[i] < 0.0f;
+        const int c = e2m1_nearest(fminf(fabsf(r[i]) * inv, 6.0f));
+        const float q = e2m1_magnitude(c) * sc;
+        r[i] = neg ? r[i] + q : r[i] - q;
+        w |= (static_cast<uint32_t>(c) | (neg && c ? 8u : 0u)) << (4 * i);
+      }
+    }
+    if (store) {
+      *reinterpret_cast<uint32_t*>(rows + j * pitch) = w;
+      if (lead) sf[j * sf_pitch] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+    }
   }
 }
 
