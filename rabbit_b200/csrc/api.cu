@@ -156,7 +156,7 @@ struct rmoe_layer {
   float* partial2 = nullptr;     // down unit parts of split tiles
   int32_t* tile_cnt = nullptr;   // [max tiles]
   unsigned* front_counter = nullptr;  // one-token front end: finished blocks
-  int* tc_work = nullptr;        // [2] claimed units / finished CTAs of the running expert kernel
+  int* tc_work = nullptr;        // [8] work counters: [0..3] gate/up, [4..7] down (they may overlap)
   size_t tc_off_down = 0;        // tile-major down region inside an expert slot
   uint8_t* tc_stage = nullptr;   // one expert in the reference layout, before retiling
   unsigned long long* tc_trace = nullptr;  // RMOE_TC_TRACE=1: gate/up stage timestamps of CTA 0
@@ -446,7 +446,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     ALLOC(L->hsf, rows * (I / 32));
     ALLOC(L->partial, moe_tc_partial_floats(static_cast<int>(H), static_cast<int>(I), k, n_slots));
     ALLOC(L->partial2, moe_tc_partial_floats(static_cast<int>(H), static_cast<int>(I), k, n_slots));
-    ALLOC(L->tc_work, 4);
+    ALLOC(L->tc_work, 8);
     const size_t max_tiles = static_cast<size_t>(max_chunks) * std::max(I / 64, H / 128);
     ALLOC(L->tile_cnt, max_tiles);
     ALLOC(L->front_counter, 1);
@@ -458,7 +458,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     }
     cudaError_t e = cudaMemset(L->tile_cnt, 0, max_tiles * 4);
     if (e == cudaSuccess) e = cudaMemset(L->front_counter, 0, 4);
-    if (e == cudaSuccess) e = cudaMemset(L->tc_work, 0, 16);
+    if (e == cudaSuccess) e = cudaMemset(L->tc_work, 0, 32);
     if (e == cudaSuccess) e = cudaMemset(L->xt, 0, rows * (H / 2));
     if (e == cudaSuccess) e = cudaMemset(L->xsf, 127, rows * (H / 32));
     if (e == cudaSuccess) e = cudaMemset(L->ht, 0, rows * (I / 2));
@@ -849,13 +849,21 @@ static rmoe_status print_tc_trace(rmoe_layer* L, cudaStream_t st, const char* wh
         fprintf(stderr, "  epi part %2d (tile*16+unit %4llu): wait from %7.2f got %7.2f done %7.2f us\n", i, tr[3072 + i * 4 + 3],
                 (double)(long long)(tr[3072 + i * 4] - t0) * 1e-3, (double)(long long)(tr[3072 + i * 4 + 1] - t0) * 1e-3,
                 (double)(long long)(tr[3072 + i * 4 + 2] - t0) * 1e-3);
+      if (off == 0 && tr[4000])
+        fprintf(stderr, "  front: block0 start 0, router blocks done %.2f, terms blocks done %.2f, last block: "
+                "enter %.2f select %.2f certificate %.2f end %.2f us (GU t0 %.2f)\n",
+                (double)(long long)(tr[4001] - tr[4000]) * 1e-3, (double)(long long)(tr[4002] - tr[4000]) * 1e-3,
+                (double)(long long)(tr[4003] - tr[4000]) * 1e-3, (double)(long long)(tr[4004] - tr[4000]) * 1e-3,
+                (double)(long long)(tr[4005] - tr[4000]) * 1e-3, (double)(long long)(tr[4006] - tr[4000]) * 1e-3,
+                (double)(long long)(t0 - tr[4000]) * 1e-3);
       for (int i = 0; i < 32 && tr[3584 + i * 4]; i++)
         fprintf(stderr, "  epi(q0) %2d: got %7.2f ld %7.2f ubuf %7.2f done %7.2f us\n", i,
                 (double)(long long)(tr[3584 + i * 4] - t0) * 1e-3, (double)(long long)(tr[3584 + i * 4 + 1] - t0) * 1e-3,
                 (double)(long long)(tr[3584 + i * 4 + 2] - t0) * 1e-3, (double)(long long)(tr[3584 + i * 4 + 3] - t0) * 1e-3);
       for (int i = 0; i < 64 && tr[i * 4]; i++)
-        fprintf(stderr, "  mma %2d cycles: sfa wait %5llu sfb wait %5llu mma issue %5llu commit %5llu\n", i, tr[2048 + i * 4],
-                tr[2048 + i * 4 + 1], tr[2048 + i * 4 + 2], tr[2048 + i * 4 + 3]);
+        fprintf(stderr, "  mma %2d: A-sf cp issued %7.2f  sfa ok %7.2f  sfb ok %7.2f  mmas issued %7.2f us\n", i,
+                (double)(long long)(tr[2048 + i * 4 + 3] - t0) * 1e-3, (double)(long long)(tr[2048 + i * 4] - t0) * 1e-3,
+                (double)(long long)(tr[2048 + i * 4 + 1] - t0) * 1e-3, (double)(long long)(tr[2048 + i * 4 + 2] - t0) * 1e-3);
       for (int i = 0; i < 64 && tr[i * 4]; i++)
         fprintf(stderr, "stage %2d issue %7.2f full %7.2f sf %7.2f mma %7.2f us\n", i, (tr[i * 4] - t0) * 1e-3,
                 (tr[i * 4 + 1] - t0) * 1e-3, (tr[i * 4 + 2] - t0) * 1e-3, (tr[i * 4 + 3] - t0) * 1e-3);
@@ -895,7 +903,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     marks.mark();  // (h is quantized inside the gate/up epilogue)
     if (T == 1) {
       e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
-                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr,
+                        L->partial2, L->tile_cnt, L->tc_work + 4, L->dev_err, st, nullptr,
                         L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace) {
@@ -906,7 +914,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       launches = terms_done ? 4 : (fused_ok ? 6 : 9);  // front (+ order resolve), gate/up, down
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
-                        L->partial2, L->tile_cnt, L->tc_work, L->dev_err, st, nullptr,
+                        L->partial2, L->tile_cnt, L->tc_work + 4, L->dev_err, st, nullptr,
                         L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace) {
@@ -1017,6 +1025,8 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
       f.fallback_count = L->fallbacks; f.order_pending_count = L->order_pending;
       f.counter = L->front_counter;
       f.d = L->d;
+      f.trace = L->tc_trace ? L->tc_trace + 4000 : nullptr;
+      if (f.trace) RMOE_CUDA(cudaMemsetAsync(f.trace, 0, 8 * 8, st), "front trace reset");
       e = launch_decode_front(f, st);
       if (e != cudaSuccess) return cuda_fail(e, "one-token front end");
       terms_done = true;

@@ -111,6 +111,8 @@ struct DecodeFront {
   unsigned* order_pending_count;
   unsigned* counter;              // finished blocks (zero between launches)
   DispatchBuffers d;
+  unsigned long long* trace;      // optional diagnostics: [0] block 0 start, [1] last router
+                                  // block end, [2] last terms block end, [3..6] last block phases
 };
 cudaError_t launch_decode_front(const DecodeFront& a, cudaStream_t st);
 

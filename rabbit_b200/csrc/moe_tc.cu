@@ -208,14 +208,6 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (a.trace && threadIdx.x == 0) a.trace[1024 + 4 * blockIdx.x] = global_ns();
-  const int nch = *a.n_chunks;
-  const int kst = a.K / kMtKStage;
-  const int ntm = MODE == kModeGateUp ? a.out_rows / 64 : a.out_rows / 128;
-  const int L = MODE == kModeDownOne ? max(1, nch * kst) : kst;
-  const int U = a.unit_stages < L && L % a.unit_stages == 0 ? a.unit_stages : L;
-  const int upt = L / U;  // units per tile
-  const int ntiles = MODE == kModeDownOne ? ntm : nch * ntm;
-  const int total_units = ntiles * upt;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
@@ -241,6 +233,22 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  // Launched with programmatic stream serialization this kernel may start while the previous
+  // one (gate/up: the front end or the activation terms; down: gate/up) still runs. Gate/up
+  // reads that kernel's routing and terms from the start and waits here; the down kernels read
+  // only data of the kernel before gate/up (routing, dispatch: complete once gate/up passed its
+  // own wait) until the h operand, which the roles needing it wait for below; their weight
+  // stream starts at once.
+  if (MODE == kModeGateUp) griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  const int nch = *a.n_chunks;
+  const int kst = a.K / kMtKStage;
+  const int ntm = MODE == kModeGateUp ? a.out_rows / 64 : a.out_rows / 128;
+  const int L = MODE == kModeDownOne ? max(1, nch * kst) : kst;
+  const int U = a.unit_stages < L && L % a.unit_stages == 0 ? a.unit_stages : L;
+  const int upt = L / U;  // units per tile
+  const int ntiles = MODE == kModeDownOne ? ntm : nch * ntm;
+  const int total_units = ntiles * upt;
   // accumulators: N <= 8 * b_boxes columns each; four when they fit in 256 columns
   const int acc_cols = ((8 * a.b_boxes + 31) / 32) * 32;
   const int nacc = acc_cols <= 64 ? 4 : 2;
@@ -327,6 +335,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   } else if (warp == 10) {
     // ------------------------------------------------------------------ activation producer
     if (lane == 0) {
+      if (MODE != kModeGateUp) griddep_wait();  // h (written by gate/up)
       tma_prefetch_desc(&maps.b);
       tma_prefetch_desc(&maps.bs);
       int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
@@ -518,6 +527,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     const int et = threadIdx.x - 192;   // 0..127 within the epilogue warps
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
     const int row = 32 * q + lane;      // accumulator row (A-tile row)
+    if (MODE != kModeGateUp) griddep_wait();  // gate/up parts (and h) complete
     if (MODE != kModeGateUp && a.gu_split) {
       // h of every position from the gate/up unit parts: one warp per (gate/up tile, 32 inter
       // rows), parts added in K order, h = silu(g) u w, written as the four-term operand
@@ -885,11 +895,15 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   cfg.blockDim = dim3(kMtThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = coop ? 1 : 0;
+  // programmatic dependent launch: set-up (TMEM, barriers, tensor maps) and, for the down
+  // kernels, the first weight stages overlap the previous kernel's tail
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, maps, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -72,4 +72,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Programmatic dependent launch (a kernel launched with programmatic stream serialization may
+// start while the previous kernel in the stream still runs): wait until that kernel completed
+// and its writes are visible / let the next kernel launch early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace rmoe

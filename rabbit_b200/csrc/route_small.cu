@@ -301,45 +301,70 @@ __device__ __noinline__ float exact_logit(const void* x, int x_dtype, const void
 // ahead of it. Writes rank-ordered ids/values to out_id/out_v[0..kk). Two independent lists are
 // ranked at once (`v2`/`out2_*`), sharing the barriers. Contains __syncthreads: call from all
 // threads.
+// Order-preserving 32-bit key of a float (larger value -> larger key; -0 and +0 equal, as the
+// float comparison in ahead() treats them).
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v + 0.0f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// One selection round over a warp: the lane entry ahead of all others (largest key, then
+// smallest id) among those not yet taken. Returns its id; *val gets its value.
+__device__ __forceinline__ int warp_pick(uint32_t key, int id, float v, bool taken, float* val) {
+  const uint32_t m = __reduce_max_sync(kFull, taken ? 0u : key);
+  const int w = __reduce_min_sync(kFull, (!taken && key == m) ? id : 0x7fffffff);
+  const unsigned who = __ballot_sync(kFull, !taken && key == m && id == w);
+  *val = __shfl_sync(kFull, v, __ffs(who) - 1);
+  return w;
+}
+
+// Top-kk of (v, id) and of (v2, id) over the block (one entry per thread, ids distinct), each
+// by (value desc, id asc) -- the order ahead() defines -- into out_id/out_v and out2_id/out2_v.
+// Every warp first selects its own top-kk of both lists (kk rounds of warp reductions); then
+// warp 0 merges the warps' sorted lists of the first and warp 1 those of the second (one list
+// head per lane, kk rounds). cand/cand_i/cand2/cand2_i: nw * kk scratch entries each.
 __device__ void block_select2(float v, float v2, int id, int kk, float* cand, int* cand_i,
                               float* cand2, int* cand2_i, int* out_id, float* out_v,
                               int* out2_id, float* out2_v) {
   const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nw = blockDim.x / 32;
-  int r1 = 0, r2 = 0;
-#pragma unroll 8
-  for (int j = 0; j < 32; j++) {
-    const float ov = __shfl_sync(kFull, v, j), ov2 = __shfl_sync(kFull, v2, j);
-    const int oid = __shfl_sync(kFull, id, j);
-    r1 += ahead(ov, oid, v, id);
-    r2 += ahead(ov2, oid, v2, id);
-  }
-  if (r1 < kk) {
-    cand[wi * kk + r1] = v;
-    cand_i[wi * kk + r1] = id;
-  }
-  if (r2 < kk) {
-    cand2[wi * kk + r2] = v2;
-    cand2_i[wi * kk + r2] = id;
+  {
+    const uint32_t k1 = order_key(v), k2 = order_key(v2);
+    bool t1 = false, t2 = false;
+    for (int r = 0; r < kk; r++) {
+      float a1, a2;
+      const int w1 = warp_pick(k1, id, v, t1, &a1);
+      const int w2 = warp_pick(k2, id, v2, t2, &a2);
+      t1 = t1 || id == w1;
+      t2 = t2 || id == w2;
+      if (lane == 0) {
+        cand[wi * kk + r] = a1;
+        cand_i[wi * kk + r] = w1;
+        cand2[wi * kk + r] = a2;
+        cand2_i[wi * kk + r] = w2;
+      }
+    }
   }
   __syncthreads();
-  const int C = nw * kk;
-  for (int t = threadIdx.x; t < 2 * C; t += blockDim.x) {
-    const bool second = t >= C;
-    const float* cv = second ? cand2 : cand;
-    const int* ci = second ? cand2_i : cand_i;
-    const int q = second ? t - C : t;
-    const float mv = cv[q];
-    const int mid = ci[q];
-    int r = 0;
-    for (int j = 0; j < C; j++) r += ahead(cv[j], ci[j], mv, mid);
-    if (r < kk) {
-      if (second) {
-        out2_id[r] = mid;
-        out2_v[r] = mv;
-      } else {
-        out_id[r] = mid;
-        out_v[r] = mv;
+  if (wi < 2) {
+    const float* cv = wi == 0 ? cand : cand2;
+    const int* ci = wi == 0 ? cand_i : cand2_i;
+    int h = 0;  // head of list `lane` (lanes >= nw hold none)
+    for (int r = 0; r < kk; r++) {
+      const bool has = lane < nw && h < kk;
+      const float hv = has ? cv[lane * kk + h] : -INFINITY;
+      const int hid = has ? ci[lane * kk + h] : 0x7fffffff;
+      float val;
+      const int w = warp_pick(has ? order_key(hv) : 0u, hid, hv, !has, &val);
+      if (has && hid == w) h++;
+      if (lane == 0) {
+        if (wi == 0) {
+          out_id[r] = w;
+          out_v[r] = val;
+        } else {
+          out2_id[r] = w;
+          out2_v[r] = val;
+        }
       }
     }
   }
@@ -724,6 +749,9 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
   const int E = a.E, H = a.H;
   const int nrb = (E + 1) / 2;  // router blocks: experts 2b, 2b + 1
   const int b = blockIdx.x;
+  if (a.trace && b == 0 && threadIdx.x == 0) a.trace[0] = global_ns();
+  // the expert kernel that follows may launch now: it waits for this grid before reading
+  if (threadIdx.x == 0) griddep_launch_dependents();
   if (b < nrb) {
     const int c = H / 512;  // multiple of 8
     const size_t off = static_cast<size_t>(threadIdx.x) * c;
@@ -829,15 +857,17 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
     }
   }
   // ---- the last block to finish runs the front end
-  __threadfence();
+  if (a.trace && threadIdx.x == 0) atomicMax(a.trace + (b < nrb ? 1 : 2), global_ns());
+  // the block's writes (ordered before thread 0 by the barrier) are released by thread 0's
+  // counter increment; the last block's thread 0 acquires everyone's through the same atomic
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned old = atomicAdd(a.counter, 1u);
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counter) : "memory");
     s_last = old == gridDim.x - 1;
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   __shared__ float c1[16 * RMOE_MAX_TOPK_DEV], c2[16 * RMOE_MAX_TOPK_DEV];
   __shared__ int c1i[16 * RMOE_MAX_TOPK_DEV], c2i[16 * RMOE_MAX_TOPK_DEV];
   __shared__ int sel_id[RMOE_MAX_TOPK_DEV], lo_id[RMOE_MAX_TOPK_DEV];
@@ -863,7 +893,9 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
     s_lo[e] = lo;
     s_hi[e] = hi;
   }
+  if (a.trace && threadIdx.x == 0) a.trace[3] = global_ns();
   block_select2(v, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  if (a.trace && threadIdx.x == 0) a.trace[4] = global_ns();
   const float Lk = lo_v[kk - 1];
   const int n_cont = __syncthreads_count(valid && hi >= Lk);
   const int rr = threadIdx.x;
@@ -879,6 +911,7 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
     block_select2(ex, ex, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
     if (threadIdx.x == 0) atomicAdd(a.fallback_count, 1u);
   }
+  if (a.trace && threadIdx.x == 0) a.trace[5] = global_ns();
   if (wi == 0) {
     if (lane == 0) {
       const int pend = set_ok && !order_ok ? 1 : 0;
@@ -924,6 +957,7 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
       a.d.offsets[a.n_loc] = n_routed;
       a.d.offsets[a.n_loc + a.has_shared] = n_routed + a.has_shared;
       *a.counter = 0;
+      if (a.trace) a.trace[6] = global_ns();
     }
   }
 }
