@@ -156,10 +156,12 @@ struct rmoe_layer {
   float* partial2 = nullptr;     // down unit parts of split tiles
   int32_t* tile_cnt = nullptr;   // [max tiles]
   unsigned* front_counter = nullptr;  // one-token front end: finished blocks
+  size_t tile_cnt_half = 0;      // tile_cnt: [0, half) gate/up tiles, [half, 2 half) down tiles
   int* tc_work = nullptr;        // [8] work counters: [0..3] gate/up, [4..7] down (they may overlap)
   size_t tc_off_down = 0;        // tile-major down region inside an expert slot
   uint8_t* tc_stage = nullptr;   // one expert in the reference layout, before retiling
   unsigned long long* tc_trace = nullptr;  // RMOE_TC_TRACE=1: gate/up stage timestamps of CTA 0
+  bool tc_trace_print = true;              // RMOE_TC_TRACE=2: record only (summary on get_stats)
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
@@ -448,15 +450,17 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     ALLOC(L->partial2, moe_tc_partial_floats(static_cast<int>(H), static_cast<int>(I), k, n_slots));
     ALLOC(L->tc_work, 8);
     const size_t max_tiles = static_cast<size_t>(max_chunks) * std::max(I / 64, H / 128);
-    ALLOC(L->tile_cnt, max_tiles);
+    L->tile_cnt_half = max_tiles;
+    ALLOC(L->tile_cnt, 2 * max_tiles);
     ALLOC(L->front_counter, 1);
     if (const char* tr = getenv("RMOE_TC_TRACE")) {
-      if (tr[0] == '1') {
+      if (tr[0] == '1' || tr[0] == '2') {
+        L->tc_trace_print = tr[0] == '1';
         ALLOC(L->tc_trace, 8192);
         if (cudaMemset(L->tc_trace, 0, 8192 * 8) != cudaSuccess) return cleanup(fail(RMOE_CUDA_ERROR, "trace"));
       }
     }
-    cudaError_t e = cudaMemset(L->tile_cnt, 0, max_tiles * 4);
+    cudaError_t e = cudaMemset(L->tile_cnt, 0, 2 * max_tiles * 4);
     if (e == cudaSuccess) e = cudaMemset(L->front_counter, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(L->tc_work, 0, 32);
     if (e == cudaSuccess) e = cudaMemset(L->xt, 0, rows * (H / 2));
@@ -531,6 +535,34 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
   unsigned op = 0;
   RMOE_CUDA(cudaMemcpy(&op, L->order_pending, 4, cudaMemcpyDeviceToHost), "read order counter");
   out->router_order_resolved = op;
+  if (L->tc_trace && !L->tc_trace_print) {
+    // diagnostics: the last one-token forward's kernel timeline (global timer, µs from the
+    // front end's start)
+    static unsigned long long tr[8192];
+    RMOE_CUDA(cudaDeviceSynchronize(), "trace sync");
+    RMOE_CUDA(cudaMemcpy(tr, L->tc_trace, sizeof(tr), cudaMemcpyDeviceToHost), "trace read");
+    const unsigned long long f0 = tr[4000];
+    auto rel = [&](unsigned long long t) { return t ? (double)(long long)(t - f0) * 1e-3 : -1.0; };
+    fprintf(stderr, "timeline: front end %.2f (router %.2f, last block %.2f..)", rel(tr[4006]), rel(tr[4001]), rel(tr[4003]));
+    for (int k = 0; k < 2; k++) {
+      const unsigned long long* b = tr + 4096 * k;
+      unsigned long long e0 = ~0ull, e1 = 0, x0 = ~0ull, x1 = 0, s1 = 0;
+      for (int c = 0; c < 148 && b[1024 + 4 * c]; c++) {
+        e0 = std::min(e0, b[1024 + 4 * c]); e1 = std::max(e1, b[1024 + 4 * c]);
+        s1 = std::max(s1, b[1024 + 4 * c + 1]);
+        x0 = std::min(x0, b[1024 + 4 * c + 3]); x1 = std::max(x1, b[1024 + 4 * c + 3]);
+      }
+      fprintf(stderr, " | %s: CTA entry %.2f..%.2f set-up done %.2f first issue %.2f exit %.2f..%.2f",
+              k ? "down" : "gate/up", rel(e0), rel(e1), rel(s1), rel(b[0]), rel(x0), rel(x1));
+    }
+    fprintf(stderr, "\n");
+    for (int k = 0; k < 2; k++) {
+      const unsigned long long* b = tr + 4096 * k;
+      fprintf(stderr, "  %s CTA 0 parts (accumulator ready -> epilogue done):", k ? "down" : "gate/up");
+      for (int i = 0; i < 16 && b[3072 + i * 4]; i++) fprintf(stderr, " %.1f->%.1f", rel(b[3072 + i * 4 + 1]), rel(b[3072 + i * 4 + 2]));
+      fprintf(stderr, "\n");
+    }
+  }
   return RMOE_OK;
 }
 
@@ -903,10 +935,10 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     marks.mark();  // (h is quantized inside the gate/up epilogue)
     if (T == 1) {
       e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
-                        L->partial2, L->tile_cnt, L->tc_work + 4, L->dev_err, st, nullptr,
+                        L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
                         L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
-      if (L->tc_trace) {
+      if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
         if ((s = print_tc_trace(L, st, "down (one token)", 4096)) != RMOE_OK) return s;
       }
@@ -914,10 +946,10 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       launches = terms_done ? 4 : (fused_ok ? 6 : 9);  // front (+ order resolve), gate/up, down
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
-                        L->partial2, L->tile_cnt, L->tc_work + 4, L->dev_err, st, nullptr,
+                        L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
                         L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
-      if (L->tc_trace) {
+      if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
         if ((s = print_tc_trace(L, st, "down", 4096)) != RMOE_OK) return s;
       }

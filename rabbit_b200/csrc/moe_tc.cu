@@ -126,6 +126,12 @@ __host__ __device__ inline MtLayout mt_layout(int stages, int b_boxes) {
   return l;
 }
 
+// Release increment without a returned value: the issuing thread does not wait for its earlier
+// stores (nor, through the preceding barrier, its CTA's) to be performed, unlike a full fence.
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -260,8 +266,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     if (lane == 0) {
       int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
       int cc = -1, ce = 0, cn = 0;  // chunk fields of the current stage
-      // claim the first unit and load its chunk fields
-      int unit = atomicAdd(a.work, 1);
+      // the first unit is this CTA's own (unit blockIdx.x); later ones are claimed from the
+      // counter, which therefore hands out units gridDim.x, gridDim.x + 1, ...
+      int unit = blockIdx.x;
       int ue = 0, up0 = 0, un = 0, ubr = 0;
       auto chunk_of = [&](int u, int& c) {  // chunk of the unit's first stage
         const int t = u / upt;
@@ -279,7 +286,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       load_unit(unit);
       for (int part = 0;; part++) {
         const bool stop = unit >= total_units || *abort_flag;
-        const int nxt = stop ? unit : atomicAdd(a.work, 1);  // next claim; used after this unit
+        int nxt = unit;  // next claim: made after this unit's first stage is issued
         if (part >= kRecRing && !mbar_wait_bounded(&rec_empty[rslot], rph ^ 1, a.err, 0x10u)) {
           *abort_flag = 1;
           break;
@@ -317,7 +324,10 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
                                (static_cast<size_t>(w.m) * kst + w.ks) * kTileBlock;
           bulk_g2s(st, blk, kTileBlock, &full[slot]);
           if (++slot == S) { slot = 0; ph ^= 1; }
-          if (j == 0) load_unit(nxt);  // next unit's fields load while this one streams
+          if (j == 0) {  // claim the next unit and load its fields while this one streams
+            nxt = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
+            load_unit(nxt);
+          }
         }
         unit = nxt;
         if (*abort_flag) break;
@@ -553,10 +563,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) {
-        __threadfence();
-        atomicAdd(a.work + 2, 1);  // this CTA's h slices are written
-      }
+      if (et == 0) red_release_gpu_add(a.work + 2, 1);  // this CTA's h slices are written
     }
     int buf = 0, seen = 0, rslot = 0, rph = 0;
     for (;;) {
@@ -646,8 +653,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     const int et = threadIdx.x - 192;
     asm volatile("bar.sync 1, 128;" ::: "memory");
     if (et == 0) {
-      __threadfence();
-      atomicAdd(a.work + 3, 1);
+      red_release_gpu_add(a.work + 3, 1);
       const uint64_t t0 = global_ns();
       while (ld_acquire_gpu(a.work + 3) < static_cast<int>(gridDim.x)) {
         if (global_ns() - t0 > 2000000000ull) {
