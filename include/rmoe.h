@@ -186,7 +186,8 @@ RMOE_API rmoe_status rmoe_dispatch(rmoe_layer* layer, const int32_t* ids, int32_
 
 /* The whole MoE block for T tokens: qwen38::generate::moe_forward (src/qwen38/generate.rs:
  * 262-351) or glm52::moe::moe (src/glm52/moe.rs:350-451). out [T, H] f32 is overwritten.
- * ids_out/w_out ([T, k]) receive the routing when non-NULL. */
+ * ids_out/w_out ([T, k]) receive the routing when non-NULL. x and out are read and written in
+ * place when 16-byte aligned (any other alignment is staged through internal buffers). */
 RMOE_API rmoe_status rmoe_moe_forward(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                              float* out, int32_t* ids_out, float* w_out, void* stream);
 

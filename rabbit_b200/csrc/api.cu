@@ -1,5 +1,6 @@
 // api.cu -- the C ABI (include/rmoe.h): contexts, layers with HBM-resident experts, uploads
 // in the reference byte layout, and the stream-ordered forward pipeline.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -72,9 +73,26 @@ struct rmoe_ctx {
 
 // One captured forward (CUDA graph) for a (T, dtype, routing-out, profiling) combination. The
 // caller's buffers are reached through memcpy nodes whose pointers are set per launch.
+// A kernel node of a captured forward whose arguments hold the staging input or output pointer:
+// the caller's x / out are written into a copy of its argument bytes at each launch.
+struct NodePatch {
+  cudaGraphNode_t node = nullptr;
+  cudaKernelNodeParams params{};
+  std::vector<std::vector<uint8_t>> args;  // argument bytes
+  std::vector<void*> arg_ptrs;             // -> args[i].data()
+  struct Site {
+    size_t arg, off;
+    bool out;
+  };
+  std::vector<Site> sites;
+};
+
 struct GraphEntry {
   cudaGraph_t graph = nullptr;  // kept alive: its node handles address the exec's nodes
   cudaGraphExec_t exec = nullptr;
+  // direct_io: the kernels read x / write out through patched arguments (no copy nodes)
+  bool direct_io = false;
+  std::vector<NodePatch> patches;
   cudaGraphNode_t in_node = nullptr, out_node = nullptr, ids_node = nullptr, w_node = nullptr;
   size_t x_bytes = 0, out_bytes = 0, rt_bytes = 0;
   const void* ids_src = nullptr;
@@ -561,6 +579,10 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
       fprintf(stderr, "  %s CTA 0 parts (accumulator ready -> epilogue done):", k ? "down" : "gate/up");
       for (int i = 0; i < 16 && b[3072 + i * 4]; i++) fprintf(stderr, " %.1f->%.1f", rel(b[3072 + i * 4 + 1]), rel(b[3072 + i * 4 + 2]));
       fprintf(stderr, "\n");
+      fprintf(stderr, "    producer role start %.2f unit fields %.2f; part stores begin %.2f %.2f %.2f %.2f\n", rel(b[1700]),
+              rel(b[1701]), rel(b[1711]), rel(b[1712]), rel(b[1713]), rel(b[1714]));
+      if (k) fprintf(stderr, "    h: act producer wait done %.2f, barrier poll from %.2f seen %.2f; epilogue wait done %.2f, finalize done %.2f;"
+                     " first B landed %.2f\n", rel(b[1720]), rel(b[1721]), rel(b[1722]), rel(b[1723]), rel(b[1724]), rel(b[1]));
     }
   }
   return RMOE_OK;
@@ -1140,6 +1162,72 @@ static rmoe_status drain_graph_profile(rmoe_layer* L, GraphEntry& g) {
 
 // Captures the forward for (T, dtype, routing out, profiling) once; the caller's x / out /
 // routing buffers are bound per launch through memcpy nodes at the graph's ends.
+// Kernel argument layout (offset, size) of argument i, from the driver (cuFuncGetParamInfo).
+typedef CUresult (*PFN_funcGetParamInfo)(CUfunction, size_t, size_t*, size_t*);
+static PFN_funcGetParamInfo param_info_fn() {
+  static PFN_funcGetParamInfo fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuFuncGetParamInfo", &p, 12040, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_funcGetParamInfo>(p);
+  });
+  return fn;
+}
+
+// Finds every kernel-argument word of the captured forward equal to the staging input (x_dev)
+// or output (out_dev) pointer. True when the forward can run on the caller's buffers directly:
+// at least one reader of x and one writer of out were found, and no copy or memset node (whose
+// pointers cannot be patched this way) touches either buffer.
+static bool find_io_patches(rmoe_layer* L, const std::vector<cudaGraphNode_t>& nodes, std::vector<NodePatch>& out) {
+  auto fn = param_info_fn();
+  if (!fn) return false;
+  const uint64_t xv = reinterpret_cast<uintptr_t>(L->x_dev), ov = reinterpret_cast<uintptr_t>(L->out_dev);
+  int nx = 0, no = 0;
+  for (cudaGraphNode_t nd : nodes) {
+    cudaGraphNodeType type;
+    if (cudaGraphNodeGetType(nd, &type) != cudaSuccess) return false;
+    if (type == cudaGraphNodeTypeMemcpy) {
+      cudaMemcpy3DParms m{};
+      if (cudaGraphMemcpyNodeGetParams(nd, &m) != cudaSuccess) return false;
+      const uint64_t a = reinterpret_cast<uintptr_t>(m.srcPtr.ptr), b = reinterpret_cast<uintptr_t>(m.dstPtr.ptr);
+      if (a == xv || a == ov || b == xv || b == ov) return false;
+      continue;
+    }
+    if (type == cudaGraphNodeTypeMemset) {
+      cudaMemsetParams m{};
+      if (cudaGraphMemsetNodeGetParams(nd, &m) != cudaSuccess) return false;
+      const uint64_t b = reinterpret_cast<uintptr_t>(m.dst);
+      if (b == xv || b == ov) return false;
+      continue;
+    }
+    if (type != cudaGraphNodeTypeKernel) continue;
+    NodePatch np;
+    np.node = nd;
+    if (cudaGraphKernelNodeGetParams(nd, &np.params) != cudaSuccess || np.params.extra) return false;
+    cudaFunction_t f = nullptr;
+    if (cudaGetFuncBySymbol(&f, np.params.func) != cudaSuccess) return false;
+    for (size_t i = 0;; i++) {
+      size_t off = 0, sz = 0;
+      if (fn(reinterpret_cast<CUfunction>(f), i, &off, &sz) != CUDA_SUCCESS) break;
+      const uint8_t* src = static_cast<const uint8_t*>(np.params.kernelParams[i]);
+      np.args.emplace_back(src, src + sz);
+      for (size_t o = 0; o + 8 <= sz; o += 8) {
+        uint64_t v;
+        memcpy(&v, src + o, 8);
+        if (v == xv || v == ov) {
+          np.sites.push_back({i, o, v == ov});
+          (v == ov ? no : nx)++;
+        }
+      }
+    }
+    if (!np.sites.empty()) out.push_back(std::move(np));
+  }
+  return nx > 0 && no > 0;  // (argument pointer arrays are set at each launch)
+}
+
 static rmoe_status capture_graph(rmoe_layer* L, int x_dtype, int T, bool want_rt, GraphEntry& g) {
   const size_t H = L->desc.hidden;
   g.x_bytes = static_cast<size_t>(T) * H * (x_dtype == RMOE_BF16 ? 2 : 4);
@@ -1182,14 +1270,18 @@ static rmoe_status capture_graph(rmoe_layer* L, int x_dtype, int T, bool want_rt
     if ((e = cudaGraphNodeGetDependentNodes(nd, nullptr, &nd_out)) != cudaSuccess) return done(e, "graph deps");
     if (nd_out == 0) leaves.push_back(nd);
   }
-  if ((e = cudaGraphAddMemcpyNode1D(&g.in_node, graph, nullptr, 0, L->x_dev, L->x_stage, g.x_bytes,
-                                    cudaMemcpyDeviceToDevice)) != cudaSuccess)
-    return done(e, "graph input node");
-  for (cudaGraphNode_t r : roots)
-    if ((e = cudaGraphAddDependencies(graph, &g.in_node, &r, 1)) != cudaSuccess) return done(e, "graph input deps");
-  if ((e = cudaGraphAddMemcpyNode1D(&g.out_node, graph, leaves.data(), leaves.size(), L->out_stage,
-                                    L->out_dev, g.out_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess)
-    return done(e, "graph output node");
+  g.direct_io = find_io_patches(L, nodes, g.patches);
+  if (!g.direct_io) {
+    g.patches.clear();
+    if ((e = cudaGraphAddMemcpyNode1D(&g.in_node, graph, nullptr, 0, L->x_dev, L->x_stage, g.x_bytes,
+                                      cudaMemcpyDeviceToDevice)) != cudaSuccess)
+      return done(e, "graph input node");
+    for (cudaGraphNode_t r : roots)
+      if ((e = cudaGraphAddDependencies(graph, &g.in_node, &r, 1)) != cudaSuccess) return done(e, "graph input deps");
+    if ((e = cudaGraphAddMemcpyNode1D(&g.out_node, graph, leaves.data(), leaves.size(), L->out_stage,
+                                      L->out_dev, g.out_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+      return done(e, "graph output node");
+  }
   if (want_rt) {
     if ((e = cudaGraphAddMemcpyNode1D(&g.ids_node, graph, leaves.data(), leaves.size(), L->ids_host_stage,
                                       g.ids_src, g.rt_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess)
@@ -1226,10 +1318,30 @@ static rmoe_status forward_graph(rmoe_layer* L, const void* x, int x_dtype, int 
   GraphEntry& g = it->second;
   rmoe_status s = drain_graph_profile(L, g);
   if (s != RMOE_OK) return s;
-  RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.in_node, L->x_dev, x, g.x_bytes, cudaMemcpyDeviceToDevice),
-            "bind x");
-  RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.out_node, out, L->out_dev, g.out_bytes, cudaMemcpyDeviceToDevice),
-            "bind out");
+  // the kernels' vector loads and stores want 16-byte aligned x and out; other buffers go
+  // through the staging ones
+  const bool staged = g.direct_io && (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16);
+  if (staged) {
+    RMOE_CUDA(cudaMemcpyAsync(L->x_dev, x, g.x_bytes, cudaMemcpyDeviceToDevice, st), "stage x");
+  }
+  if (g.direct_io) {
+    const uint64_t xv = reinterpret_cast<uintptr_t>(staged ? L->x_dev : x);
+    const uint64_t ov = reinterpret_cast<uintptr_t>(staged ? L->out_dev : out);
+    for (NodePatch& np : g.patches) {
+      // (pointers into this entry's own argument copies: the entry may have been copied)
+      np.arg_ptrs.resize(np.args.size());
+      for (size_t i = 0; i < np.args.size(); i++) np.arg_ptrs[i] = np.args[i].data();
+      np.params.kernelParams = np.arg_ptrs.data();
+      for (const NodePatch::Site& st : np.sites) memcpy(np.args[st.arg].data() + st.off, st.out ? &ov : &xv, 8);
+      RMOE_CUDA(cudaGraphExecKernelNodeSetParams(g.exec, np.node, &np.params), "bind x / out");
+    }
+  } else {
+    RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.in_node, L->x_dev, x, g.x_bytes, cudaMemcpyDeviceToDevice),
+              "bind x");
+    RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.out_node, out, L->out_dev, g.out_bytes,
+                                                 cudaMemcpyDeviceToDevice),
+              "bind out");
+  }
   if (want_rt) {
     RMOE_CUDA(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.ids_node, ids_out ? static_cast<void*>(ids_out) : L->ids_host_stage,
                                                  g.ids_src, g.rt_bytes, cudaMemcpyDeviceToDevice),
@@ -1239,6 +1351,7 @@ static rmoe_status forward_graph(rmoe_layer* L, const void* x, int x_dtype, int 
               "bind weights");
   }
   RMOE_CUDA(cudaGraphLaunch(g.exec, st), "graph launch");
+  if (staged) RMOE_CUDA(cudaMemcpyAsync(out, L->out_dev, g.out_bytes, cudaMemcpyDeviceToDevice, st), "unstage out");
   g.pending = g.profiled;
   L->stats.kernel_launches += g.launches;
   L->stats.forward_calls++;
@@ -1253,7 +1366,17 @@ static rmoe_status forward_into(rmoe_layer* L, const void* x, int x_dtype, int T
   rmoe_status s = check_uploaded(L);
   if (s != RMOE_OK) return s;
   if (graph_path(L, T)) return forward_graph(L, x, x_dtype, T, out, ids_out, w_out, st);
-  return forward_direct(L, x, x_dtype, T, out, ids_out, w_out, st);
+  // the kernels' vector loads and stores want 16-byte aligned x and out: others are staged
+  const bool staged = reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16;
+  if (!staged) return forward_direct(L, x, x_dtype, T, out, ids_out, w_out, st);
+  const size_t H = L->desc.hidden;
+  RMOE_CUDA(cudaMemcpyAsync(L->x_dev, x, static_cast<size_t>(T) * H * (x_dtype == RMOE_BF16 ? 2 : 4),
+                            cudaMemcpyDeviceToDevice, st),
+            "stage x");
+  if ((s = forward_direct(L, L->x_dev, x_dtype, T, L->out_dev, ids_out, w_out, st)) != RMOE_OK) return s;
+  RMOE_CUDA(cudaMemcpyAsync(out, L->out_dev, static_cast<size_t>(T) * H * 4, cudaMemcpyDeviceToDevice, st),
+            "unstage out");
+  return RMOE_OK;
 }
 
 
@@ -1290,6 +1413,16 @@ extern "C" rmoe_status rmoe_moe_forward_routed(rmoe_layer* L, const void* x, int
   const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
   const bool hs = with_shared && L->has_shared;
   const bool gated = hs && D.shared_gated;
+  // 16-byte aligned x and out are used in place; others go through the staging buffers
+  float* const out_user = out;
+  const bool staged = reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16;
+  if (staged) {
+    RMOE_CUDA(cudaMemcpyAsync(L->x_dev, x, static_cast<size_t>(T) * H * (x_dtype == RMOE_BF16 ? 2 : 4),
+                              cudaMemcpyDeviceToDevice, st),
+              "stage x");
+    x = L->x_dev;
+    out = L->out_dev;
+  }
   const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
   const size_t n = static_cast<size_t>(T) * k;
   RMOE_CUDA(cudaMemcpyAsync(L->ids, ids, n * 4, cudaMemcpyDefault, st), "routed ids");
@@ -1305,6 +1438,9 @@ extern "C" rmoe_status rmoe_moe_forward_routed(rmoe_layer* L, const void* x, int
   s = enqueue_experts(L, x, xdt, T, mt, hs, false, false, out, st, marks, &launches);
   L->profiling = prof;
   if (s != RMOE_OK) return s;
+  if (staged)
+    RMOE_CUDA(cudaMemcpyAsync(out_user, out, static_cast<size_t>(T) * H * 4, cudaMemcpyDeviceToDevice, st),
+              "unstage out");
   L->stats.kernel_launches += launches;
   L->stats.forward_calls++;
   L->stats.tokens_routed += T;

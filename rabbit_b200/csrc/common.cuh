@@ -116,5 +116,9 @@ __device__ __forceinline__ float sigmoid_ref(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32(-x)));
 }
 __device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, exp_f32(-x))); }
+// silu with the single-precision expf (<= 2 ulp): for h that is expanded into E2M1 terms next
+// (~11 bits kept), where the reference's correctly rounded exp buys nothing and costs a
+// double-precision exp per element.
+__device__ __forceinline__ float silu_f32(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
 }  // namespace rmoe

@@ -153,6 +153,47 @@ __device__ __forceinline__ bool epi_all(bool p) {
   return r != 0;
 }
 
+// Down kernels after a split gate/up pass: h of every position from the gate/up unit parts. One
+// warp per (gate/up tile, 32 inter rows): parts added in K order (loads issued four at a time),
+// h = silu(g) u w, written as the four-term operand. `hw` = this warp's index among the `nhw`
+// helper warps of the CTA.
+__device__ __forceinline__ void h_from_parts(const MoeTcArgs& a, int nch, int hw, int nhw, int lane) {
+  const int items = 2 * nch * a.ntm_gu;
+  for (int it = blockIdx.x * nhw + hw; it < items; it += gridDim.x * nhw) {
+    const int tile = it / 2, hf = it % 2;
+    const int c = tile / a.ntm_gu, m = tile % a.ntm_gu;
+    const int p0 = __ldg(a.ch_pos + c), n = __ldg(a.ch_n + c);
+    const int i0 = m * 64 + hf * 32;
+    for (int t = 0; t < n; t++) {
+      const float* base = a.partial_in + static_cast<size_t>(tile) * a.upt_gu * 8 * 128 + t * 128 + hf * 32 + lane;
+      float g = 0.0f, u = 0.0f;
+      int j = 0;
+      for (; j + 4 <= a.upt_gu; j += 4) {
+        float gg[4], uu[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          gg[q] = __ldcg(base + static_cast<size_t>(j + q) * 8 * 128);
+          uu[q] = __ldcg(base + static_cast<size_t>(j + q) * 8 * 128 + 64);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          g += gg[q];
+          u += uu[q];
+        }
+      }
+      for (; j < a.upt_gu; j++) {
+        g += __ldcg(base + static_cast<size_t>(j) * 8 * 128);
+        u += __ldcg(base + static_cast<size_t>(j) * 8 * 128 + 64);
+      }
+      const int p = p0 + t;
+      const float hv = __fmul_rn(silu_f32(g), u) * __ldg(a.perm_w + p);
+      const size_t trow = static_cast<size_t>(4 * p);
+      warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2, a.hsf + trow * (a.inter / 32) + i0 / 32,
+                  a.inter / 32);
+    }
+  }
+}
+
 // Walks consecutive stages of the flat list (tile-major, L stages per tile) from stage s.
 template <int MODE>
 struct StageWalker {
@@ -283,7 +324,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         un = MODE == kModeDownOne ? 1 : __ldg(a.ch_n + c);
         ubr = 4 * (a.b_tok ? __ldg(a.b_tok + up0) : up0);
       };
+      if (a.trace && blockIdx.x == 0) a.trace[1700] = global_ns();
       load_unit(unit);
+      if (a.trace && blockIdx.x == 0) a.trace[1701] = global_ns();
       for (int part = 0;; part++) {
         const bool stop = unit >= total_units || *abort_flag;
         int nxt = unit;  // next claim: made after this unit's first stage is issued
@@ -346,12 +389,14 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     // ------------------------------------------------------------------ activation producer
     if (lane == 0) {
       if (MODE != kModeGateUp) griddep_wait();  // h (written by gate/up)
+      if (a.trace && blockIdx.x == 0) a.trace[1720] = global_ns();
       tma_prefetch_desc(&maps.b);
       tma_prefetch_desc(&maps.bs);
       int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
       if (MODE != kModeGateUp && a.gu_split) {
         // the activation operand is h: wait until every CTA has written its h slices
         const uint64_t t0 = global_ns();
+        if (a.trace && blockIdx.x == 0) a.trace[1721] = global_ns();
         while (ld_acquire_gpu(a.work + 2) < static_cast<int>(gridDim.x)) {
           if (global_ns() - t0 > 2000000000ull) {
             atomicOr(a.err, 0x40000u);
@@ -361,6 +406,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           __nanosleep(32);
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");  // h was written by plain stores
+        if (a.trace && blockIdx.x == 0) a.trace[1722] = global_ns();
       }
       for (;;) {
         if (!mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x20u)) break;
@@ -474,6 +520,12 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ B scale factors -> TMEM
+    if (MODE != kModeGateUp && a.gu_split) {
+      // first, with the epilogue warps, h from the gate/up parts (the B operand of every stage)
+      griddep_wait();
+      h_from_parts(a, nch, warp - 2, 8, lane);
+      asm volatile("bar.sync 3, 256;" ::: "memory");
+    }
     const int q = warp & 3;
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
     int i = 0, rslot = 0, rph = 0;
@@ -538,32 +590,12 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
     const int row = 32 * q + lane;      // accumulator row (A-tile row)
     if (MODE != kModeGateUp) griddep_wait();  // gate/up parts (and h) complete
+    if (a.trace && blockIdx.x == 0 && threadIdx.x == 192) a.trace[1723] = global_ns();
     if (MODE != kModeGateUp && a.gu_split) {
-      // h of every position from the gate/up unit parts: one warp per (gate/up tile, 32 inter
-      // rows), parts added in K order, h = silu(g) u w, written as the four-term operand
-      const int ew = et / 32;
-      const int items = 2 * nch * a.ntm_gu;
-      for (int it = blockIdx.x * 4 + ew; it < items; it += gridDim.x * 4) {
-        const int tile = it / 2, hf = it % 2;
-        const int c = tile / a.ntm_gu, m = tile % a.ntm_gu;
-        const int p0 = __ldg(a.ch_pos + c), n = __ldg(a.ch_n + c);
-        const int i0 = m * 64 + hf * 32;
-        for (int t = 0; t < n; t++) {
-          float g = 0.0f, u = 0.0f;
-          for (int j = 0; j < a.upt_gu; j++) {
-            const float* qp = a.partial_in + static_cast<size_t>(tile * a.upt_gu + j) * 8 * 128 + t * 128;
-            g += __ldcg(qp + hf * 32 + lane);
-            u += __ldcg(qp + 64 + hf * 32 + lane);
-          }
-          const int p = p0 + t;
-          const float hv = __fmul_rn(silu_ref(g), u) * __ldg(a.perm_w + p);
-          const size_t trow = static_cast<size_t>(4 * p);
-          warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2,
-                      a.hsf + trow * (a.inter / 32) + i0 / 32, a.inter / 32);
-        }
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      h_from_parts(a, nch, 4 + et / 32, 8, lane);  // (with the scale-factor warps)
+      asm volatile("bar.sync 3, 256;" ::: "memory");
       if (et == 0) red_release_gpu_add(a.work + 2, 1);  // this CTA's h slices are written
+      if (a.trace && blockIdx.x == 0 && et == 0) a.trace[1724] = global_ns();
     }
     int buf = 0, seen = 0, rslot = 0, rph = 0;
     for (;;) {
@@ -605,6 +637,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         // that needs the tile (the down kernel's prologue for gate/up, the end of this kernel
         // for the one-token down projection)
         float* pp = a.partial + static_cast<size_t>(r.unit) * 8 * 128;
+        if (a.trace && blockIdx.x == 0 && et == 0 && seen <= 4) a.trace[1710 + seen] = global_ns();
         for (int t = 0; t < n; t++) pp[t * 128 + row] = v[t];
         if (a.trace && blockIdx.x == 0 && et == 0 && seen <= 128) a.trace[3072 + (seen - 1) * 4 + 2] = global_ns();
         continue;
@@ -631,7 +664,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           for (int i = 0; i < 8; i++) {
             const int rr = hb * 32 + 8 * s4 + i;
             const float g = ubuf[rr * 33 + t], u = ubuf[(64 + rr) * 33 + t];
-            h[i] = valid ? __fmul_rn(silu_ref(g), u) * wp : 0.0f;
+            h[i] = valid ? __fmul_rn(silu_f32(g), u) * wp : 0.0f;
           }
           const int i0 = mm * 64 + hb * 32;
           const size_t trow = static_cast<size_t>(4 * p);

@@ -109,6 +109,31 @@ def test_host_entry_point_matches_device_path(qwen_layer):
     assert np.array_equal(dev, out)
 
 
+def test_graph_replays_bind_the_callers_buffers(qwen_layer):
+    """Cached forward graphs read x and write out through the caller's buffers (kernel arguments
+    rebound per launch; misaligned buffers go through staging): every call, in any order, gives
+    the bits a fresh single call gives."""
+    import torch
+
+    cfg, L = qwen_layer
+    for T in (1, 3, 40):
+        xs = [x_device(cfg, synth.activations(cfg, tokens=T, token_offset=o)) for o in (0, 5000)]
+        ref = [L.moe_forward(x).clone() for x in xs]
+        assert not torch.equal(ref[0], ref[1])
+        for _ in range(2):
+            for i in (1, 0):
+                out = torch.full((T, cfg.hidden), float("nan"), device="cuda")
+                assert torch.equal(L.moe_forward(xs[i], out=out), ref[i])
+        # a 4-byte offset view of x and of out: the staged path
+        xb = torch.empty(T * cfg.hidden + 2, dtype=xs[0].dtype, device="cuda")
+        xv = xb[2:].view(T, cfg.hidden)
+        xv.copy_(xs[0])
+        ob = torch.empty(T * cfg.hidden + 1, dtype=torch.float32, device="cuda")
+        ov = ob[1:].view(T, cfg.hidden)
+        L.moe_forward(xv, out=ov)
+        assert torch.equal(ov, ref[0])
+
+
 def test_c4_glm_int4_layer(cuda_ctx):
     cfg = synth.CONFIGS["c4_glm_int4"]
     L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens, scale_dtype="bf16")
