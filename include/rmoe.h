@@ -26,7 +26,7 @@ extern "C" {
 #define RMOE_API
 #endif
 
-#define RMOE_ABI_VERSION 1
+#define RMOE_ABI_VERSION 2
 #define RMOE_MAX_TOPK 32
 
 typedef enum rmoe_status {
@@ -54,6 +54,14 @@ typedef enum rmoe_weight_format {
 
 typedef enum rmoe_dtype { RMOE_F32 = 0, RMOE_BF16 = 1 } rmoe_dtype;
 
+/* The expert gating activation (glm52::moe::Activation, src/glm52/moe.rs:49-70). */
+typedef enum rmoe_activation {
+  RMOE_ACT_SILU = 0,  /* silu(g) * u */
+  /* Kimi K3 SituAndMul: beta tanh(g / beta) sigmoid(g) * u', u' = lb tanh(u / lb) when a linear
+   * beta lb is set (situ_linear_beta > 0), else u */
+  RMOE_ACT_SITU = 1
+} rmoe_activation;
+
 typedef struct rmoe_ctx rmoe_ctx;
 typedef struct rmoe_layer rmoe_layer;
 
@@ -77,6 +85,13 @@ typedef struct rmoe_layer_desc {
   int32_t max_tokens;     /* largest T any call will pass (sizes the workspace) */
   int32_t ep_rank;        /* expert parallel rank (0 when unsharded) */
   int32_t ep_size;        /* expert parallel world size (1 when unsharded) */
+  int32_t activation;     /* rmoe_activation (0 = SiLU) */
+  float situ_beta;        /* RMOE_ACT_SITU: beta (> 0) */
+  float situ_linear_beta; /* RMOE_ACT_SITU: linear beta; <= 0 = none */
+  /* Kimi K3 latent MoE (kimi_k3::moe::latent_moe, src/kimi_k3/moe.rs:64-116): the router and
+   * the caller's x are router_hidden wide while the experts work at `hidden` (the latent width);
+   * 0 = the same as hidden. A layer with router_hidden != hidden runs through rmoe_latent_moe. */
+  int32_t router_hidden;
 } rmoe_layer_desc;
 
 typedef struct rmoe_layer_stats {
@@ -190,6 +205,22 @@ RMOE_API rmoe_status rmoe_dispatch(rmoe_layer* layer, const int32_t* ids, int32_
  * place when 16-byte aligned (any other alignment is staged through internal buffers). */
 RMOE_API rmoe_status rmoe_moe_forward(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                              float* out, int32_t* ids_out, float* w_out, void* stream);
+
+/* Weights of the latent wrapper of a layer created with router_hidden != hidden: down_proj
+ * [hidden][router_hidden] and up_proj [router_hidden][hidden], row-major, proj_dtype RMOE_F32 or
+ * RMOE_BF16 (host or device pointers); norm [hidden] f32 (the routed-expert RMSNorm weight) or
+ * NULL for none; eps its epsilon. (LatentMoeWeights, src/kimi_k3/moe.rs:42-56.) */
+RMOE_API rmoe_status rmoe_upload_latent(rmoe_layer* layer, const void* down_proj, const void* up_proj,
+                               int32_t proj_dtype, const float* norm, float eps);
+
+/* Kimi K3 latent MoE for T tokens (kimi_k3::moe::latent_moe, src/kimi_k3/moe.rs:64-116): routes
+ * x [T, router_hidden] with the layer's router, projects x down to the experts' width, runs the
+ * routed experts there (the shared expert is not included: the caller adds it, as in the
+ * reference), RMSNorms each token's summed routed row when a norm weight was uploaded, and
+ * projects it back up into out [T, router_hidden] f32 (overwritten). ids_out/w_out ([T, k]) get
+ * the routing when non-NULL. Device pointers. */
+RMOE_API rmoe_status rmoe_latent_moe(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T, float* out,
+                            int32_t* ids_out, float* w_out, void* stream);
 
 /* The expert loop with routing given (glm52::moe::moe's loop over Routing via apply_single_expert,
  * src/glm52/moe.rs:463-513): out[t] = sum_j weights[t][j] * expert_{ids[t][j]}(x[t]), plus the

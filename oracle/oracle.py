@@ -283,6 +283,74 @@ def moe_glm(x, router, bias, experts, e, k, inter, n_group, topk_group, norm_top
     return out.reshape(s, d), ids.reshape(s, k), w.reshape(s, k)
 
 
+# ---------------------------------------------------------------- Kimi K3 latent MoE
+def act_mul(g, u, act=("silu",)):
+    """glm52::moe::Activation::combine (src/glm52/moe.rs:58-70) elementwise in f32: SiLU via the
+    C oracle's siluf, or ("situ", beta, linear_beta) = beta tanh(g / beta) sigmoid(g) * u'
+    with u' = lb tanh(u / lb) when lb is not None (kimi_linear::ops::situ_and_mul,
+    src/kimi_linear/ops.rs); numpy's float32 tanh/exp stand for Rust's f32 libm calls."""
+    g = _f32(g)
+    u = _f32(u)
+    if act[0] == "silu":
+        sg = np.array([siluf(float(v)) for v in g.reshape(-1)], np.float32).reshape(g.shape)
+        return (sg * u).astype(np.float32)
+    beta, lb = np.float32(act[1]), act[2]
+    if lb is not None:
+        lb = np.float32(lb)
+        u = (lb * np.tanh(u / lb)).astype(np.float32)
+    sig = (np.float32(1.0) / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+    situ = ((beta * np.tanh(g / beta)).astype(np.float32) * sig).astype(np.float32)
+    return (situ * u).astype(np.float32)
+
+
+def rmsnorm_rows(v, w, eps):
+    """kimi_linear::ops::rmsnorm (src/kimi_linear/ops.rs:46-53) on each row: the mean of squares
+    summed sequentially in f64, r = 1 / sqrt(f32(ms / n) + eps) in f32, v *= r * w."""
+    v = _f32(v).copy()
+    w = _f32(w)
+    n = v.shape[1]
+    for row in v:
+        ms = np.add.accumulate(row.astype(np.float64) ** 2)[-1]
+        r = np.float32(1.0) / np.sqrt(np.float32(ms / n) + np.float32(eps))
+        row *= (r * w).astype(np.float32)
+    return v
+
+
+def latent_moe(x, router, bias, experts, e, k, n_group, topk_group, norm_topk, routed_scale, down_proj,
+               up_proj, norm, eps, moe_hidden, inter, act=("silu",), fmt=0, gs=32):
+    """kimi_k3::moe::latent_moe (src/kimi_k3/moe.rs:64-116) minus the cache: route on the full-width
+    x (glm52 routing, :84-86), x_latent = x . down_proj^T (:91-92), apply_single_expert for every
+    unique expert in first-occurrence order at the latent width (:94-104,
+    src/glm52/moe.rs:463-513), RMSNorm of each summed row if norm is not None (:106-110),
+    out = routed . up_proj^T (:112). Returns (out, ids, weights)."""
+    x = _f32(x)
+    s, hf = x.shape
+    ids, w = glm_route(x, router, bias, s, hf, e, k, n_group, topk_group, norm_topk, routed_scale)
+    xl = matmul(x, down_proj, s, hf, moe_hidden)
+    routed = np.zeros((s, moe_hidden), np.float32)
+    for eid in unique_experts(ids):
+        rows, rw = expert_rows(ids, w, int(eid))
+        ex = experts[int(eid)]
+        xs = np.ascontiguousarray(xl[rows])
+        nr = len(rows)
+        if fmt == 0:
+            g = matmul_mxfp4(xs, ex["gate"], ex["gate_scale"], nr, moe_hidden, inter)
+            u = matmul_mxfp4(xs, ex["up"], ex["up_scale"], nr, moe_hidden, inter)
+            h = act_mul(g, u, act)
+            y = matmul_mxfp4(h, ex["down"], ex["down_scale"], nr, inter, moe_hidden)
+        else:
+            g = matmul_i4_grouped(xs, ex["gate"], ex["gate_scale"], gs, nr, moe_hidden, inter)
+            u = matmul_i4_grouped(xs, ex["up"], ex["up_scale"], gs, nr, moe_hidden, inter)
+            h = act_mul(g, u, act)
+            y = matmul_i4_grouped(h, ex["down"], ex["down_scale"], gs, nr, inter, moe_hidden)
+        for r, t in enumerate(rows):
+            routed[t] = (routed[t] + (np.float32(rw[r]) * y[r]).astype(np.float32)).astype(np.float32)
+    if norm is not None:
+        routed = rmsnorm_rows(routed, norm, eps)
+    out = matmul(routed, up_proj, s, moe_hidden, hf)
+    return out, ids, w
+
+
 def set_threads(n: int):
     lib().orc_set_threads(n)
 

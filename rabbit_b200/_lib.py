@@ -31,7 +31,8 @@ class LayerDesc(C.Structure):
                 ("routed_scale", C.c_float), ("weight_format", C.c_int32),
                 ("group_size", C.c_int32), ("scale_dtype", C.c_int32),
                 ("shared_gated", C.c_int32), ("max_tokens", C.c_int32), ("ep_rank", C.c_int32),
-                ("ep_size", C.c_int32)]
+                ("ep_size", C.c_int32), ("activation", C.c_int32), ("situ_beta", C.c_float),
+                ("situ_linear_beta", C.c_float), ("router_hidden", C.c_int32)]
 
 
 class LayerStats(C.Structure):
@@ -63,6 +64,8 @@ PROTOTYPES = {
     "rmoe_layer_set_profiling": (C.c_int, [P, C.c_int]),
     "rmoe_layer_get_profile": (C.c_int, [P, C.POINTER(Profile)]),
     "rmoe_upload_router": (C.c_int, [P, P, I32, SZ]),
+    "rmoe_upload_latent": (C.c_int, [P, P, P, I32, P, F32]),
+    "rmoe_latent_moe": (C.c_int, [P, P, I32, I32, P, P, P, P]),
     "rmoe_upload_router_bias": (C.c_int, [P, P, SZ]),
     "rmoe_upload_expert": (C.c_int, [P, I32, P, SZ, P, SZ, P, SZ, P, SZ, P, SZ, P, SZ]),
     "rmoe_upload_expert_fused": (C.c_int, [P, I32, P, SZ, P, SZ, P, SZ, P, SZ]),

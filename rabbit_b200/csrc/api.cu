@@ -112,6 +112,16 @@ struct rmoe_layer {
   // weights
   void* router = nullptr;
   int router_dtype = kF32;
+  int hr = 0;  // router width = width of the caller's x (the latent layers' full hidden size)
+  // latent wrapper (router_hidden != hidden): projections, norm, activations between them
+  void* lat_down = nullptr;   // [hidden][hr]
+  void* lat_up = nullptr;     // [hr][hidden]
+  int lat_dtype = kF32;
+  float* lat_norm = nullptr;  // [hidden]
+  float lat_eps = 0.0f;
+  bool has_latent = false, lat_has_norm = false;
+  float* lat_x = nullptr;     // [max_tokens][hidden]
+  float* lat_y = nullptr;     // [max_tokens][hidden]
   float* router_bias = nullptr;
   bool has_router = false, has_bias = false, has_shared_w = false;
   uint8_t* experts = nullptr;
@@ -307,6 +317,13 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   } else {
     return fail(RMOE_INVALID_ARG, "rmoe_layer_create: weight_format %d", D.weight_format);
   }
+  if (D.activation != RMOE_ACT_SILU && D.activation != RMOE_ACT_SITU)
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: activation %d", D.activation);
+  if (D.activation == RMOE_ACT_SITU && !(D.situ_beta > 0.0f))
+    return fail(RMOE_INVALID_ARG, "rmoe_layer_create: Situ needs situ_beta > 0");
+  f.act = ActParams{D.activation, D.situ_beta, D.situ_linear_beta > 0.0f ? D.situ_linear_beta : 0.0f};
+  if (D.router_hidden < 0 || (D.router_hidden && D.router_hidden % 32))
+    return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: router_hidden %d (a multiple of 32)", D.router_hidden);
   const int ep_size = D.ep_size <= 0 ? 1 : D.ep_size;
   if (D.n_experts % ep_size || D.ep_rank < 0 || D.ep_rank >= ep_size)
     return fail(RMOE_INVALID_ARG, "rmoe_layer_create: ep_rank %d / ep_size %d / n_experts %d", D.ep_rank, ep_size, D.n_experts);
@@ -392,10 +409,22 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     ALLOC(L->shared_gate_vec, H);
   }
   ALLOC(L->router_bias, E);
+  L->hr = D.router_hidden > 0 ? D.router_hidden : static_cast<int>(H);
   {
     uint8_t* r = nullptr;
-    ALLOC(r, E * H * 4);
+    ALLOC(r, E * L->hr * 4);
     L->router = r;
+  }
+  if (L->hr != static_cast<int>(H)) {
+    uint8_t* dp = nullptr;
+    uint8_t* up = nullptr;
+    ALLOC(dp, H * L->hr * 4);
+    ALLOC(up, H * L->hr * 4);
+    L->lat_down = dp;
+    L->lat_up = up;
+    ALLOC(L->lat_norm, H);
+    ALLOC(L->lat_x, static_cast<size_t>(D.max_tokens) * H);
+    ALLOC(L->lat_y, static_cast<size_t>(D.max_tokens) * H);
   }
   // workspace
   const int T = D.max_tokens, k = D.topk;
@@ -626,10 +655,10 @@ extern "C" rmoe_status rmoe_layer_get_profile(rmoe_layer* L, rmoe_profile* out) 
 extern "C" rmoe_status rmoe_upload_router(rmoe_layer* L, const void* w, int32_t dtype, size_t bytes) {
   if (!L || !w) return fail(RMOE_INVALID_ARG, "rmoe_upload_router: null argument");
   if (dtype != RMOE_F32 && dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "rmoe_upload_router: dtype %d", dtype);
-  const size_t want = static_cast<size_t>(L->desc.n_experts) * L->desc.hidden * (dtype == RMOE_BF16 ? 2 : 4);
+  const size_t want = static_cast<size_t>(L->desc.n_experts) * L->hr * (dtype == RMOE_BF16 ? 2 : 4);
   if (bytes != want)
     return fail(RMOE_SHAPE_MISMATCH, "rmoe_upload_router: %zu bytes, [%d, %d] needs %zu", bytes,
-                L->desc.n_experts, L->desc.hidden, want);
+                L->desc.n_experts, L->hr, want);
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   RMOE_CUDA(cudaMemcpy(L->router, w, bytes, cudaMemcpyDefault), "rmoe_upload_router copy");
   L->router_dtype = dtype == RMOE_BF16 ? kBF16 : kF32;
@@ -807,7 +836,7 @@ static rmoe_status route_into(rmoe_layer* L, const void* x, int x_dtype, int T, 
                               StageMarks* marks = nullptr) {
   const rmoe_layer_desc& D = L->desc;
   cudaError_t e = launch_router_logits_exact(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, L->router,
-                                             L->router_dtype, L->logits, T, D.hidden, D.n_experts, st);
+                                             L->router_dtype, L->logits, T, L->hr, D.n_experts, st);
   if (e != cudaSuccess) return cuda_fail(e, "router logits");
   if (marks) marks->mark();
   if (D.router_kind == RMOE_ROUTER_SOFTMAX_TOPK)
@@ -838,7 +867,7 @@ extern "C" rmoe_status rmoe_route(rmoe_layer* L, const void* x, int32_t x_dtype,
 // The decode-sized front end: softmax router, T <= 32, H a multiple of 256.
 static bool small_path(const rmoe_layer* L, int T) {
   return T <= 32 && L->desc.router_kind == RMOE_ROUTER_SOFTMAX_TOPK && L->desc.hidden % 256 == 0 &&
-         L->desc.topk <= 32;
+         L->desc.topk <= 32 && L->hr == L->desc.hidden;
 }
 
 static int chunk_tokens(int T) { return T >= 8 ? 8 : (T >= 4 ? 4 : (T >= 2 ? 2 : 1)); }
@@ -950,7 +979,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     // one token: every position reads the token's own term rows (0..3)
     e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
                       L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
-                      L->tc_trace);
+                      L->tc_trace, nullptr, L->fmt.act);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
 
     marks.mark();
@@ -958,7 +987,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     if (T == 1) {
       e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial, L->fmt.act);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -969,7 +998,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial, L->fmt.act);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -1384,6 +1413,8 @@ extern "C" rmoe_status rmoe_moe_forward(rmoe_layer* L, const void* x, int32_t x_
                                         float* out, int32_t* ids_out, float* w_out, void* stream) {
   rmoe_status s = check_ready(L, "rmoe_moe_forward", T, x_dtype);
   if (s != RMOE_OK) return s;
+  if (L->hr != L->desc.hidden)
+    return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: a latent layer (router_hidden != hidden) runs through rmoe_latent_moe");
   if (T == 0) return RMOE_OK;
   if (!x || !out) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward: null x/out");
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
@@ -1394,6 +1425,28 @@ extern "C" rmoe_status rmoe_moe_forward(rmoe_layer* L, const void* x, int32_t x_
 // the expert loop of glm52::moe::moe with its Routing (apply_single_expert, src/glm52/moe.rs:463-513).
 // Slots naming an expert that is not resident here (or -1) contribute nothing, so expert-parallel
 // ranks run it on the token rows they receive.
+// The expert products for the routing already in L->ids / L->rw (T tokens of x, `hs`: with
+// the shared expert): activation prep, dispatch, gate/up, down, combine into out.
+static rmoe_status experts_for_routing(rmoe_layer* L, const void* x, int xdt, int T, bool hs, float* out,
+                                       cudaStream_t st) {
+  const rmoe_layer_desc& D = L->desc;
+  const bool gated = hs && D.shared_gated;
+  const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
+  cudaError_t e = launch_prep_tokens(x, xdt, T, D.hidden, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr, L->xq,
+                                     L->xexp, L->gate, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
+  rmoe_status s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs);
+  if (s != RMOE_OK) return s;
+  StageMarks marks(L, st);
+  const bool prof = L->profiling;
+  L->profiling = false;  // (stage events cover rmoe_moe_forward only)
+  int launches = 0;
+  s = enqueue_experts(L, x, xdt, T, mt, hs, false, false, out, st, marks, &launches);
+  L->profiling = prof;
+  L->stats.kernel_launches += launches;
+  return s;
+}
+
 extern "C" rmoe_status rmoe_moe_forward_routed(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T,
                                                const int32_t* ids, const float* weights, int32_t with_shared,
                                                float* out, void* stream) {
@@ -1423,25 +1476,66 @@ extern "C" rmoe_status rmoe_moe_forward_routed(rmoe_layer* L, const void* x, int
     x = L->x_dev;
     out = L->out_dev;
   }
-  const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
   const size_t n = static_cast<size_t>(T) * k;
   RMOE_CUDA(cudaMemcpyAsync(L->ids, ids, n * 4, cudaMemcpyDefault, st), "routed ids");
   RMOE_CUDA(cudaMemcpyAsync(L->rw, weights, n * 4, cudaMemcpyDefault, st), "routed weights");
-  cudaError_t e = launch_prep_tokens(x, xdt, T, H, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr, L->xq,
-                                     L->xexp, L->gate, st);
-  if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
-  if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs)) != RMOE_OK) return s;
-  StageMarks marks(L, st);
-  const bool prof = L->profiling;
-  L->profiling = false;  // (stage events cover rmoe_moe_forward only)
-  int launches = 0;
-  s = enqueue_experts(L, x, xdt, T, mt, hs, false, false, out, st, marks, &launches);
-  L->profiling = prof;
-  if (s != RMOE_OK) return s;
+  if ((s = experts_for_routing(L, x, xdt, T, hs, out, st)) != RMOE_OK) return s;
   if (staged)
     RMOE_CUDA(cudaMemcpyAsync(out_user, out, static_cast<size_t>(T) * H * 4, cudaMemcpyDeviceToDevice, st),
               "unstage out");
-  L->stats.kernel_launches += launches;
+  L->stats.forward_calls++;
+  L->stats.tokens_routed += T;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_upload_latent(rmoe_layer* L, const void* down_proj, const void* up_proj, int32_t proj_dtype,
+                                          const float* norm, float eps) {
+  const char* what = "rmoe_upload_latent";
+  if (!L || !down_proj || !up_proj) return fail(RMOE_INVALID_ARG, "%s: null argument", what);
+  if (L->hr == L->desc.hidden) return fail(RMOE_INVALID_ARG, "%s: not a latent layer (router_hidden == hidden)", what);
+  if (proj_dtype != RMOE_F32 && proj_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: dtype %d", what, proj_dtype);
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const size_t bytes = static_cast<size_t>(L->desc.hidden) * L->hr * (proj_dtype == RMOE_BF16 ? 2 : 4);
+  RMOE_CUDA(cudaMemcpy(L->lat_down, down_proj, bytes, cudaMemcpyDefault), "latent down_proj");
+  RMOE_CUDA(cudaMemcpy(L->lat_up, up_proj, bytes, cudaMemcpyDefault), "latent up_proj");
+  L->lat_dtype = proj_dtype == RMOE_BF16 ? kBF16 : kF32;
+  L->lat_has_norm = norm != nullptr;
+  if (norm) RMOE_CUDA(cudaMemcpy(L->lat_norm, norm, static_cast<size_t>(L->desc.hidden) * 4, cudaMemcpyDefault), "latent norm");
+  L->lat_eps = eps;
+  L->has_latent = true;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_latent_moe(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T, float* out,
+                                       int32_t* ids_out, float* w_out, void* stream) {
+  const char* what = "rmoe_latent_moe";
+  rmoe_status s = check_ready(L, what, T, x_dtype);
+  if (s != RMOE_OK) return s;
+  if (!L->has_latent) return fail(RMOE_INVALID_ARG, "%s: latent projections were never uploaded", what);
+  if (T == 0) return RMOE_OK;
+  if (!x || !out) return fail(RMOE_INVALID_ARG, "%s: null x/out", what);
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(RMOE_INVALID_ARG, "%s: x and out must be 16-byte aligned", what);
+  if ((s = check_uploaded(L)) != RMOE_OK) return s;
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int H = L->desc.hidden, Hr = L->hr, k = L->desc.topk;
+  const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
+  // routing at the full width, on x itself (src/kimi_k3/moe.rs:84-86)
+  if ((s = route_into(L, x, x_dtype, T, st)) != RMOE_OK) return s;
+  // x_latent = x . down^T (:91-92)
+  cudaError_t e = launch_latent_proj(L->lat_down, L->lat_dtype, x, xdt, T, Hr, H, L->lat_x, st);
+  if (e != cudaSuccess) return cuda_fail(e, "latent down projection");
+  // the routed experts at the latent width (:94-104); no shared expert here (the caller's)
+  if ((s = experts_for_routing(L, L->lat_x, kF32, T, false, L->lat_y, st)) != RMOE_OK) return s;
+  // RMSNorm of each token's summed routed row (:106-110), then out = y . up^T (:112)
+  if (L->lat_has_norm && (e = launch_rmsnorm_rows(L->lat_y, T, H, L->lat_norm, L->lat_eps, st)) != cudaSuccess)
+    return cuda_fail(e, "latent norm");
+  if ((e = launch_latent_proj(L->lat_up, L->lat_dtype, L->lat_y, kF32, T, H, Hr, out, st)) != cudaSuccess)
+    return cuda_fail(e, "latent up projection");
+  const size_t n = static_cast<size_t>(T) * k;
+  if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, L->ids, n * 4, cudaMemcpyDeviceToDevice, st), "latent ids");
+  if (w_out) RMOE_CUDA(cudaMemcpyAsync(w_out, L->rw, n * 4, cudaMemcpyDeviceToDevice, st), "latent weights");
   L->stats.forward_calls++;
   L->stats.tokens_routed += T;
   return RMOE_OK;
@@ -1452,6 +1546,8 @@ extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, 
                                              float* w_host) {
   rmoe_status s = check_ready(L, "rmoe_moe_forward_host", T, x_dtype);
   if (s != RMOE_OK) return s;
+  if (L->hr != L->desc.hidden)
+    return fail(RMOE_INVALID_ARG, "rmoe_moe_forward_host: a latent layer runs through rmoe_latent_moe");
   if (T == 0) return RMOE_OK;
   if (!x_host || !out_host) return fail(RMOE_INVALID_ARG, "rmoe_moe_forward_host: null x/out");
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");

@@ -116,6 +116,20 @@ __device__ __forceinline__ float sigmoid_ref(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32(-x)));
 }
 __device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, exp_f32(-x))); }
+// The expert gate (glm52::moe::Activation::combine, src/glm52/moe.rs:58-70): SiLU, or Kimi
+// K3's SituAndMul beta tanh(g / beta) sigmoid(g) * u' (u' = lb tanh(u / lb) with a linear beta lb,
+// kimi_linear::ops::situ_and_mul). kind: 0 SiLU, 1 Situ. `exact_silu` selects the correctly
+// rounded exp of the reference for SiLU (the CUDA-core paths keep it; the tensor-core paths
+// expand h into E2M1 terms next and use expf).
+__device__ __forceinline__ float silu_f32(float x);
+__device__ __forceinline__ float act_gate(int kind, float beta, float linear_beta, float g, float u,
+                                          bool exact_silu) {
+  if (kind == 0) return __fmul_rn(exact_silu ? silu_ref(g) : silu_f32(g), u);
+  const float uu = linear_beta > 0.0f ? linear_beta * tanhf(u / linear_beta) : u;
+  const float situ = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
+  return situ * uu;
+}
+
 // silu with the single-precision expf (<= 2 ulp): for h that is expanded into E2M1 terms next
 // (~11 bits kept), where the reference's correctly rounded exp buys nothing and costs a
 // double-precision exp per element.

@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(256) gemv_gate_up_kernel(ExpertTable tab, Expe
         const float unscale = exp2i(-xexp[tok[m]]);
         const float g = (lane == 0 ? acc[0][m] : acc[1][m]) * unscale;
         const float u = (lane == 0 ? acc[2][m] : acc[3][m]) * unscale;
-        const float hv = __fmul_rn(silu_ref(g), u);
+        const float hv = act_gate(f.act.kind, f.act.beta, f.act.linear_beta, g, u, true);
         h[static_cast<size_t>(p0 + m) * h_ld + r0 + lane] = hv;
         atomicMax(hmax + p0 + m, __float_as_uint(fabsf(hv)));
       }

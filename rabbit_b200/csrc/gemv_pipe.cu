@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe_kernel(PipeArgs a) 
           if (lane == m) {
             const float unscale = exp2i(-xe[m]);
             const float g = acc[0][m] * unscale, u = acc[NR > 1 ? 1 : 0][m] * unscale;
-            const float hv = __fmul_rn(silu_ref(g), u);
+            const float hv = act_gate(a.f.act.kind, a.f.act.beta, a.f.act.linear_beta, g, u, true);
             a.out[static_cast<size_t>(p0 + m) * a.out_ld + r] = hv;
             atomicMax(const_cast<uint32_t*>(a.hmax) + p0 + m, __float_as_uint(fabsf(hv)));
           }

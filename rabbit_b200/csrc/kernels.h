@@ -19,10 +19,18 @@ struct ExpertPtrs {
 };
 
 // Format of every expert of a layer.
+// The expert gating activation: kind 0 silu(g) u; kind 1 Kimi K3's SituAndMul,
+// beta tanh(g / beta) sigmoid(g) u' with u' = lb tanh(u / lb) when lb = linear_beta > 0.
+struct ActParams {
+  int kind;
+  float beta, linear_beta;
+};
+
 struct ExpertFormat {
   int fmt;          // kMxfp4 | kInt4g
   int group_size;   // int4 elements per scale (multiple of 32); 32 for MXFP4
   int scale_dtype;  // int4 scale storage kF32 | kBF16
+  ActParams act;    // gating activation of the experts
 };
 
 // Device-side expert table: local routed experts are contiguous, `stride` bytes apart, each
@@ -214,12 +222,19 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st,
                           const int32_t* b_token_rows = nullptr, unsigned long long* trace = nullptr,
-                          const float* partial_in = nullptr);
+                          const float* partial_in = nullptr, ActParams act = ActParams{0, 0.0f, 0.0f});
 // Unit parts of split tiles (floats) a layer must provide for batches of up to 8 tokens.
 size_t moe_tc_partial_floats(int H, int I, int k, int n_slots);
 
 // ---- synthetic bytes (synth.cu) ----
 cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,
                                cudaStream_t st);
+
+// ---- latent MoE wrapper (latent.cu) ----
+// y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)
+cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
+                               cudaStream_t st);
+// v[r] *= w / sqrt(mean(v[r]^2) + eps) for each of `rows` rows of n
+cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st);
 
 }  // namespace rmoe

@@ -82,6 +82,7 @@ struct MoeTcArgs {
   unsigned long long* trace;  // optional: CTA 0's per-stage timestamps [stage][4] (ns)
   int* work;           // [4] units claimed, CTAs finished, h slices ready, parts stored (zero between launches)
   int unit_stages;     // stages per claimed unit (split tiles when smaller than a tile)
+  ActParams act;       // gating activation (gate/up epilogue, h from the parts)
   // down kernels after a split gate/up pass: the gate/up unit parts, summed here into h terms
   const float* partial_in;
   int gu_split;        // 1: gate/up left unit parts (sum them in the prologue)
@@ -186,7 +187,7 @@ __device__ __forceinline__ void h_from_parts(const MoeTcArgs& a, int nch, int hw
         u += __ldcg(base + static_cast<size_t>(j) * 8 * 128 + 64);
       }
       const int p = p0 + t;
-      const float hv = __fmul_rn(silu_f32(g), u) * __ldg(a.perm_w + p);
+      const float hv = act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * __ldg(a.perm_w + p);
       const size_t trow = static_cast<size_t>(4 * p);
       warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2, a.hsf + trow * (a.inter / 32) + i0 / 32,
                   a.inter / 32);
@@ -664,7 +665,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           for (int i = 0; i < 8; i++) {
             const int rr = hb * 32 + 8 * s4 + i;
             const float g = ubuf[rr * 33 + t], u = ubuf[(64 + rr) * 33 + t];
-            h[i] = valid ? __fmul_rn(silu_f32(g), u) * wp : 0.0f;
+            h[i] = valid ? act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * wp : 0.0f;
           }
           const int i0 = mm * 64 + hb * 32;
           const size_t trow = static_cast<size_t>(4 * p);
@@ -888,7 +889,7 @@ static size_t moe_tc_smem(int stages, int b_boxes) {
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st, const int32_t* b_token_rows,
-                          unsigned long long* trace, const float* partial_in) {
+                          unsigned long long* trace, const float* partial_in, ActParams act) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   MoeTcArgs a{};
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.ch_n = d.ch_n; a.n_chunks = d.n_chunks;
@@ -912,6 +913,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   }
   a.ntm_gu = I / 64;
   a.partial_in = partial_in;
+  a.act = act;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, a.b_boxes) > 227 * 1024) stages--;
   a.stages = stages;

@@ -100,7 +100,8 @@ class MoeLayer:
                  topk_group: int = 1, norm_topk: bool = True, routed_scale: float = 1.0,
                  fmt: str = "mxfp4", group_size: int = 32, scale_dtype: str = "f32",
                  shared_gated: bool = False, max_tokens: int = 1, ep_rank: int = 0,
-                 ep_size: int = 1):
+                 ep_size: int = 1, activation: str = "silu", situ_beta: float = 0.0,
+                 situ_linear_beta: float = 0.0, router_hidden: int = 0):
         self.lib = ctx.lib
         self.ctx = ctx
         d = LayerDesc()
@@ -114,11 +115,15 @@ class MoeLayer:
         d.scale_dtype = DT_BF16 if scale_dtype == "bf16" else DT_F32
         d.shared_gated, d.max_tokens = int(shared_gated), max_tokens
         d.ep_rank, d.ep_size = ep_rank, ep_size
+        d.activation = 1 if activation == "situ" else 0
+        d.situ_beta, d.situ_linear_beta = situ_beta, situ_linear_beta
+        d.router_hidden = router_hidden
         self.desc = d
         h = C.c_void_p()
         check(self.lib.rmoe_layer_create(ctx.handle, C.byref(d), C.byref(h)))
         self.handle = h
         self.hidden, self.topk, self.n_experts = hidden, topk, n_experts
+        self.router_hidden = router_hidden or hidden
         self.max_tokens = max_tokens
 
     # ---- lifetime
@@ -233,6 +238,31 @@ class MoeLayer:
         check(self.lib.rmoe_moe_forward_routed(self.handle, _ptr(x), _dtype_code(x), T, _ptr(ids), _ptr(weights),
                                                1 if with_shared else 0, _ptr(out), _stream(stream)))
         return out
+
+    def upload_latent(self, down_proj, up_proj, norm=None, eps=1e-5):
+        """LatentMoeWeights (src/kimi_k3/moe.rs:42-56): down_proj [hidden, router_hidden] and
+        up_proj [router_hidden, hidden] (f32 numpy, or bf16 bits as uint16 numpy / bf16 torch),
+        norm [hidden] f32 or None."""
+        down = down_proj if torch is not None and isinstance(down_proj, torch.Tensor) else np.ascontiguousarray(down_proj)
+        up = up_proj if torch is not None and isinstance(up_proj, torch.Tensor) else np.ascontiguousarray(up_proj)
+        dt = _dtype_code(down)
+        nrm = None if norm is None else np.ascontiguousarray(norm, np.float32)
+        check(self.lib.rmoe_upload_latent(self.handle, _ptr(down), _ptr(up), dt, _ptr(nrm), float(eps)))
+
+    def latent_moe(self, x, out=None, return_routing=False, stream=None):
+        """kimi_k3::moe::latent_moe (src/kimi_k3/moe.rs:64-116): x [T, router_hidden] -> out
+        [T, router_hidden] f32 (routed experts only, the caller adds the shared expert)."""
+        _require_cuda(x)
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty((T, self.router_hidden), dtype=torch.float32, device=x.device)
+        ids = w = None
+        if return_routing:
+            ids = torch.empty((T, self.topk), dtype=torch.int32, device=x.device)
+            w = torch.empty((T, self.topk), dtype=torch.float32, device=x.device)
+        check(self.lib.rmoe_latent_moe(self.handle, _ptr(x), _dtype_code(x), T, _ptr(out), _ptr(ids), _ptr(w),
+                                       _stream(stream)))
+        return (out, ids, w) if return_routing else out
 
     def moe_forward_host(self, x, out=None):
         """Host buffers in and out (x: f32 or bf16 bits as uint16; pinned torch tensors work

@@ -29,6 +29,7 @@ MASK64 = (1 << 64) - 1
 
 # tensor roles inside a stream tag
 ROLE_ROUTER, ROLE_X, ROLE_DATA, ROLE_SCALE, ROLE_ZIPF, ROLE_SHGATE, ROLE_BIAS = 1, 2, 3, 4, 5, 6, 7
+ROLE_LATENT = 8  # latent MoE wrapper: tensor 0 down_proj, 1 up_proj, 2 norm
 GATE, UP, DOWN = 0, 1, 2
 
 
@@ -117,6 +118,24 @@ class MoeConfig:
     int4_scale_sigma: float = 0.01
     bias_sigma: float = 0.01
     n_layers: int = 1
+    # Kimi K3 latent MoE: the router and x are router_hidden wide, the experts `hidden` wide
+    router_hidden: int = 0
+    activation: str = "silu"         # "silu" | "situ" (Kimi K3 SituAndMul)
+    situ_beta: float = 0.0
+    situ_linear_beta: float = 0.0    # 0 = none
+    latent_norm: bool = False
+
+    @property
+    def full_hidden(self) -> int:
+        """Width of the router and of the layer's input x."""
+        return self.router_hidden or self.hidden
+
+    @property
+    def act(self):
+        """The activation as the oracle takes it."""
+        if self.activation == "silu":
+            return ("silu",)
+        return ("situ", self.situ_beta, self.situ_linear_beta or None)
 
     @property
     def fmt_id(self) -> int:
@@ -147,6 +166,17 @@ CONFIGS = {
                              inter=2048, shared_inter=2048, router="sigmoid_grouped",
                              fmt="int4g", shared_gated=False, n_group=8, topk_group=4,
                              routed_scale=2.5, norm_topk=True),
+    # Kimi K3's latent MoE at the real checkpoint's shapes (hidden 7168 routed, experts at 3584,
+    # moe_intermediate 3072, 896 experts, top-16, sigmoid router, Situ beta 4 / linear 25, norm
+    # on; src/kimi_k3/config.rs:255-265). Not a BASELINE config: the supplementary row a14.
+    "c5_k3_latent": MoeConfig("c5_k3_latent", tokens=1, hidden=3584, n_experts=896, topk=16,
+                              inter=3072, shared_inter=0, router="sigmoid_grouped", shared_gated=False,
+                              e8m0_lo=-8, e8m0_hi=-3, router_hidden=7168, activation="situ",
+                              situ_beta=4.0, situ_linear_beta=25.0, latent_norm=True),
+    "c5_tiny_latent": MoeConfig("c5_tiny_latent", tokens=6, hidden=512, n_experts=32, topk=4,
+                                inter=512, shared_inter=0, router="sigmoid_grouped", shared_gated=False,
+                                e8m0_lo=-6, e8m0_hi=-3, router_hidden=1024, activation="situ",
+                                situ_beta=4.0, situ_linear_beta=25.0, latent_norm=True),
 }
 
 
@@ -157,9 +187,9 @@ def _normal_tensor(seed, t, n, sigma, bf16):
 
 def router_weights(cfg: MoeConfig, seed: int = 0, layer: int = 0) -> np.ndarray:
     """[E, H] f32 (bf16-representable when the config is bf16): N(0, 0.02)."""
-    n = cfg.n_experts * cfg.hidden
+    n = cfg.n_experts * cfg.full_hidden
     return _normal_tensor(seed, tag(layer, ROLE_ROUTER), n, 0.02, cfg.bf16_inputs).reshape(
-        cfg.n_experts, cfg.hidden)
+        cfg.n_experts, cfg.full_hidden)
 
 
 def activations(cfg: MoeConfig, seed: int = 0, layer: int = 0, tokens: int | None = None,
@@ -167,7 +197,7 @@ def activations(cfg: MoeConfig, seed: int = 0, layer: int = 0, tokens: int | Non
     """[T, H] f32 (bf16-representable when the config is bf16): N(0, 1)."""
     t = cfg.tokens if tokens is None else tokens
     key = stream_key(seed, tag(layer, ROLE_X))
-    h = cfg.hidden
+    h = cfg.full_hidden
     # token rows are independent slices of one stream, so any token range can be regenerated
     z = normals_range(key, token_offset * h, t * h).astype(np.float32)
     z = round_bf16(z) if cfg.bf16_inputs else z
@@ -207,6 +237,19 @@ def correction_bias(cfg: MoeConfig, seed: int = 0, layer: int = 0) -> np.ndarray
         return None
     return (normals(stream_key(seed, tag(layer, ROLE_BIAS)), cfg.n_experts) *
             cfg.bias_sigma).astype(np.float32)
+
+
+def latent_weights(cfg: MoeConfig, seed: int = 0, layer: int = 0):
+    """(down_proj [hidden, router_hidden], up_proj [router_hidden, hidden]) as bf16-representable
+    f32 with N(0, 1/fan_in) entries, and the norm weight [hidden] = 1 + 0.1 N(0, 1) (None when
+    the config has no norm)."""
+    rh, h = cfg.router_hidden, cfg.hidden
+    down = _normal_tensor(seed, tag(layer, ROLE_LATENT, 0, 0), h * rh, 1.0 / math.sqrt(rh), True).reshape(h, rh)
+    up = _normal_tensor(seed, tag(layer, ROLE_LATENT, 0, 1), rh * h, 1.0 / math.sqrt(h), True).reshape(rh, h)
+    norm = None
+    if cfg.latent_norm:
+        norm = (1.0 + 0.1 * normals(stream_key(seed, tag(layer, ROLE_LATENT, 0, 2)), h)).astype(np.float32)
+    return down, up, norm
 
 
 def shared_gate(cfg: MoeConfig, seed: int = 0, layer: int = 0) -> np.ndarray | None:
@@ -291,7 +334,9 @@ def build_layer(ctx, cfg, max_tokens, seed=0, layer=0, scale_dtype="f32", ep_ran
                     topk_group=cfg.topk_group, norm_topk=cfg.norm_topk,
                     routed_scale=cfg.routed_scale, fmt=cfg.fmt, group_size=cfg.group_size,
                     scale_dtype=scale_dtype, shared_gated=cfg.shared_gated,
-                    max_tokens=max_tokens, ep_rank=ep_rank, ep_size=ep_size)
+                    max_tokens=max_tokens, ep_rank=ep_rank, ep_size=ep_size,
+                    activation=cfg.activation, situ_beta=cfg.situ_beta,
+                    situ_linear_beta=cfg.situ_linear_beta, router_hidden=cfg.router_hidden)
     router = router_weights(cfg, seed, layer)
     if cfg.bf16_inputs:
         L.upload_router(f32_to_bf16_bits(router))
@@ -305,6 +350,9 @@ def build_layer(ctx, cfg, max_tokens, seed=0, layer=0, scale_dtype="f32", ep_ran
         ex = gpu_expert(cfg, eid, seed, layer, scale_dtype=scale_dtype)
         L.upload_expert_dict(eid, ex)
     torch.cuda.synchronize()
+    if cfg.router_hidden:
+        down, up, norm = latent_weights(cfg, seed, layer)
+        L.upload_latent(f32_to_bf16_bits(down), f32_to_bf16_bits(up), norm)
     if cfg.shared_inter:
         sh = gpu_expert(cfg, cfg.n_experts, seed, layer, scale_dtype=scale_dtype)
         L.upload_shared(sh["gate"], sh["gate_scale"], sh["up"], sh["up_scale"], sh["down"],

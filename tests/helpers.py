@@ -50,3 +50,18 @@ def oracle_forward(cfg, x, seed=0, layer=0, scale_dtype="f32"):
                        cfg.topk, cfg.inter, cfg.n_group, cfg.topk_group, cfg.norm_topk,
                        cfg.routed_scale, shared=shared, shared_inter=cfg.shared_inter,
                        fmt=cfg.fmt_id, gs=cfg.group_size)
+
+
+def oracle_latent(cfg, x, seed=0, layer=0):
+    """The reference latent MoE (kimi_k3::moe::latent_moe) for x [T, router_hidden]: (out, ids, w)."""
+    from oracle import oracle as orc
+
+    router = synth.router_weights(cfg, seed, layer)
+    bias = synth.correction_bias(cfg, seed, layer)
+    ids, _ = orc.glm_route(x, router, bias, x.shape[0], cfg.full_hidden, cfg.n_experts, cfg.topk, cfg.n_group,
+                           cfg.topk_group, cfg.norm_topk, cfg.routed_scale)
+    experts = {int(e): synth.expert(cfg, int(e), seed, layer) for e in np.unique(ids) if e >= 0}
+    down, up, norm = synth.latent_weights(cfg, seed, layer)
+    return orc.latent_moe(x, router, bias, experts, cfg.n_experts, cfg.topk, cfg.n_group, cfg.topk_group,
+                          cfg.norm_topk, cfg.routed_scale, down, up, norm, 1e-5, cfg.hidden, cfg.inter,
+                          act=cfg.act, fmt=cfg.fmt_id, gs=cfg.group_size)
