@@ -305,6 +305,58 @@ def run_ep(args, ctx, dev, rank, world, flush):
     return res
 
 
+LATENT_CFG = "c5_k3_latent"
+
+
+def run_latent(args, ctx, dev, rank, world, flush):
+    """Row a14: Kimi K3's latent MoE at the real checkpoint's shapes, decoding one token per step
+    (route 896 experts at 7168, down-project to 3584, 16 MXFP4 experts with SituAndMul, RMSNorm,
+    up-project), inputs resident, L2 flushed between steps. Each rank runs its own replica."""
+    import torch
+    import torch.distributed as dist
+
+    from rabbit_b200.synth import build_layer, x_device
+
+    cfg = synth.CONFIGS[LATENT_CFG]
+    L = build_layer(ctx, cfg, max_tokens=1)
+    n_steps = args.warmup + args.latent_steps
+    xs = synth.activations(cfg, tokens=n_steps, token_offset=rank * n_steps)
+    xd = x_device(cfg, xs)
+    out = torch.empty((1, cfg.full_hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        flush.zero_()
+        L.latent_moe(xd[i:i + 1], out=out)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.latent_steps)]
+    for j in range(args.latent_steps):
+        flush.zero_()
+        ev[j][0].record(stream)
+        L.latent_moe(xd[args.warmup + j:args.warmup + j + 1], out=out)
+        ev[j][1].record(stream)
+    torch.cuda.synchronize()
+    us = sum(a.elapsed_time(b) for a, b in ev) * 1e3 / args.latent_steps
+    t = torch.tensor([us], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t.item())
+    # algorithmic bytes of one token: its k distinct experts, the router, both projections, x, out
+    h, rh, i = cfg.hidden, cfg.full_hidden, cfg.inter
+    expert = 3 * h * i // 2 + 3 * h * i // 32
+    nbytes = cfg.topk * expert + cfg.n_experts * rh * 2 + 2 * rh * h * 2 + rh * 2 + rh * 4
+    hbm_peak, _, peak_kind = peaks()
+    res = {"metric": "k3_latent_moe_decode_us_per_token", "value": us, "unit": "us/token",
+           "steps": args.latent_steps, "warmup": args.warmup,
+           "config": {"workload": LATENT_CFG, "router_hidden": rh, "expert_hidden": h, "inter": i,
+                      "n_experts": cfg.n_experts, "topk": cfg.topk, "activation": "situ (beta 4, linear 25)",
+                      "latent_norm": True, "projections": "bf16", "experts": "mxfp4",
+                      "l2": "flushed between steps"},
+           "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (us * 1e-6) / 1e9,
+           "hbm_frac": nbytes / (us * 1e-6) / 1e9 / hbm_peak, "peak_kind": peak_kind}
+    L.close()
+    return res
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -497,6 +549,12 @@ def run_gpu(args):
         layer = None
         torch.cuda.empty_cache()
         line["ep"] = run_ep(args, ctx, dev, rank, world, flush)
+    if not args.no_latent:
+        if layer is not None:
+            layer.close()
+            layer = None
+        torch.cuda.empty_cache()
+        line["latent"] = run_latent(args, ctx, dev, rank, world, flush)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, n, used = cpu_decode_time(dcfg, budget_s=args.cpu_budget, threads=physical_cores())
         line["cpu_baseline"] = {
@@ -524,6 +582,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel stack (config 3)")
     ap.add_argument("--ep-steps", type=int, default=5)
+    ap.add_argument("--no-latent", action="store_true", help="skip the K3 latent MoE decode (row a14)")
+    ap.add_argument("--latent-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--small-experts", type=int, default=0,
                     help="profiling only: resident experts (same shapes); not a bench config")

@@ -324,6 +324,8 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   f.act = ActParams{D.activation, D.situ_beta, D.situ_linear_beta > 0.0f ? D.situ_linear_beta : 0.0f};
   if (D.router_hidden < 0 || (D.router_hidden && D.router_hidden % 32))
     return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: router_hidden %d (a multiple of 32)", D.router_hidden);
+  if (D.router_hidden && D.router_hidden != D.hidden && D.hidden > 8192)
+    return fail(RMOE_NOT_SUPPORTED, "rmoe_layer_create: a latent layer's expert width %d exceeds 8192", D.hidden);
   const int ep_size = D.ep_size <= 0 ? 1 : D.ep_size;
   if (D.n_experts % ep_size || D.ep_rank < 0 || D.ep_rank >= ep_size)
     return fail(RMOE_INVALID_ARG, "rmoe_layer_create: ep_rank %d / ep_size %d / n_experts %d", D.ep_rank, ep_size, D.n_experts);
@@ -1432,9 +1434,11 @@ static rmoe_status experts_for_routing(rmoe_layer* L, const void* x, int xdt, in
   const rmoe_layer_desc& D = L->desc;
   const bool gated = hs && D.shared_gated;
   const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
-  cudaError_t e = launch_prep_tokens(x, xdt, T, D.hidden, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr, L->xq,
-                                     L->xexp, L->gate, st);
-  if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
+  if (!L->use_tc || gated) {  // (the tensor-core path forms its own activation terms)
+    cudaError_t e = launch_prep_tokens(x, xdt, T, D.hidden, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr, L->xq,
+                                       L->xexp, L->gate, st);
+    if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
+  }
   rmoe_status s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs);
   if (s != RMOE_OK) return s;
   StageMarks marks(L, st);

@@ -140,25 +140,27 @@ __global__ void __launch_bounds__(1024) dispatch_place_kernel(
                            : n_routed_chunks * tpc_gu + (nc - n_routed_chunks) * tpc_gu_shared;
     d.ch_task_dn[nc] = nc * tpc_dn;
   }
-  // first-occurrence order of the local experts that were picked
-  int n_u = 0;
-  for (int el = tid; el < n_loc; el += blockDim.x) {
-    const int cnt = s_off[el + 1] - s_off[el];
-    if (cnt == 0) continue;
-    const int f = d.first_occ[el];
-    int r = 0;
-    for (int o = 0; o < n_loc; o++)
-      if (s_off[o + 1] > s_off[o] && d.first_occ[o] < f) r++;
-    d.uniq[r] = e_begin + el;
-    n_u++;
+  // first-occurrence order of the local experts that were picked: slot q is the first
+  // occurrence of its expert iff first_occ[expert] == q, so the order is a prefix count over
+  // the slots (O(T k), not a scan of every expert per picked expert)
+  {
+    int carry = 0;
+    for (int base = 0; base < T * k; base += blockDim.x) {
+      const int q = base + tid;
+      int flag = 0, e = -1;
+      if (q < T * k) {
+        e = ids[q];
+        const int el = e - e_begin;
+        flag = e >= 0 && el >= 0 && el < n_loc && d.first_occ[el] == q;
+      }
+      int ex;
+      const int tot = block_exclusive_scan(flag, ex);
+      if (flag) d.uniq[carry + ex] = e;
+      carry += tot;
+      __syncthreads();
+    }
+    if (tid == 0) d.n_uniq[0] = carry;
   }
-  // count of picked experts
-  __shared__ int s_nu;
-  if (tid == 0) s_nu = 0;
-  __syncthreads();
-  atomicAdd(&s_nu, n_u);
-  __syncthreads();
-  if (tid == 0) d.n_uniq[0] = s_nu;
   // stable placement
   for (int q = tid; q < T * k; q += blockDim.x) {
     const int e = ids[q];

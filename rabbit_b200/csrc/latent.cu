@@ -45,16 +45,23 @@ __global__ void __launch_bounds__(256) latent_proj_kernel(const void* __restrict
       float acc[kProjTok];
 #pragma unroll
       for (int t = 0; t < kProjTok; t++) acc[t] = 0.0f;
-      for (int k = lane * 8; k < K; k += 256) {
-        float wv[8];
-        load_w8<WD>(w, static_cast<size_t>(n) * K + k, wv);
+      for (int k0 = lane * 8; k0 < K; k0 += 4 * 256) {
+        float wv[4][8];  // four 16-byte weight loads in flight per lane
 #pragma unroll
-        for (int t = 0; t < kProjTok; t++) {
-          if (t >= nt) break;
-          float xv[8];
-          load_w8<XD>(x, static_cast<size_t>(t0 + t) * K + k, xv);
+        for (int u = 0; u < 4; u++)
+          if (k0 + u * 256 < K) load_w8<WD>(w, static_cast<size_t>(n) * K + k0 + u * 256, wv[u]);
 #pragma unroll
-          for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[j], acc[t]);
+        for (int u = 0; u < 4; u++) {
+          const int k = k0 + u * 256;
+          if (k >= K) break;
+#pragma unroll
+          for (int t = 0; t < kProjTok; t++) {
+            if (t >= nt) break;
+            float xv[8];
+            load_w8<XD>(x, static_cast<size_t>(t0 + t) * K + k, xv);
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[u][j], acc[t]);
+          }
         }
       }
 #pragma unroll
@@ -67,17 +74,23 @@ __global__ void __launch_bounds__(256) latent_proj_kernel(const void* __restrict
   }
 }
 
-// In place, one block per row: v *= r * w with r = 1 / sqrt(mean(v^2) + eps), the mean of
-// squares accumulated in f64 as the reference does.
-__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(float* __restrict__ v, int n, const float* __restrict__ w,
-                                                           float eps) {
-  __shared__ double part[8];
+// In place, one 1024-thread block per row: v *= r * w with r = 1 / sqrt(mean(v^2) + eps), the
+// mean of squares accumulated in f64 as the reference does. The row is read once into registers
+// (up to kNormPer values per thread, loads issued together).
+constexpr int kNormPer = 8;
+__global__ void __launch_bounds__(1024) rmsnorm_rows_kernel(float* __restrict__ v, int n, const float* __restrict__ w,
+                                                            float eps) {
+  __shared__ double part[32];
   float* row = v + static_cast<size_t>(blockIdx.x) * n;
-  double s = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const double a = row[i];
-    s += a * a;
+  float a[kNormPer];
+#pragma unroll
+  for (int j = 0; j < kNormPer; j++) {
+    const int i = threadIdx.x + j * blockDim.x;
+    a[j] = i < n ? row[i] : 0.0f;
   }
+  double s = 0.0;
+#pragma unroll
+  for (int j = 0; j < kNormPer; j++) s += static_cast<double>(a[j]) * static_cast<double>(a[j]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
   if (threadIdx.x % 32 == 0) part[threadIdx.x / 32] = s;
@@ -86,7 +99,11 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(float* __restrict__ v
   for (int i = 0; i < static_cast<int>(blockDim.x / 32); i++) tot += part[i];
   const float ms = static_cast<float>(tot / static_cast<double>(n));
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) row[i] = row[i] * __fmul_rn(r, w[i]);
+#pragma unroll
+  for (int j = 0; j < kNormPer; j++) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n) row[i] = a[j] * __fmul_rn(r, w[i]);
+  }
 }
 
 }  // namespace
@@ -105,7 +122,8 @@ cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_
 
 cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(v, n, w, eps);
+  if (n > 1024 * kNormPer) return cudaErrorInvalidValue;
+  rmsnorm_rows_kernel<<<rows, 1024, 0, st>>>(v, n, w, eps);
   return cudaGetLastError();
 }
 

@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "select.cuh"
 
 namespace rmoe {
 
@@ -118,9 +119,102 @@ __global__ void __launch_bounds__(256) router_exact_tiled_kernel(
   }
 }
 
+// Few tokens: one warp per (token, expert) chain, 8 experts of one token per 256-thread block
+// with the token's row in shared memory. Per 1024-element chunk the lanes form the products
+// (fmul, coalesced weight loads) into the warp's buffer and lane 0 adds them in k order; the
+// next chunk's weights are loaded before that serial run, so their latency hides behind it.
+// The chain (x[k] * w[e][k] added from -0.0 in k order) is exactly the reference matmul's.
+constexpr int kRwChunk = 1024;
+template <int D>
+__device__ __forceinline__ void load8_t(const void* p, size_t i, float (&v)[8]) {
+  if (D == kBF16) {
+    const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
+    const uint32_t q[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      v[2 * j] = __uint_as_float(q[j] << 16);
+      v[2 * j + 1] = __uint_as_float(q[j] & 0xffff0000u);
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// H % 1024 == 0. Lane l holds elements u * 256 + 8 l .. + 7 of a chunk (u < 4), 16-byte loads.
+template <int XD, int WD>
+__global__ void __launch_bounds__(256) router_exact_warp_kernel(const void* __restrict__ x, const void* __restrict__ w,
+                                                                float* __restrict__ logits, int T, int H, int E) {
+  extern __shared__ __align__(16) float rw_smem[];
+  float* xs = rw_smem;                                           // [H]
+  const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float* buf = rw_smem + H + wi * kRwChunk;                     // [kRwChunk] per warp
+  const int blocks_per_t = (E + 7) / 8;
+  const int t = blockIdx.x / blocks_per_t;
+  const int e = (blockIdx.x % blocks_per_t) * 8 + wi;
+  for (int k = threadIdx.x * 8; k < H; k += blockDim.x * 8) {
+    float v[8];
+    load8_t<XD>(x, static_cast<size_t>(t) * H + k, v);
+#pragma unroll
+    for (int j = 0; j < 8; j++) xs[k + j] = v[j];
+  }
+  __syncthreads();
+  if (e >= E) return;
+  const size_t wrow = static_cast<size_t>(e) * H;
+  float wv[4][8];
+  auto load_chunk = [&](int c0) {
+#pragma unroll
+    for (int u = 0; u < 4; u++) load8_t<WD>(w, wrow + c0 + u * 256 + lane * 8, wv[u]);
+  };
+  float acc = -0.0f;
+  load_chunk(0);
+  for (int c0 = 0; c0 < H; c0 += kRwChunk) {
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int kk = u * 256 + lane * 8 + j;
+        buf[kk] = __fmul_rn(xs[c0 + kk], wv[u][j]);
+      }
+    if (c0 + kRwChunk < H) load_chunk(c0 + kRwChunk);
+    __syncwarp();
+    if (lane == 0) {
+      // 16 products per step, their shared-memory loads issued before the dependent adds
+      for (int i = 0; i < kRwChunk; i += 16) {
+        float4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) q[u] = *reinterpret_cast<const float4*>(buf + i + 4 * u);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          acc = __fadd_rn(acc, q[u].x);
+          acc = __fadd_rn(acc, q[u].y);
+          acc = __fadd_rn(acc, q[u].z);
+          acc = __fadd_rn(acc, q[u].w);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  if (lane == 0) logits[static_cast<size_t>(t) * E + e] = acc;
+}
+
 cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
                                        float* logits, int T, int H, int E, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
+  const size_t warp_smem = (static_cast<size_t>(H) + 8 * kRwChunk) * 4;
+  if (T <= 16 && H % kRwChunk == 0 && warp_smem <= 160 * 1024) {
+    void (*kern)(const void*, const void*, float*, int, int, int) =
+        x_dtype == kBF16 ? (w_dtype == kBF16 ? router_exact_warp_kernel<kBF16, kBF16> : router_exact_warp_kernel<kBF16, kF32>)
+                         : (w_dtype == kBF16 ? router_exact_warp_kernel<kF32, kBF16> : router_exact_warp_kernel<kF32, kF32>);
+    if (warp_smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(warp_smem));
+      if (e != cudaSuccess) return e;
+    }
+    kern<<<T * ((E + 7) / 8), 256, warp_smem, st>>>(x, w, logits, T, H, E);
+    return cudaGetLastError();
+  }
   if (T >= 64) {
     dim3 grid((E + 63) / 64, (T + 63) / 64);
     router_exact_tiled_kernel<<<grid, 256, 0, st>>>(x, x_dtype, w, w_dtype, logits, T, H, E);
@@ -343,6 +437,67 @@ __global__ void topk_grouped_kernel(const float* __restrict__ logits, const floa
   }
 }
 
+// Ungrouped sigmoid router (n_group <= 1): one 1024-thread block per token, one thread per
+// expert, with a certificate. The choice values c = sigmoid(logit) + bias are first bounded from
+// the single-precision expf (<= 2 ulp; the bound used is 2^-20 relative, widened outward with
+// directed rounding), which decides who can be in the top k at all: every expert whose upper
+// bound reaches the k-th largest lower bound. Only those contenders evaluate the reference's
+// correctly rounded sigmoid (an f64 exp, slow on this part, here one per contender thread in
+// parallel) and are ranked exactly by (c desc, id asc); the weights are those exact sigmoids,
+// normalized and scaled as in glm52::moe::route. Both selections are block-wide warp-reduction
+// rounds (select.cuh).
+__global__ void __launch_bounds__(1024) topk_sigmoid_block_kernel(const float* __restrict__ logits,
+                                                                  const float* __restrict__ bias, int T, int E, int k,
+                                                                  int norm_topk, float routed_scale,
+                                                                  int32_t* __restrict__ ids, float* __restrict__ wout) {
+  __shared__ float c1[32 * 32], c2[32 * 32];
+  __shared__ int c1i[32 * 32], c2i[32 * 32];
+  __shared__ int sel_id[32], lo_id[32];
+  __shared__ float sel_v[32], lo_v[32];
+  __shared__ float s_sig[1024];
+  const int t = blockIdx.x, e = threadIdx.x;
+  const bool valid = e < E;
+  const int id = valid ? e : 0x40000000 + e;
+  const float* row = logits + static_cast<size_t>(t) * E;
+  const int kk = min(k, E);
+  float x = 0.0f, b = 0.0f, lo = -INFINITY, hi = -INFINITY;
+  if (valid) {
+    x = row[e];
+    b = bias ? bias[e] : 0.0f;
+    const float sf = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    // |sf - sigmoid| <= 3 * 2^-23 sf (expf 2 ulp, then two roundings) and the reference's value
+    // is within 1.5 * 2^-23 sf of the same sigmoid: 2^-20 sf covers both, with room
+    const float d = fmaf(sf, 9.54e-7f, 1e-37f);
+    lo = __fadd_rd(__fsub_rd(sf, d), b);
+    hi = __fadd_ru(__fadd_ru(sf, d), b);
+  }
+  block_select2(lo, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  const float Lk = sel_v[kk - 1];
+  float sx = 0.0f, cx = -INFINITY;
+  if (valid && hi >= Lk) {
+    sx = sigmoid_ref(x);
+    cx = __fadd_rn(sx, b);
+  }
+  s_sig[e] = sx;
+  __syncthreads();
+  block_select2(cx, cx, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float w = lane < kk ? s_sig[sel_id[lane]] : 0.0f;
+    if (norm_topk) {
+      float sum = -0.0f;
+      for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, w, j));
+      sum = __fadd_rn(sum, 1e-20f);
+      w = __fdiv_rn(w, sum);
+    }
+    w = __fmul_rn(w, routed_scale);
+    if (lane < k) {
+      ids[static_cast<size_t>(t) * k + lane] = lane < kk ? sel_id[lane] : -1;
+      wout[static_cast<size_t>(t) * k + lane] = lane < kk ? w : 0.0f;
+    }
+  }
+}
+
 template <int PL>
 static void launch_grouped_pl(const float* logits, const float* bias, int T, int E, int k,
                               int n_group, int topk_group, int norm_topk, float routed_scale,
@@ -359,6 +514,10 @@ cudaError_t launch_topk_grouped(const float* logits, const float* bias, int T, i
   if (T <= 0) return cudaSuccess;
   if (E > kMaxE || k > 32 || k < 1 || n_group > 32) return cudaErrorInvalidValue;
   if (n_group > 1 && E % n_group != 0) return cudaErrorInvalidValue;
+  if (n_group <= 1) {
+    topk_sigmoid_block_kernel<<<T, 1024, 0, st>>>(logits, bias, T, E, k, norm_topk, routed_scale, ids, w);
+    return cudaGetLastError();
+  }
   if (E <= 32) launch_grouped_pl<1>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
   else if (E <= 64) launch_grouped_pl<2>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
   else if (E <= 128) launch_grouped_pl<4>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
