@@ -4,8 +4,10 @@
 // src/kimi_linear/ops.rs:46-53), out = y . up^T after them.
 //
 // The projections are memory-bound matrix-vector products for decode-sized T: one warp per
-// output row streams that row of W once (16-byte loads) and multiplies it against up to eight
-// tokens at a time (x stays in L1/L2; larger T take several passes over W).
+// output row streams that row of W once (16-byte loads, four in flight per lane) against the
+// tokens of x staged in shared memory, eight tokens per pass (larger T: several passes over W).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,44 +33,63 @@ __device__ __forceinline__ void load_w8(const void* w, size_t i, float (&v)[8]) 
   }
 }
 
-constexpr int kProjTok = 8;  // tokens per pass over W
+constexpr int kProjTok = 8;        // tokens per pass over W
+constexpr int kProjWarps = 16;     // output rows per block
+constexpr int kProjSmem = 96 * 1024;
 
-// y[t][n] = sum_k x[t][k] w[n][k] for tokens t0 .. t0 + nt - 1 (nt <= kProjTok); K % 8 == 0.
+// y[t][n] = sum_k x[t][k] w[n][k]; K % 8 == 0. Each block stages up to `tg` tokens of x in
+// shared memory (f32) and its 16 warps each stream one row of W against them.
 template <int WD, int XD>
-__global__ void __launch_bounds__(256) latent_proj_kernel(const void* __restrict__ w, const void* __restrict__ x,
-                                                          int T, int K, int N, float* __restrict__ y) {
-  const int lane = threadIdx.x % 32;
-  const int warps = gridDim.x * (blockDim.x / 32);
-  for (int n = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; n < N; n += warps) {
-    for (int t0 = 0; t0 < T; t0 += kProjTok) {
-      const int nt = min(kProjTok, T - t0);
-      float acc[kProjTok];
+__global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void* __restrict__ w,
+                                                                      const void* __restrict__ x, int T, int K, int N,
+                                                                      int tg, float* __restrict__ y) {
+  extern __shared__ __align__(16) float px[];  // [tg][K]
+  const int lane = threadIdx.x % 32, wi = threadIdx.x / 32;
+  for (int n0 = blockIdx.x * kProjWarps; n0 < N; n0 += gridDim.x * kProjWarps) {
+    const int n = n0 + wi;
+    for (int t0 = 0; t0 < T; t0 += tg) {
+      const int nt = min(tg, T - t0);
+      __syncthreads();  // (the previous group's reads are done)
+      for (int i = threadIdx.x * 8; i < nt * K; i += blockDim.x * 8) {
+        float v[8];
+        load_w8<XD>(x, static_cast<size_t>(t0) * K + i, v);
 #pragma unroll
-      for (int t = 0; t < kProjTok; t++) acc[t] = 0.0f;
-      for (int k0 = lane * 8; k0 < K; k0 += 4 * 256) {
-        float wv[4][8];  // four 16-byte weight loads in flight per lane
+        for (int j = 0; j < 8; j++) px[i + j] = v[j];
+      }
+      __syncthreads();
+      if (n >= N) continue;
+      for (int ts = 0; ts < nt; ts += kProjTok) {
+        const int ns = min(kProjTok, nt - ts);
+        float acc[kProjTok];
 #pragma unroll
-        for (int u = 0; u < 4; u++)
-          if (k0 + u * 256 < K) load_w8<WD>(w, static_cast<size_t>(n) * K + k0 + u * 256, wv[u]);
+        for (int t = 0; t < kProjTok; t++) acc[t] = 0.0f;
+        for (int k0 = lane * 8; k0 < K; k0 += 4 * 256) {
+          float wv[4][8];  // four 16-byte weight loads in flight per lane
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int k = k0 + u * 256;
-          if (k >= K) break;
+          for (int u = 0; u < 4; u++)
+            if (k0 + u * 256 < K) load_w8<WD>(w, static_cast<size_t>(n) * K + k0 + u * 256, wv[u]);
 #pragma unroll
-          for (int t = 0; t < kProjTok; t++) {
-            if (t >= nt) break;
-            float xv[8];
-            load_w8<XD>(x, static_cast<size_t>(t0 + t) * K + k, xv);
+          for (int u = 0; u < 4; u++) {
+            const int k = k0 + u * 256;
+            if (k >= K) break;
 #pragma unroll
-            for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[u][j], acc[t]);
+            for (int t = 0; t < kProjTok; t++) {
+              if (t >= ns) break;
+              const float* xr = px + static_cast<size_t>(ts + t) * K + k;
+              const float4 a = *reinterpret_cast<const float4*>(xr);
+              const float4 b = *reinterpret_cast<const float4*>(xr + 4);
+              const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+              for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[u][j], acc[t]);
+            }
           }
         }
-      }
 #pragma unroll
-      for (int t = 0; t < kProjTok; t++) {
-        if (t >= nt) break;
-        const float s = warp_sum(acc[t]);
-        if (lane == 0) y[static_cast<size_t>(t0 + t) * N + n] = s;
+        for (int t = 0; t < kProjTok; t++) {
+          if (t >= ns) break;
+          const float sum = warp_sum(acc[t]);
+          if (lane == 0) y[static_cast<size_t>(t0 + ts + t) * N + n] = sum;
+        }
       }
     }
   }
@@ -111,12 +132,18 @@ __global__ void __launch_bounds__(1024) rmsnorm_rows_kernel(float* __restrict__ 
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
                                cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
-  if (K % 8) return cudaErrorInvalidValue;
-  const int blocks = (N + 7) / 8;
-  if (w_dtype == kBF16 && x_dtype == kBF16) latent_proj_kernel<kBF16, kBF16><<<blocks, 256, 0, st>>>(w, x, T, K, N, y);
-  else if (w_dtype == kBF16) latent_proj_kernel<kBF16, kF32><<<blocks, 256, 0, st>>>(w, x, T, K, N, y);
-  else if (x_dtype == kBF16) latent_proj_kernel<kF32, kBF16><<<blocks, 256, 0, st>>>(w, x, T, K, N, y);
-  else latent_proj_kernel<kF32, kF32><<<blocks, 256, 0, st>>>(w, x, T, K, N, y);
+  if (K % 8 || static_cast<size_t>(K) * 4 > kProjSmem) return cudaErrorInvalidValue;
+  const int tg = std::min(T, static_cast<int>(kProjSmem / (static_cast<size_t>(K) * 4)));
+  const size_t smem = static_cast<size_t>(tg) * K * 4;
+  void (*kern)(const void*, const void*, int, int, int, int, float*) =
+      w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16> : latent_proj_kernel<kBF16, kF32>)
+                       : (x_dtype == kBF16 ? latent_proj_kernel<kF32, kBF16> : latent_proj_kernel<kF32, kF32>);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, 148 * 4);
+  kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y);
   return cudaGetLastError();
 }
 

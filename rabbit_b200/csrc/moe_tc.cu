@@ -797,10 +797,17 @@ static int sm_count() {
   return n;
 }
 
+// Stages per work unit for batches of <= 8 tokens: 4 when that divides the per-expert stage
+// count kst (then it also divides the one-token down projection's run over experts), else whole
+// tiles. (Smaller units balance better on paper but their per-unit epilogue and part traffic
+// cost more than they save: measured at the K3 shapes, kst 7 and 6.)
+static int small_unit_stages(int kst) { return kst % 4 == 0 ? 4 : kst; }
+
 size_t moe_tc_partial_floats(int H, int I, int k, int n_slots) {
   const size_t chunks = static_cast<size_t>(8) * k + 8 + n_slots;  // at most, with <= 8 tokens
-  const size_t gu = chunks * (I / 64) * ((H / kMtKStage + 3) / 4);
-  const size_t dn = chunks * (H / 128) * ((I / kMtKStage + 3) / 4);
+  const int kst_gu = H / kMtKStage, kst_dn = I / kMtKStage;
+  const size_t gu = chunks * (I / 64) * (kst_gu / small_unit_stages(kst_gu));      // units of split tiles
+  const size_t dn = chunks * (H / 128) * (kst_dn / small_unit_stages(kst_dn));
   return (std::max(gu, dn) + 64) * 8 * 128;
 }
 
@@ -905,11 +912,16 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   a.b_tok = b_token_rows;
   a.trace = trace;
   a.work = work;
-  a.unit_stages = mt <= 8 ? 4 : 1 << 30;  // small batches: split tiles into 4-stage units
+  // Small batches split tiles into 4-stage units (small_unit_stages), so ~10 units per SM
+  // balance the streams.
+  const int kst_own = (mode == 0 ? H : I) / kMtKStage;
+  // (the several-token down projection never splits: its epilogue writes whole tiles)
+  a.unit_stages = mt <= 8 && mode != 1 ? small_unit_stages(kst_own) : 1 << 30;
   {
     const int kst_gu = H / kMtKStage;  // the gate/up pass split its tiles exactly when this holds
-    a.gu_split = (mode != 0 && mt <= 8 && kst_gu > 4 && kst_gu % 4 == 0) ? 1 : 0;
-    a.upt_gu = kst_gu / 4;
+    const int u_gu = small_unit_stages(kst_gu);
+    a.gu_split = (mode != 0 && mt <= 8 && u_gu < kst_gu) ? 1 : 0;
+    a.upt_gu = kst_gu / u_gu;
   }
   a.ntm_gu = I / 64;
   a.partial_in = partial_in;
