@@ -981,7 +981,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     // one token: every position reads the token's own term rows (0..3)
     e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
                       L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
-                      L->tc_trace, nullptr, L->fmt.act);
+                      L->tc_trace, L->fmt.act, L->tile_cnt, L->tc_work + 6);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
 
     marks.mark();
@@ -989,7 +989,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     if (T == 1) {
       e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial, L->fmt.act);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -1000,7 +1000,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->partial, L->fmt.act);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;

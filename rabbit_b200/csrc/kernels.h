@@ -222,7 +222,8 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st,
                           const int32_t* b_token_rows = nullptr, unsigned long long* trace = nullptr,
-                          const float* partial_in = nullptr, ActParams act = ActParams{0, 0.0f, 0.0f});
+                          ActParams act = ActParams{0, 0.0f, 0.0f}, int32_t* gu_tile_cnt = nullptr,
+                          int* h_done = nullptr);
 // Unit parts of split tiles (floats) a layer must provide for batches of up to 8 tokens.
 size_t moe_tc_partial_floats(int H, int I, int k, int n_slots);
 

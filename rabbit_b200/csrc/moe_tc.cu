@@ -83,11 +83,11 @@ struct MoeTcArgs {
   int* work;           // [4] units claimed, CTAs finished, h slices ready, parts stored (zero between launches)
   int unit_stages;     // stages per claimed unit (split tiles when smaller than a tile)
   ActParams act;       // gating activation (gate/up epilogue, h from the parts)
-  // down kernels after a split gate/up pass: the gate/up unit parts, summed here into h terms
-  const float* partial_in;
-  int gu_split;        // 1: gate/up left unit parts (sum them in the prologue)
-  int upt_gu;          // gate/up units per tile
-  int ntm_gu;          // gate/up tiles per chunk (inter / 64)
+  // gate/up with split tiles: parts stored per tile (each part released on this counter; the
+  // last CTA out zeroes them); the CTAs' idle warps form h of a tile once all its parts are in
+  int* gu_tile_cnt;
+  int* h_done;         // gate/up: h items finished (released per item; the down kernel's counter)
+  int h_split;         // down: gate/up split its tiles, its helper warps write h (wait on h_done)
 };
 
 struct StageMeta {
@@ -154,44 +154,55 @@ __device__ __forceinline__ bool epi_all(bool p) {
   return r != 0;
 }
 
-// Down kernels after a split gate/up pass: h of every position from the gate/up unit parts. One
-// warp per (gate/up tile, 32 inter rows): parts added in K order (loads issued four at a time),
-// h = silu(g) u w, written as the four-term operand. `hw` = this warp's index among the `nhw`
-// helper warps of the CTA.
-__device__ __forceinline__ void h_from_parts(const MoeTcArgs& a, int nch, int hw, int nhw, int lane) {
-  const int items = 2 * nch * a.ntm_gu;
-  for (int it = blockIdx.x * nhw + hw; it < items; it += gridDim.x * nhw) {
-    const int tile = it / 2, hf = it % 2;
-    const int c = tile / a.ntm_gu, m = tile % a.ntm_gu;
-    const int p0 = __ldg(a.ch_pos + c), n = __ldg(a.ch_n + c);
-    const int i0 = m * 64 + hf * 32;
-    for (int t = 0; t < n; t++) {
-      const float* base = a.partial_in + static_cast<size_t>(tile) * a.upt_gu * 8 * 128 + t * 128 + hf * 32 + lane;
-      float g = 0.0f, u = 0.0f;
-      int j = 0;
-      for (; j + 4 <= a.upt_gu; j += 4) {
-        float gg[4], uu[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          gg[q] = __ldcg(base + static_cast<size_t>(j + q) * 8 * 128);
-          uu[q] = __ldcg(base + static_cast<size_t>(j + q) * 8 * 128 + 64);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          g += gg[q];
-          u += uu[q];
-        }
+// Gate/up with split tiles: h of one (tile, 32 inter rows) item from the tile's unit parts, once
+// all of them are in (the tile's counter, released per part, reaches the units per tile):
+// parts added in K order (loads issued four at a time), h = act(g, u) w, written as the four-term
+// operand of the down GEMM. One warp.
+__device__ __forceinline__ void h_item(const MoeTcArgs& a, int it, int ntm, int upt, unsigned* err, int lane) {
+  const int tile = it / 2, hf = it % 2;
+  const int c = tile / ntm, m = tile % ntm;
+  const int p0 = __ldg(a.ch_pos + c), n = __ldg(a.ch_n + c);
+  const int i0 = m * 64 + hf * 32;
+  bool ready = true;
+  if (lane == 0) {
+    const uint64_t t0 = global_ns();
+    while (ld_acquire_gpu(a.gu_tile_cnt + tile) < upt) {
+      if (global_ns() - t0 > 2000000000ull) {
+        atomicOr(err, 0x80000u);
+        ready = false;
+        break;
       }
-      for (; j < a.upt_gu; j++) {
-        g += __ldcg(base + static_cast<size_t>(j) * 8 * 128);
-        u += __ldcg(base + static_cast<size_t>(j) * 8 * 128 + 64);
-      }
-      const int p = p0 + t;
-      const float hv = act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * __ldg(a.perm_w + p);
-      const size_t trow = static_cast<size_t>(4 * p);
-      warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2, a.hsf + trow * (a.inter / 32) + i0 / 32,
-                  a.inter / 32);
+      __nanosleep(64);
     }
+  }
+  if (!__shfl_sync(kFull, ready, 0)) return;
+  __syncwarp();
+  for (int t = 0; t < n; t++) {
+    const float* base = a.partial + static_cast<size_t>(tile) * upt * 8 * 128 + t * 128 + hf * 32 + lane;
+    float g = 0.0f, u = 0.0f;
+    int j = 0;
+    for (; j + 4 <= upt; j += 4) {
+      float gg[4], uu[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        gg[q] = __ldcg(base + static_cast<size_t>(j + q) * 8 * 128);
+        uu[q] = __ldcg(base + static_cast<size_t>(j + q) * 8 * 128 + 64);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        g += gg[q];
+        u += uu[q];
+      }
+    }
+    for (; j < upt; j++) {
+      g += __ldcg(base + static_cast<size_t>(j) * 8 * 128);
+      u += __ldcg(base + static_cast<size_t>(j) * 8 * 128 + 64);
+    }
+    const int p = p0 + t;
+    const float hv = act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * __ldg(a.perm_w + p);
+    const size_t trow = static_cast<size_t>(4 * p);
+    warp_terms4(hv, a.ht + trow * (a.inter / 2) + i0 / 2, a.inter / 2, a.hsf + trow * (a.inter / 32) + i0 / 32,
+                a.inter / 32);
   }
 }
 
@@ -389,26 +400,30 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   } else if (warp == 10) {
     // ------------------------------------------------------------------ activation producer
     if (lane == 0) {
-      if (MODE != kModeGateUp) griddep_wait();  // h (written by gate/up)
+      if (MODE != kModeGateUp) {
+        // the activation operand is h, written by gate/up with plain stores: for split tiles by
+        // its helper warps, each finished item released on this kernel's work[2] (acquired here,
+        // without waiting for gate/up's whole grid to complete); else by its epilogue (grid wait)
+        if (a.h_split) {
+          const int items = 2 * nch * (a.inter / 64);
+          const uint64_t t0 = global_ns();
+          while (ld_acquire_gpu(a.work + 2) < items) {
+            if (global_ns() - t0 > 2000000000ull) {
+              atomicOr(a.err, 0x40000u);
+              *abort_flag = 1;
+              break;
+            }
+            __nanosleep(32);
+          }
+        } else {
+          griddep_wait();
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
       if (a.trace && blockIdx.x == 0) a.trace[1720] = global_ns();
       tma_prefetch_desc(&maps.b);
       tma_prefetch_desc(&maps.bs);
       int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
-      if (MODE != kModeGateUp && a.gu_split) {
-        // the activation operand is h: wait until every CTA has written its h slices
-        const uint64_t t0 = global_ns();
-        if (a.trace && blockIdx.x == 0) a.trace[1721] = global_ns();
-        while (ld_acquire_gpu(a.work + 2) < static_cast<int>(gridDim.x)) {
-          if (global_ns() - t0 > 2000000000ull) {
-            atomicOr(a.err, 0x40000u);
-            *abort_flag = 1;
-            break;
-          }
-          __nanosleep(32);
-        }
-        asm volatile("fence.proxy.async.global;" ::: "memory");  // h was written by plain stores
-        if (a.trace && blockIdx.x == 0) a.trace[1722] = global_ns();
-      }
       for (;;) {
         if (!mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x20u)) break;
         const PartRec r = recs[rslot];
@@ -521,12 +536,6 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ B scale factors -> TMEM
-    if (MODE != kModeGateUp && a.gu_split) {
-      // first, with the epilogue warps, h from the gate/up parts (the B operand of every stage)
-      griddep_wait();
-      h_from_parts(a, nch, warp - 2, 8, lane);
-      asm volatile("bar.sync 3, 256;" ::: "memory");
-    }
     const int q = warp & 3;
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
     int i = 0, rslot = 0, rph = 0;
@@ -590,14 +599,6 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     const int et = threadIdx.x - 192;   // 0..127 within the epilogue warps
     const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
     const int row = 32 * q + lane;      // accumulator row (A-tile row)
-    if (MODE != kModeGateUp) griddep_wait();  // gate/up parts (and h) complete
-    if (a.trace && blockIdx.x == 0 && threadIdx.x == 192) a.trace[1723] = global_ns();
-    if (MODE != kModeGateUp && a.gu_split) {
-      h_from_parts(a, nch, 4 + et / 32, 8, lane);  // (with the scale-factor warps)
-      asm volatile("bar.sync 3, 256;" ::: "memory");
-      if (et == 0) red_release_gpu_add(a.work + 2, 1);  // this CTA's h slices are written
-      if (a.trace && blockIdx.x == 0 && et == 0) a.trace[1724] = global_ns();
-    }
     int buf = 0, seen = 0, rslot = 0, rph = 0;
     for (;;) {
       const bool gotr = mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u);
@@ -640,6 +641,11 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         float* pp = a.partial + static_cast<size_t>(r.unit) * 8 * 128;
         if (a.trace && blockIdx.x == 0 && et == 0 && seen <= 4) a.trace[1710 + seen] = global_ns();
         for (int t = 0; t < n; t++) pp[t * 128 + row] = v[t];
+        if (MODE == kModeGateUp && a.gu_tile_cnt) {
+          // the part is in: count it for its tile (a release that nothing here waits for)
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (et == 0) red_release_gpu_add(a.gu_tile_cnt + r.tile, 1);
+        }
         if (a.trace && blockIdx.x == 0 && et == 0 && seen <= 128) a.trace[3072 + (seen - 1) * 4 + 2] = global_ns();
         continue;
       }
@@ -708,6 +714,20 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       }
     }
   }
+  if (MODE == kModeGateUp && upt > 1 && a.gu_tile_cnt && warp >= 2 && warp < 10) {
+    // this CTA's units are done: its scale-factor and epilogue warps finish h of split tiles,
+    // items claimed in tile order from the counter (a tile's item waits for its last part)
+    const int items = 2 * nch * ntm;
+    for (;;) {
+      int it = 0;
+      if (lane == 0) it = atomicAdd(a.work + 2, 1);
+      it = __shfl_sync(kFull, it, 0);
+      if (it >= items || *abort_flag) break;
+      h_item(a, it, ntm, upt, a.err, lane);
+      __syncwarp();
+      if (lane == 0) red_release_gpu_add(a.h_done, 1);  // (the item's stores precede, warp-ordered)
+    }
+  }
   if (a.trace && warp == 6 && lane == 0) a.trace[1024 + 4 * blockIdx.x + 2] = global_ns();
   tc_fence_before();
   __syncthreads();
@@ -724,6 +744,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       a.work[1] = 0;
       a.work[2] = 0;
       a.work[3] = 0;
+      // every h item of this launch is done: zero the tile counters for the next forward
+      if (MODE == kModeGateUp && upt > 1 && a.gu_tile_cnt)
+        for (int i = 0; i < nch * ntm; i++) a.gu_tile_cnt[i] = 0;
     }
   }
   if (a.trace && threadIdx.x == 32) a.trace[1024 + 4 * blockIdx.x + 3] = global_ns();
@@ -896,7 +919,7 @@ static size_t moe_tc_smem(int stages, int b_boxes) {
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st, const int32_t* b_token_rows,
-                          unsigned long long* trace, const float* partial_in, ActParams act) {
+                          unsigned long long* trace, ActParams act, int32_t* gu_tile_cnt, int* h_done) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   MoeTcArgs a{};
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.ch_n = d.ch_n; a.n_chunks = d.n_chunks;
@@ -917,15 +940,10 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   const int kst_own = (mode == 0 ? H : I) / kMtKStage;
   // (the several-token down projection never splits: its epilogue writes whole tiles)
   a.unit_stages = mt <= 8 && mode != 1 ? small_unit_stages(kst_own) : 1 << 30;
-  {
-    const int kst_gu = H / kMtKStage;  // the gate/up pass split its tiles exactly when this holds
-    const int u_gu = small_unit_stages(kst_gu);
-    a.gu_split = (mode != 0 && mt <= 8 && u_gu < kst_gu) ? 1 : 0;
-    a.upt_gu = kst_gu / u_gu;
-  }
-  a.ntm_gu = I / 64;
-  a.partial_in = partial_in;
   a.act = act;
+  a.gu_tile_cnt = gu_tile_cnt;
+  a.h_done = h_done;
+  a.h_split = (mode != 0 && mt <= 8 && small_unit_stages(H / kMtKStage) < H / kMtKStage) ? 1 : 0;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, a.b_boxes) > 227 * 1024) stages--;
   a.stages = stages;
