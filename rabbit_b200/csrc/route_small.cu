@@ -326,6 +326,8 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
     __shared__ int sel_id[RMOE_MAX_TOPK_DEV], lo_id[RMOE_MAX_TOPK_DEV];
     __shared__ float sel_v[RMOE_MAX_TOPK_DEV], lo_v[RMOE_MAX_TOPK_DEV];
     __shared__ float s_lo[1024], s_hi[1024];
+    __shared__ float s_lk;
+    __shared__ int s_nc;
     const int e = threadIdx.x;
     const bool valid = e < E;
     const int id = valid ? e : 0x40000000 + e;
@@ -347,13 +349,16 @@ __global__ void __launch_bounds__(512) prologue_small_kernel(SmallPrologue a, Di
         s_hi[e] = hi;
       }
       // winners by value, and the kk-th largest lower bound
-      block_select2(v, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
-      const float Lk = lo_v[kk - 1];
-      const int n_cont = __syncthreads_count(valid && hi >= Lk);
-      const int r = threadIdx.x;
-      const bool pair_ok = r >= kk - 1 || s_lo[sel_id[r]] > s_hi[sel_id[r + 1]];
-      const bool order_ok = __syncthreads_and(pair_ok);
+      // certified set: the kk-th largest lower bound Lk; exactly kk experts reaching it with
+      // their upper bounds are the top kk, ranked by their values
+      const float Lk = block_kth_largest(lo, id, kk, c1, c1i, &s_lk);
+      const bool cont = valid && hi >= Lk;
+      const int n_cont = __syncthreads_count(cont);
       const bool set_ok = n_cont == kk;
+      if (set_ok) block_rank_few(cont, v, id, kk, c2, c2i, &s_nc, sel_id, sel_v);
+      const int r = threadIdx.x;
+      const bool pair_ok = !set_ok || r >= kk - 1 || s_lo[sel_id[r]] > s_hi[sel_id[r + 1]];
+      const bool order_ok = __syncthreads_and(pair_ok);
       if (!set_ok) {
         // exact chains for every contender, then the selection on exact values
         float ex = -INFINITY;
@@ -826,14 +831,19 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
     s_hi[e] = hi;
   }
   if (a.trace && threadIdx.x == 0) a.trace[3] = global_ns();
-  block_select2(v, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  // certified set: the kk-th largest lower bound Lk; exactly kk experts reaching it with their
+  // upper bounds are the top kk (every other value is below all of theirs), ranked by value
+  __shared__ float s_lk;
+  __shared__ int s_nc;
+  const float Lk = block_kth_largest(lo, id, kk, c1, c1i, &s_lk);
   if (a.trace && threadIdx.x == 0) a.trace[4] = global_ns();
-  const float Lk = lo_v[kk - 1];
-  const int n_cont = __syncthreads_count(valid && hi >= Lk);
-  const int rr = threadIdx.x;
-  const bool pair_ok = rr >= kk - 1 || s_lo[sel_id[rr]] > s_hi[sel_id[rr + 1]];
-  const bool order_ok = __syncthreads_and(pair_ok);
+  const bool cont = valid && hi >= Lk;
+  const int n_cont = __syncthreads_count(cont);
   const bool set_ok = n_cont == kk;
+  if (set_ok) block_rank_few(cont, v, id, kk, c2, c2i, &s_nc, sel_id, sel_v);
+  const int rr = threadIdx.x;
+  const bool pair_ok = !set_ok || rr >= kk - 1 || s_lo[sel_id[rr]] > s_hi[sel_id[rr + 1]];
+  const bool order_ok = __syncthreads_and(pair_ok);
   if (!set_ok) {
     float ex = -INFINITY;
     if (valid && hi >= Lk) {

@@ -75,4 +75,73 @@ __device__ __forceinline__ void block_select2(float v, float v2, int id, int kk,
   __syncthreads();
 }
 
+// The value ranked kk - 1 by (value desc, id asc) over the block (one entry per thread, ids
+// distinct), to every thread: each warp selects its own top kk, warp 0 merges the warps' lists.
+// cand/cand_i: nw * kk scratch entries; s_out: one shared float.
+__device__ __forceinline__ float block_kth_largest(float v, int id, int kk, float* cand, int* cand_i, float* s_out) {
+  const int wi = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nw = blockDim.x / 32;
+  {
+    const uint32_t key = order_key(v);
+    bool taken = false;
+    for (int r = 0; r < kk; r++) {
+      float a;
+      const int w = warp_pick(key, id, v, taken, &a);
+      taken = taken || id == w;
+      if (lane == 0) {
+        cand[wi * kk + r] = a;
+        cand_i[wi * kk + r] = w;
+      }
+    }
+  }
+  __syncthreads();
+  if (wi == 0) {
+    int h = 0;
+    float last = 0.0f;
+    for (int r = 0; r < kk; r++) {
+      const bool has = lane < nw && h < kk;
+      const float hv = has ? cand[lane * kk + h] : -INFINITY;
+      const int hid = has ? cand_i[lane * kk + h] : 0x7fffffff;
+      const int w = warp_pick(has ? order_key(hv) : 0u, hid, hv, !has, &last);
+      if (has && hid == w) h++;
+    }
+    if (lane == 0) *s_out = last;
+  }
+  __syncthreads();
+  return *s_out;
+}
+
+// Exactly kk (<= 32) threads of the block have cont set: their (v, id) ranked by (value desc,
+// id asc) into out_id/out_v[0 .. kk) (one warp ranks them). cv/ci: 32 scratch entries; s_cnt: a
+// shared int.
+__device__ __forceinline__ void block_rank_few(bool cont, float v, int id, int kk, float* cv, int* ci, int* s_cnt,
+                                               int* out_id, float* out_v) {
+  if (threadIdx.x == 0) *s_cnt = 0;
+  __syncthreads();
+  if (cont) {
+    const int slot = atomicAdd(s_cnt, 1);
+    cv[slot] = v;
+    ci[slot] = id;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const bool has = lane < kk;
+    const float hv = has ? cv[lane] : -INFINITY;
+    const int hid = has ? ci[lane] : 0x7fffffff;
+    const uint32_t key = has ? order_key(hv) : 0u;
+    bool taken = !has;
+    for (int r = 0; r < kk; r++) {
+      float a;
+      const int w = warp_pick(key, hid, hv, taken, &a);
+      taken = taken || hid == w;
+      if (lane == 0) {
+        out_id[r] = w;
+        out_v[r] = a;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 }  // namespace rmoe
