@@ -190,6 +190,7 @@ struct rmoe_layer {
   uint8_t* tc_stage = nullptr;   // one expert in the reference layout, before retiling
   unsigned long long* tc_trace = nullptr;  // RMOE_TC_TRACE=1: gate/up stage timestamps of CTA 0
   bool tc_trace_print = true;              // RMOE_TC_TRACE=2: record only (summary on get_stats)
+  bool use_fused = true;                   // one token: the fused gate/up + down kernel (RMOE_DISABLE_FUSED=1: two kernels)
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
@@ -502,6 +503,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     L->tile_cnt_half = max_tiles;
     ALLOC(L->tile_cnt, 2 * max_tiles);
     ALLOC(L->front_counter, 1);
+    if (const char* nf = getenv("RMOE_DISABLE_FUSED")) L->use_fused = nf[0] != '1';
     if (const char* tr = getenv("RMOE_TC_TRACE")) {
       if (tr[0] == '1' || tr[0] == '2') {
         L->tc_trace_print = tr[0] == '1';
@@ -978,6 +980,19 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       if (e != cudaSuccess) return cuda_fail(e, "activation terms");
     }
     marks.mark();
+    if (T == 1 && terms_done && L->use_fused && !L->tc_trace) {
+      // one token after the fused front end: gate/up and down of all its experts in one launch
+      e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
+                                  L->hsf, L->partial, L->partial2, L->tile_cnt, L->tile_cnt + L->tile_cnt_half,
+                                  L->tc_work, L->dev_err, out, L->fmt.act, st);
+      if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
+      marks.mark();
+      marks.mark();
+      marks.mark();
+      marks.mark();
+      launches = 3;  // front, order resolve (side stream), fused experts
+      return RMOE_OK;
+    }
     // one token: every position reads the token's own term rows (0..3)
     e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
                       L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,

@@ -231,6 +231,12 @@ size_t moe_tc_partial_floats(int H, int I, int k, int n_slots);
 cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int lo, int hi,
                                cudaStream_t st);
 
+// One token after the fused front end: gate/up and down of all its experts in one launch.
+cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, int H, int I, const uint8_t* arena,
+                                    size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
+                                    float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
+                                    float* out, ActParams act, cudaStream_t st);
+
 // ---- latent MoE wrapper (latent.cu) ----
 // y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,

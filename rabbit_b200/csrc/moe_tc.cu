@@ -752,6 +752,437 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   if (a.trace && threadIdx.x == 32) a.trace[1024 + 4 * blockIdx.x + 3] = global_ns();
 }
 
+// ---------------------------------------------------------------------- one token, fused experts
+// The whole expert part of a one-token forward in one persistent kernel: every CTA claims work
+// units from one counter, first the gate/up units (U_gu stages of a 64-row gate + 64-row up tile
+// of a chunk's expert), then the down units (all stages of one 128-row down tile of one expert,
+// expert-major), so SMs flow from gate/up into down work without a kernel boundary. A gate/up
+// tile whose last part lands is finished by the epilogue that stored it (parts added in K order,
+// h = act(g, u) w, four-term operand) and counted per chunk; a down unit's activation loads wait
+// only for its own chunk's h. The down parts are added per output row in chunk order after one
+// bounded grid barrier. The roles and rings are those of moe_tc_kernel.
+struct FusedArgs {
+  const int32_t* ch_expert;
+  const int32_t* ch_pos;
+  const float* perm_w;
+  const int32_t* n_chunks;
+  int H, I;
+  const uint8_t* arena;
+  size_t stride, off_down;
+  uint8_t* ht;
+  uint8_t* hsf;
+  float* part_gu;   // [gate/up units][128]
+  float* part_dn;   // [down units][128]
+  int* tile_cnt;    // [chunks * I / 64] gate/up parts stored per tile
+  int* h_ready;     // [chunks] gate/up tiles whose h is written
+  int* work;        // [4] units claimed, CTAs finished, down parts stored (zero between launches)
+  unsigned* err;
+  float* out;       // [H]
+  ActParams act;
+  int stages;
+  int u_gu;         // stages per gate/up unit
+};
+
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const __grid_constant__ MoeTcMaps mgu,
+                                                                       const __grid_constant__ MoeTcMaps mdn,
+                                                                       FusedArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  constexpr int kBoxes = 1;                 // one token: 4 term rows in one 8-row box
+  const int bsub = kBoxes * 1024;
+  const MtLayout lay = mt_layout(S, kBoxes);
+  const int stage_pitch = lay.stage_pitch;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.off_bar);
+  uint64_t* sf_full = full + S;
+  uint64_t* empty = sf_full + S;
+  uint64_t* bfull = empty + S;
+  uint64_t* acc_full = bfull + S;
+  uint64_t* acc_empty = acc_full + 4;
+  uint64_t* rec_full = acc_empty + 4;
+  uint64_t* rec_empty = rec_full + kRecRing;
+  uint64_t* sfa_done = rec_empty + kRecRing;
+  PartRec* recs = reinterpret_cast<PartRec*>(smem + lay.off_rec);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + lay.off_misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&sf_full[i], 128);
+      mbar_init(&empty[i], 1);
+      mbar_init(&bfull[i], 1);
+      mbar_init(&sfa_done[i], 1);
+    }
+    for (int i = 0; i < 4; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    for (int i = 0; i < kRecRing; i++) {
+      mbar_init(&rec_full[i], 1);
+      mbar_init(&rec_empty[i], 2 + 128 + 128);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kMtTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  griddep_wait();  // routing, dispatch and the token's terms (the front end)
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  const int nch = *a.n_chunks;
+  const int kst_gu = a.H / kMtKStage, kst_dn = a.I / kMtKStage;
+  const int ntm_gu = a.I / 64, ntm_dn = a.H / 128;
+  const int U_gu = a.u_gu, upt_gu = kst_gu / U_gu;
+  const int n_gu = nch * ntm_gu * upt_gu, n_dn = nch * ntm_dn;
+  const int total_units = n_gu + n_dn;
+  constexpr int acc_cols = 32, nacc = 4;
+  const uint32_t sf_base = tbase + 256;
+
+  // unit u -> (kind, tile, uit, chunk, stages, first stage)
+  struct Unit {
+    int kind, tile, uit, c, m, ns, ks0;
+  };
+  auto decode = [&](int u) {
+    Unit x;
+    if (u < n_gu) {
+      x.kind = 0;
+      x.tile = u / upt_gu;
+      x.uit = u % upt_gu;
+      x.c = x.tile / ntm_gu;
+      x.m = x.tile % ntm_gu;
+      x.ns = U_gu;
+      x.ks0 = x.uit * U_gu;
+    } else {
+      const int d = u - n_gu;
+      x.kind = 1;
+      x.c = d / ntm_dn;
+      x.m = d % ntm_dn;
+      x.tile = x.m;
+      x.uit = 0;
+      x.ns = kst_dn;
+      x.ks0 = 0;
+    }
+    return x;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
+      int unit = blockIdx.x;
+      for (int part = 0;; part++) {
+        const bool stop = unit >= total_units || *abort_flag;
+        int nxt = unit;
+        if (part >= kRecRing && !mbar_wait_bounded(&rec_empty[rslot], rph ^ 1, a.err, 0x10u)) {
+          *abort_flag = 1;
+          break;
+        }
+        Unit x{};
+        int e = 0, p = 0;
+        if (!stop) {
+          x = decode(unit);
+          e = __ldg(a.ch_expert + x.c);
+          p = __ldg(a.ch_pos + x.c);
+        }
+        PartRec& r = recs[rslot];
+        r.tile = stop ? -1 : x.tile;
+        r.uit = x.ns;    // (stages of this unit)
+        r.unit = unit;
+        r.e = e;
+        r.p0 = p;
+        r.n = x.c;
+        r.brow = x.kind ? 4 * p : 0;  // one token: its terms are rows 0..3; h of position p
+        r.pad = x.kind;
+        mbar_arrive(&rec_full[rslot]);
+        if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+        if (stop) break;
+        const uint8_t* base = a.arena + static_cast<size_t>(e) * a.stride + (x.kind ? a.off_down : 0);
+        const int kst = x.kind ? kst_dn : kst_gu;
+        for (int j = 0; j < x.ns; j++, issued++) {
+          if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[slot], kTileBlock);
+          bulk_g2s(smem + slot * stage_pitch, base + (static_cast<size_t>(x.m) * kst + x.ks0 + j) * kTileBlock,
+                   kTileBlock, &full[slot]);
+          if (++slot == S) { slot = 0; ph ^= 1; }
+          if (j == 0) nxt = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
+        }
+        unit = nxt;
+        if (*abort_flag) break;
+      }
+      if (*abort_flag)
+        for (int i = 0; i < kRecRing; i++) recs[i].tile = -1;
+      for (int i = (issued > S ? issued - S : 0); i < issued; i++)
+        mbar_wait_bounded(&full[i % S], (i / S) & 1, a.err, 0x200u);
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------------ activation producer
+    if (lane == 0) {
+      tma_prefetch_desc(&mgu.b);
+      tma_prefetch_desc(&mdn.b);
+      int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
+      for (;;) {
+        if (!mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x20u)) break;
+        const PartRec r = recs[rslot];
+        mbar_arrive(&rec_empty[rslot]);
+        if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+        if (r.tile < 0 || *abort_flag) break;
+        const int kind = r.pad, ns = r.uit, c = r.n;
+        if (kind == 1) {
+          // this expert's h: all of its gate/up tiles finished
+          const uint64_t t0 = global_ns();
+          while (ld_acquire_gpu(a.h_ready + c) < ntm_gu) {
+            if (global_ns() - t0 > 2000000000ull) {
+              atomicOr(a.err, 0x40000u);
+              *abort_flag = 1;
+              break;
+            }
+            __nanosleep(32);
+          }
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // h: plain stores
+        }
+        const Unit x = decode(r.unit);
+        const MoeTcMaps& mp = kind ? mdn : mgu;
+        bool ok = true;
+        for (int j = 0; j < ns; j++, issued++) {
+          if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + slot * stage_pitch + kBOff;
+          const int ks = x.ks0 + j;
+          mbar_arrive_expect_tx(&bfull[slot], 2 * 1024 + 128);
+          tma_load_2d(sb, &mp.b, ks * (kMtKStage / 2), r.brow, &bfull[slot]);
+          tma_load_2d(sb + bsub, &mp.b, ks * (kMtKStage / 2) + 128, r.brow, &bfull[slot]);
+          tma_load_2d(sb + 2 * bsub, &mp.bs, ks * (kMtKStage / 32), r.brow, &bfull[slot]);
+          if (++slot == S) { slot = 0; ph ^= 1; }
+        }
+        if (!ok || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+      for (int i = (issued > S ? issued - S : 0); i < issued; i++)
+        mbar_wait_bounded(&bfull[i % S], (i / S) & 1, a.err, 0x200u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int i = 0, buf = 0, parts = 0, rslot = 0, rph = 0;
+      bool ok = true;
+      const uint64_t da0 = sw128_desc(smem), db0 = sw128_desc(smem + kBOff);
+      const uint32_t idesc = mxf4_idesc(8);
+      for (;;) {
+        if (!mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x20u)) break;
+        const int tile = recs[rslot].tile, ns = recs[rslot].uit;
+        mbar_arrive(&rec_empty[rslot]);
+        if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+        if (tile < 0 || *abort_flag) break;
+        if (parts >= nacc && !mbar_wait_bounded(&acc_empty[buf], ((parts / nacc) - 1) & 1, a.err, 0x1000u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dacc = tbase + buf * acc_cols;
+        for (int j = 0; j < ns && ok; j++, i++) {
+          const int slot = i % S;
+          const uint32_t ph = (i / S) & 1;
+          if (!mbar_wait_bounded(&sfa_done[slot], ph, a.err, 0x800u) ||
+              !mbar_wait_bounded(&sf_full[slot], ph, a.err, 0x800u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = da0 + static_cast<uint64_t>((slot * stage_pitch) >> 4);
+          const uint64_t db = db0 + static_cast<uint64_t>((slot * stage_pitch) >> 4);
+          const uint32_t sfa = sf_base + slot * kMtSfCols, sfb = sfa + 16;
+          uint64_t dak[8], dbk[8];
+          uint32_t idk[8], sak[8], sbk[8];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const uint32_t adv = (32 * (k & 3)) >> 4;
+            dak[k] = da + ((k >> 2) * (16384 >> 4) + adv);
+            dbk[k] = db + ((k >> 2) * (bsub >> 4) + adv);
+            const uint32_t sid = static_cast<uint32_t>(2 * (k & 1));
+            sak[k] = (sfa + 4 * (k >> 1)) | (sid << 30);
+            sbk[k] = (sfb + 4 * (k >> 1)) | (sid << 30);
+            idk[k] = idesc | (sid << 29) | (sid << 4);
+          }
+          const uint32_t acc0 = j == 0 ? 0u : 1u;
+#pragma unroll
+          for (int k = 0; k < 8; k++) mma_mxf4_run(dacc, dak[k], dbk[k], idk[k], sak[k], sbk[k], k == 0 ? acc0 : 1u);
+          tc_commit(&empty[slot]);
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+        if (++buf == nacc) buf = 0;
+        parts++;
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------------ scale factors -> TMEM
+    const int q = warp & 3;
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
+    int i = 0, rslot = 0, rph = 0;
+    bool ok = true;
+    while (ok) {
+      if (!__all_sync(kFull, mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u))) break;
+      const int tile = recs[rslot].tile, ns = recs[rslot].uit;
+      mbar_arrive(&rec_empty[rslot]);
+      if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+      if (tile < 0) break;
+      for (int j = 0; j < ns; j++, i++) {
+        const int slot = i % S;
+        if (q == 2) {
+          bool got = lane != 0 || mbar_wait_bounded(&full[slot], (i / S) & 1, a.err, 0x4000u);
+          got = __shfl_sync(kFull, got, 0);
+          if (!got) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            tc_fence_after();
+            const uint8_t* ssa = smem + slot * stage_pitch + 32768;
+            const uint32_t sfa = sf_base + slot * kMtSfCols;
+#pragma unroll
+            for (int g = 0; g < 4; g++) tmem_cp_rows16_x4(sfa + 4 * g, rows16_desc(ssa + g * 512));
+            tc_commit(&sfa_done[slot]);
+          }
+          __syncwarp();
+        }
+        const bool gotb = mbar_wait_bounded(&bfull[slot], (i / S) & 1, a.err, 0x4000u) && !*abort_flag;
+        if (!__all_sync(kFull, gotb)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ssb = smem + slot * stage_pitch + kBOff + 2 * bsub;
+        const uint32_t sfb = sf_base + slot * kMtSfCols + 16;
+        uint4 rb[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const int n = lane + 32 * jj;
+          rb[jj] = n < 8 ? *reinterpret_cast<const uint4*>(ssb + n * 16)
+                         : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+        }
+        tmem_st4(lane_addr | (sfb + 0), rb[0].x, rb[1].x, rb[2].x, rb[3].x);
+        tmem_st4(lane_addr | (sfb + 4), rb[0].y, rb[1].y, rb[2].y, rb[3].y);
+        tmem_st4(lane_addr | (sfb + 8), rb[0].z, rb[1].z, rb[2].z, rb[3].z);
+        tmem_st4(lane_addr | (sfb + 12), rb[0].w, rb[1].w, rb[2].w, rb[3].w);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sf_full[slot]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int et = threadIdx.x - 192;
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
+    const int row = 32 * q + lane;
+    int buf = 0, seen = 0, rslot = 0, rph = 0;
+    for (;;) {
+      const bool gotr = mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u);
+      if (!epi_all(gotr)) break;
+      const PartRec r = recs[rslot];
+      mbar_arrive(&rec_empty[rslot]);
+      if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
+      if (r.tile < 0) break;
+      const bool got = mbar_wait_bounded(&acc_full[buf], (seen / nacc) & 1, a.err, 0x8000u);
+      if (!epi_all(got && !*abort_flag)) break;
+      tc_fence_after();
+      float rr[8];
+      tmem_ld8(tbase + buf * acc_cols + lane_addr, rr);
+      const float v = ((rr[0] + rr[1]) + rr[2]) + rr[3];
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      if (++buf == nacc) buf = 0;
+      seen++;
+      if (r.pad == 1) {
+        a.part_dn[static_cast<size_t>(r.unit - n_gu) * 128 + row] = v;
+        continue;
+      }
+      // gate/up part; the CTA storing a tile's last part finishes the tile's h
+      a.part_gu[static_cast<size_t>(r.unit) * 128 + row] = v;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (et == 0) *last_flag = atom_add_acq_rel_gpu(a.tile_cnt + r.tile, 1) + 1 == upt_gu;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!*last_flag) continue;
+      const int ew = et / 32;
+      if (ew < 2) {
+        const float* base = a.part_gu + static_cast<size_t>(r.tile) * upt_gu * 128 + ew * 32 + lane;
+        float g = 0.0f, u = 0.0f;
+        for (int j = 0; j < upt_gu; j++) {
+          g += __ldcg(base + static_cast<size_t>(j) * 128);
+          u += __ldcg(base + static_cast<size_t>(j) * 128 + 64);
+        }
+        const int p = r.p0;
+        const int i0 = (r.tile % ntm_gu) * 64 + ew * 32;
+        const float hv = act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * __ldg(a.perm_w + p);
+        const size_t trow = static_cast<size_t>(4 * p);
+        warp_terms4(hv, a.ht + trow * (a.I / 2) + i0 / 2, a.I / 2, a.hsf + trow * (a.I / 32) + i0 / 32, a.I / 32);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (et == 0) red_release_gpu_add(a.h_ready + r.n, 1);  // (r.n: the chunk)
+    }
+    // every CTA's down parts stored -> each CTA adds the parts of its share of output rows in
+    // chunk order
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (et == 0) {
+      red_release_gpu_add(a.work + 2, 1);
+      const uint64_t t0 = global_ns();
+      while (ld_acquire_gpu(a.work + 2) < static_cast<int>(gridDim.x)) {
+        if (global_ns() - t0 > 2000000000ull) {
+          atomicOr(a.err, 0x20000u);
+          *abort_flag = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (!*abort_flag) {
+      for (int orow = blockIdx.x * 128 + et; orow < a.H; orow += gridDim.x * 128) {
+        const int m = orow / 128, rr = orow % 128;
+        float acc = 0.0f;
+        for (int c = 0; c < nch; c++) acc += __ldcg(a.part_dn + static_cast<size_t>(c * ntm_dn + m) * 128 + rr);
+        a.out[orow] = acc;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kMtTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(a.work + 1, 1);
+    if (old == static_cast<int>(gridDim.x) - 1) {
+      // the last CTA out zeroes every counter of this launch for the next one
+      a.work[0] = 0;
+      a.work[1] = 0;
+      a.work[2] = 0;
+      a.work[3] = 0;
+      for (int i = 0; i < nch * ntm_gu; i++) a.tile_cnt[i] = 0;
+      for (int i = 0; i < nch; i++) a.h_ready[i] = 0;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------- activation terms per position
 // xt rows 4p..4p+3 = terms of the token of position p. One warp per (token, 32-block): the terms
 // are computed once and stored at each of the token's routed positions (inv) and its shared one.
@@ -976,6 +1407,44 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, maps, a);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+// One token after the fused front end: the gate/up and down units of every routed expert and
+// the shared one in one persistent launch (moe_decode_fused_kernel), out = the combined row.
+cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, int H, int I, const uint8_t* arena,
+                                    size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
+                                    float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
+                                    float* out, ActParams act, cudaStream_t st) {
+  const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
+  FusedArgs a{};
+  a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.perm_w = d.perm_w; a.n_chunks = d.n_chunks;
+  a.H = H; a.I = I;
+  a.arena = arena; a.stride = stride; a.off_down = off_down;
+  a.ht = ht; a.hsf = hsf;
+  a.part_gu = part_gu; a.part_dn = part_dn;
+  a.tile_cnt = tile_cnt; a.h_ready = h_ready; a.work = work; a.err = err; a.out = out;
+  a.act = act;
+  a.u_gu = small_unit_stages(H / kMtKStage);
+  int stages = kMtMaxStages;
+  while (stages > 2 && moe_tc_smem(stages, 1) > 227 * 1024) stages--;
+  a.stages = stages;
+  const size_t smem = moe_tc_smem(stages, 1);
+  cudaError_t e = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(kMtThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p->gu, p->dn, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
