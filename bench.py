@@ -451,9 +451,19 @@ def run_gpu(args):
     per_step = [expert_touch_bytes(dcfg, ids_np[j:j + 1]) for j in range(args.steps)]
     layer_bytes = float(np.mean([p[0] for p in per_step]))
     gu_bytes = float(np.mean([p[1] for p in per_step]))
+    expert_bytes = float(np.mean([(p[2] + 1) * dcfg.expert_bytes() for p in per_step]))
     hbm_peak, _, peak_kind = peaks()
     gu_ms = prof["gate_up"] / max(1, prof["calls"])
     dn_ms = prof["down"] / max(1, prof["calls"])
+    # one token: gate/up and down of its experts run as one fused kernel (its time is the
+    # gate_up stage) unless RMOE_DISABLE_FUSED=1 selects the two-kernel path
+    fused = os.environ.get("RMOE_DISABLE_FUSED", "0") != "1"
+    if fused:
+        rf_name = "moe_decode_fused_kernel (tcgen05 kind::mxf4: gate/up + SwiGLU + down of the token's 11 experts)"
+        rf_bytes, rf_ms, rf_key = expert_bytes, gu_ms, "moe_decode_fused_kernel_bytes"
+    else:
+        rf_name = "moe_tc_kernel<gate_up> (tcgen05 kind::mxf4, SwiGLU epilogue)"
+        rf_bytes, rf_ms, rf_key = gu_bytes, gu_ms, "moe_tc_kernel_gate_up_decode_bytes"
     stages_us = {k: prof[k] * 1e3 / max(1, prof["calls"]) for k in prof if k != "calls"}
 
     # end to end through the host-buffer entry point (pinned host in/out, copies inside)
@@ -523,16 +533,16 @@ def run_gpu(args):
                    "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
                    "l2": "flushed between timed steps (256 MiB write, then a 256 MiB read that drains the write-backs)",
                    "layer_algorithmic_bytes": layer_bytes},
-        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel<gate_up> (tcgen05 kind::mxf4, SwiGLU epilogue)",
-                     "achieved": gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None,
+        "roofline": {"bound": "hbm", "kernel": rf_name,
+                     "achieved": rf_bytes / (rf_ms / 1e3) / 1e9 if rf_ms > 0 else None,
                      "peak": hbm_peak, "unit": "GB/s", "peak_kind": peak_kind,
-                     "frac": (gu_bytes / (gu_ms / 1e3) / 1e9 / hbm_peak) if gu_ms > 0 else None,
-                     "traffic": ncu_traffic("moe_tc_kernel_gate_up_decode_bytes"),
+                     "frac": (rf_bytes / (rf_ms / 1e3) / 1e9 / hbm_peak) if rf_ms > 0 else None,
+                     "traffic": ncu_traffic(rf_key),
                      "traffic_source": "profiles/moe_tc_kernel_decode_small.md (ncu, per launch)",
-                     "kernel_us": gu_ms * 1e3, "kernel_bytes": gu_bytes,
+                     "kernel_us": rf_ms * 1e3, "kernel_bytes": rf_bytes,
+                     "kernel_timing": "CUDA events around the kernel on its stream, profiling pass over the timed tokens",
                      "layer_achieved_gbs": layer_bytes / (ms_per_step / 1e3) / 1e9,
-                     "layer_frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / hbm_peak,
-                     "down_us": dn_ms * 1e3},
+                     "layer_frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / hbm_peak},
         "stages_us": stages_us,
         "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": cfg.hidden * 2,
                 "d2h_bytes_per_step": cfg.hidden * 4,
