@@ -595,6 +595,22 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
     const unsigned long long f0 = tr[4000];
     auto rel = [&](unsigned long long t) { return t ? (double)(long long)(t - f0) * 1e-3 : -1.0; };
     fprintf(stderr, "timeline: front end %.2f (router %.2f, last block %.2f..)", rel(tr[4006]), rel(tr[4001]), rel(tr[4003]));
+    if (L->use_fused) {
+      const unsigned long long* b = tr + 4096 + 2048;
+      const char* nm[7] = {"entry", "set-up", "first copy", "first down unit", "epilogue done", "barrier passed", "exit"};
+      for (int f = 0; f < 7; f++) {
+        unsigned long long lo = ~0ull, hi = 0;
+        for (int c = 0; c < 148; c++) {
+          const unsigned long long v = b[8 * c + f];
+          if (!v) continue;
+          lo = std::min(lo, v);
+          hi = std::max(hi, v);
+        }
+        if (hi) fprintf(stderr, " | fused %s %.2f..%.2f", nm[f], rel(lo), rel(hi));
+      }
+      fprintf(stderr, "\n");
+      RMOE_CUDA(cudaMemset(L->tc_trace + 4096 + 2048, 0, 148 * 8 * 8), "fused trace reset");
+    }
     for (int k = 0; k < 2; k++) {
       const unsigned long long* b = tr + 4096 * k;
       unsigned long long e0 = ~0ull, e1 = 0, x0 = ~0ull, x1 = 0, s1 = 0;
@@ -980,11 +996,12 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       if (e != cudaSuccess) return cuda_fail(e, "activation terms");
     }
     marks.mark();
-    if (T == 1 && terms_done && L->use_fused && !L->tc_trace) {
+    if (T == 1 && terms_done && L->use_fused && (!L->tc_trace || !L->tc_trace_print)) {
       // one token after the fused front end: gate/up and down of all its experts in one launch
       e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
                                   L->hsf, L->partial, L->partial2, L->tile_cnt, L->tile_cnt + L->tile_cnt_half,
-                                  L->tc_work, L->dev_err, out, L->fmt.act, st);
+                                  L->tc_work, L->dev_err, out, L->fmt.act, st,
+                                  L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr);
       if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
       marks.mark();
       marks.mark();

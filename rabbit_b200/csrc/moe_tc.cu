@@ -756,10 +756,11 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
 // The whole expert part of a one-token forward in one persistent kernel: every CTA claims work
 // units from one counter, first the gate/up units (U_gu stages of a 64-row gate + 64-row up tile
 // of a chunk's expert), then the down units (all stages of one 128-row down tile of one expert,
-// expert-major), so SMs flow from gate/up into down work without a kernel boundary. A gate/up
-// tile whose last part lands is finished by the epilogue that stored it (parts added in K order,
-// h = act(g, u) w, four-term operand) and counted per chunk; a down unit's activation loads wait
-// only for its own chunk's h. The down parts are added per output row in chunk order after one
+// expert-major), so SMs flow from gate/up into down work without a kernel boundary. Gate/up parts
+// are released per tile; each CTA's warp 11 forms h of its share of the tiles (tile-major, about
+// the order they finish) once a tile's parts are all in (parts added in K order, h = act(g, u) w,
+// four-term operand) and counts it per chunk; a down unit's activation loads wait only for its
+// own chunk's h. The down parts are added per output row in chunk order after one
 // bounded grid barrier. The roles and rings are those of moe_tc_kernel.
 struct FusedArgs {
   const int32_t* ch_expert;
@@ -781,15 +782,13 @@ struct FusedArgs {
   ActParams act;
   int stages;
   int u_gu;         // stages per gate/up unit
+  unsigned long long* trace;  // optional: per CTA [8] entry, set-up, first copy, first down unit,
+                              // epilogue done, barrier passed, exit (global timer)
 };
 
-__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
+constexpr int kFusedThreads = kMtThreads + 32;  // + warp 11: forms h of finished gate/up tiles
 
-__global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const __grid_constant__ MoeTcMaps mgu,
+__global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ MoeTcMaps mgu,
                                                                        const __grid_constant__ MoeTcMaps mdn,
                                                                        FusedArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -811,8 +810,12 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
   PartRec* recs = reinterpret_cast<PartRec*>(smem + lay.off_rec);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + lay.off_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_flag = abort_flag + 1;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  unsigned long long* trc = a.trace ? a.trace + 8 * blockIdx.x : nullptr;
+  if (trc && threadIdx.x == 0) {
+    trc[0] = global_ns();
+    trc[3] = 0;
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
       mbar_init(&full[i], 1);
@@ -838,6 +841,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   griddep_wait();  // routing, dispatch and the token's terms (the front end)
+  if (trc && threadIdx.x == 0) trc[1] = global_ns();
   if (threadIdx.x == 0) griddep_launch_dependents();
   const int nch = *a.n_chunks;
   const int kst_gu = a.H / kMtKStage, kst_dn = a.I / kMtKStage;
@@ -908,6 +912,8 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
         if (stop) break;
         const uint8_t* base = a.arena + static_cast<size_t>(e) * a.stride + (x.kind ? a.off_down : 0);
         const int kst = x.kind ? kst_dn : kst_gu;
+        if (trc && part == 0) trc[2] = global_ns();
+        if (trc && x.kind == 1 && !trc[3]) trc[3] = global_ns();
         for (int j = 0; j < x.ns; j++, issued++) {
           if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
             *abort_flag = 1;
@@ -1032,6 +1038,41 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
       }
       if (!ok) *abort_flag = 1;
     }
+  } else if (warp == 11) {
+    // ------------------------------------------------------------------ h of finished gate/up tiles
+    for (int tile = blockIdx.x; tile < nch * ntm_gu && !*abort_flag; tile += gridDim.x) {
+      bool ready = true;
+      if (lane == 0) {
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_gpu(a.tile_cnt + tile) < upt_gu) {
+          if (global_ns() - t0 > 2000000000ull || *abort_flag) {
+            atomicOr(a.err, 0x80000u);
+            ready = false;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      if (!__shfl_sync(kFull, ready, 0)) break;
+      __syncwarp();
+      const int c = tile / ntm_gu, m = tile % ntm_gu;
+      const int p = __ldg(a.ch_pos + c);
+      const float wp = __ldg(a.perm_w + p);
+      for (int hf = 0; hf < 2; hf++) {
+        const float* base = a.part_gu + static_cast<size_t>(tile) * upt_gu * 128 + hf * 32 + lane;
+        float g = 0.0f, u = 0.0f;
+        for (int j = 0; j < upt_gu; j++) {
+          g += __ldcg(base + static_cast<size_t>(j) * 128);
+          u += __ldcg(base + static_cast<size_t>(j) * 128 + 64);
+        }
+        const int i0 = m * 64 + hf * 32;
+        const float hv = act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * wp;
+        const size_t trow = static_cast<size_t>(4 * p);
+        warp_terms4(hv, a.ht + trow * (a.I / 2) + i0 / 2, a.I / 2, a.hsf + trow * (a.I / 32) + i0 / 32, a.I / 32);
+      }
+      __syncwarp();
+      if (lane == 0) red_release_gpu_add(a.h_ready + c, 1);
+    }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ scale factors -> TMEM
     const int q = warp & 3;
@@ -1086,7 +1127,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
         mbar_arrive(&sf_full[slot]);
       }
     }
-  } else {
+  } else if (warp < 10) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int et = threadIdx.x - 192;
@@ -1114,32 +1155,15 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
         a.part_dn[static_cast<size_t>(r.unit - n_gu) * 128 + row] = v;
         continue;
       }
-      // gate/up part; the CTA storing a tile's last part finishes the tile's h
+      // gate/up part, released on its tile's counter (warp 11 of some CTA forms the tile's h)
       a.part_gu[static_cast<size_t>(r.unit) * 128 + row] = v;
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) *last_flag = atom_add_acq_rel_gpu(a.tile_cnt + r.tile, 1) + 1 == upt_gu;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (!*last_flag) continue;
-      const int ew = et / 32;
-      if (ew < 2) {
-        const float* base = a.part_gu + static_cast<size_t>(r.tile) * upt_gu * 128 + ew * 32 + lane;
-        float g = 0.0f, u = 0.0f;
-        for (int j = 0; j < upt_gu; j++) {
-          g += __ldcg(base + static_cast<size_t>(j) * 128);
-          u += __ldcg(base + static_cast<size_t>(j) * 128 + 64);
-        }
-        const int p = r.p0;
-        const int i0 = (r.tile % ntm_gu) * 64 + ew * 32;
-        const float hv = act_gate(a.act.kind, a.act.beta, a.act.linear_beta, g, u, false) * __ldg(a.perm_w + p);
-        const size_t trow = static_cast<size_t>(4 * p);
-        warp_terms4(hv, a.ht + trow * (a.I / 2) + i0 / 2, a.I / 2, a.hsf + trow * (a.I / 32) + i0 / 32, a.I / 32);
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) red_release_gpu_add(a.h_ready + r.n, 1);  // (r.n: the chunk)
+      if (et == 0) red_release_gpu_add(a.tile_cnt + r.tile, 1);
     }
     // every CTA's down parts stored -> each CTA adds the parts of its share of output rows in
     // chunk order
     asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (trc && et == 0) trc[4] = global_ns();
     if (et == 0) {
       red_release_gpu_add(a.work + 2, 1);
       const uint64_t t0 = global_ns();
@@ -1153,6 +1177,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
       }
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (trc && et == 0) trc[5] = global_ns();
     if (!*abort_flag) {
       for (int orow = blockIdx.x * 128 + et; orow < a.H; orow += gridDim.x * 128) {
         const int m = orow / 128, rr = orow % 128;
@@ -1180,6 +1205,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_decode_fused_kernel(const _
       for (int i = 0; i < nch * ntm_gu; i++) a.tile_cnt[i] = 0;
       for (int i = 0; i < nch; i++) a.h_ready[i] = 0;
     }
+    if (trc) trc[6] = global_ns();
   }
 }
 
@@ -1416,9 +1442,10 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
 cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, int H, int I, const uint8_t* arena,
                                     size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
                                     float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
-                                    float* out, ActParams act, cudaStream_t st) {
+                                    float* out, ActParams act, cudaStream_t st, unsigned long long* trace) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   FusedArgs a{};
+  a.trace = trace;
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.perm_w = d.perm_w; a.n_chunks = d.n_chunks;
   a.H = H; a.I = I;
   a.arena = arena; a.stride = stride; a.off_down = off_down;
@@ -1436,7 +1463,7 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(sm_count());
-  cfg.blockDim = dim3(kMtThreads);
+  cfg.blockDim = dim3(kFusedThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
