@@ -923,7 +923,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
           bulk_g2s(smem + slot * stage_pitch, base + (static_cast<size_t>(x.m) * kst + x.ks0 + j) * kTileBlock,
                    kTileBlock, &full[slot]);
           if (++slot == S) { slot = 0; ph ^= 1; }
-          if (j == 0) nxt = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
+          // the next claim at the unit's last stage (the ring still holds the stages before it):
+          // near the end a CTA then holds one unit ahead, not two
+          if (j == x.ns - 1) nxt = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
         }
         unit = nxt;
         if (*abort_flag) break;
