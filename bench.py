@@ -525,6 +525,8 @@ def run_gpu(args):
     line = {
         "metric": "moe_layer_decode_us_per_token", "value": us_per_token, "unit": "us/token",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "step_us_spread": {"min": round(min(step_ms) * 1e3, 2), "median": round(float(np.median(step_ms)) * 1e3, 2),
+                           "max": round(max(step_ms) * 1e3, 2)},
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
         "dtype": "mxfp4 weights x 4-term e2m1 activations (tcgen05 kind::mxf4), f32 accumulate", "data": "synthetic",
         "config": {"workload": DECODE_CFG, "tokens_per_step_per_gpu": 1, "hidden": cfg.hidden,

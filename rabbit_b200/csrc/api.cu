@@ -139,6 +139,8 @@ struct rmoe_layer {
   int32_t* pending = nullptr;    // [min(T, 32)] per-token order-pending flags
   int32_t* ids_final = nullptr;  // [T][k] routing in the reference's rank order
   float* w_final = nullptr;
+  float* exact_v = nullptr;      // [min(T, 32)][k] exact router values of order-pending tokens
+  int32_t* resolve_cnt = nullptr;  // [min(T, 32)] chains finished per token (zero between calls)
   cudaStream_t side = nullptr;   // resolves rank order concurrently with the expert GEMVs
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   bool use_pipe = false;         // TMA-staged GEMVs (shape permitting)
@@ -445,10 +447,13 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->pending, std::min(T, 32));
   ALLOC(L->ids_final, static_cast<size_t>(T) * k);
   ALLOC(L->w_final, static_cast<size_t>(T) * k);
+  ALLOC(L->exact_v, static_cast<size_t>(std::min(T, 32)) * k);
+  ALLOC(L->resolve_cnt, std::min(T, 32));
   {
     cudaError_t e = cudaMemset(L->fallbacks, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(L->dev_err, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(L->order_pending, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(L->resolve_cnt, 0, 4 * std::min(T, 32));
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset"));
   }
   {
@@ -1013,7 +1018,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     // one token: every position reads the token's own term rows (0..3)
     e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
                       L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
-                      L->tc_trace, L->fmt.act, L->tile_cnt, L->tc_work + 6);
+                      L->tc_trace, L->fmt.act, L->tile_cnt, L->tc_work + 6, T <= mt);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
 
     marks.mark();
@@ -1021,7 +1026,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     if (T == 1) {
       e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr, nullptr, T <= mt);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -1032,7 +1037,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr, nullptr, T <= mt);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -1156,7 +1161,7 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
     // rank order of near-tied winners: resolved on a side stream, joined before returning
     RMOE_CUDA(cudaEventRecord(L->ev_fork, st), "fork");
     RMOE_CUDA(cudaStreamWaitEvent(L->side, L->ev_fork, 0), "fork wait");
-    e = launch_resolve_order(a, L->ids_final, L->w_final, L->side);
+    e = launch_resolve_order(a, L->ids_final, L->w_final, L->exact_v, L->resolve_cnt, L->side);
     if (e != cudaSuccess) return cuda_fail(e, "order resolve");
     RMOE_CUDA(cudaEventRecord(L->ev_join, L->side), "join");
     resolved = true;

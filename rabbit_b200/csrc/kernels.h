@@ -131,9 +131,10 @@ cudaError_t launch_router_certified(const void* x, int x_dtype, const void* w, i
 // Top-k + certificate (+ exact fallback), dispatch, activation prep in one block.
 cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers& d,
                                   cudaStream_t st);
-// Final reference-order routing (exact chains for order-pending tokens); one warp per token.
-cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final,
-                                 cudaStream_t st);
+// Final reference-order routing (exact chains for order-pending tokens); one block per
+// (token, winner). exact_v: [T][k] scratch; done_cnt: [T] zeroed counters (left zeroed).
+cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final, float* exact_v,
+                                 int32_t* done_cnt, cudaStream_t st);
 // logits[T][E] = exact reference chain of x[t] . w[e] (fmul then fadd per element, from -0.0)
 cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
                                        float* logits, int T, int H, int E, cudaStream_t st);
@@ -223,7 +224,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st,
                           const int32_t* b_token_rows = nullptr, unsigned long long* trace = nullptr,
                           ActParams act = ActParams{0, 0.0f, 0.0f}, int32_t* gu_tile_cnt = nullptr,
-                          int* h_done = nullptr);
+                          int* h_done = nullptr, bool weights_once = false);
 // Unit parts of split tiles (floats) a layer must provide for batches of up to 8 tokens.
 size_t moe_tc_partial_floats(int H, int I, int k, int n_slots);
 

@@ -88,6 +88,7 @@ struct MoeTcArgs {
   int* gu_tile_cnt;
   int* h_done;         // gate/up: h items finished (released per item; the down kernel's counter)
   int h_split;         // down: gate/up split its tiles, its helper warps write h (wait on h_done)
+  int weights_once;    // every weight tile is read by one unit only (one chunk per expert): evict-first
 };
 
 struct StageMeta {
@@ -377,7 +378,10 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           mbar_arrive_expect_tx(&full[slot], kTileBlock);
           const uint8_t* blk = a.wbase + static_cast<size_t>(ce) * a.wstride +
                                (static_cast<size_t>(w.m) * kst + w.ks) * kTileBlock;
-          bulk_g2s(st, blk, kTileBlock, &full[slot]);
+          if (a.weights_once)
+            bulk_g2s_once(st, blk, kTileBlock, &full[slot]);
+          else
+            bulk_g2s(st, blk, kTileBlock, &full[slot]);
           if (++slot == S) { slot = 0; ph ^= 1; }
           if (j == 0) {  // claim the next unit and load its fields while this one streams
             nxt = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
@@ -776,7 +780,7 @@ struct FusedArgs {
   float* part_dn;   // [down units][128]
   int* tile_cnt;    // [chunks * I / 64] gate/up parts stored per tile
   int* h_ready;     // [chunks] gate/up tiles whose h is written
-  int* work;        // [4] units claimed, CTAs finished, down parts stored (zero between launches)
+  int* work;        // [4] units claimed, CTAs finished, down parts stored, h tiles claimed (zero between launches)
   unsigned* err;
   float* out;       // [H]
   ActParams act;
@@ -920,7 +924,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             break;
           }
           mbar_arrive_expect_tx(&full[slot], kTileBlock);
-          bulk_g2s(smem + slot * stage_pitch, base + (static_cast<size_t>(x.m) * kst + x.ks0 + j) * kTileBlock,
+          bulk_g2s_once(smem + slot * stage_pitch, base + (static_cast<size_t>(x.m) * kst + x.ks0 + j) * kTileBlock,
                    kTileBlock, &full[slot]);
           if (++slot == S) { slot = 0; ph ^= 1; }
           // the next claim at the unit's last stage (the ring still holds the stages before it):
@@ -1042,7 +1046,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------------ h of finished gate/up tiles
-    for (int tile = blockIdx.x; tile < nch * ntm_gu && !*abort_flag; tile += gridDim.x) {
+    // tiles claimed in order from work[3] (a CTA that starts late, e.g. on an SM still busy with
+    // another kernel, then holds up no tile)
+    for (;;) {
+      int tile = 0;
+      if (lane == 0) tile = atomicAdd(a.work + 3, 1);
+      tile = __shfl_sync(kFull, tile, 0);
+      if (tile >= nch * ntm_gu || *abort_flag) break;
       bool ready = true;
       if (lane == 0) {
         const uint64_t t0 = global_ns();
@@ -1378,7 +1388,8 @@ static size_t moe_tc_smem(int stages, int b_boxes) {
 cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, int mt, int H, int I,
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st, const int32_t* b_token_rows,
-                          unsigned long long* trace, ActParams act, int32_t* gu_tile_cnt, int* h_done) {
+                          unsigned long long* trace, ActParams act, int32_t* gu_tile_cnt, int* h_done,
+                          bool weights_once) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   MoeTcArgs a{};
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.ch_n = d.ch_n; a.n_chunks = d.n_chunks;
@@ -1402,6 +1413,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   a.act = act;
   a.gu_tile_cnt = gu_tile_cnt;
   a.h_done = h_done;
+  a.weights_once = weights_once ? 1 : 0;
   a.h_split = (mode != 0 && mt <= 8 && small_unit_stages(H / kMtKStage) < H / kMtKStage) ? 1 : 0;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, a.b_boxes) > 227 * 1024) stages--;

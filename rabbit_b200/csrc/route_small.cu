@@ -18,6 +18,8 @@
 // by the 1.01 and 2nu factors for any H with n*u < 0.01.
 #include <float.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "pipe.cuh"
@@ -914,87 +916,100 @@ cudaError_t launch_decode_front(const DecodeFront& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// The reference chain for one (token, expert) with the token's activations and the expert's
-// router row both staged in shared memory: a = -0.0; a = fl(a + fl(x_k * w_k)), k ascending.
-// Two 8-element chunks are read ahead, so only the add latency (~4 cycles per element) remains.
-template <int XD, int WD>
-__device__ __forceinline__ float exact_chain_smem(const uint8_t* xs, const uint8_t* ws, int H) {
-  constexpr int XB = XD == kBF16 ? 16 : 32, WB = WD == kBF16 ? 16 : 32;  // bytes per 8 elements
-  auto ld = [](const uint8_t* p, int dt, uint4 (&r)[2]) {
-    r[0] = *reinterpret_cast<const uint4*>(p);
-    if (dt == kF32) r[1] = *reinterpret_cast<const uint4*>(p + 16);
-  };
-  const int nch = H / 8;
-  uint4 xr[2][2], wr[2][2];
-  ld(xs, XD, xr[0]);
-  ld(ws, WD, wr[0]);
-  float acc = -0.0f;
-  for (int c = 0; c < nch; c += 2) {
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-      if (c + j >= nch) break;
-      if (c + j + 1 < nch) {
-        ld(xs + (c + j + 1) * XB, XD, xr[(j + 1) & 1]);
-        ld(ws + (c + j + 1) * WB, WD, wr[(j + 1) & 1]);
-      }
-      float xv[8], wv[8];
-      expand8<XD>(xr[j], xv);
-      expand8<WD>(wr[j], wv);
-#pragma unroll
-      for (int i = 0; i < 8; i++) acc = __fadd_rn(acc, __fmul_rn(xv[i], wv[i]));
-    }
-  }
-  return acc;
-}
+constexpr int kResolveThreads = 128;  // threads per (token, winner) chain
+constexpr int kResolvePer = 64;       // elements each thread holds per segment
+constexpr int kResolveSeg = kResolveThreads * kResolvePer;
 
-// Final routing in the reference's rank order. Tokens whose order certificate failed get exact
-// chains for their k winners (the set is already certain), one lane per winner, on the token's
-// activations and the winners' router rows bulk-copied into shared memory; they are re-ranked on
-// those values. Other tokens are copied. Runs beside the expert GEMMs.
+// Final routing in the reference's rank order. Tokens whose order certificate failed get the
+// exact reference chain for each of their k winners (the set is already certain) --
+// a = -0.0; a = fl(a + fl(x_i * w_i)), i ascending -- and are re-ranked on those values; other
+// tokens are copied. One 128-thread block per (token, winner): the token's activations and the
+// winner's router row are loaded into registers at once (64 elements a thread), then the chain
+// runs through the threads in element order, each adding its own products and handing the sum to
+// the next (shuffles inside a warp, shared memory between warps). The block is small (no dynamic
+// shared memory) so it runs beside the expert kernels on the side stream. The last block of a
+// token (per-token counter) ranks the k exact values and writes the token's routing.
 template <int XD, int WD>
-__global__ void __launch_bounds__(32) resolve_order_kernel(SmallPrologue a, int32_t* ids_final,
-                                                           float* w_final) {
-  extern __shared__ __align__(128) uint8_t rs_smem[];
-  __shared__ uint64_t bar;
-  const int t = blockIdx.x, lane = threadIdx.x;
+__global__ void __launch_bounds__(kResolveThreads) resolve_order_kernel(SmallPrologue a, int32_t* ids_final,
+                                                                        float* w_final, float* exact_v,
+                                                                        int32_t* done_cnt) {
+  constexpr int XV = XD == kBF16 ? 1 : 2, WV = WD == kBF16 ? 1 : 2;  // uint4 per 8 elements
+  __shared__ float hand[kResolveThreads / 32];
+  __shared__ int last;
   const int k = a.k, kk = min(a.k, a.E);
+  const int t = blockIdx.x / kk, j = blockIdx.x % kk;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   if (!a.pending[t]) {
-    if (lane < k) {
-      ids_final[t * k + lane] = a.ids[t * k + lane];
-      w_final[t * k + lane] = a.rw[t * k + lane];
+    if (j == 0 && tid < k) {
+      ids_final[t * k + tid] = a.ids[t * k + tid];
+      w_final[t * k + tid] = a.rw[t * k + tid];
     }
     return;
   }
-  const uint32_t xbytes = static_cast<uint32_t>(a.H) * (XD == kBF16 ? 2 : 4);
-  const uint32_t wbytes = static_cast<uint32_t>(a.H) * (WD == kBF16 ? 2 : 4);
-  const int e = lane < kk ? a.ids[t * k + lane] : -1;
-  if (lane == 0) {
-    mbar_init(&bar, 1);
-    mbar_fence_init();
-    mbar_arrive_expect_tx(&bar, xbytes + kk * wbytes);
-    bulk_g2s(rs_smem, static_cast<const uint8_t*>(a.x) + static_cast<size_t>(t) * xbytes, xbytes, &bar);
+  const int e = a.ids[t * k + j];
+  const uint4* xg = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) +
+                                                   static_cast<size_t>(t) * a.H * (XD == kBF16 ? 2 : 4));
+  const uint4* wg = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.w) +
+                                                   static_cast<size_t>(e) * a.H * (WD == kBF16 ? 2 : 4));
+  float acc = -0.0f;
+  for (int seg = 0; seg < a.H; seg += kResolveSeg) {
+    const int i0 = seg + tid * kResolvePer;
+    const int n = max(0, min(kResolvePer, a.H - i0));  // a multiple of 16 (H % 16 == 0)
+    uint4 xr[kResolvePer / 8][XV], wr[kResolvePer / 8][WV];
+#pragma unroll
+    for (int c = 0; c < kResolvePer / 8; c++) {
+      if (8 * c < n) {
+#pragma unroll
+        for (int q = 0; q < XV; q++) xr[c][q] = __ldg(xg + (i0 / 8 + c) * XV + q);
+#pragma unroll
+        for (int q = 0; q < WV; q++) wr[c][q] = __ldg(wg + (i0 / 8 + c) * WV + q);
+      }
+    }
+    for (int w = 0; w < kResolveThreads / 32; w++) {
+      if (warp == w) {
+        for (int l = 0; l < 32; l++) {
+          if (lane == l) {
+#pragma unroll
+            for (int c = 0; c < kResolvePer / 8; c++) {
+              if (8 * c < n) {
+                float xv[8], wv[8];
+                uint4 x2[2] = {xr[c][0], xr[c][XV - 1]}, w2[2] = {wr[c][0], wr[c][WV - 1]};
+                expand8<XD>(x2, xv);
+                expand8<WD>(w2, wv);
+#pragma unroll
+                for (int i = 0; i < 8; i++) acc = __fadd_rn(acc, __fmul_rn(xv[i], wv[i]));
+              }
+            }
+          }
+          acc = __shfl_sync(kFull, acc, l);
+        }
+        if (lane == 0) hand[w] = acc;
+      }
+      __syncthreads();
+      acc = hand[w];
+    }
   }
-  __syncwarp();
-  for (int j = 0; j < kk; j++) {
-    const int ej = __shfl_sync(kFull, e, j);
-    if (lane == 0)
-      bulk_g2s(rs_smem + xbytes + j * wbytes, static_cast<const uint8_t*>(a.w) + static_cast<size_t>(ej) * wbytes,
-               wbytes, &bar);
+  if (tid == 0) {
+    if (a.bias) acc = __fadd_rn(acc, a.bias[e]);
+    exact_v[t * k + j] = acc;
+    __threadfence();
+    last = atomicAdd(done_cnt + t, 1) == kk - 1;
   }
-  const bool got = mbar_wait_bounded(&bar, 0, a.errflag, 0x100000u);
-  float v = -INFINITY;
-  if (got && e >= 0) {
-    v = exact_chain_smem<XD, WD>(rs_smem, rs_smem + xbytes + lane * wbytes, a.H);
-    if (a.bias) v = __fadd_rn(v, a.bias[e]);
-  }
+  __syncthreads();
+  if (!last || warp != 0) return;
+  __threadfence();
+  // the token's last block: rank the kk exact values (ties: lower expert id first)
+  const int el = lane < kk ? a.ids[t * k + lane] : -1;
+  const float v = lane < kk ? __ldcg(exact_v + t * k + lane) : -INFINITY;
+  if (lane == 0) done_cnt[t] = 0;  // (zero for the next call)
   unsigned tk = 0;
   int sel_id = -1;
   float sel_v = -INFINITY;
   for (int r = 0; r < kk; r++) {
-    float bv = (e >= 0 && !tk) ? v : -INFINITY;
-    int bid = (e >= 0 && !tk) ? e : 0x7fffffff;
+    float bv = (el >= 0 && !tk) ? v : -INFINITY;
+    int bid = (el >= 0 && !tk) ? el : 0x7fffffff;
     warp_best(bv, bid);
-    if (bid == e) tk = 1;
+    if (bid == el) tk = 1;
     if (lane == r) {
       sel_id = bid;
       sel_v = bv;
@@ -1003,23 +1018,20 @@ __global__ void __launch_bounds__(32) resolve_order_kernel(SmallPrologue a, int3
   const float mx = __shfl_sync(kFull, sel_v, 0);
   const float exv = lane < kk ? exp_f32(__fsub_rn(sel_v, mx)) : 0.0f;
   float sum = 0.0f;
-  for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, exv, j));
+  for (int i = 0; i < kk; i++) sum = __fadd_rn(sum, __shfl_sync(kFull, exv, i));
   if (lane < k) {
     ids_final[t * k + lane] = lane < kk ? sel_id : -1;
     w_final[t * k + lane] = lane < kk ? __fdiv_rn(exv, sum) : 0.0f;
   }
 }
 
-cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final,
-                                 cudaStream_t st) {
+cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final, float* exact_v,
+                                 int32_t* done_cnt, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
-  const int xs = a.x_dtype == kBF16 ? 2 : 4, ws = a.w_dtype == kBF16 ? 2 : 4;
-  const size_t smem = static_cast<size_t>(a.H) * xs + static_cast<size_t>(min(a.k, a.E)) * a.H * ws;
-  if (a.H % 16 != 0 || smem > 220 * 1024) return cudaErrorInvalidValue;
+  const int kk = min(a.k, a.E);
+  if (a.H % 16 != 0 || kk <= 0) return cudaErrorInvalidValue;
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    kern<<<a.T, 32, smem, st>>>(a, ids_final, w_final);
+    kern<<<a.T * kk, kResolveThreads, 0, st>>>(a, ids_final, w_final, exact_v, done_cnt);
     return cudaGetLastError();
   };
   if (a.x_dtype == kBF16 && a.w_dtype == kBF16) return go(resolve_order_kernel<kBF16, kBF16>);
