@@ -187,6 +187,8 @@ struct rmoe_layer {
   int32_t* tile_cnt = nullptr;   // [max tiles]
   unsigned* front_counter = nullptr;  // one-token front end: finished blocks
   size_t tile_cnt_half = 0;      // tile_cnt: [0, half) gate/up tiles, [half, 2 half) down tiles
+  int32_t* fused_cnt = nullptr;  // one-token fused kernel: [8] work, [fused_tiles] tiles, [33] h ready
+  int fused_tiles = 0;           // (zeroed by the one-token front end before each launch)
   int* tc_work = nullptr;        // [8] work counters: [0..3] gate/up, [4..7] down (they may overlap)
   size_t tc_off_down = 0;        // tile-major down region inside an expert slot
   uint8_t* tc_stage = nullptr;   // one expert in the reference layout, before retiling
@@ -508,6 +510,8 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     L->tile_cnt_half = max_tiles;
     ALLOC(L->tile_cnt, 2 * max_tiles);
     ALLOC(L->front_counter, 1);
+    L->fused_tiles = (RMOE_MAX_TOPK_DEV + 1) * static_cast<int>(I / 64);
+    ALLOC(L->fused_cnt, 8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1);
     if (const char* nf = getenv("RMOE_DISABLE_FUSED")) L->use_fused = nf[0] != '1';
     if (const char* tr = getenv("RMOE_TC_TRACE")) {
       if (tr[0] == '1' || tr[0] == '2') {
@@ -517,6 +521,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
       }
     }
     cudaError_t e = cudaMemset(L->tile_cnt, 0, 2 * max_tiles * 4);
+    if (e == cudaSuccess) e = cudaMemset(L->fused_cnt, 0, (8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1) * 4);
     if (e == cudaSuccess) e = cudaMemset(L->front_counter, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(L->tc_work, 0, 32);
     if (e == cudaSuccess) e = cudaMemset(L->xt, 0, rows * (H / 2));
@@ -599,7 +604,8 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
     RMOE_CUDA(cudaMemcpy(tr, L->tc_trace, sizeof(tr), cudaMemcpyDeviceToHost), "trace read");
     const unsigned long long f0 = tr[4000];
     auto rel = [&](unsigned long long t) { return t ? (double)(long long)(t - f0) * 1e-3 : -1.0; };
-    fprintf(stderr, "timeline: front end %.2f (router %.2f, last block %.2f..)", rel(tr[4006]), rel(tr[4001]), rel(tr[4003]));
+    fprintf(stderr, "timeline: front end %.2f (router blocks %.2f, other blocks %.2f, last block %.2f, select %.2f, certificate %.2f)",
+            rel(tr[4006]), rel(tr[4001]), rel(tr[4002]), rel(tr[4003]), rel(tr[4004]), rel(tr[4005]));
     if (L->use_fused) {
       const unsigned long long* b = tr + 4096 + 2048;
       const char* nm[7] = {"entry", "set-up", "first copy", "first down unit", "epilogue done", "barrier passed", "exit"};
@@ -613,6 +619,12 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
         }
         if (hi) fprintf(stderr, " | fused %s %.2f..%.2f", nm[f], rel(lo), rel(hi));
       }
+      fprintf(stderr, "\n");
+      // per CTA: epilogue done, barrier passed, exit
+      fprintf(stderr, "fused per CTA (epilogue done / barrier / exit):");
+      for (int c = 0; c < 148; c++)
+        fprintf(stderr, "%s%d:%.1f/%.1f/%.1f", c % 8 ? " " : "\n  ", c, rel(b[8 * c + 4]), rel(b[8 * c + 5]),
+                rel(b[8 * c + 6]));
       fprintf(stderr, "\n");
       RMOE_CUDA(cudaMemset(L->tc_trace + 4096 + 2048, 0, 148 * 8 * 8), "fused trace reset");
     }
@@ -1004,8 +1016,8 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     if (T == 1 && terms_done && L->use_fused && (!L->tc_trace || !L->tc_trace_print)) {
       // one token after the fused front end: gate/up and down of all its experts in one launch
       e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
-                                  L->hsf, L->partial, L->partial2, L->tile_cnt, L->tile_cnt + L->tile_cnt_half,
-                                  L->tc_work, L->dev_err, out, L->fmt.act, st,
+                                  L->hsf, L->partial, L->partial2, L->fused_cnt + 8, L->fused_cnt + 8 + L->fused_tiles,
+                                  L->fused_cnt, L->dev_err, out, L->fmt.act, (L->has_shared && !getenv("RMOE_NO_PRELOAD")) ? L->n_loc : -1, st,
                                   L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr);
       if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
       marks.mark();
@@ -1146,6 +1158,8 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
       f.ids = L->ids; f.rw = L->rw; f.pending = L->pending;
       f.fallback_count = L->fallbacks; f.order_pending_count = L->order_pending;
       f.counter = L->front_counter;
+      f.zero_buf = L->fused_cnt;  // (null unless the tensor-core path allocated it)
+      f.zero_n = L->fused_cnt ? 8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1 : 0;
       f.d = L->d;
       f.trace = L->tc_trace ? L->tc_trace + 4000 : nullptr;
       if (f.trace) RMOE_CUDA(cudaMemsetAsync(f.trace, 0, 8 * 8, st), "front trace reset");

@@ -118,6 +118,8 @@ struct DecodeFront {
   unsigned* fallback_count;
   unsigned* order_pending_count;
   unsigned* counter;              // finished blocks (zero between launches)
+  int32_t* zero_buf;              // zeroed by the front end (the expert kernel's counters), or null
+  int zero_n;
   DispatchBuffers d;
   unsigned long long* trace;      // optional diagnostics: [0] block 0 start, [1] last router
                                   // block end, [2] last terms block end, [3..6] last block phases
@@ -236,7 +238,8 @@ cudaError_t launch_synth_bytes(void* dst, size_t n, uint64_t key, int mode, int 
 cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, int H, int I, const uint8_t* arena,
                                     size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
                                     float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
-                                    float* out, ActParams act, cudaStream_t st, unsigned long long* trace = nullptr);
+                                    float* out, ActParams act, int sh_slot, cudaStream_t st,
+                                    unsigned long long* trace = nullptr);
 
 // ---- latent MoE wrapper (latent.cu) ----
 // y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)

@@ -771,6 +771,7 @@ struct FusedArgs {
   const int32_t* ch_pos;
   const float* perm_w;
   const int32_t* n_chunks;
+  int max_chunks;   // entries of ch_expert / ch_pos
   int H, I;
   const uint8_t* arena;
   size_t stride, off_down;
@@ -780,12 +781,13 @@ struct FusedArgs {
   float* part_dn;   // [down units][128]
   int* tile_cnt;    // [chunks * I / 64] gate/up parts stored per tile
   int* h_ready;     // [chunks] gate/up tiles whose h is written
-  int* work;        // [4] units claimed, CTAs finished, down parts stored, h tiles claimed (zero between launches)
+  int* work;        // [4] units claimed, -, down parts stored, h tiles claimed (zeroed by the front end)
   unsigned* err;
   float* out;       // [H]
   ActParams act;
   int stages;
   int u_gu;         // stages per gate/up unit
+  int sh_slot;      // expert slot of the shared expert (the last chunk), -1: none
   unsigned long long* trace;  // optional: per CTA [8] entry, set-up, first copy, first down unit,
                               // epilogue done, barrier passed, exit (global timer)
 };
@@ -844,15 +846,47 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  griddep_wait();  // routing, dispatch and the token's terms (the front end)
-  if (trc && threadIdx.x == 0) trc[1] = global_ns();
-  if (threadIdx.x == 0) griddep_launch_dependents();
-  const int nch = *a.n_chunks;
   const int kst_gu = a.H / kMtKStage, kst_dn = a.I / kMtKStage;
   const int ntm_gu = a.I / 64, ntm_dn = a.H / 128;
   const int U_gu = a.u_gu, upt_gu = kst_gu / U_gu;
-  const int n_gu = nch * ntm_gu * upt_gu, n_dn = nch * ntm_dn;
+  // The shared expert (always the last chunk) does not depend on the routing: CTA b < n_pre
+  // starts the weight copies of the shared expert's gate/up unit b before the front end is done
+  const int n_pre = a.sh_slot >= 0 ? ntm_gu * upt_gu : 0;
+  const int pre = static_cast<int>(blockIdx.x) < n_pre ? min(U_gu, S) : 0;
+  if (warp == 0 && lane == 0 && pre) {
+    const int b = blockIdx.x;
+    const uint8_t* base = a.arena + static_cast<size_t>(a.sh_slot) * a.stride;
+    const size_t blk0 = static_cast<size_t>(b / upt_gu) * kst_gu + (b % upt_gu) * U_gu;
+    for (int j = 0; j < pre; j++) {
+      mbar_arrive_expect_tx(&full[j], kTileBlock);
+      bulk_g2s_once(smem + j * stage_pitch, base + (blk0 + j) * kTileBlock, kTileBlock, &full[j]);
+    }
+    if (trc) trc[2] = global_ns();
+  }
+  griddep_wait();  // routing, dispatch and the token's terms (the front end)
+  if (trc && threadIdx.x == 0) trc[1] = global_ns();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  // the first 32 chunks' experts and positions, loaded together with the chunk count (the
+  // weight producer's first units need them at once)
+  __shared__ int s_ce[32], s_cp[32];
+  if (warp == 0 && lane < a.max_chunks) {
+    s_ce[lane] = __ldg(a.ch_expert + lane);
+    s_cp[lane] = __ldg(a.ch_pos + lane);
+  }
+  if (warp == 0) __syncwarp();
+  const int nch = *a.n_chunks;
+  // down units: a tile's K in dsplit parts (smaller last units: the CTAs finish closer together)
+  const int dsplit = kst_dn % 2 == 0 ? 2 : 1;
+  const int n_gu = nch * ntm_gu * upt_gu, n_dn = nch * ntm_dn * dsplit;
   const int total_units = n_gu + n_dn;
+  // claim index -> unit: the shared expert's gate/up units first (claims 0..n_pre-1, the CTAs
+  // that preloaded them), then every other unit in order
+  const int sh_gu0 = (nch - 1) * ntm_gu * upt_gu;
+  auto unit_of_claim = [&](int q) {
+    if (q < n_pre) return sh_gu0 + q;
+    const int r = q - n_pre;
+    return r < sh_gu0 ? r : r + n_pre;
+  };
   constexpr int acc_cols = 32, nacc = 4;
   const uint32_t sf_base = tbase + 256;
 
@@ -871,14 +905,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
       x.ns = U_gu;
       x.ks0 = x.uit * U_gu;
     } else {
-      const int d = u - n_gu;
+      const int d = u - n_gu, dt = d / dsplit;
       x.kind = 1;
-      x.c = d / ntm_dn;
-      x.m = d % ntm_dn;
+      x.c = dt / ntm_dn;
+      x.m = dt % ntm_dn;
       x.tile = x.m;
-      x.uit = 0;
-      x.ns = kst_dn;
-      x.ks0 = 0;
+      x.uit = d % dsplit;
+      x.ns = kst_dn / dsplit;
+      x.ks0 = x.uit * x.ns;
     }
     return x;
   };
@@ -887,7 +921,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     // ------------------------------------------------------------------ weight producer
     if (lane == 0) {
       int slot = 0, ph = 0, rslot = 0, rph = 0, issued = 0;
-      int unit = blockIdx.x;
+      int unit = static_cast<int>(blockIdx.x) < total_units ? unit_of_claim(blockIdx.x) : total_units;
+      if (n_pre && (nch - 1 < 32 ? s_ce[nch - 1] : __ldg(a.ch_expert + nch - 1)) != a.sh_slot) {  // (the dispatch put it last)
+        atomicOr(a.err, 0x200000u);
+        *abort_flag = 1;
+      }
       for (int part = 0;; part++) {
         const bool stop = unit >= total_units || *abort_flag;
         int nxt = unit;
@@ -899,8 +937,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         int e = 0, p = 0;
         if (!stop) {
           x = decode(unit);
-          e = __ldg(a.ch_expert + x.c);
-          p = __ldg(a.ch_pos + x.c);
+          e = x.c < 32 ? s_ce[x.c] : __ldg(a.ch_expert + x.c);
+          p = x.c < 32 ? s_cp[x.c] : __ldg(a.ch_pos + x.c);
         }
         PartRec& r = recs[rslot];
         r.tile = stop ? -1 : x.tile;
@@ -916,26 +954,32 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         if (stop) break;
         const uint8_t* base = a.arena + static_cast<size_t>(e) * a.stride + (x.kind ? a.off_down : 0);
         const int kst = x.kind ? kst_dn : kst_gu;
-        if (trc && part == 0) trc[2] = global_ns();
+        if (trc && part == 0 && !pre) trc[2] = global_ns();
         if (trc && x.kind == 1 && !trc[3]) trc[3] = global_ns();
         for (int j = 0; j < x.ns; j++, issued++) {
-          if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
-            *abort_flag = 1;
-            break;
+          if (part > 0 || j >= pre) {  // (the preloaded stages were issued before the front end)
+            if (issued >= S && !mbar_wait_bounded(&empty[slot], ph ^ 1, a.err, 0x100u)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[slot], kTileBlock);
+            bulk_g2s_once(smem + slot * stage_pitch,
+                          base + (static_cast<size_t>(x.m) * kst + x.ks0 + j) * kTileBlock, kTileBlock, &full[slot]);
           }
-          mbar_arrive_expect_tx(&full[slot], kTileBlock);
-          bulk_g2s_once(smem + slot * stage_pitch, base + (static_cast<size_t>(x.m) * kst + x.ks0 + j) * kTileBlock,
-                   kTileBlock, &full[slot]);
           if (++slot == S) { slot = 0; ph ^= 1; }
           // the next claim at the unit's last stage (the ring still holds the stages before it):
           // near the end a CTA then holds one unit ahead, not two
-          if (j == x.ns - 1) nxt = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
+          if (j == x.ns - 1) {
+            const int q = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
+            nxt = q < total_units ? unit_of_claim(q) : total_units;
+          }
         }
         unit = nxt;
         if (*abort_flag) break;
       }
       if (*abort_flag)
         for (int i = 0; i < kRecRing; i++) recs[i].tile = -1;
+      if (issued < pre) issued = pre;  // (stopped before the preloaded unit: its copies are in flight)
       for (int i = (issued > S ? issued - S : 0); i < issued; i++)
         mbar_wait_bounded(&full[i % S], (i / S) & 1, a.err, 0x200u);
     }
@@ -1172,8 +1216,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (et == 0) red_release_gpu_add(a.tile_cnt + r.tile, 1);
     }
-    // every CTA's down parts stored -> each CTA adds the parts of its share of output rows in
-    // chunk order
+    // every CTA's down parts stored (grid barrier), then the whole grid adds them up below
     asm volatile("bar.sync 1, 128;" ::: "memory");
     if (trc && et == 0) trc[4] = global_ns();
     if (et == 0) {
@@ -1187,16 +1230,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         }
         __nanosleep(64);
       }
-    }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (trc && et == 0) trc[5] = global_ns();
-    if (!*abort_flag) {
-      for (int orow = blockIdx.x * 128 + et; orow < a.H; orow += gridDim.x * 128) {
-        const int m = orow / 128, rr = orow % 128;
-        float acc = 0.0f;
-        for (int c = 0; c < nch; c++) acc += __ldcg(a.part_dn + static_cast<size_t>(c * ntm_dn + m) * 128 + rr);
-        a.out[orow] = acc;
-      }
+      if (trc) trc[5] = global_ns();
     }
   }
   tc_fence_before();
@@ -1205,20 +1239,36 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     tc_fence_after();
     tmem_dealloc(tbase, kMtTmemCols);
   }
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int old = atomicAdd(a.work + 1, 1);
-    if (old == static_cast<int>(gridDim.x) - 1) {
-      // the last CTA out zeroes every counter of this launch for the next one
-      a.work[0] = 0;
-      a.work[1] = 0;
-      a.work[2] = 0;
-      a.work[3] = 0;
-      for (int i = 0; i < nch * ntm_gu; i++) a.tile_cnt[i] = 0;
-      for (int i = 0; i < nch; i++) a.h_ready[i] = 0;
+  // out[row] = the sum of the row's nch * dsplit down parts: four threads per row (every thread
+  // of the grid, one round of loads), each adding every fourth part in order, then the four sums
+  // combined in a fixed tree -- a deterministic order
+  if (!*abort_flag) {
+    const int np = nch * dsplit, rows_per_cta = blockDim.x / 4, q4 = threadIdx.x % 4;
+    for (int r0 = blockIdx.x * rows_per_cta; r0 < a.H; r0 += gridDim.x * rows_per_cta) {
+      const int orow = r0 + threadIdx.x / 4;
+      const bool on = orow < a.H;
+      const int m = on ? orow / 128 : 0, rr = orow % 128;
+      float pv[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int qi = q4 + 4 * j, c = qi / dsplit, h = qi % dsplit;
+        pv[j] = on && qi < np ? __ldcg(a.part_dn + static_cast<size_t>((c * ntm_dn + m) * dsplit + h) * 128 + rr)
+                              : 0.0f;
+      }
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc += pv[j];
+      for (int qi = q4 + 32; qi < np; qi += 4) {  // (more than 32 parts: rare)
+        const int c = qi / dsplit, h = qi % dsplit;
+        if (on) acc += __ldcg(a.part_dn + static_cast<size_t>((c * ntm_dn + m) * dsplit + h) * 128 + rr);
+      }
+      acc += __shfl_xor_sync(kFull, acc, 1);
+      acc += __shfl_xor_sync(kFull, acc, 2);
+      if (on && q4 == 0) a.out[orow] = acc;
     }
-    if (trc) trc[6] = global_ns();
   }
+  // (the counters are zeroed by the next launch's front end)
+  if (trc && threadIdx.x == 0) trc[6] = global_ns();
 }
 
 // ---------------------------------------------------------------------- activation terms per position
@@ -1456,11 +1506,13 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
 cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, int H, int I, const uint8_t* arena,
                                     size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
                                     float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
-                                    float* out, ActParams act, cudaStream_t st, unsigned long long* trace) {
+                                    float* out, ActParams act, int sh_slot, cudaStream_t st,
+                                    unsigned long long* trace) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   FusedArgs a{};
   a.trace = trace;
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.perm_w = d.perm_w; a.n_chunks = d.n_chunks;
+  a.max_chunks = d.max_chunks;
   a.H = H; a.I = I;
   a.arena = arena; a.stride = stride; a.off_down = off_down;
   a.ht = ht; a.hsf = hsf;
@@ -1468,6 +1520,7 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
   a.tile_cnt = tile_cnt; a.h_ready = h_ready; a.work = work; a.err = err; a.out = out;
   a.act = act;
   a.u_gu = small_unit_stages(H / kMtKStage);
+  a.sh_slot = sh_slot;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, 1) > 227 * 1024) stages--;
   a.stages = stages;

@@ -769,6 +769,8 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
       a.err[2 * b + q] = (1.01f + 2.0f * n * u) * u * (tt + Pt * (1.0f + n * u)) + 1e-37f;
     }
   } else if (b == nrb) {
+    // the one-token expert kernel's counters (it reads them only after this grid completes)
+    for (int i = threadIdx.x; i < a.zero_n; i += blockDim.x) a.zero_buf[i] = 0;
     if (a.gvec) {
       float dot = 0.0f;
       for (int i = threadIdx.x * 8; i < H; i += 512 * 8) {
@@ -811,7 +813,13 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
   __shared__ int c1i[16 * RMOE_MAX_TOPK_DEV], c2i[16 * RMOE_MAX_TOPK_DEV];
   __shared__ int sel_id[RMOE_MAX_TOPK_DEV], lo_id[RMOE_MAX_TOPK_DEV];
   __shared__ float sel_v[RMOE_MAX_TOPK_DEV], lo_v[RMOE_MAX_TOPK_DEV];
-  __shared__ float s_lo[512], s_hi[512];
+  __shared__ float s_lo[512], s_hi[512], s_v[512];
+  __shared__ __align__(16) uint32_t s_key[512];
+  __shared__ __align__(16) unsigned long long s_cand[16 * RMOE_MAX_TOPK_DEV];
+  __shared__ int s_top[RMOE_MAX_TOPK_DEV];
+  __shared__ float s_lk;
+  // (the shared expert's gate, read at the end: its load is issued now)
+  const float gate_pf = threadIdx.x == 0 && a.has_shared ? __ldcg(a.gate) : 0.0f;
   const int k = a.k, kk = min(k, E);
   const int e = threadIdx.x;
   const bool valid = e < E;
@@ -829,23 +837,78 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
       hi = __fadd_rn(hi, bb);
       v = __fadd_rn(v, bb);
     }
-    s_lo[e] = lo;
-    s_hi[e] = hi;
   }
+  s_lo[e] = lo;
+  s_hi[e] = hi;
+  s_v[e] = v;
   if (a.trace && threadIdx.x == 0) a.trace[3] = global_ns();
   // certified set: the kk-th largest lower bound Lk; exactly kk experts reaching it with their
-  // upper bounds are the top kk (every other value is below all of theirs), ranked by value
-  __shared__ float s_lk;
-  __shared__ int s_nc;
-  const float Lk = block_kth_largest(lo, id, kk, c1, c1i, &s_lk);
+  // upper bounds are the top kk (every other value is below all of theirs), ranked by value.
+  // Lk by counting, in two levels: each entry's rank by (lo desc, id asc) inside its warp (the
+  // warp's keys through shared memory), then the warps' first kk entries ranked against each
+  // other; the one of rank kk - 1 holds Lk. Ids ascend with the thread index (invalid entries
+  // after every expert), so ties go to the lower index.
+  const uint32_t klo = order_key(lo);
+  s_key[e] = klo;
+  __syncwarp();
+  {
+    int wr = 0;
+    const uint32_t* wk = s_key + wi * 32;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const uint4 q = *reinterpret_cast<const uint4*>(wk + j);
+      wr += (q.x > klo || (q.x == klo && j + 0 < lane)) ? 1 : 0;
+      wr += (q.y > klo || (q.y == klo && j + 1 < lane)) ? 1 : 0;
+      wr += (q.z > klo || (q.z == klo && j + 2 < lane)) ? 1 : 0;
+      wr += (q.w > klo || (q.w == klo && j + 3 < lane)) ? 1 : 0;
+    }
+    if (wr < kk) s_cand[wi * kk + wr] = (static_cast<unsigned long long>(klo) << 32) | (0xffffffffu - e);
+  }
+  __syncthreads();
+  const int nc = (blockDim.x / 32) * kk;  // even
+  if (e < nc) {
+    const unsigned long long me = s_cand[e];
+    int gr = 0;
+#pragma unroll 8
+    for (int j = 0; j < nc; j += 2) {
+      const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(s_cand + j);
+      gr += (q.x > me ? 1 : 0) + (q.y > me ? 1 : 0);
+    }
+    if (gr < kk) {
+      const int idx = static_cast<int>(0xffffffffu - static_cast<uint32_t>(me));
+      s_top[gr] = idx;
+      if (gr == kk - 1) s_lk = s_lo[idx];
+    }
+  }
+  __syncthreads();
+  const float Lk = s_lk;
   if (a.trace && threadIdx.x == 0) a.trace[4] = global_ns();
   const bool cont = valid && hi >= Lk;
   const int n_cont = __syncthreads_count(cont);
   const bool set_ok = n_cont == kk;
-  if (set_ok) block_rank_few(cont, v, id, kk, c2, c2i, &s_nc, sel_id, sel_v);
-  const int rr = threadIdx.x;
-  const bool pair_ok = !set_ok || rr >= kk - 1 || s_lo[sel_id[rr]] > s_hi[sel_id[rr + 1]];
-  const bool order_ok = __syncthreads_and(pair_ok);
+  bool order_ok = true;
+  if (set_ok) {
+    // the kk contenders are the top kk by lo (hi >= lo >= Lk for each): warp 0 ranks them by
+    // (value desc, id asc) and checks that neighbours' intervals are apart
+    if (wi != 0) return;
+    const bool has = lane < kk;
+    const int ei = has ? s_top[lane] : 0x7fffffff;
+    const float vi = has ? s_v[ei] : -INFINITY;
+    const uint32_t kv = has ? order_key(vi) : 0u;
+    int vr = 0;
+    for (int j = 0; j < kk; j++) {
+      const uint32_t kj = __shfl_sync(kFull, kv, j);
+      const int ej = __shfl_sync(kFull, ei, j);
+      vr += (kj > kv || (kj == kv && ej < ei)) ? 1 : 0;
+    }
+    if (has) {
+      sel_id[vr] = ei;
+      sel_v[vr] = vi;
+    }
+    __syncwarp();
+    const bool pok = lane >= kk - 1 || s_lo[sel_id[lane]] > s_hi[sel_id[lane + 1]];
+    order_ok = __all_sync(kFull, pok);
+  }
   if (!set_ok) {
     float ex = -INFINITY;
     if (valid && hi >= Lk) {
@@ -895,7 +958,7 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
         a.d.ch_pos[n_routed] = n_routed;
         a.d.ch_n[n_routed] = 1;
         a.d.perm_tok[n_routed] = 0;
-        a.d.perm_w[n_routed] = __ldcg(a.gate);
+        a.d.perm_w[n_routed] = gate_pf;
       }
       a.d.n_chunks[0] = n_routed + a.has_shared;
       a.d.offsets[a.n_loc] = n_routed;
