@@ -1017,7 +1017,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       // one token after the fused front end: gate/up and down of all its experts in one launch
       e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
                                   L->hsf, L->partial, L->partial2, L->fused_cnt + 8, L->fused_cnt + 8 + L->fused_tiles,
-                                  L->fused_cnt, L->dev_err, out, L->fmt.act, (L->has_shared && !getenv("RMOE_NO_PRELOAD")) ? L->n_loc : -1, st,
+                                  L->fused_cnt, L->dev_err, out, L->fmt.act, L->has_shared ? L->n_loc : -1, st,
                                   L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr);
       if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
       marks.mark();
