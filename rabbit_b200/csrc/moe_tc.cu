@@ -869,6 +869,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
   // the first 32 chunks' experts and positions, loaded together with the chunk count (the
   // weight producer's first units need them at once)
   __shared__ int s_ce[32], s_cp[32];
+  // a CTA whose first unit was preloaded claims its second one now, beside these loads
+  int claim2 = 0;
+  if (warp == 0 && lane == 0 && pre) claim2 = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
   if (warp == 0 && lane < a.max_chunks) {
     s_ce[lane] = __ldg(a.ch_expert + lane);
     s_cp[lane] = __ldg(a.ch_pos + lane);
@@ -970,7 +973,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
           // the next claim at the unit's last stage (the ring still holds the stages before it):
           // near the end a CTA then holds one unit ahead, not two
           if (j == x.ns - 1) {
-            const int q = static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
+            const int q = part == 0 && pre ? claim2 : static_cast<int>(gridDim.x) + atomicAdd(a.work, 1);
             nxt = q < total_units ? unit_of_claim(q) : total_units;
           }
         }
