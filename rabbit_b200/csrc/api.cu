@@ -1013,18 +1013,24 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       if (e != cudaSuccess) return cuda_fail(e, "activation terms");
     }
     marks.mark();
-    if (T == 1 && terms_done && L->use_fused && (!L->tc_trace || !L->tc_trace_print)) {
-      // one token after the fused front end: gate/up and down of all its experts in one launch
+    if (T == 1 && L->use_fused && (!L->tc_trace || !L->tc_trace_print)) {
+      // one token: gate/up and down of all its experts in one launch. The one-token front end
+      // zeroes the kernel's counters and puts the shared expert last (its copies may start
+      // before the front end is done); other callers zero them here and preload nothing.
+      if (!terms_done)
+        RMOE_CUDA(cudaMemsetAsync(L->fused_cnt, 0, (8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1) * 4, st),
+                  "fused counters");
       e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
                                   L->hsf, L->partial, L->partial2, L->fused_cnt + 8, L->fused_cnt + 8 + L->fused_tiles,
-                                  L->fused_cnt, L->dev_err, out, L->fmt.act, L->has_shared ? L->n_loc : -1, st,
+                                  L->fused_cnt, L->dev_err, out, L->fmt.act, terms_done && L->has_shared ? L->n_loc : -1, st,
                                   L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr);
       if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
       marks.mark();
       marks.mark();
       marks.mark();
       marks.mark();
-      launches = 3;  // front, order resolve (side stream), fused experts
+      // front, order resolve (side stream), fused experts; or the generic front plus terms
+      launches = terms_done ? 3 : (fused_ok ? 5 : 8);
       return RMOE_OK;
     }
     // one token: every position reads the token's own term rows (0..3)
