@@ -1496,8 +1496,15 @@ static rmoe_status experts_for_routing(rmoe_layer* L, const void* x, int xdt, in
                                        L->xexp, L->gate, st);
     if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
   }
-  rmoe_status s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs);
-  if (s != RMOE_OK) return s;
+  rmoe_status s = RMOE_OK;
+  if (T == 1 && L->use_tc && L->use_fused && (!L->tc_trace || !L->tc_trace_print) && D.topk <= 32) {
+    // (the one-token expert kernel reads only the chunk table: one warp builds it)
+    cudaError_t e = launch_dispatch_one_token(L->ids, L->rw, D.topk, L->e_begin, L->e_end, L->n_loc, hs ? 1 : 0,
+                                              gated ? L->gate : nullptr, L->d, st);
+    if (e != cudaSuccess) return cuda_fail(e, "one-token dispatch");
+  } else if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs)) != RMOE_OK) {
+    return s;
+  }
   StageMarks marks(L, st);
   const bool prof = L->profiling;
   L->profiling = false;  // (stage events cover rmoe_moe_forward only)
@@ -1590,9 +1597,9 @@ extern "C" rmoe_status rmoe_latent_moe(rmoe_layer* L, const void* x, int32_t x_d
   // the routed experts at the latent width (:94-104); no shared expert here (the caller's)
   if ((s = experts_for_routing(L, L->lat_x, kF32, T, false, L->lat_y, st)) != RMOE_OK) return s;
   // RMSNorm of each token's summed routed row (:106-110), then out = y . up^T (:112)
-  if (L->lat_has_norm && (e = launch_rmsnorm_rows(L->lat_y, T, H, L->lat_norm, L->lat_eps, st)) != cudaSuccess)
-    return cuda_fail(e, "latent norm");
-  if ((e = launch_latent_proj(L->lat_up, L->lat_dtype, L->lat_y, kF32, T, H, Hr, out, st)) != cudaSuccess)
+  // (the norm is applied by the up projection's blocks to their staged copy of y)
+  if ((e = launch_latent_proj(L->lat_up, L->lat_dtype, L->lat_y, kF32, T, H, Hr, out, st,
+                              L->lat_has_norm ? L->lat_norm : nullptr, L->lat_eps)) != cudaSuccess)
     return cuda_fail(e, "latent up projection");
   const size_t n = static_cast<size_t>(T) * k;
   if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, L->ids, n * 4, cudaMemcpyDeviceToDevice, st), "latent ids");

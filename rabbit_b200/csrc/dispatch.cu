@@ -212,4 +212,50 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* w, int T, int k, in
   return cudaGetLastError();
 }
 
+// One token for the one-token expert kernel: positions by ascending expert id among the local
+// slots, one chunk per position, the shared expert last. Fills what that kernel and the
+// activation terms read (inv, the chunk table, perm_tok / perm_w, n_chunks, the shared offsets).
+__global__ void dispatch_one_token_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w, int k,
+                                          int e_begin, int e_end, int n_loc, int has_shared,
+                                          const float* __restrict__ shared_gate_w, DispatchBuffers d) {
+  const int lane = threadIdx.x;
+  const int sid = lane < k ? ids[lane] : -1;
+  const float wv = lane < k ? w[lane] : 0.0f;
+  const bool local = lane < k && sid >= e_begin && sid < e_end;
+  int pos = 0;
+  for (int j = 0; j < k; j++) {
+    const int o = __shfl_sync(kFull, sid, j);
+    pos += (o >= e_begin && o < e_end && o < sid) ? 1 : 0;
+  }
+  const int n_routed = __popc(__ballot_sync(kFull, local));
+  if (lane < k) d.inv[lane] = local ? pos : -1;
+  if (local) {
+    d.ch_expert[pos] = sid - e_begin;
+    d.ch_pos[pos] = pos;
+    d.ch_n[pos] = 1;
+    d.perm_tok[pos] = 0;
+    d.perm_w[pos] = wv;
+  }
+  if (lane == 0) {
+    if (has_shared) {
+      d.ch_expert[n_routed] = n_loc;
+      d.ch_pos[n_routed] = n_routed;
+      d.ch_n[n_routed] = 1;
+      d.perm_tok[n_routed] = 0;
+      d.perm_w[n_routed] = shared_gate_w ? shared_gate_w[0] : 1.0f;
+    }
+    d.n_chunks[0] = n_routed + has_shared;
+    d.offsets[n_loc] = n_routed;
+    d.offsets[n_loc + has_shared] = n_routed + has_shared;
+  }
+}
+
+cudaError_t launch_dispatch_one_token(const int32_t* ids, const float* w, int k, int e_begin, int e_end, int n_loc,
+                                      int has_shared, const float* shared_gate_w, const DispatchBuffers& d,
+                                      cudaStream_t st) {
+  if (k > 32) return cudaErrorInvalidValue;
+  dispatch_one_token_kernel<<<1, 32, 0, st>>>(ids, w, k, e_begin, e_end, n_loc, has_shared, shared_gate_w, d);
+  return cudaGetLastError();
+}
+
 }  // namespace rmoe

@@ -155,6 +155,10 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* w, int T, int k, in
                             int e_end, int mt, int has_shared, const float* shared_gate_w,
                             int inter, int shared_inter, int hidden, int rows_per_task_gu,
                             int rows_per_task_dn, const DispatchBuffers& d, cudaStream_t st);
+// One token (k <= 32) for the one-token expert kernel: inv, chunk table, perm, n_chunks only.
+cudaError_t launch_dispatch_one_token(const int32_t* ids, const float* w, int k, int e_begin, int e_end, int n_loc,
+                                      int has_shared, const float* shared_gate_w, const DispatchBuffers& d,
+                                      cudaStream_t st);
 
 // ---- expert compute (experts.cu) ----
 // x[T][H] -> xq[T][H] f16 (power-of-two scaled, format pairing), xexp[T] (the exponent), and
@@ -242,10 +246,9 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
                                     unsigned long long* trace = nullptr);
 
 // ---- latent MoE wrapper (latent.cu) ----
-// y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)
+// y[T][N] = x'[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0); x' = x, or with
+// `norm` each row of x RMS-normalized (f64 mean of squares, weight norm[K], eps)
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
-                               cudaStream_t st);
-// v[r] *= w / sqrt(mean(v[r]^2) + eps) for each of `rows` rows of n
-cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st);
+                               cudaStream_t st, const float* norm = nullptr, float eps = 0.0f);
 
 }  // namespace rmoe
