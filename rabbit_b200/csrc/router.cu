@@ -181,11 +181,16 @@ __global__ void __launch_bounds__(256) router_exact_warp_kernel(const void* __re
     if (c0 + kRwChunk < H) load_chunk(c0 + kRwChunk);
     __syncwarp();
     if (lane == 0) {
-      // 16 products per step, their shared-memory loads issued before the dependent adds
-      for (int i = 0; i < kRwChunk; i += 16) {
-        float4 q[4];
+      // 16 products per step; the next step's shared-memory loads are issued before this step's
+      // dependent adds, so only the add latency remains
+      float4 q[4], nq[4];
 #pragma unroll
-        for (int u = 0; u < 4; u++) q[u] = *reinterpret_cast<const float4*>(buf + i + 4 * u);
+      for (int u = 0; u < 4; u++) q[u] = *reinterpret_cast<const float4*>(buf + 4 * u);
+      for (int i = 0; i < kRwChunk; i += 16) {
+        if (i + 16 < kRwChunk) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) nq[u] = *reinterpret_cast<const float4*>(buf + i + 16 + 4 * u);
+        }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
           acc = __fadd_rn(acc, q[u].x);
@@ -193,6 +198,8 @@ __global__ void __launch_bounds__(256) router_exact_warp_kernel(const void* __re
           acc = __fadd_rn(acc, q[u].z);
           acc = __fadd_rn(acc, q[u].w);
         }
+#pragma unroll
+        for (int u = 0; u < 4; u++) q[u] = nq[u];
       }
     }
     __syncwarp();
