@@ -246,9 +246,10 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
                                     unsigned long long* trace = nullptr);
 
 // ---- latent MoE wrapper (latent.cu) ----
-// y[T][N] = x'[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0); x' = x, or with
-// `norm` each row of x RMS-normalized (f64 mean of squares, weight norm[K], eps)
+// y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
-                               cudaStream_t st, const float* norm = nullptr, float eps = 0.0f);
+                               cudaStream_t st);
+// v[r] *= w / sqrt(mean(v[r]^2) + eps) for each of `rows` rows of n
+cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st);
 
 }  // namespace rmoe

@@ -4,9 +4,8 @@
 // src/kimi_linear/ops.rs:46-53), out = y . up^T after them.
 //
 // The projections are memory-bound matrix-vector products for decode-sized T: one warp per
-// output row streams that row of W once (16-byte loads, eight in flight per lane) against the
+// output row streams that row of W once (16-byte loads, four in flight per lane) against the
 // tokens of x staged in shared memory, eight tokens per pass (larger T: several passes over W).
-// The norm runs inside the up projection, on each block's staged copy of the rows.
 #include <algorithm>
 
 #include "common.cuh"
@@ -37,20 +36,14 @@ __device__ __forceinline__ void load_w8(const void* w, size_t i, float (&v)[8]) 
 constexpr int kProjTok = 8;        // tokens per pass over W
 constexpr int kProjWarps = 16;     // output rows per block
 constexpr int kProjSmem = 96 * 1024;
-constexpr int kProjLoads = 8;      // 16-byte weight loads in flight per lane
 
-// y[t][n] = sum_k x'[t][k] w[n][k]; K % 8 == 0. Each block stages up to `tg` tokens of x in
-// shared memory (f32) and its 16 warps each stream one row of W against them. With `norm`
-// set, x' is each token's row RMS-normalized on the way in (x * (r * norm[k]),
-// r = 1 / sqrt(mean(x^2) + eps), the mean of squares accumulated in f64): every block normalizes
-// its staged copy itself, so the norm needs no launch of its own.
+// y[t][n] = sum_k x[t][k] w[n][k]; K % 8 == 0. Each block stages up to `tg` tokens of x in
+// shared memory (f32) and its 16 warps each stream one row of W against them.
 template <int WD, int XD>
 __global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void* __restrict__ w,
                                                                       const void* __restrict__ x, int T, int K, int N,
-                                                                      int tg, const float* __restrict__ norm, float eps,
-                                                                      float* __restrict__ y) {
+                                                                      int tg, float* __restrict__ y) {
   extern __shared__ __align__(16) float px[];  // [tg][K]
-  __shared__ double red[kProjWarps];
   const int lane = threadIdx.x % 32, wi = threadIdx.x / 32;
   for (int n0 = blockIdx.x * kProjWarps; n0 < N; n0 += gridDim.x * kProjWarps) {
     const int n = n0 + wi;
@@ -64,37 +57,19 @@ __global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void
         for (int j = 0; j < 8; j++) px[i + j] = v[j];
       }
       __syncthreads();
-      if (norm) {
-        for (int t = 0; t < nt; t++) {
-          float* row = px + static_cast<size_t>(t) * K;
-          double ss = 0.0;
-          for (int i = threadIdx.x; i < K; i += blockDim.x) ss += static_cast<double>(row[i]) * row[i];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-          if (lane == 0) red[wi] = ss;
-          __syncthreads();
-          double tot = 0.0;
-          for (int q = 0; q < kProjWarps; q++) tot += red[q];
-          const float ms = static_cast<float>(tot / static_cast<double>(K));
-          const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-          __syncthreads();  // (red is read by every thread before the next token's sums)
-          for (int i = threadIdx.x; i < K; i += blockDim.x) row[i] = row[i] * __fmul_rn(r, norm[i]);
-        }
-        __syncthreads();
-      }
       if (n >= N) continue;
       for (int ts = 0; ts < nt; ts += kProjTok) {
         const int ns = min(kProjTok, nt - ts);
         float acc[kProjTok];
 #pragma unroll
         for (int t = 0; t < kProjTok; t++) acc[t] = 0.0f;
-        for (int k0 = lane * 8; k0 < K; k0 += kProjLoads * 256) {
-          float wv[kProjLoads][8];  // kProjLoads 16-byte weight loads in flight per lane
+        for (int k0 = lane * 8; k0 < K; k0 += 4 * 256) {
+          float wv[4][8];  // four 16-byte weight loads in flight per lane
 #pragma unroll
-          for (int u = 0; u < kProjLoads; u++)
+          for (int u = 0; u < 4; u++)
             if (k0 + u * 256 < K) load_w8<WD>(w, static_cast<size_t>(n) * K + k0 + u * 256, wv[u]);
 #pragma unroll
-          for (int u = 0; u < kProjLoads; u++) {
+          for (int u = 0; u < 4; u++) {
             const int k = k0 + u * 256;
             if (k >= K) break;
 #pragma unroll
@@ -120,15 +95,47 @@ __global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void
   }
 }
 
+// In place, one 1024-thread block per row: v *= r * w with r = 1 / sqrt(mean(v^2) + eps), the
+// mean of squares accumulated in f64 as the reference does. The row is read once into registers
+// (up to kNormPer values per thread, loads issued together).
+constexpr int kNormPer = 8;
+__global__ void __launch_bounds__(1024) rmsnorm_rows_kernel(float* __restrict__ v, int n, const float* __restrict__ w,
+                                                            float eps) {
+  __shared__ double part[32];
+  float* row = v + static_cast<size_t>(blockIdx.x) * n;
+  float a[kNormPer];
+#pragma unroll
+  for (int j = 0; j < kNormPer; j++) {
+    const int i = threadIdx.x + j * blockDim.x;
+    a[j] = i < n ? row[i] : 0.0f;
+  }
+  double s = 0.0;
+#pragma unroll
+  for (int j = 0; j < kNormPer; j++) s += static_cast<double>(a[j]) * static_cast<double>(a[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  if (threadIdx.x % 32 == 0) part[threadIdx.x / 32] = s;
+  __syncthreads();
+  double tot = 0.0;
+  for (int i = 0; i < static_cast<int>(blockDim.x / 32); i++) tot += part[i];
+  const float ms = static_cast<float>(tot / static_cast<double>(n));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+#pragma unroll
+  for (int j = 0; j < kNormPer; j++) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n) row[i] = a[j] * __fmul_rn(r, w[i]);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
-                               cudaStream_t st, const float* norm, float eps) {
+                               cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   if (K % 8 || static_cast<size_t>(K) * 4 > kProjSmem) return cudaErrorInvalidValue;
   const int tg = std::min(T, static_cast<int>(kProjSmem / (static_cast<size_t>(K) * 4)));
   const size_t smem = static_cast<size_t>(tg) * K * 4;
-  void (*kern)(const void*, const void*, int, int, int, int, const float*, float, float*) =
+  void (*kern)(const void*, const void*, int, int, int, int, float*) =
       w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16> : latent_proj_kernel<kBF16, kF32>)
                        : (x_dtype == kBF16 ? latent_proj_kernel<kF32, kBF16> : latent_proj_kernel<kF32, kF32>);
   if (smem > 48 * 1024) {
@@ -136,7 +143,14 @@ cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_
     if (e != cudaSuccess) return e;
   }
   const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, 148 * 4);
-  kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, norm, eps, y);
+  kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (n > 1024 * kNormPer) return cudaErrorInvalidValue;
+  rmsnorm_rows_kernel<<<rows, 1024, 0, st>>>(v, n, w, eps);
   return cudaGetLastError();
 }
 
