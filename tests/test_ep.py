@@ -204,3 +204,29 @@ def test_expert_parallel_two_gpus():
     sel = [0, 1, 20, 39]
     want, _, _ = oracle_forward(cfg, x[sel])
     assert rel_l2(got[sel], want) < 1e-2
+
+
+@pytest.mark.gpu
+def test_forward_routed_one_token(cuda_ctx):
+    """One token through forward_routed (the fused one-token kernel behind a one-warp dispatch,
+    no front end): with the layer's own routing it is the layer forward, with and without the
+    shared expert, and with half the slots dropped it is the sum of the kept slots."""
+    import torch
+
+    cfg = _mid_cfg()
+    L = synth.build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    xa = synth.activations(cfg)
+    for t in (0, 7):
+        x = synth.x_device(cfg, xa[t:t + 1])
+        full, ids, w = L.moe_forward(x, return_routing=True)
+        routed = L.forward_routed(x, ids, w)
+        assert rel_l2(routed.cpu().numpy(), full.cpu().numpy()) < 1e-5
+        none = torch.full_like(ids, -1)
+        shared = L.forward_routed(x, none, torch.zeros_like(w), with_shared=True)
+        keep = torch.arange(ids.shape[1], device=ids.device) % 2 == 0
+        a = L.forward_routed(x, torch.where(keep, ids, none), torch.where(keep, w, torch.zeros_like(w)),
+                             with_shared=False)
+        b = L.forward_routed(x, torch.where(keep, none, ids), torch.where(keep, torch.zeros_like(w), w),
+                             with_shared=False)
+        assert rel_l2((a + b + shared).cpu().numpy(), full.cpu().numpy()) < 1e-5
+    L.close()
