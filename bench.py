@@ -144,6 +144,33 @@ def cpu_decode_time(cfg, budget_s=12.0, min_tokens=3, threads=None, setup=None):
     return el / n, n, orc.get_threads()
 
 
+def cpu_decode_warm_cold(cfg, setup, reps=3):
+    """Seconds per decode token with warm caches (the same token again) and cold ones (a buffer
+    larger than L3 written before each call), as benches/kernels.rs:355-408 times its kernels."""
+    from oracle import oracle as orc
+
+    x, router, experts, shared = setup
+    sg, lb = synth.shared_gate(cfg), synth.logit_bias(cfg)
+
+    def one():
+        orc.moe_forward_qwen(x[:1], router, experts, cfg.n_experts, cfg.topk, cfg.inter, shared=shared,
+                             shared_gate=sg, logit_bias=lb, shared_inter=cfg.shared_inter, tier="avx512")
+
+    one()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one()
+    warm = (time.perf_counter() - t0) / reps
+    evict = np.zeros(512 << 20, np.uint8)
+    cold = 0.0
+    for r in range(reps):
+        evict[::64] = r + 1
+        t0 = time.perf_counter()
+        one()
+        cold += time.perf_counter() - t0
+    return warm, cold / reps
+
+
 def physical_cores():
     try:
         import psutil
@@ -161,6 +188,16 @@ def cpu_model():
     except OSError:
         pass
     return "unknown"
+
+
+def decode_config(world):
+    """The headline workload's config object: the same dict on both arms of the bench."""
+    cfg = synth.CONFIGS[DECODE_CFG]
+    return {"workload": DECODE_CFG, "tokens_per_step_per_gpu": 1, "hidden": cfg.hidden,
+            "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+            "shared_inter": cfg.shared_inter, "weights": "mxfp4 (E2M1 + E8M0/32)",
+            "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
+            "l2": "flushed between timed steps (256 MiB write, then a 256 MiB read that drains the write-backs)"}
 
 
 def run_reference(args):
@@ -183,9 +220,8 @@ def run_reference(args):
         "unit": "us/token", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sec * 1e3, "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": DECODE_CFG, "tokens_per_step": 1, "hidden": cfg.hidden,
-                   "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
-                   "weights": "mxfp4", "cpu": cpu_model()},
+        "config": decode_config(world),
+        "cpu": cpu_model(),
         "cpu_baseline": {"value": us, "unit": "us/token", "cores": used, "kind": "port",
                          "sample": f"{n} decode tokens round-robin over 4 seeded tokens; C "
                                    "restatement of rabbit's AVX-512 MXFP4 tier + f32 router, "
@@ -217,6 +253,7 @@ def expert_touch_bytes(cfg, ids_np, with_shared=True):
 
 
 EP_CFG = "c3_qwen_ep"
+EP_PARITY_TOKENS = 16
 
 
 def run_ep(args, ctx, dev, rank, world, flush):
@@ -240,11 +277,14 @@ def run_ep(args, ctx, dev, rank, world, flush):
     x0 = x_device(cfg, synth.activations(cfg, tokens=t_local, token_offset=rank * t_local))
     stream = torch.cuda.current_stream()
 
-    def step():
+    def step(keep=None):
         x, ids_l = x0, []
         for ep in eps:
             out, ids, _ = ep.forward(x)
             ids_l.append(ids)
+            if keep is not None:
+                keep.append((x[:EP_PARITY_TOKENS].clone(), out[:EP_PARITY_TOKENS].clone(),
+                             ids[:EP_PARITY_TOKENS].clone()))
             x = out.to(torch.bfloat16)
         return x, ids_l
 
@@ -285,6 +325,31 @@ def run_ep(args, ctx, dev, rank, world, flush):
         distinct = len(np.unique(a[(a >= lo) & (a < hi)]))
         rbytes += (distinct + 1) * cfg.expert_bytes() + cfg.n_experts * cfg.hidden * 2 + \
             t_local * cfg.hidden * (2 + 4)
+    # parity at this N: rank 0's first tokens, layer by layer, against one GPU holding all the
+    # layer's experts (moe_forward on the same layer input): routing ids bit-exact, output rel-L2
+    keep = []
+    step(keep)
+    torch.cuda.synchronize()
+    for L in layers:
+        L.close()
+    layers = []
+    torch.cuda.empty_cache()
+    parity = None
+    if rank == 0:
+        rels, ids_equal = [], True
+        for l, (xin, got, got_ids) in enumerate(keep):
+            full = build_layer(ctx, cfg, max_tokens=EP_PARITY_TOKENS, layer=l)
+            want, want_ids, _ = full.moe_forward(xin, return_routing=True)
+            torch.cuda.synchronize()
+            full.close()
+            ids_equal &= bool(torch.equal(got_ids, want_ids))
+            rels.append(float((got - want).norm() / want.norm()))
+        parity = {"reference": "one GPU holding all 512 experts of each layer (moe_forward on the same layer input)",
+                  "tokens": EP_PARITY_TOKENS, "layers": cfg.n_layers, "ids_bit_exact": ids_equal,
+                  "max_rel_l2": max(rels), "tolerance": 1e-2,
+                  "ok": ids_equal and max(rels) < 1e-2}
+    if world > 1:
+        dist.barrier()
     rb_t = torch.tensor([rbytes, float(np.mean(xbytes))], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(rb_t, op=dist.ReduceOp.MAX)
@@ -299,13 +364,12 @@ def run_ep(args, ctx, dev, rank, world, flush):
            "max_rank_algorithmic_bytes": max_bytes,
            "achieved_gbs_per_gpu": max_bytes / (ms / 1e3) / 1e9,
            "hbm_frac_per_gpu": max_bytes / (ms / 1e3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
-           "remote_bytes_per_gpu_per_step": max_x, "build_s": build_s}
-    for L in layers:
-        L.close()
+           "remote_bytes_per_gpu_per_step": max_x, "build_s": build_s, "parity": parity}
     return res
 
 
 LATENT_CFG = "c5_k3_latent"
+C4_CFG = "c4_glm_int4"
 
 
 def run_latent(args, ctx, dev, rank, world, flush):
@@ -355,6 +419,83 @@ def run_latent(args, ctx, dev, rank, world, flush):
            "hbm_frac": nbytes / (us * 1e-6) / 1e9 / hbm_peak, "peak_kind": peak_kind}
     L.close()
     return res
+
+
+def run_c4(args, ctx, dev, rank, world, flush):
+    """Config 4: the GLM-style grouped-int4 layer, 512 tokens per step (sigmoid grouped router,
+    256 experts top-8, symmetric int4 with a bf16 scale per 32, always-on shared expert), inputs
+    resident, L2 flushed between steps. Each rank runs its own replica."""
+    import torch
+    import torch.distributed as dist
+
+    from rabbit_b200.synth import build_layer, x_device
+
+    cfg = synth.CONFIGS[C4_CFG]
+    L = build_layer(ctx, cfg, max_tokens=cfg.tokens, scale_dtype="bf16")
+    xd = x_device(cfg, synth.activations(cfg, tokens=cfg.tokens, token_offset=rank * cfg.tokens))
+    out = torch.empty((cfg.tokens, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        flush.zero_()
+        L.moe_forward(xd, out=out)
+    torch.cuda.synchronize()
+    L.set_profiling(True)
+    L.profile()
+    ev = []
+    for _ in range(args.c4_steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        L.moe_forward(xd, out=out)
+        b.record(stream)
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    prof = L.profile()
+    L.set_profiling(False)
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.c4_steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ids = L.route(xd)[0].cpu().numpy()
+    L.check()
+    L.close()
+    distinct = len(np.unique(ids))
+    eb = cfg.expert_bytes(scale_bytes=2)  # bf16 scales: 21,233,664 B per expert
+    nbytes = (distinct + 1) * eb + cfg.n_experts * cfg.hidden * 2 + cfg.tokens * cfg.hidden * (2 + 4)
+    hbm_peak, _, peak_kind = peaks()
+    return {"metric": "glm_int4_layer_us_per_step", "value": ms * 1e3, "unit": "us/step",
+            "tokens_per_s": cfg.tokens * world / (ms / 1e3), "ms_per_step": ms, "steps": args.c4_steps,
+            "config": {"workload": C4_CFG, "tokens_per_step_per_gpu": cfg.tokens, "hidden": cfg.hidden,
+                       "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+                       "weights": "int4 (offset-binary nibbles) + bf16 scale per 32",
+                       "router": "sigmoid + correction bias, 8 groups top-4, scale 2.5",
+                       "l2": "flushed between steps"},
+            "distinct_experts": distinct, "expert_bytes": eb, "algorithmic_bytes": nbytes,
+            "achieved_gbs": nbytes / (ms / 1e3) / 1e9, "hbm_frac": nbytes / (ms / 1e3) / 1e9 / hbm_peak,
+            "peak_kind": peak_kind,
+            "stages_ms": {k: prof[k] / max(1, prof["calls"]) for k in prof if k != "calls"}}
+
+
+def cpu_c4_time(threads, n_tokens=8):
+    """Seconds per step of config 4 on the host: the reference's GLM path restated in C (exact f32
+    router chains, sigmoid grouped top-k, scalar matmul_i4_grouped as in src/kernels.rs:276-296,
+    OpenMP over output rows like its rayon), over a bounded batch of n_tokens tokens."""
+    from oracle import oracle as orc
+
+    cfg = synth.CONFIGS[C4_CFG]
+    orc.set_threads(threads)
+    x = synth.activations(cfg, tokens=n_tokens, token_offset=20_000)
+    router, bias = synth.router_weights(cfg), synth.correction_bias(cfg)
+    ids, _ = orc.glm_route(x, router, bias, n_tokens, cfg.hidden, cfg.n_experts, cfg.topk, cfg.n_group,
+                           cfg.topk_group, cfg.norm_topk, cfg.routed_scale)
+    experts = {int(e): synth.expert(cfg, int(e)) for e in np.unique(ids)}
+    shared = synth.expert(cfg, cfg.n_experts)
+    t0 = time.perf_counter()
+    orc.moe_glm(x, router, bias, experts, cfg.n_experts, cfg.topk, cfg.inter, cfg.n_group, cfg.topk_group,
+                cfg.norm_topk, cfg.routed_scale, shared=shared, shared_inter=cfg.shared_inter,
+                fmt=cfg.fmt_id, gs=cfg.group_size)
+    return time.perf_counter() - t0
 
 
 def run_gpu(args):
@@ -531,12 +672,7 @@ def run_gpu(args):
                            "max": round(max(step_ms) * 1e3, 2), "argmax": int(np.argmax(step_ms))},
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
         "dtype": "mxfp4 weights x 4-term e2m1 activations (tcgen05 kind::mxf4), f32 accumulate", "data": "synthetic",
-        "config": {"workload": DECODE_CFG, "tokens_per_step_per_gpu": 1, "hidden": cfg.hidden,
-                   "n_experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
-                   "shared_inter": cfg.shared_inter, "weights": "mxfp4 (E2M1 + E8M0/32)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
-                   "l2": "flushed between timed steps (256 MiB write, then a 256 MiB read that drains the write-backs)",
-                   "layer_algorithmic_bytes": layer_bytes},
+        "config": decode_config(world),
         "roofline": {"bound": "hbm", "kernel": rf_name,
                      "achieved": rf_bytes / (rf_ms / 1e3) / 1e9 if rf_ms > 0 else None,
                      "peak": hbm_peak, "unit": "GB/s", "peak_kind": peak_kind,
@@ -545,6 +681,7 @@ def run_gpu(args):
                      "traffic_source": "profiles/moe_tc_kernel_decode_small.md (ncu, per launch)",
                      "kernel_us": rf_ms * 1e3, "kernel_bytes": rf_bytes,
                      "kernel_timing": "CUDA events around the kernel on its stream, profiling pass over the timed tokens",
+                     "layer_algorithmic_bytes": layer_bytes,
                      "layer_achieved_gbs": layer_bytes / (ms_per_step / 1e3) / 1e9,
                      "layer_frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / hbm_peak},
         "stages_us": stages_us,
@@ -563,6 +700,12 @@ def run_gpu(args):
         layer = None
         torch.cuda.empty_cache()
         line["ep"] = run_ep(args, ctx, dev, rank, world, flush)
+    if not args.no_c4:
+        if layer is not None:
+            layer.close()
+            layer = None
+        torch.cuda.empty_cache()
+        line["c4"] = run_c4(args, ctx, dev, rank, world, flush)
     if not args.no_latent:
         if layer is not None:
             layer.close()
@@ -570,12 +713,21 @@ def run_gpu(args):
         torch.cuda.empty_cache()
         line["latent"] = run_latent(args, ctx, dev, rank, world, flush)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, n, used = cpu_decode_time(dcfg, budget_s=args.cpu_budget, threads=physical_cores())
+        setup = cpu_decode_setup(dcfg)
+        sec, n, used = cpu_decode_time(dcfg, budget_s=args.cpu_budget, threads=physical_cores(), setup=setup)
+        warm, cold = cpu_decode_warm_cold(dcfg, setup)
         line["cpu_baseline"] = {
             "value": sec * 1e6, "unit": "us/token", "cores": used, "kind": "port",
             "cpu": cpu_model(),
+            "warm_us": warm * 1e6, "cold_us": cold * 1e6,
             "sample": f"{n} decode tokens round-robin over 4 seeded tokens (~{args.cpu_budget:.0f} s); "
-                      "C restatement of rabbit's AVX-512 MXFP4 tier + f32 router, OpenMP over rows"}
+                      "C restatement of rabbit's AVX-512 MXFP4 tier + f32 router, OpenMP over rows. "
+                      "warm: one token repeated; cold: a 512 MiB write before each call evicts the caches"}
+        if not args.no_c4:
+            c4_s = cpu_c4_time(physical_cores())
+            line["cpu_baseline"]["c4"] = {
+                "value": c4_s * 1e6 / 8, "unit": "us/token", "tokens_per_s": 8 / c4_s, "cores": used,
+                "kind": "port", "sample": "8 tokens of config 4 through the restated GLM layer (scalar int4)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if layer is not None:
@@ -583,6 +735,50 @@ def run_gpu(args):
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_profile_case(args):
+    """A profiling workload, not a bench line: build one layer and run --forwards forwards of one
+    case, the last one inside a cudaProfilerStart/Stop range when --profile-last is given (so that
+    `ncu --profile-from-start off` captures exactly that call). --small-experts shrinks the
+    resident experts (same shapes and kernels) so that a multi-metric capture stays small.
+    Cases: prefill (c2, 2048 tokens), decode (c1, one token), latent (K3 latent MoE, one token),
+    int4 (c4, 512 tokens)."""
+    import dataclasses
+
+    import torch
+
+    import rabbit_b200 as rb
+    from rabbit_b200.synth import build_layer, x_device
+
+    name = {"prefill": PREFILL_CFG, "decode": DECODE_CFG, "latent": LATENT_CFG, "int4": C4_CFG}[args.profile_case]
+    cfg = synth.CONFIGS[name]
+    if args.small_experts:
+        cfg = dataclasses.replace(cfg, n_experts=args.small_experts)
+    ctx = rb.Context(0)
+    layer = build_layer(ctx, cfg, max_tokens=cfg.tokens, scale_dtype="bf16" if cfg.fmt != "mxfp4" else "f32")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for i in range(args.forwards):
+        x = x_device(cfg, synth.activations(cfg, tokens=cfg.tokens, token_offset=100_000 + i * cfg.tokens))
+        flush.zero_()
+        torch.cuda.synchronize()
+        last = i == args.forwards - 1
+        if last and args.profile_last:
+            torch.cuda.cudart().cudaProfilerStart()
+        if args.profile_case == "latent":
+            layer.latent_moe(x)
+        else:
+            layer.moe_forward(x)
+        torch.cuda.synchronize()
+        if last and args.profile_last:
+            torch.cuda.cudart().cudaProfilerStop()
+    layer.check()
+    errs = layer.stats()["device_error_flags"]
+    layer.close()
+    ctx.close()
+    print(f"{args.profile_case}: {args.forwards} forwards of {cfg.name} ({cfg.n_experts} experts), "
+          f"device error flags {errs}")
+    return 0 if errs == 0 else 1
 
 
 def main():
@@ -598,10 +794,19 @@ def main():
     ap.add_argument("--ep-steps", type=int, default=5)
     ap.add_argument("--no-latent", action="store_true", help="skip the K3 latent MoE decode (row a14)")
     ap.add_argument("--latent-steps", type=int, default=10)
+    ap.add_argument("--no-c4", action="store_true", help="skip the GLM int4 layer (config 4)")
+    ap.add_argument("--c4-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--small-experts", type=int, default=0,
                     help="profiling only: resident experts (same shapes); not a bench config")
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "latent", "int4"], default=None,
+                    help="profiling workload only (no bench line): see run_profile_case")
+    ap.add_argument("--forwards", type=int, default=3, help="--profile-case: forwards to run")
+    ap.add_argument("--profile-last", action="store_true",
+                    help="--profile-case: last forward inside cudaProfilerStart/Stop")
     args = ap.parse_args()
+    if args.profile_case:
+        raise SystemExit(run_profile_case(args))
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

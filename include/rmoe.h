@@ -26,7 +26,7 @@ extern "C" {
 #define RMOE_API
 #endif
 
-#define RMOE_ABI_VERSION 2
+#define RMOE_ABI_VERSION 3
 #define RMOE_MAX_TOPK 32
 
 typedef enum rmoe_status {
@@ -37,7 +37,9 @@ typedef enum rmoe_status {
   RMOE_NCCL_ERROR = 4,
   RMOE_TIMEOUT = 5,         /* a bounded device-side wait gave up */
   RMOE_NOT_SUPPORTED = 6,   /* a shape the kernels do not handle (see rmoe_layer_create) */
-  RMOE_OUT_OF_MEMORY = 7
+  RMOE_OUT_OF_MEMORY = 7,
+  RMOE_IO_ERROR = 8,        /* a checkpoint file could not be read, or its header is malformed */
+  RMOE_MISSING_TENSOR = 9   /* a checkpoint has no tensor of the requested name */
 } rmoe_status;
 
 typedef enum rmoe_router_kind {
@@ -64,6 +66,33 @@ typedef enum rmoe_activation {
 
 typedef struct rmoe_ctx rmoe_ctx;
 typedef struct rmoe_layer rmoe_layer;
+typedef struct rmoe_shards rmoe_shards;
+
+/* The on-disk tensor names of a routed expert (ExpertNaming, src/expert_cache.rs:66-131). */
+typedef enum rmoe_expert_naming {
+  /* model.layers.{L}.mlp.experts.{E}.{gate,up,down}_proj.weight (+ .qs int4 scales) */
+  RMOE_NAMING_GLM52 = 0,
+  /* model.layers.{L}.mlp.experts.{E}.{gate_up,down}_proj.weight, gate_up = [2I, H] */
+  RMOE_NAMING_GLM52_FUSED_GATE_UP = 1,
+  /* model.layers.{L}.block_sparse_moe.experts.{E}.{w1,w3,w2}.weight (w1 gate, w3 up, w2 down) */
+  RMOE_NAMING_KIMI_LINEAR = 2,
+  /* the same under language_model. */
+  RMOE_NAMING_KIMI_K3 = 3,
+  /* K3's MXFP4 checkpoint: {base}.weight_packed + {base}.weight_scale per matrix */
+  RMOE_NAMING_KIMI_K3_MXFP4 = 4,
+  /* Qwen3.8's MXFP4 checkpoint: model.layers.{L}.mlp.experts.{E}.{gate,up,down}_proj.weight +
+   * .weight_scale */
+  RMOE_NAMING_QWEN38_MXFP4 = 5
+} rmoe_expert_naming;
+
+/* Whose MoeWeights tensor names rmoe_load_moe_weights reads (router, bias, shared expert). */
+typedef enum rmoe_model_family {
+  RMOE_FAMILY_QWEN38 = 0,  /* qwen38::model (src/qwen38/model.rs:319-326) */
+  RMOE_FAMILY_GLM52 = 1    /* glm52::model (src/glm52/model.rs:249-253) */
+} rmoe_model_family;
+
+#define RMOE_DTYPE_NAME_BYTES 16
+#define RMOE_MAX_TENSOR_DIMS 8
 
 /* Mirrors the routing/expert fields of qwen38::config::Cfg (src/qwen38/config.rs:71-102) and
  * glm52::config::Cfg (src/glm52/config.rs:26-46). */
@@ -138,12 +167,28 @@ RMOE_API rmoe_status rmoe_shutdown(rmoe_ctx* ctx);
 RMOE_API rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* desc, rmoe_layer** out);
 RMOE_API rmoe_status rmoe_layer_destroy(rmoe_layer* layer);
 RMOE_API rmoe_status rmoe_layer_get_stats(const rmoe_layer* layer, rmoe_layer_stats* out);
+/* The descriptor the layer was created with (no counterpart in the reference, whose Cfg the caller
+ * already holds). */
+RMOE_API rmoe_status rmoe_layer_get_desc(const rmoe_layer* layer, rmoe_layer_desc* out);
 /* Per-stage CUDA-event timing of forward calls (no counterpart in the reference, whose
  * Phases/StepProfile timers in src/generate.rs:192-203 play this role on the CPU). While on,
  * every forward records one event per stage boundary on its stream. get_profile waits for
  * those events, returns the sums since the last read and resets them. */
 RMOE_API rmoe_status rmoe_layer_set_profiling(rmoe_layer* layer, int on);
 RMOE_API rmoe_status rmoe_layer_get_profile(rmoe_layer* layer, rmoe_profile* out);
+
+/* Error status of the work already queued on a layer (the counterpart of the reference's
+ * Result<_, ModelError> on every MoE call, src/glm52/moe.rs:350-362, for the asynchronous
+ * device-pointer entry points). Synchronizes `stream` and the layer's own streams; returns
+ * RMOE_TIMEOUT when a bounded device-side wait of the layer's kernels ran out since the last
+ * check (the outputs of those calls are invalid; the layer resets its work counters and is usable
+ * again), else RMOE_OK. rmoe_moe_forward_host performs this check itself before returning. */
+RMOE_API rmoe_status rmoe_layer_check(rmoe_layer* layer, void* stream);
+/* No counterpart in the reference. Limit, in nanoseconds, of each wait of the layer's persistent
+ * kernels on another CTA's progress (grid barriers, readiness of h); 0 = the default, 2 s. The
+ * kernels assume all their CTAs are resident together (one per SM); if other work holds SMs
+ * those waits can run out, and the call then reports RMOE_TIMEOUT instead of hanging. */
+RMOE_API rmoe_status rmoe_layer_set_wait_limit(rmoe_layer* layer, uint64_t ns);
 
 /* ---- weights, taken in the reference's byte layout verbatim. Pointers may be host or device
  *      memory (unified addressing). Byte counts are checked like mxfp4_from_raw
@@ -181,6 +226,40 @@ RMOE_API rmoe_status rmoe_upload_shared(rmoe_layer* layer,
                                const void* down, size_t down_bytes,
                                const void* down_scale, size_t down_scale_bytes,
                                const float* shared_gate);
+
+/* ---- checkpoints: .safetensors shards straight into the HBM expert tables (the replacement of
+ *      the reference's expert streaming tier, src/expert_cache.rs; host file I/O, no GPU work
+ *      besides the uploads) ---- */
+
+/* Shards::open_multi (src/safetensors.rs:248-349): every *.safetensors file of the n_dirs
+ * directories, sorted by file name, headers parsed and checked (header length within the file,
+ * data_offsets ordered and inside it). Errors: RMOE_IO_ERROR (unreadable file, malformed header). */
+RMOE_API rmoe_status rmoe_shards_open(const char* const* dirs, int32_t n_dirs, rmoe_shards** out);
+RMOE_API rmoe_status rmoe_shards_close(rmoe_shards* shards);
+RMOE_API rmoe_status rmoe_shards_count(const rmoe_shards* shards, int64_t* n_tensors);
+/* Shards::find (:355): dtype (e.g. "U8", "F32", "BF16"; RMOE_DTYPE_NAME_BYTES bytes, NUL-padded),
+ * shape (up to RMOE_MAX_TENSOR_DIMS dims), ndim and byte count of one tensor; any output may be
+ * NULL. RMOE_MISSING_TENSOR when absent. */
+RMOE_API rmoe_status rmoe_shards_tensor(const rmoe_shards* shards, const char* name, char* dtype, uint64_t* shape,
+                                        int32_t* ndim, uint64_t* nbytes);
+/* Shards::read_raw (:438-447): the tensor's bytes verbatim into host memory; dst_bytes must equal
+ * the tensor's size (else RMOE_SHAPE_MISMATCH). */
+RMOE_API rmoe_status rmoe_shards_read_raw(const rmoe_shards* shards, const char* name, void* dst, size_t dst_bytes);
+/* One routed expert of checkpoint layer `layer_index` into `layer` (ExpertCache::load_expert with
+ * qt_load_mxfp4 / mxfp4_from_raw, src/expert_cache.rs:1232-1256, or qt_load with a .qs sidecar,
+ * src/glm52/model.rs:137-156): MXFP4 namings read the packed + scale pair verbatim (lengths
+ * rows*ceil(cols/2) and rows*ceil(cols/32), else RMOE_SHAPE_MISMATCH naming the tensor); the other
+ * namings read int4 bytes + f32 .qs group scales (layer format RMOE_FMT_I4_GROUPED, scale_dtype
+ * RMOE_F32). Plain float expert tensors, which the reference quantizes while loading, are
+ * RMOE_NOT_SUPPORTED. */
+RMOE_API rmoe_status rmoe_load_expert(rmoe_layer* layer, const rmoe_shards* shards, int32_t naming,
+                                      int32_t layer_index, int32_t eid);
+/* The rest of a layer's MoeWeights: the router [E, H] (F32 kept f32, BF16 kept bf16, F16 widened),
+ * GLM's e_score_correction_bias [E], and the shared expert (Qwen: shared_expert.* plus
+ * shared_expert_gate.weight when the layer is gated; GLM: shared_experts.*) in the layer's
+ * weight format (MXFP4 pair or int4 + .qs). */
+RMOE_API rmoe_status rmoe_load_moe_weights(rmoe_layer* layer, const rmoe_shards* shards, int32_t family,
+                                           int32_t layer_index);
 
 /* ---- the hot path (device pointers) ---- */
 
@@ -226,10 +305,21 @@ RMOE_API rmoe_status rmoe_latent_moe(rmoe_layer* layer, const void* x, int32_t x
  * src/glm52/moe.rs:463-513): out[t] = sum_j weights[t][j] * expert_{ids[t][j]}(x[t]), plus the
  * (gated) shared expert when with_shared != 0. ids/weights [T][k] (device or host pointers); slots
  * with id -1 or an expert not resident on this layer's EP rank contribute nothing (the building
- * block of expert parallelism: each rank runs it on the token rows it receives). */
+ * block of expert parallelism: each rank runs it on the token rows it receives). A token that
+ * names one expert in several slots gets it once, with the first such slot's weight (the
+ * reference's first-match row gather, src/glm52/moe.rs:465-470). */
 RMOE_API rmoe_status rmoe_moe_forward_routed(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                                     const int32_t* ids, const float* weights, int32_t with_shared,
                                     float* out, void* stream);
+
+/* Owner-side combine of expert parallelism: out[r] = ((parts[0][r] + parts[1][r]) + ... +
+ * parts[n_parts-1][r]) + last[r] for rows x hidden floats, parts [n_parts][rows][hidden] (each
+ * rank's partial sum of the token's routed slots, in rank order), last [rows][hidden] the gated
+ * shared expert or NULL -- routed contributions first and the shared expert last, the order of
+ * qwen38::generate::moe_forward (src/qwen38/generate.rs:324-349). hidden % 4 == 0, 16-byte
+ * aligned device pointers; deterministic (no atomics). */
+RMOE_API rmoe_status rmoe_sum_rank_parts(float* out, const float* parts, int32_t n_parts, int64_t rows,
+                                         int32_t hidden, const float* last, void* stream);
 
 /* Same, with HOST buffers as the Rust call sites hold them (x: &[f32] / bf16 bits, out:
  * &mut [f32]): copies in, runs, copies out and synchronizes. The drop-in for moe_forward's
@@ -255,7 +345,10 @@ RMOE_API rmoe_status rmoe_matmul_mxfp4_tc(float* y, const void* x, int32_t x_dty
  * that cannot allocate on the hot path (device memory reserved by their own arena). Scratch is a
  * fixed device array of RMOE_NOALLOC_SCRATCH_BYTES; shapes needing more (16-bit s*i + 4*s + 256
  * bytes) are rejected with RMOE_INVALID_ARG. The first call on each device (with that device
- * current) resolves the array's address; make it before any stream capture. Calls that overlap
+ * current) resolves the array's address and caches it for the process: make it before any stream
+ * capture, and do not call this entry point after cudaDeviceReset on that device (the cached
+ * address would be stale). Only i % 32 == 0 uses the scratch (other i take a scalar kernel that
+ * needs none, so the size limit does not apply to them). Calls that overlap
  * in time on one device share the scratch and race: order them on one stream. */
 #define RMOE_NOALLOC_SCRATCH_BYTES ((8u << 20) + 4096u) /* s*i <= 4M at s <= 512, e.g. 512 x 8192 */
 RMOE_API rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_t x_dtype,

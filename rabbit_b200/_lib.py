@@ -9,10 +9,15 @@ LIB_PATH = os.path.join(HERE, "librmoe.so")
 
 RMOE_OK = 0
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "SHAPE_MISMATCH", 3: "CUDA_ERROR", 4: "NCCL_ERROR",
-                5: "TIMEOUT", 6: "NOT_SUPPORTED", 7: "OUT_OF_MEMORY"}
+                5: "TIMEOUT", 6: "NOT_SUPPORTED", 7: "OUT_OF_MEMORY", 8: "IO_ERROR", 9: "MISSING_TENSOR"}
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_GROUPED = 0, 1
 FMT_MXFP4, FMT_I4_GROUPED = 0, 1
 DT_F32, DT_BF16 = 0, 1
+# rmoe_expert_naming / rmoe_model_family
+NAMINGS = {"glm52": 0, "glm52_fused_gate_up": 1, "kimi_linear": 2, "kimi_k3": 3, "kimi_k3_mxfp4": 4,
+           "qwen38_mxfp4": 5}
+FAMILIES = {"qwen38": 0, "glm52": 1}
+DTYPE_NAME_BYTES, MAX_TENSOR_DIMS = 16, 8
 
 
 class RmoeError(RuntimeError):
@@ -61,6 +66,16 @@ PROTOTYPES = {
     "rmoe_layer_create": (C.c_int, [P, C.POINTER(LayerDesc), C.POINTER(P)]),
     "rmoe_layer_destroy": (C.c_int, [P]),
     "rmoe_layer_get_stats": (C.c_int, [P, C.POINTER(LayerStats)]),
+    "rmoe_layer_get_desc": (C.c_int, [P, C.POINTER(LayerDesc)]),
+    "rmoe_shards_open": (C.c_int, [C.POINTER(C.c_char_p), I32, C.POINTER(P)]),
+    "rmoe_shards_close": (C.c_int, [P]),
+    "rmoe_shards_count": (C.c_int, [P, C.POINTER(C.c_int64)]),
+    "rmoe_shards_tensor": (C.c_int, [P, C.c_char_p, P, P, C.POINTER(I32), C.POINTER(C.c_uint64)]),
+    "rmoe_shards_read_raw": (C.c_int, [P, C.c_char_p, P, SZ]),
+    "rmoe_load_expert": (C.c_int, [P, P, I32, I32, I32]),
+    "rmoe_load_moe_weights": (C.c_int, [P, P, I32, I32]),
+    "rmoe_layer_check": (C.c_int, [P, P]),
+    "rmoe_layer_set_wait_limit": (C.c_int, [P, C.c_uint64]),
     "rmoe_layer_set_profiling": (C.c_int, [P, C.c_int]),
     "rmoe_layer_get_profile": (C.c_int, [P, C.POINTER(Profile)]),
     "rmoe_upload_router": (C.c_int, [P, P, I32, SZ]),
@@ -75,6 +90,7 @@ PROTOTYPES = {
     "rmoe_moe_forward": (C.c_int, [P, P, I32, I32, P, P, P, P]),
     "rmoe_moe_forward_routed": (C.c_int, [P, P, I32, I32, P, P, I32, P, P]),
     "rmoe_moe_forward_host": (C.c_int, [P, P, I32, I32, P, P, P]),
+    "rmoe_sum_rank_parts": (C.c_int, [P, P, I32, C.c_int64, I32, P, P]),
     "rmoe_matmul_mxfp4": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_mxfp4_tc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_mxfp4_noalloc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),

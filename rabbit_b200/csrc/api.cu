@@ -67,6 +67,9 @@ struct DevArena {
 
 }  // namespace
 
+// The thread's error text, for the other translation units of the library (the checkpoint loader).
+void rmoe_set_error(const char* msg) { g_last_error = msg; }
+
 struct rmoe_ctx {
   int device;
 };
@@ -195,6 +198,10 @@ struct rmoe_layer {
   unsigned long long* tc_trace = nullptr;  // RMOE_TC_TRACE=1: gate/up stage timestamps of CTA 0
   bool tc_trace_print = true;              // RMOE_TC_TRACE=2: record only (summary on get_stats)
   bool use_fused = true;                   // one token: the fused gate/up + down kernel (RMOE_DISABLE_FUSED=1: two kernels)
+  unsigned long long spin_ns = kDefaultSpinNs;  // limit of the kernels' waits on other CTAs
+  unsigned err_seen = 0;                   // device error flags already reported (and cleared)
+  bool diag_host = false;                  // RMOE_DIAG_HOST=1: kernel trace in mapped host memory
+  void* diag_buf = nullptr;
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
     for (cudaEvent_t e : ev_pending) cudaEventDestroy(e);
@@ -205,6 +212,7 @@ struct rmoe_layer {
         if (e) cudaEventDestroy(e);
     }
     if (cap) cudaStreamDestroy(cap);
+    if (diag_buf) cudaFreeHost(diag_buf);
     free(tc_plan);
   }
 };
@@ -258,6 +266,8 @@ extern "C" const char* rmoe_status_string(rmoe_status s) {
     case RMOE_CUDA_ERROR: return "cuda error";
     case RMOE_NCCL_ERROR: return "nccl error";
     case RMOE_TIMEOUT: return "timeout";
+    case RMOE_IO_ERROR: return "i/o error";
+    case RMOE_MISSING_TENSOR: return "missing tensor";
     case RMOE_NOT_SUPPORTED: return "not supported";
     case RMOE_OUT_OF_MEMORY: return "out of memory";
   }
@@ -444,6 +454,20 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
   ALLOC(L->logits, static_cast<size_t>(T) * E);
   ALLOC(L->logit_err, static_cast<size_t>(std::min(T, 32)) * E);
   ALLOC(L->fallbacks, 1);
+  if (const char* dg = getenv("RMOE_DIAG_HOST")) L->diag_host = dg[0] == '1';
+  if (L->diag_host) {
+    // diagnostics: the kernel trace in mapped host memory (plain stores only), readable on the
+    // host even after a fault has ended the context
+    void* hp = nullptr;
+    if (cudaHostAlloc(&hp, 8192 * 8 + 64, cudaHostAllocMapped) != cudaSuccess)
+      return cleanup(fail(RMOE_CUDA_ERROR, "diagnostic host buffer"));
+    memset(hp, 0, 8192 * 8 + 64);
+    L->diag_buf = hp;
+    void* dp = nullptr;
+    if (cudaHostGetDevicePointer(&dp, hp, 0) != cudaSuccess) return cleanup(fail(RMOE_CUDA_ERROR, "diagnostic map"));
+    L->tc_trace = static_cast<unsigned long long*>(dp);
+    L->tc_trace_print = false;
+  }
   ALLOC(L->dev_err, 1);
   ALLOC(L->order_pending, 1);
   ALLOC(L->pending, std::min(T, 32));
@@ -513,7 +537,7 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     L->fused_tiles = (RMOE_MAX_TOPK_DEV + 1) * static_cast<int>(I / 64);
     ALLOC(L->fused_cnt, 8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1);
     if (const char* nf = getenv("RMOE_DISABLE_FUSED")) L->use_fused = nf[0] != '1';
-    if (const char* tr = getenv("RMOE_TC_TRACE")) {
+    if (const char* tr = getenv("RMOE_TC_TRACE"); tr && !L->diag_host) {
       if (tr[0] == '1' || tr[0] == '2') {
         L->tc_trace_print = tr[0] == '1';
         ALLOC(L->tc_trace, 8192);
@@ -583,6 +607,12 @@ extern "C" rmoe_status rmoe_layer_destroy(rmoe_layer* L) {
   return RMOE_OK;
 }
 
+extern "C" rmoe_status rmoe_layer_get_desc(const rmoe_layer* L, rmoe_layer_desc* out) {
+  if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_desc: null argument");
+  *out = L->desc;
+  return RMOE_OK;
+}
+
 extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stats* out) {
   if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_stats: null argument");
   *out = L->stats;
@@ -592,7 +622,7 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
   out->router_fallbacks = fb;
   unsigned ef = 0;
   RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
-  out->device_error_flags = ef;
+  out->device_error_flags = ef | L->err_seen;
   unsigned op = 0;
   RMOE_CUDA(cudaMemcpy(&op, L->order_pending, 4, cudaMemcpyDeviceToHost), "read order counter");
   out->router_order_resolved = op;
@@ -661,6 +691,57 @@ extern "C" rmoe_status rmoe_layer_set_profiling(rmoe_layer* L, int on) {
 }
 
 static rmoe_status drain_graph_profile(rmoe_layer* L, GraphEntry& g);
+
+// Reads the layer's device error flags (bounded waits of its kernels that ran out) once the
+// work on the layer's streams is done. Nonzero: the outputs of the calls since the last check
+// are invalid, and the persistent kernels' work counters may be left mid-count, so they are
+// zeroed (with the device idle) and the flags cleared: the next call runs normally.
+static rmoe_status take_device_errors(rmoe_layer* L, const char* what) {
+  unsigned ef = 0;
+  RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
+  if (!ef) return RMOE_OK;
+  RMOE_CUDA(cudaDeviceSynchronize(), "timeout recovery: synchronize");
+  const int T = L->max_tokens;
+  RMOE_CUDA(cudaMemset(L->dev_err, 0, 4), "timeout recovery");
+  RMOE_CUDA(cudaMemset(L->resolve_cnt, 0, 4 * std::min(T, 32)), "timeout recovery");
+  if (L->use_tc) {
+    RMOE_CUDA(cudaMemset(L->tile_cnt, 0, 2 * L->tile_cnt_half * 4), "timeout recovery");
+    RMOE_CUDA(cudaMemset(L->fused_cnt, 0, (8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1) * 4), "timeout recovery");
+    RMOE_CUDA(cudaMemset(L->front_counter, 0, 4), "timeout recovery");
+    RMOE_CUDA(cudaMemset(L->tc_work, 0, 32), "timeout recovery");
+  }
+  L->err_seen |= ef;
+  return fail(RMOE_TIMEOUT,
+              "%s: a bounded device-side wait ran out (flags 0x%x); the outputs of the calls since the "
+              "last check are invalid; the layer's counters were reset for the next call",
+              what, ef);
+}
+
+extern "C" rmoe_status rmoe_layer_check(rmoe_layer* L, void* stream) {
+  if (!L) return fail(RMOE_INVALID_ARG, "rmoe_layer_check: null layer");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  RMOE_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "rmoe_layer_check synchronize");
+  RMOE_CUDA(cudaStreamSynchronize(L->side), "rmoe_layer_check synchronize");
+  return take_device_errors(L, "rmoe_layer_check");
+}
+
+extern "C" rmoe_status rmoe_layer_set_wait_limit(rmoe_layer* L, uint64_t ns) {
+  if (!L) return fail(RMOE_INVALID_ARG, "rmoe_layer_set_wait_limit: null layer");
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const unsigned long long v = ns ? ns : kDefaultSpinNs;
+  if (v == L->spin_ns) return RMOE_OK;
+  // the captured one-token graphs hold the old limit in their kernel arguments
+  RMOE_CUDA(cudaDeviceSynchronize(), "rmoe_layer_set_wait_limit synchronize");
+  for (auto& kv : L->graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+    for (cudaEvent_t e : kv.second.ev)
+      if (e) cudaEventDestroy(e);
+  }
+  L->graphs.clear();
+  L->spin_ns = v;
+  return RMOE_OK;
+}
 
 extern "C" rmoe_status rmoe_layer_get_profile(rmoe_layer* L, rmoe_profile* out) {
   if (!L || !out) return fail(RMOE_INVALID_ARG, "rmoe_layer_get_profile: null argument");
@@ -1023,7 +1104,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
       e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
                                   L->hsf, L->partial, L->partial2, L->fused_cnt + 8, L->fused_cnt + 8 + L->fused_tiles,
                                   L->fused_cnt, L->dev_err, out, L->fmt.act, terms_done && L->has_shared ? L->n_loc : -1, st,
-                                  L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr);
+                                  L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr, L->spin_ns);
       if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
       marks.mark();
       marks.mark();
@@ -1036,7 +1117,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     // one token: every position reads the token's own term rows (0..3)
     e = launch_moe_tc(0, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, nullptr,
                       L->partial, L->tile_cnt, L->tc_work, L->dev_err, st, terms_done ? L->d.perm_tok : nullptr,
-                      L->tc_trace, L->fmt.act, L->tile_cnt, L->tc_work + 6, T <= mt);
+                      L->tc_trace, L->fmt.act, L->tile_cnt, L->tc_work + 6, T <= mt, L->spin_ns);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (tensor cores)");
 
     marks.mark();
@@ -1044,7 +1125,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     if (T == 1) {
       e = launch_moe_tc(2, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, out,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr, nullptr, T <= mt);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr, nullptr, T <= mt, L->spin_ns);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -1055,7 +1136,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     } else {
       e = launch_moe_tc(1, L->tc_plan, L->d, mt, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht, L->hsf, L->y,
                         L->partial2, L->tile_cnt + L->tile_cnt_half, L->tc_work + 4, L->dev_err, st, nullptr,
-                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr, nullptr, T <= mt);
+                        L->tc_trace ? L->tc_trace + 4096 : nullptr, L->fmt.act, nullptr, nullptr, T <= mt, L->spin_ns);
       if (e != cudaSuccess) return cuda_fail(e, "down (tensor cores)");
       if (L->tc_trace && L->tc_trace_print) {
         if ((s = print_tc_trace(L, st, "gate/up", 0)) != RMOE_OK) return s;
@@ -1609,6 +1690,24 @@ extern "C" rmoe_status rmoe_latent_moe(rmoe_layer* L, const void* x, int32_t x_d
   return RMOE_OK;
 }
 
+// RMOE_DIAG_HOST=1: after a failed call, the fused one-token kernel's per-CTA
+// timeline (read from mapped host memory, so also after a fault) to stderr.
+static void diag_dump(const rmoe_layer* L) {
+  if (!L->diag_buf) return;
+  const volatile unsigned long long* tr = static_cast<const volatile unsigned long long*>(L->diag_buf);
+  const unsigned long long f0 = tr[4000];
+  fprintf(stderr, "diag: front end start %llu\n", f0);
+  const char* nm[8] = {"entry", "set-up", "first copy", "first down", "epilogue done", "barrier", "exit", "mma drained"};
+  for (int c = 0; c < 148; c++) {
+    fprintf(stderr, "diag cta %3d:", c);
+    for (int f = 0; f < 8; f++) {
+      const unsigned long long v = tr[4096 + 2048 + 8 * c + f];
+      fprintf(stderr, " %s=%.2f", nm[f], v && f0 ? (double)(long long)(v - f0) * 1e-3 : -1.0);
+    }
+    fprintf(stderr, "\n");
+  }
+}
+
 extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, int32_t x_dtype,
                                              int32_t T, float* out_host, int32_t* ids_host,
                                              float* w_host) {
@@ -1631,8 +1730,14 @@ extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, 
             "out to host");
   if (ids_host) RMOE_CUDA(cudaMemcpyAsync(ids_host, L->ids_host_stage, n * 4, cudaMemcpyDeviceToHost, L->stream), "ids to host");
   if (w_host) RMOE_CUDA(cudaMemcpyAsync(w_host, L->w_host_stage, n * 4, cudaMemcpyDeviceToHost, L->stream), "weights to host");
-  RMOE_CUDA(cudaStreamSynchronize(L->stream), "rmoe_moe_forward_host synchronize");
-  return RMOE_OK;
+  {
+    cudaError_t e = cudaStreamSynchronize(L->stream);
+    if (e != cudaSuccess) {
+      diag_dump(L);
+      return cuda_fail(e, "rmoe_moe_forward_host synchronize");
+    }
+  }
+  return take_device_errors(L, "rmoe_moe_forward_host");
 }
 
 // ------------------------------------------------------------------------------ matmuls
@@ -1715,6 +1820,21 @@ extern "C" rmoe_status rmoe_synth_bytes(void* dst, size_t n, uint64_t key, int32
   return RMOE_OK;
 }
 
+extern "C" rmoe_status rmoe_sum_rank_parts(float* out, const float* parts, int32_t n_parts, int64_t rows,
+                                           int32_t hidden, const float* last, void* stream) {
+  const char* what = "rmoe_sum_rank_parts";
+  if (n_parts <= 0 || rows < 0 || hidden <= 0) return fail(RMOE_INVALID_ARG, "%s: n_parts=%d rows=%lld hidden=%d", what, n_parts, static_cast<long long>(rows), hidden);
+  if (rows == 0) return RMOE_OK;
+  if (!out || !parts) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  if (hidden % 4 || reinterpret_cast<uintptr_t>(out) % 16 || reinterpret_cast<uintptr_t>(parts) % 16 ||
+      reinterpret_cast<uintptr_t>(last) % 16)
+    return fail(RMOE_INVALID_ARG, "%s: hidden %% 4 and 16-byte aligned buffers required", what);
+  cudaError_t e = launch_sum_rank_parts(parts, n_parts, static_cast<size_t>(rows) * hidden, last, out,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return RMOE_OK;
+}
+
 // ------------------------------------------------------------------- no-allocation matmul
 // rmoe_matmul_mxfp4 takes its activation scratch (f16 rows + per-row exponents) from
 // cudaMallocAsync on every call. Some callers cannot allocate at that point: a serving loop
@@ -1744,7 +1864,8 @@ extern "C" rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_
   if (!y || !x || !data || !block_scale) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
   if (s < 0 || i <= 0 || o < 0) return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d o=%d", what, s, i, o);
   if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
-  const size_t ws = matmul_q_workspace_bytes(s, i);
+  // only the vectorised path (i a multiple of 32) uses the scratch; others need none
+  const size_t ws = i % 32 == 0 ? matmul_q_workspace_bytes(s, i) : 0;
   if (ws > RMOE_NOALLOC_SCRATCH_BYTES)
     return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d needs %zu scratch bytes, above the fixed %zu (split the rows)",
                 what, s, i, ws, static_cast<size_t>(RMOE_NOALLOC_SCRATCH_BYTES));
@@ -1753,7 +1874,9 @@ extern "C" rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_
   if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(RMOE_INVALID_ARG, "%s: device %d", what, dev);
   void* scratch = nullptr;
   {
-    // First call on a device (that device current): resolve the array's address once.
+    // First call on a device (that device current): resolve the array's address once. The
+    // cached address belongs to the device's primary context: after cudaDeviceReset (or any
+    // teardown of that context) it is stale, so this entry point must not be used afterwards.
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_ptr[dev]) {
       void* p = nullptr;
@@ -1763,7 +1886,7 @@ extern "C" rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_
     scratch = g_noalloc_ptr[dev];
   }
   cudaError_t e = launch_matmul_q(y, x, x_dtype == RMOE_BF16 ? kBF16 : kF32, data, block_scale,
-                                  ExpertFormat{kMxfp4, 32, kF32}, s, i, o, scratch, ws,
+                                  ExpertFormat{kMxfp4, 32, kF32}, s, i, o, ws ? scratch : nullptr, ws,
                                   static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, what);
   return RMOE_OK;

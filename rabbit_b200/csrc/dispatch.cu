@@ -170,6 +170,14 @@ __global__ void __launch_bounds__(1024) dispatch_place_kernel(
       continue;
     }
     const int t = q / k;
+    // a token that names an expert in two slots gets it once, with the first slot's weight
+    // (apply_single_expert takes the first matching pick, src/glm52/moe.rs:465-470)
+    bool dup = false;
+    for (int j = t * k; j < q; j++) dup |= ids[j] == e;
+    if (dup) {
+      d.inv[q] = -1;
+      continue;
+    }
     const uint32_t word = d.bits[static_cast<size_t>(el) * words + (t >> 5)];
     const int rank = d.wpre[static_cast<size_t>(el) * words + (t >> 5)] +
                      __popc(word & ((1u << (t & 31)) - 1u));
@@ -221,13 +229,21 @@ __global__ void dispatch_one_token_kernel(const int32_t* __restrict__ ids, const
   const int lane = threadIdx.x;
   const int sid = lane < k ? ids[lane] : -1;
   const float wv = lane < k ? w[lane] : 0.0f;
-  const bool local = lane < k && sid >= e_begin && sid < e_end;
+  // a repeated expert counts once, at its first slot (the reference applies the first
+  // matching pick, src/glm52/moe.rs:465-470); later repeats contribute nothing
+  bool first = true;
+  for (int j = 0; j < k; j++) {
+    const int o = __shfl_sync(kFull, sid, j);
+    first &= !(j < lane && o == sid);
+  }
+  const bool local = lane < k && first && sid >= e_begin && sid < e_end;
+  const uint32_t local_mask = __ballot_sync(kFull, local);
   int pos = 0;
   for (int j = 0; j < k; j++) {
     const int o = __shfl_sync(kFull, sid, j);
-    pos += (o >= e_begin && o < e_end && o < sid) ? 1 : 0;
+    pos += ((local_mask >> j) & 1u) && o < sid ? 1 : 0;
   }
-  const int n_routed = __popc(__ballot_sync(kFull, local));
+  const int n_routed = __popc(local_mask);
   if (lane < k) d.inv[lane] = local ? pos : -1;
   if (local) {
     d.ch_expert[pos] = sid - e_begin;

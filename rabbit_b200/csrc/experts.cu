@@ -153,7 +153,7 @@ static void launch_gu_fmt(int mt, dim3 grid, const ExpertTable& tab, const Exper
 static int gemv_grid(int max_tasks) {
   const int warps_per_block = 8;
   int blocks = (max_tasks + warps_per_block - 1) / warps_per_block;
-  return std::max(1, std::min(blocks, 148 * 4));
+  return std::max(1, std::min(blocks, device_sm_count() * 4));
 }
 
 cudaError_t launch_gemv_gate_up(const ExpertTable& tab, const ExpertFormat& f,
@@ -313,6 +313,44 @@ cudaError_t launch_combine(const float* y, const DispatchBuffers& d, const float
   dim3 grid((H / 4 + 255) / 256, T);
   combine_kernel<<<grid, 256, 0, st>>>(y, d.inv, rw, d.offsets + shared_slot, d.perm_w, k, H,
                                        has_shared, out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ rank-order sum
+// out[r] = ((parts[0][r] + parts[1][r]) + ... + parts[n-1][r]) + last[r]: the owner-side combine
+// of expert parallelism, every rank's partial sum of a token's routed slots added in rank order
+// and the (gated) shared expert last, as moe_forward adds it after the routed experts
+// (src/qwen38/generate.rs:324-349). One thread per 4 consecutive floats of the rows.
+__global__ void __launch_bounds__(256) sum_rank_parts_kernel(const float* __restrict__ parts, int n,
+                                                             size_t count4, const float* __restrict__ last,
+                                                             float* __restrict__ out) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count4; i += stride) {
+    float4 acc = __ldcs(reinterpret_cast<const float4*>(parts) + i);
+    for (int r = 1; r < n; r++) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(parts) + static_cast<size_t>(r) * count4 + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (last) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(last) + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    reinterpret_cast<float4*>(out)[i] = acc;
+  }
+}
+
+cudaError_t launch_sum_rank_parts(const float* parts, int n, size_t count, const float* last, float* out,
+                                  cudaStream_t st) {
+  if (count == 0 || n <= 0) return cudaSuccess;
+  const size_t count4 = count / 4;
+  const int blocks = static_cast<int>(std::min<size_t>((count4 + 255) / 256, static_cast<size_t>(device_sm_count()) * 8));
+  sum_rank_parts_kernel<<<blocks, 256, 0, st>>>(parts, n, count4, last, out);
   return cudaGetLastError();
 }
 

@@ -463,16 +463,7 @@ bool pipe_supported(const ExpertFormat& f, int H, int inter, int shared_inter) {
   return true;
 }
 
-static int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+static int num_sms() { return device_sm_count(); }
 
 static size_t pipe_smem(int slot_bytes) {
   return static_cast<size_t>(kStages) * slot_bytes + kStages * 16 + kStages * sizeof(SlotMeta);

@@ -7,6 +7,18 @@
 
 namespace rmoe {
 
+// Limit of a persistent kernel's wait on another CTA's counter (grid barriers, h readiness):
+// 2 s, after which the kernel records a device error flag and stops (rmoe_layer_set_wait_limit).
+constexpr unsigned long long kDefaultSpinNs = 2000000000ull;
+
+// SMs of the current device (grids of the persistent and grid-stride kernels scale with it).
+inline int device_sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
 // Where one expert's six tensors live on the device. gate/up: [inter, hidden]; down:
 // [hidden, inter]. scales are E8M0 bytes (MXFP4) or f32/bf16 per group (int4).
 struct ExpertPtrs {
@@ -194,6 +206,10 @@ cudaError_t launch_pipe_down(const ExpertTable& tab, const ExpertFormat& f,
                              const DispatchBuffers& d, const float* h, const uint32_t* hmax,
                              int H, int mt, int h_ld, float* y, unsigned* err_flag,
                              cudaStream_t st);
+// out = parts[0] + ... + parts[n-1] (+ last), in that order; count floats per part (multiple of 4,
+// 16-byte aligned pointers).
+cudaError_t launch_sum_rank_parts(const float* parts, int n, size_t count, const float* last, float* out,
+                                  cudaStream_t st);
 // Down projection fused with the weighted combine and the gated shared expert (small T).
 cudaError_t launch_pipe_down_combine(const ExpertTable& tab, const ExpertFormat& f,
                                      const DispatchBuffers& d, const float* h,
@@ -230,7 +246,8 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st,
                           const int32_t* b_token_rows = nullptr, unsigned long long* trace = nullptr,
                           ActParams act = ActParams{0, 0.0f, 0.0f}, int32_t* gu_tile_cnt = nullptr,
-                          int* h_done = nullptr, bool weights_once = false);
+                          int* h_done = nullptr, bool weights_once = false,
+                          unsigned long long spin_ns = kDefaultSpinNs);
 // Unit parts of split tiles (floats) a layer must provide for batches of up to 8 tokens.
 size_t moe_tc_partial_floats(int H, int I, int k, int n_slots);
 
@@ -243,7 +260,8 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
                                     size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
                                     float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
                                     float* out, ActParams act, int sh_slot, cudaStream_t st,
-                                    unsigned long long* trace = nullptr);
+                                    unsigned long long* trace = nullptr,
+                                    unsigned long long spin_ns = kDefaultSpinNs);
 
 // ---- latent MoE wrapper (latent.cu) ----
 // y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)

@@ -142,7 +142,7 @@ cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, 148 * 4);
+  const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, device_sm_count() * 4);
   kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y);
   return cudaGetLastError();
 }

@@ -89,6 +89,7 @@ struct MoeTcArgs {
   int* h_done;         // gate/up: h items finished (released per item; the down kernel's counter)
   int h_split;         // down: gate/up split its tiles, its helper warps write h (wait on h_done)
   int weights_once;    // every weight tile is read by one unit only (one chunk per expert): evict-first
+  unsigned long long spin_ns;  // limit of each wait on another CTA's counter (then err, abort)
 };
 
 struct StageMeta {
@@ -111,6 +112,14 @@ constexpr int kRecRing = 4;
 constexpr int kBOff = (kTileBlock + 1023) & ~1023;
 
 // Shared-memory carve-up (offsets from the 1024-aligned base).
+// Completion of every tcgen05 operation this thread issued (MMAs, scale-factor copies) before
+// the CTA frees its TMEM: on a run that stopped early (a bounded wait ran out) no consumer waited
+// for the last ones. `bar` is a one-use mbarrier (count 1); the wait is bounded too.
+__device__ __forceinline__ void tc_drain(uint64_t* bar, unsigned* err) {
+  tc_commit(bar);
+  mbar_wait_bounded(bar, 0, err, 0x400000u);
+}
+
 struct MtLayout {
   int stage_pitch, off_bar, off_meta, off_rec, off_misc, off_ubuf, total;
 };
@@ -122,8 +131,9 @@ __host__ __device__ inline MtLayout mt_layout(int stages, int b_boxes) {
   l.off_bar = stages * l.stage_pitch;  // 5 * stages + 8 + 2 * kRecRing mbarriers
   l.off_meta = l.off_bar + (5 * stages + 8 + 2 * kRecRing) * 8;
   l.off_rec = l.off_meta + stages * static_cast<int>(sizeof(StageMeta));
-  l.off_misc = l.off_rec + kRecRing * static_cast<int>(sizeof(PartRec));
-  l.off_ubuf = (l.off_misc + 16 + 15) & ~15;  // tmem slot, abort, last flag
+  l.off_misc = (l.off_rec + kRecRing * static_cast<int>(sizeof(PartRec)) + 15) & ~15;
+  // tmem slot, abort, last flag, pad, then two drain mbarriers (tc_drain)
+  l.off_ubuf = (l.off_misc + 32 + 15) & ~15;
   l.total = l.off_ubuf + 128 * 33 * 4;  // [128 tile rows][32 positions] (+1 pad)
   return l;
 }
@@ -168,7 +178,7 @@ __device__ __forceinline__ void h_item(const MoeTcArgs& a, int it, int ntm, int 
   if (lane == 0) {
     const uint64_t t0 = global_ns();
     while (ld_acquire_gpu(a.gu_tile_cnt + tile) < upt) {
-      if (global_ns() - t0 > 2000000000ull) {
+      if (global_ns() - t0 > a.spin_ns) {
         atomicOr(err, 0x80000u);
         ready = false;
         break;
@@ -263,6 +273,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
   PartRec* recs = reinterpret_cast<PartRec*>(smem + lay.off_rec);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + lay.off_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* drain = reinterpret_cast<uint64_t*>(smem + lay.off_misc + 16);  // [2] one-use (tc_drain)
   volatile int* last_flag = abort_flag + 1;
   float* ubuf = reinterpret_cast<float*>(smem + lay.off_ubuf);  // [32][64] up values (GATE_UP)
 
@@ -286,6 +297,8 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       mbar_init(&rec_empty[i], 2 + 128 + 128);  // activation producer, MMA issuer, epilogue, scale warps
     }
     *abort_flag = 0;
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     mbar_fence_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kMtTmemCols);
@@ -388,14 +401,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
             load_unit(nxt);
           }
         }
+        // (after an abort the loop's next pass publishes an end record in ring order: a record
+        // is never rewritten while a consumer may still be reading it)
         unit = nxt;
-        if (*abort_flag) break;
-      }
-      if (*abort_flag) {
-        // unblock the roles waiting for a record: an end record in every ring slot they may read
-        for (int i = 0; i < kRecRing; i++) {
-          recs[i].tile = -1;
-        }
       }
       // copies still landing (only after an abort) finish before the CTA exits
       for (int i = (issued > S ? issued - S : 0); i < issued; i++)
@@ -412,7 +420,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
           const int items = 2 * nch * (a.inter / 64);
           const uint64_t t0 = global_ns();
           while (ld_acquire_gpu(a.work + 2) < items) {
-            if (global_ns() - t0 > 2000000000ull) {
+            if (global_ns() - t0 > a.spin_ns) {
               atomicOr(a.err, 0x40000u);
               *abort_flag = 1;
               break;
@@ -537,6 +545,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         parts++;
       }
       if (!ok) *abort_flag = 1;
+      tc_drain(&drain[0], a.err);
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ B scale factors -> TMEM
@@ -546,7 +555,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
     bool ok = true;
     while (ok) {
       if (!__all_sync(kFull, mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u))) break;
-      const int tile = recs[rslot].tile;
+      const int tile = __shfl_sync(kFull, recs[rslot].tile, 0);  // (one value for the warp)
       mbar_arrive(&rec_empty[rslot]);
       if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
       if (tile < 0) break;
@@ -597,6 +606,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
         mbar_arrive(&sf_full[slot]);
       }
     }
+    if (q == 2 && lane == 0) tc_drain(&drain[1], a.err);  // (its scale-factor copies)
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -610,9 +620,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       const PartRec r = recs[rslot];
       mbar_arrive(&rec_empty[rslot]);
       if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
-      if (r.tile < 0) break;
       const unsigned long long e0 = a.trace && blockIdx.x == 0 ? global_ns() : 0;
-      const bool got = mbar_wait_bounded(&acc_full[buf], (seen / nacc) & 1, a.err, 0x8000u);
+      // (the end record and every exit are decided by all 128 threads together)
+      const bool got = r.tile >= 0 && mbar_wait_bounded(&acc_full[buf], (seen / nacc) & 1, a.err, 0x8000u);
       if (!epi_all(got && !*abort_flag)) break;
       if (a.trace && blockIdx.x == 0 && et == 0 && seen < 128) {
         a.trace[3072 + seen * 4 + 0] = e0;
@@ -700,7 +710,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(const __grid_cons
       red_release_gpu_add(a.work + 3, 1);
       const uint64_t t0 = global_ns();
       while (ld_acquire_gpu(a.work + 3) < static_cast<int>(gridDim.x)) {
-        if (global_ns() - t0 > 2000000000ull) {
+        if (global_ns() - t0 > a.spin_ns) {
           atomicOr(a.err, 0x20000u);
           *abort_flag = 1;
           break;
@@ -790,6 +800,7 @@ struct FusedArgs {
   int sh_slot;      // expert slot of the shared expert (the last chunk), -1: none
   unsigned long long* trace;  // optional: per CTA [8] entry, set-up, first copy, first down unit,
                               // epilogue done, barrier passed, exit (global timer)
+  unsigned long long spin_ns;  // limit of each wait on another CTA's counter (then err, abort)
 };
 
 constexpr int kFusedThreads = kMtThreads + 32;  // + warp 11: forms h of finished gate/up tiles
@@ -816,6 +827,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
   PartRec* recs = reinterpret_cast<PartRec*>(smem + lay.off_rec);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + lay.off_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* drain = reinterpret_cast<uint64_t*>(smem + lay.off_misc + 16);  // [2] one-use (tc_drain)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   unsigned long long* trc = a.trace ? a.trace + 8 * blockIdx.x : nullptr;
   if (trc && threadIdx.x == 0) {
@@ -839,6 +851,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
       mbar_init(&rec_empty[i], 2 + 128 + 128);
     }
     *abort_flag = 0;
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     mbar_fence_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kMtTmemCols);
@@ -977,11 +991,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             nxt = q < total_units ? unit_of_claim(q) : total_units;
           }
         }
+        // (after an abort the loop's next pass publishes an end record in ring order: a record
+        // is never rewritten while a consumer may still be reading it)
         unit = nxt;
-        if (*abort_flag) break;
       }
-      if (*abort_flag)
-        for (int i = 0; i < kRecRing; i++) recs[i].tile = -1;
       if (issued < pre) issued = pre;  // (stopped before the preloaded unit: its copies are in flight)
       for (int i = (issued > S ? issued - S : 0); i < issued; i++)
         mbar_wait_bounded(&full[i % S], (i / S) & 1, a.err, 0x200u);
@@ -1003,7 +1016,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
           // this expert's h: all of its gate/up tiles finished
           const uint64_t t0 = global_ns();
           while (ld_acquire_gpu(a.h_ready + c) < ntm_gu) {
-            if (global_ns() - t0 > 2000000000ull) {
+            if (global_ns() - t0 > a.spin_ns) {
               atomicOr(a.err, 0x40000u);
               *abort_flag = 1;
               break;
@@ -1090,6 +1103,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         parts++;
       }
       if (!ok) *abort_flag = 1;
+      tc_drain(&drain[0], a.err);
+      if (trc) trc[7] = global_ns();
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------------ h of finished gate/up tiles
@@ -1104,7 +1119,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
       if (lane == 0) {
         const uint64_t t0 = global_ns();
         while (ld_acquire_gpu(a.tile_cnt + tile) < upt_gu) {
-          if (global_ns() - t0 > 2000000000ull || *abort_flag) {
+          if (global_ns() - t0 > a.spin_ns || *abort_flag) {
             atomicOr(a.err, 0x80000u);
             ready = false;
             break;
@@ -1140,7 +1155,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     bool ok = true;
     while (ok) {
       if (!__all_sync(kFull, mbar_wait_bounded(&rec_full[rslot], rph, a.err, 0x40u))) break;
-      const int tile = recs[rslot].tile, ns = recs[rslot].uit;
+      const int tile = __shfl_sync(kFull, recs[rslot].tile, 0);  // (one value for the warp)
+      const int ns = __shfl_sync(kFull, recs[rslot].uit, 0);
       mbar_arrive(&rec_empty[rslot]);
       if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
       if (tile < 0) break;
@@ -1186,6 +1202,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         mbar_arrive(&sf_full[slot]);
       }
     }
+    if (q == 2 && lane == 0) tc_drain(&drain[1], a.err);  // (its scale-factor copies)
   } else if (warp < 10) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -1199,8 +1216,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
       const PartRec r = recs[rslot];
       mbar_arrive(&rec_empty[rslot]);
       if (++rslot == kRecRing) { rslot = 0; rph ^= 1; }
-      if (r.tile < 0) break;
-      const bool got = mbar_wait_bounded(&acc_full[buf], (seen / nacc) & 1, a.err, 0x8000u);
+      // (the end record and every exit are decided by all 128 threads together)
+      const bool got = r.tile >= 0 && mbar_wait_bounded(&acc_full[buf], (seen / nacc) & 1, a.err, 0x8000u);
       if (!epi_all(got && !*abort_flag)) break;
       tc_fence_after();
       float rr[8];
@@ -1226,7 +1243,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
       red_release_gpu_add(a.work + 2, 1);
       const uint64_t t0 = global_ns();
       while (ld_acquire_gpu(a.work + 2) < static_cast<int>(gridDim.x)) {
-        if (global_ns() - t0 > 2000000000ull) {
+        if (global_ns() - t0 > a.spin_ns) {
           atomicOr(a.err, 0x20000u);
           *abort_flag = 1;
           break;
@@ -1331,15 +1348,18 @@ struct MoeTcPlanImpl {
   MoeTcMaps gu, dn;
 };
 
-static int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+static int sm_count() { return device_sm_count(); }
+
+// Grid of a persistent kernel whose CTAs wait on one another: as many CTAs as can be resident
+// at once (SMs x the occupancy the kernel's shared memory allows, which is one per SM for these
+// kernels), so every CTA of the grid runs together. If other work holds SMs when the kernel
+// starts (another context, an MPS client limit), a CTA can still wait for a peer that never
+// arrives; those waits are bounded (~2 s) and end the call with RMOE_TIMEOUT rather than hang.
+static int resident_grid(const void* kern, int threads, size_t smem) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  return sm_count() * per_sm;
 }
 
 // Stages per work unit for batches of <= 8 tokens: 4 when that divides the per-expert stage
@@ -1442,7 +1462,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
                           const uint8_t* arena, size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* y, float* partial,
                           int32_t* tile_cnt, int* work, unsigned* err, cudaStream_t st, const int32_t* b_token_rows,
                           unsigned long long* trace, ActParams act, int32_t* gu_tile_cnt, int* h_done,
-                          bool weights_once) {
+                          bool weights_once, unsigned long long spin_ns) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   MoeTcArgs a{};
   a.ch_expert = d.ch_expert; a.ch_pos = d.ch_pos; a.ch_n = d.ch_n; a.n_chunks = d.n_chunks;
@@ -1467,6 +1487,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   a.gu_tile_cnt = gu_tile_cnt;
   a.h_done = h_done;
   a.weights_once = weights_once ? 1 : 0;
+  a.spin_ns = spin_ns;
   a.h_split = (mode != 0 && mt <= 8 && small_unit_stages(H / kMtKStage) < H / kMtKStage) ? 1 : 0;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, a.b_boxes) > 227 * 1024) stages--;
@@ -1474,7 +1495,6 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
   const size_t smem = moe_tc_smem(stages, a.b_boxes);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const MoeTcMaps& maps = mode == 0 ? p->gu : p->dn;
-  const int grid = sm_count();
   // Down kernels whose CTAs wait on each other (h slices, the one-token output sum) rely on all
   // CTAs being resident together: the grid is one CTA per SM and a CTA needs most of an SM's
   // shared memory, so no two of them share an SM; the waits are bounded either way. (A
@@ -1485,6 +1505,7 @@ cudaError_t launch_moe_tc(int mode, const void* plan, const DispatchBuffers& d, 
                                              : mode == 1 ? moe_tc_kernel<kModeDown> : moe_tc_kernel<kModeDownOne>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
+  const int grid = resident_grid(reinterpret_cast<const void*>(kern), kMtThreads, smem);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kMtThreads);
@@ -1510,7 +1531,7 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
                                     size_t stride, size_t off_down, uint8_t* ht, uint8_t* hsf, float* part_gu,
                                     float* part_dn, int32_t* tile_cnt, int32_t* h_ready, int* work, unsigned* err,
                                     float* out, ActParams act, int sh_slot, cudaStream_t st,
-                                    unsigned long long* trace) {
+                                    unsigned long long* trace, unsigned long long spin_ns) {
   const MoeTcPlanImpl* p = static_cast<const MoeTcPlanImpl*>(plan);
   FusedArgs a{};
   a.trace = trace;
@@ -1524,6 +1545,7 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
   a.act = act;
   a.u_gu = small_unit_stages(H / kMtKStage);
   a.sh_slot = sh_slot;
+  a.spin_ns = spin_ns;
   int stages = kMtMaxStages;
   while (stages > 2 && moe_tc_smem(stages, 1) > 227 * 1024) stages--;
   a.stages = stages;
@@ -1532,7 +1554,7 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(sm_count());
+  cfg.gridDim = dim3(resident_grid(reinterpret_cast<const void*>(moe_decode_fused_kernel), kFusedThreads, smem));
   cfg.blockDim = dim3(kFusedThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -2,24 +2,27 @@
 blocks (expert e on rank e // (E / N)), tokens owned by the rank that holds them, router and shared
 expert replicated.
 
-One forward on every rank:
+One forward on every rank, with no host synchronisation (every size is fixed by T and N, so no
+count is read back to the host, and every step is queued on the device):
 
-1. route the rank's own tokens with the replicated router (bit-exact, same kernel as one GPU);
-2. exchange counts, then token rows with ``all_to_all_single`` (variable splits): a token goes
-   once to every rank owning at least one of its k experts, with its [k] ids and weights (slots
-   of other ranks set to -1 / 0);
-3. run the received rows through the local experts with the routing weights folded in
-   (``forward_routed``: rabbit's ``apply_single_expert`` loop, src/glm52/moe.rs:463-513), which
-   sums each row's local slots in slot order;
-4. send those per-(token, rank) partial sums back the same way;
-5. on the token's owner: ``out[t] = ((p_0 + p_1) + ... + p_{N-1}) + shared(x_t)`` over the ranks in
-   order, the gated shared expert last (qwen38/generate.rs:324-349). The order is fixed for a
-   world size; against one GPU the slot sums are only regrouped (f32 rounding).
+1. route the rank's own tokens with the replicated router (bit-exact, the one-GPU kernels);
+2. start the exchange of every rank's token rows and their routing: ``all_gather`` of x [T, H]
+   and of the routing row [T, 2k] (ids, and the weights' bits), asynchronously;
+3. meanwhile compute the gated shared expert of the rank's own tokens (it needs no routing);
+4. run all N*T gathered rows through the local experts (``forward_routed``: rabbit's
+   ``apply_single_expert`` loop, src/glm52/moe.rs:463-513): each row sums its slots whose expert
+   is resident here, in slot order; slots of other ranks' experts contribute nothing, so a row
+   with no local slot costs no expert work;
+5. return each owner its rows' partial sums with one equal-split ``all_to_all`` ([N, T, H] f32);
+6. on the owner: ``out[t] = ((p_0 + p_1) + ... + p_{N-1}) + shared(x_t)``, ranks in order and the
+   shared expert last (qwen38/generate.rs:324-349), in one kernel (``sum_rank_parts``). The order
+   is fixed for a world size; against one GPU the routed slot sums are only regrouped (f32
+   rounding).
 
-There is no all-reduce: the only collectives are the two data exchanges (and the counts), which
-the reference has no counterpart for (it runs on one host). The compute side is any object with
-``route(x) -> (ids, weights)``, ``forward_routed(x, ids, weights, with_shared) -> out`` and
-``hidden``/``topk``/``n_experts`` attributes: the device layer (``MoeLayer``) on GPUs.
+The exchanges are collectives the reference has no counterpart for (it runs on one host). The
+compute side is any object with ``route(x)``, ``forward_routed(x, ids, weights, with_shared, out)``,
+``sum_rank_parts(parts, last)`` and ``hidden``/``topk``/``n_experts`` attributes: the device layer
+(``MoeLayer``) on GPUs, or a CPU stand-in for the host-side tests.
 """
 from __future__ import annotations
 
@@ -28,7 +31,7 @@ import torch.distributed as dist
 
 
 class ExpertParallelMoe:
-    def __init__(self, layer, group=None, max_rows=None):
+    def __init__(self, layer, group=None):
         self.layer = layer
         self.group = group
         solo = group is None and not dist.is_initialized()
@@ -38,53 +41,38 @@ class ExpertParallelMoe:
         if layer.n_experts % self.world:
             raise ValueError(f"{layer.n_experts} experts do not split over {self.world} ranks")
         self.per_rank = layer.n_experts // self.world
-        # rows per forward_routed call: at most the layer's max_tokens
-        self.max_rows = max_rows or getattr(layer, "max_tokens", None)
+        self._gloo = not solo and dist.get_backend(group) == "gloo"
 
-    def _exchange(self, send, send_counts, recv_counts):
-        """Variable-split all-to-all of the leading dimension."""
-        out = torch.empty((int(sum(recv_counts)),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-        dist.all_to_all_single(out, send.contiguous(), [int(c) for c in recv_counts], [int(c) for c in send_counts],
-                               group=self.group)
-        return out
+    def _all_gather(self, t):
+        """[T, ...] on every rank -> [N*T, ...] in rank order (asynchronous work handle)."""
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        if self._gloo:  # (gloo has the list form only)
+            parts = list(out.chunk(self.world))
+            dist.all_gather(parts, t.contiguous(), group=self.group)
+            return out, None
+        return out, dist.all_gather_into_tensor(out, t.contiguous(), group=self.group, async_op=True)
 
     def forward(self, x):
         """x [T_local, H] on this rank's device -> (out [T_local, H] f32, ids, weights)."""
         lay = self.layer
         T, k, H, N = x.shape[0], lay.topk, lay.hidden, self.world
-        dev = x.device
         ids, w = lay.route(x)                                   # [T, k] rank order, bit-exact
         if N == 1:  # every expert local: the one-device layer
+            self.last_exchange_bytes = 0
             return lay.forward_routed(x, ids, w, with_shared=True), ids, w
-        dest = torch.where(ids >= 0, ids.long() // self.per_rank, torch.full_like(ids, -1, dtype=torch.long))
-        # one row per (destination rank, token) that has a slot there, rank-major, token order
-        hit = (dest.unsqueeze(2) == torch.arange(N, device=dev)).any(dim=1)      # [T, N]
-        r_idx, t_idx = hit.t().nonzero(as_tuple=True)
-        send_counts = torch.bincount(r_idx, minlength=N)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
-        mine = dest[t_idx] == r_idx.unsqueeze(1)                                  # slots on that rank
-        send_ids = torch.where(mine, ids[t_idx], torch.full_like(ids[t_idx], -1))
-        send_w = torch.where(mine, w[t_idx], torch.zeros_like(w[t_idx]))
-        recv_x = self._exchange(x[t_idx], sc, rc)
-        recv_ids = self._exchange(send_ids, sc, rc)
-        recv_w = self._exchange(send_w, sc, rc)
-        # the local experts over every received row (up to k slots each, weights folded in)
-        R = recv_x.shape[0]
-        y = torch.empty((R, H), dtype=torch.float32, device=dev)
-        step = self.max_rows or max(R, 1)
-        for r0 in range(0, R, step):
-            r1 = min(R, r0 + step)
-            lay.forward_routed(recv_x[r0:r1], recv_ids[r0:r1], recv_w[r0:r1], with_shared=False, out=y[r0:r1])
-        back = self._exchange(y, rc, sc)                        # partial sums, in send order
-        self.last_exchange_bytes = (t_idx.numel() * (H * x.element_size() + k * 8)
-                                    + R * H * 4) - (sc[self.rank] * (H * x.element_size() + k * 8)
-                                                    + rc[self.rank] * H * 4)
-        parts = torch.zeros((N, T, H), dtype=torch.float32, device=dev)
-        parts[r_idx, t_idx] = back
+        meta = torch.cat([ids, w.view(torch.int32)], dim=1)     # [T, 2k] int32
+        x_all, wx = self._all_gather(x)
+        meta_all, wm = self._all_gather(meta)
+        # the shared expert of the own tokens overlaps the exchange (it needs no routing)
         shared = lay.forward_routed(x, torch.full_like(ids, -1), torch.zeros_like(w), with_shared=True)
-        out = parts[0].clone()
-        for r in range(1, N):
-            out += parts[r]
-        return out + shared, ids, w
+        for work in (wx, wm):
+            if work is not None:
+                work.wait()
+        ids_all = meta_all[:, :k].contiguous()
+        w_all = meta_all[:, k:].contiguous().view(torch.float32)
+        y = lay.forward_routed(x_all, ids_all, w_all, with_shared=False)   # [N*T, H] partial sums
+        parts = torch.empty_like(y)
+        dist.all_to_all_single(parts, y, group=self.group)      # block r: rank r's sums of my rows
+        self.last_exchange_bytes = (N - 1) * T * (H * x.element_size() + 2 * k * 4 + H * 4)
+        out = lay.sum_rank_parts(parts.view(N, T, H), last=shared)
+        return out, ids, w

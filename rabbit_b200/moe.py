@@ -15,6 +15,7 @@ All compute runs in librmoe.so on the GPU; torch only holds device memory and st
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -143,6 +144,15 @@ class MoeLayer:
         check(self.lib.rmoe_layer_get_stats(self.handle, C.byref(s)))
         return {f: getattr(s, f) for f, _ in LayerStats._fields_}
 
+    def check(self, stream=None):
+        """Synchronize and raise RmoeError(TIMEOUT) if a bounded device wait of this layer's
+        kernels ran out since the last check (the layer is usable again afterwards)."""
+        check(self.lib.rmoe_layer_check(self.handle, _stream(stream)))
+
+    def set_wait_limit(self, ns: int = 0):
+        """Limit of the kernels' waits on other CTAs in nanoseconds (0: the default 2 s)."""
+        check(self.lib.rmoe_layer_set_wait_limit(self.handle, int(ns)))
+
     def set_profiling(self, on: bool = True):
         check(self.lib.rmoe_layer_set_profiling(self.handle, int(on)))
 
@@ -184,6 +194,20 @@ class MoeLayer:
                                           _ptr(up_scale), _nbytes(up_scale), _ptr(down),
                                           _nbytes(down), _ptr(down_scale), _nbytes(down_scale),
                                           _ptr(sg)))
+
+    def load_expert(self, shards: "Shards", naming: str, layer_index: int, eid: int):
+        """One routed expert of a checkpoint layer into this layer (rmoe_load_expert)."""
+        check(self.lib.rmoe_load_expert(self.handle, shards.handle, _lib.NAMINGS[naming], layer_index, eid))
+
+    def load_experts(self, shards: "Shards", naming: str, layer_index: int):
+        """Every expert resident on this layer's EP rank."""
+        st = self.stats()
+        for eid in range(st["local_expert_begin"], st["local_expert_end"]):
+            self.load_expert(shards, naming, layer_index, eid)
+
+    def load_moe_weights(self, shards: "Shards", family: str, layer_index: int):
+        """Router (+ GLM correction bias) and shared expert of a checkpoint layer."""
+        check(self.lib.rmoe_load_moe_weights(self.handle, shards.handle, _lib.FAMILIES[family], layer_index))
 
     def upload_expert_dict(self, eid, ex: dict):
         self.upload_expert(eid, ex["gate"], ex["gate_scale"], ex["up"], ex["up_scale"],
@@ -237,6 +261,18 @@ class MoeLayer:
             out = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
         check(self.lib.rmoe_moe_forward_routed(self.handle, _ptr(x), _dtype_code(x), T, _ptr(ids), _ptr(weights),
                                                1 if with_shared else 0, _ptr(out), _stream(stream)))
+        return out
+
+    def sum_rank_parts(self, parts, last=None, out=None, stream=None):
+        """parts [N, T, H] f32 -> out [T, H] = parts[0] + ... + parts[N-1] (+ last), in rank
+        order (rmoe_sum_rank_parts): expert parallelism's owner-side combine."""
+        _require_cuda(parts)
+        parts = parts.contiguous()
+        n, T, H = parts.shape
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.float32, device=parts.device)
+        check(self.lib.rmoe_sum_rank_parts(_ptr(out), _ptr(parts), n, T, H,
+                                           _ptr(last) if last is not None else None, _stream(stream)))
         return out
 
     def upload_latent(self, down_proj, up_proj, norm=None, eps=1e-5):
@@ -324,3 +360,54 @@ def synth_bytes(t, key: int, mode: int = 0, lo: int = 0, hi: int = 0, stream=Non
     check(_lib.load().rmoe_synth_bytes(_ptr(t), _nbytes(t), C.c_uint64(key), mode, lo, hi,
                                        _stream(stream)))
     return t
+
+
+class Shards:
+    """A checkpoint's .safetensors shards (rabbit's Shards::open_multi): headers parsed once,
+    tensors read on demand. Host-only: works without a GPU."""
+
+    def __init__(self, *dirs):
+        self.lib = _lib.load()
+        arr = (C.c_char_p * len(dirs))(*[os.fsencode(d) for d in dirs])
+        h = C.c_void_p()
+        check(self.lib.rmoe_shards_open(arr, len(dirs), C.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            self.lib.rmoe_shards_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self):
+        n = C.c_int64()
+        check(self.lib.rmoe_shards_count(self.handle, C.byref(n)))
+        return n.value
+
+    def tensor(self, name: str) -> dict:
+        """dtype, shape and byte count of one tensor (RmoeError MISSING_TENSOR when absent)."""
+        dt = C.create_string_buffer(_lib.DTYPE_NAME_BYTES)
+        shape = (C.c_uint64 * _lib.MAX_TENSOR_DIMS)()
+        nd, nb = C.c_int32(), C.c_uint64()
+        check(self.lib.rmoe_shards_tensor(self.handle, name.encode(), dt, shape, C.byref(nd), C.byref(nb)))
+        return {"dtype": dt.value.decode(), "shape": [shape[i] for i in range(nd.value)], "nbytes": nb.value}
+
+    def has(self, name: str) -> bool:
+        try:
+            self.tensor(name)
+            return True
+        except RmoeError as e:
+            if e.status_name == "MISSING_TENSOR":
+                return False
+            raise
+
+    def read_raw(self, name: str) -> np.ndarray:
+        """The tensor's bytes verbatim (uint8)."""
+        out = np.empty(self.tensor(name)["nbytes"], np.uint8)
+        check(self.lib.rmoe_shards_read_raw(self.handle, name.encode(), out.ctypes.data, out.nbytes))
+        return out

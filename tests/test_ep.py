@@ -70,6 +70,13 @@ class OracleLayer:
         return torch.from_numpy(out)
 
 
+    def sum_rank_parts(self, parts, last=None):
+        out = parts[0].clone()
+        for r in range(1, parts.shape[0]):
+            out += parts[r]
+        return out + last if last is not None else out
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -229,4 +236,48 @@ def test_forward_routed_one_token(cuda_ctx):
         b = L.forward_routed(x, torch.where(keep, none, ids), torch.where(keep, torch.zeros_like(w), w),
                              with_shared=False)
         assert rel_l2((a + b + shared).cpu().numpy(), full.cpu().numpy()) < 1e-5
+    L.close()
+
+
+@pytest.mark.gpu
+def test_forward_routed_repeated_expert(cuda_ctx):
+    """A token whose routing names one expert in two slots gets that expert once, with the first
+    slot's weight, as apply_single_expert's first-match row gather does (src/glm52/moe.rs:465-470):
+    the result equals the same routing with the repeat removed, at T = 1 (one-warp dispatch) and
+    T > 1 (the general dispatch)."""
+    import torch
+
+    cfg = _mid_cfg()
+    L = synth.build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    xa = synth.activations(cfg)
+    for t0, t1 in ((3, 4), (0, cfg.tokens)):
+        x = synth.x_device(cfg, xa[t0:t1])
+        _, ids, w = L.moe_forward(x, return_routing=True)
+        dup_ids, dup_w = ids.clone(), w.clone()
+        dup_ids[:, 3] = ids[:, 1]          # slot 3 repeats slot 1's expert with its own weight
+        dup_w[:, 3] = 0.75
+        ref_ids = dup_ids.clone()
+        ref_ids[:, 3] = -1
+        got = L.forward_routed(x, dup_ids, dup_w)
+        want = L.forward_routed(x, ref_ids, dup_w)
+        assert rel_l2(got.cpu().numpy(), want.cpu().numpy()) < 1e-6
+    L.close()
+
+
+@pytest.mark.gpu
+def test_sum_rank_parts_is_rank_order(cuda_ctx):
+    """rmoe_sum_rank_parts adds the ranks' partial sums in rank order and the shared expert last:
+    bit-identical to the sequential sum, with and without the last term."""
+    import torch
+
+    L = synth.build_layer(cuda_ctx, synth.CONFIGS["c0_tiny"], max_tokens=4)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for n in (1, 2, 8):
+        parts = torch.randn((n, 37, 256), device="cuda", generator=g) * 1e3
+        last = torch.randn((37, 256), device="cuda", generator=g)
+        want = parts[0].clone()
+        for r in range(1, n):
+            want = want + parts[r]
+        assert torch.equal(L.sum_rank_parts(parts), want)
+        assert torch.equal(L.sum_rank_parts(parts, last=last), want + last)
     L.close()

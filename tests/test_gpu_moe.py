@@ -3,7 +3,7 @@ layer output within 1e-2 relative L2 (the north star's bf16-accumulation toleran
 import numpy as np
 import pytest
 
-from helpers import build_layer, oracle_forward, oracle_routing, x_device
+from helpers import build_layer, hard_prefill_tokens, oracle_forward, oracle_routing, per_token_rel_l2, x_device
 from rabbit_b200 import synth
 from refvec import rel_l2
 
@@ -69,9 +69,29 @@ def test_c2_prefill_routing_exact_and_output_subset(qwen_layer):
     want_ids, want_w = oracle_routing(cfg, x)
     assert np.array_equal(ids.cpu().numpy(), want_ids)
     assert np.max(np.abs(w.cpu().numpy() - want_w)) < 1e-6
-    sel = [0, 777, 2047]
+    # the layer is per-token independent: the hard tokens' reference output is the same alone
+    sel = hard_prefill_tokens(want_ids)
+    assert len(sel) >= 64
     want, _, _ = oracle_forward(cfg, x[sel])
     assert rel_l2(out.cpu().numpy()[sel], want) < OUT_RTOL
+    assert per_token_rel_l2(out.cpu().numpy()[sel], want).max() < OUT_RTOL
+
+
+def test_c2_shaped_64_experts_every_token(cuda_ctx):
+    """A C2-shaped layer (H 8192, I 2048, top-10, gated shared expert, Zipf skew) with 64 experts
+    at T = 2048: every expert takes ~320 rows, i.e. ten position chunks, and every one of the
+    2048 token outputs is checked against the reference (AVX-512 tier)."""
+    import dataclasses
+
+    cfg = dataclasses.replace(synth.CONFIGS["c2_qwen_prefill"], name="c2_64", n_experts=64)
+    L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    x = synth.activations(cfg)
+    out, ids, _ = L.moe_forward(x_device(cfg, x), return_routing=True)
+    out = out.cpu().numpy()
+    L.close()
+    want, want_ids, _ = oracle_forward(cfg, x, tier="avx512")
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert per_token_rel_l2(out, want).max() < OUT_RTOL
 
 
 def test_decode_router_certificate_matches_exact_routing(qwen_layer):
@@ -142,9 +162,79 @@ def test_c4_glm_int4_layer(cuda_ctx):
     want_ids, want_w = oracle_routing(cfg, x)
     assert np.array_equal(ids.cpu().numpy(), want_ids)
     assert np.max(np.abs(w.cpu().numpy() - want_w)) < 1e-5
-    sel = [3, 300]
+    sel = hard_prefill_tokens(want_ids, at_least=32)[:48]
     want, _, _ = oracle_forward(cfg, x[sel])
     assert rel_l2(out.cpu().numpy()[sel], want) < OUT_RTOL
+    assert per_token_rel_l2(out.cpu().numpy()[sel], want).max() < OUT_RTOL
+    L.close()
+
+
+def _fused_gate_up(ex):
+    """GateUp::Fused from the separate tensors: [2I, H] = gate rows, then up rows (the layout
+    fuse_gate_up writes, src/expert_cache.rs:69-74)."""
+    import torch
+
+    return torch.cat([ex["gate"], ex["up"]]), torch.cat([ex["gate_scale"], ex["up_scale"]])
+
+
+@pytest.mark.parametrize("name", ["c0_tiny", "c2_64"])
+def test_fused_gate_up_upload_is_bit_identical(cuda_ctx, name):
+    """An expert uploaded as GateUp::Fused computes exactly what the Separate upload computes
+    (the reference pins the two slot kinds equal, src/glm52/moe.rs:592-626): both layouts end in
+    the same device bytes, so the outputs are bit-identical on the GEMV (c0) and tensor-core
+    (C2-shaped, T = 1 and T = 40) paths."""
+    import dataclasses
+
+    import torch
+
+    if name == "c0_tiny":
+        cfg = synth.CONFIGS["c0_tiny"]
+        Ts = (1, cfg.tokens)
+    else:
+        cfg = dataclasses.replace(synth.CONFIGS["c2_qwen_prefill"], name=name, n_experts=64, tokens=40)
+        Ts = (1, 40)
+    sep = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    fus = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    for eid in range(cfg.n_experts):
+        ex = synth.gpu_expert(cfg, eid)
+        gu, gus = _fused_gate_up(ex)
+        # overwrite with a different expert first, so a no-op upload cannot pass
+        fus.upload_expert_dict(eid, synth.gpu_expert(cfg, (eid + 1) % cfg.n_experts))
+        fus.upload_expert_fused(eid, gu, gus, ex["down"], ex["down_scale"])
+    torch.cuda.synchronize()
+    x = synth.activations(cfg)
+    for T in Ts:
+        xd = x_device(cfg, x[:T])
+        assert torch.equal(sep.moe_forward(xd), fus.moe_forward(xd))
+    with pytest.raises(Exception, match="SHAPE_MISMATCH"):
+        ex = synth.gpu_expert(cfg, 0)
+        gu, gus = _fused_gate_up(ex)
+        fus.upload_expert_fused(0, gu[:-1], gus, ex["down"], ex["down_scale"])
+    sep.close()
+    fus.close()
+
+
+def test_bounded_wait_reports_timeout_and_layer_recovers(cuda_ctx):
+    """A wait limit far below the kernels' own run time makes a bounded device wait (the fused
+    one-token kernel's wait for an expert's h, its closing grid barrier) run out: the host entry
+    point returns RMOE_TIMEOUT instead of garbage with OK. With the default limit back, the next
+    call succeeds and gives the bits of a call on a layer that never timed out."""
+    import dataclasses
+
+    import rabbit_b200 as rb
+
+    cfg = dataclasses.replace(synth.CONFIGS["c2_qwen_prefill"], name="c2_64", n_experts=64, tokens=4)
+    L = build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+    x = synth.f32_to_bf16_bits(synth.activations(cfg, tokens=1))
+    good = L.moe_forward_host(x)
+    L.set_wait_limit(100)  # 100 ns: a CTA's wait for another CTA's progress runs out
+    with pytest.raises(rb.RmoeError, match="TIMEOUT"):
+        L.moe_forward_host(x)
+    assert L.stats()["device_error_flags"] != 0
+    L.set_wait_limit(0)
+    again = L.moe_forward_host(x)
+    assert np.array_equal(again, good)
+    L.check()  # nothing pending
     L.close()
 
 

@@ -18,7 +18,8 @@ def _t(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("s,i,o", [(1, 8192, 256), (8, 1024, 96), (512, 8192, 16), (5, 40, 7)])
+@pytest.mark.parametrize("s,i,o", [(1, 8192, 256), (8, 1024, 96), (512, 8192, 16), (5, 40, 7),
+                                   (1030, 4100, 3)])  # (i % 32 != 0: no scratch, no limit)
 def test_noalloc_matches_allocating_entry_point(cuda_ctx, s, i, o):
     import torch
 
