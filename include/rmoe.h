@@ -190,6 +190,17 @@ RMOE_API rmoe_status rmoe_layer_check(rmoe_layer* layer, void* stream);
  * those waits can run out, and the call then reports RMOE_TIMEOUT instead of hanging. */
 RMOE_API rmoe_status rmoe_layer_set_wait_limit(rmoe_layer* layer, uint64_t ns);
 
+/* Opt-in CACHE_ROUTE routing for the sigmoid router (RouteConfig + route_cache_aware,
+ * src/glm52/moe.rs:99-127, :272-323), off by default: the top route_j experts by choice are always
+ * taken; the remaining k - route_j slots prefer experts marked resident among the next ranked up to
+ * max(route_m, k), in rank order, then fall back to rank order. Like the reference it ranks over
+ * all experts (no grouping). resident: [n_experts] bytes, nonzero = resident (host or device),
+ * or NULL = every expert resident (then the selection equals plain top-k). cache_route = 0 restores
+ * the plain router. RMOE_NOT_SUPPORTED on a softmax-router layer (the reference has no
+ * CACHE_ROUTE there). */
+RMOE_API rmoe_status rmoe_set_route_config(rmoe_layer* layer, int32_t cache_route, int32_t route_j, int32_t route_m,
+                                           const uint8_t* resident);
+
 /* ---- weights, taken in the reference's byte layout verbatim. Pointers may be host or device
  *      memory (unified addressing). Byte counts are checked like mxfp4_from_raw
  *      (src/expert_cache.rs:1245-1256): MXFP4 data = rows*ceil(cols/2), scales =
@@ -358,6 +369,25 @@ RMOE_API rmoe_status rmoe_matmul_mxfp4_noalloc(float* y, const void* x, int32_t 
 RMOE_API rmoe_status rmoe_matmul_i4_grouped(float* y, const void* x, int32_t x_dtype, const uint8_t* q4,
                                    const void* scale, int32_t scale_dtype, int32_t group_size,
                                    int32_t s, int32_t i, int32_t o, void* stream);
+/* The QT kinds of quant::QTKind (src/quant.rs:80-109). */
+typedef enum rmoe_qt_kind {
+  RMOE_QT_F32 = 0,        /* f32 [O, I] */
+  RMOE_QT_I8 = 1,         /* int8 [O, I] + f32 scale per row */
+  RMOE_QT_I4 = 2,         /* offset-binary nibbles [O, ceil(I/2)] (low first) + f32 scale per row */
+  RMOE_QT_I2 = 3,         /* 2-bit values + 2, 4 per byte low bits first [O, ceil(I/4)] + f32 scale per row */
+  RMOE_QT_I4_GROUPED = 4, /* nibbles + f32 scale per group_size elements of a row */
+  RMOE_QT_MXFP4 = 5       /* E2M1 nibbles + E8M0 byte per 32 */
+} rmoe_qt_kind;
+
+/* kernels::matmul_qt (src/kernels.rs:1104-1132), the dispatcher every layer calls: y[S,O] =
+ * x[S,I] . W^T for a weight of any QT kind, with the reference's per-kind paths -- I8 always and
+ * I4 at s >= 2 through integer dot products against int8-quantized activations (qrow_i8 per row,
+ * y = float(dot) * scale[o] * sx[s]: bit-exact with the reference), I4 at s == 1 and I2 as
+ * float-weight products, F32 as rmoe_matmul_f32 (exact chains), I4_GROUPED and MXFP4 as
+ * rmoe_matmul_i4_grouped / rmoe_matmul_mxfp4. Device pointers; group_size only for I4_GROUPED. */
+RMOE_API rmoe_status rmoe_matmul_qt(float* y, const void* x, int32_t x_dtype, int32_t kind, const void* data,
+                                    const void* scale, int32_t group_size, int32_t s, int32_t i, int32_t o,
+                                    void* stream);
 /* kernels::matmul (src/kernels.rs:113-124) for f32/bf16 weights: each y element is the
  * reference's exact left-to-right f32 chain (separate multiply and add, from -0.0). */
 RMOE_API rmoe_status rmoe_matmul_f32(float* y, const void* x, int32_t x_dtype, const void* w,

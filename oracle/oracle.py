@@ -66,6 +66,17 @@ def lib():
         L.orc_rank_top_grouped.argtypes = [F32P, F32P, SZ, SZ, SZ, SZ, I32P, F32P]
         L.orc_glm_route.argtypes = [F32P, F32P, F32P, SZ, SZ, SZ, SZ, SZ, SZ, C.c_int, C.c_float,
                                     I32P, F32P]
+        L.orc_glm_route_cache.argtypes = [F32P, F32P, F32P, SZ, SZ, SZ, SZ, SZ, SZ, C.c_void_p, C.c_int,
+                                          C.c_float, C.c_void_p, C.c_void_p]
+        L.orc_cache_route_select.restype = SZ
+        L.orc_cache_route_select.argtypes = [F32P, F32P, SZ, SZ, SZ, SZ, C.c_void_p, I32P, F32P]
+        L.orc_qrow_i8.restype = C.c_float
+        L.orc_qrow_i8.argtypes = [F32P, SZ, C.c_void_p]
+        L.orc_dot_i8i8.restype = C.c_int32
+        L.orc_dot_i8i8.argtypes = [C.c_void_p, C.c_void_p, SZ]
+        L.orc_dot_i4i8.restype = C.c_int32
+        L.orc_dot_i4i8.argtypes = [C.c_void_p, C.c_void_p, SZ]
+        L.orc_matmul_qt_kind.argtypes = [F32P, F32P, C.c_int, C.c_void_p, C.c_void_p, SZ, SZ, SZ, SZ]
         L.orc_unique_experts.restype = SZ
         L.orc_unique_experts.argtypes = [I32P, SZ, SZ, I32P]
         L.orc_expert_rows.restype = SZ
@@ -150,6 +161,36 @@ def matmul_mxfp4(x, data, bs, s, i, o, tier="scalar"):
     return y.reshape(s, o)
 
 
+QT_KINDS = {"f32": 0, "i8": 1, "i4": 2, "i2": 3, "i4_grouped": 4, "mxfp4": 5}
+
+
+def qrow_i8(x):
+    """kernels::qrow_i8 -> (int8 array, scale)."""
+    x = _f32(x).reshape(-1)
+    q = np.zeros(x.size, np.int8)
+    sc = lib().orc_qrow_i8(x, x.size, q.ctypes.data)
+    return q, np.float32(sc)
+
+
+def dot_i8i8(w, x):
+    w, x = np.ascontiguousarray(w, np.int8), np.ascontiguousarray(x, np.int8)
+    return int(lib().orc_dot_i8i8(w.ctypes.data, x.ctypes.data, w.size))
+
+
+def dot_i4i8(w4, x, n):
+    w4, x = np.ascontiguousarray(w4, np.uint8), np.ascontiguousarray(x, np.int8)
+    return int(lib().orc_dot_i4i8(w4.ctypes.data, x.ctypes.data, n))
+
+
+def matmul_qt(x, kind, data, scale, s, i, o, gs=32):
+    """kernels::matmul_qt for a QT of `kind` (QT_KINDS): y [s, o] f32."""
+    y = np.zeros(s * o, np.float32)
+    d = np.ascontiguousarray(data)
+    sc = np.ascontiguousarray(scale)
+    lib().orc_matmul_qt_kind(y, _f32(x).reshape(-1), QT_KINDS[kind], d.ctypes.data, sc.ctypes.data, gs, s, i, o)
+    return y.reshape(s, o)
+
+
 def matmul_i4_grouped(x, q4, scale, gs, s, i, o):
     y = np.zeros(s * o, np.float32)
     lib().orc_matmul_i4_grouped(y, _f32(x).reshape(-1), np.ascontiguousarray(q4).reshape(-1),
@@ -187,6 +228,28 @@ def rank_top_grouped(choice, logit, k, n_group, topk_group):
     w = np.zeros(max(k, 1), np.float32)
     kk = lib().orc_rank_top_grouped(c, l, c.size, k, n_group, topk_group, ids, w)
     return [(int(ids[j]), float(w[j])) for j in range(kk)]
+
+
+def glm_route_cache(x, router, bias, s, d, e, k, route_j, route_m, resident, norm_topk, routed_scale):
+    """CACHE_ROUTE selection (glm52::moe::route_cache_aware); resident: [E] bool or None."""
+    ids = np.zeros(s * k, np.int32)
+    w = np.zeros(s * k, np.float32)
+    res = None if resident is None else np.ascontiguousarray(resident, np.uint8)
+    lib().orc_glm_route_cache(_f32(x).reshape(-1), _f32(router).reshape(-1), _f32(bias).reshape(-1), s, d, e, k,
+                              route_j, route_m, res.ctypes.data if res is not None else None, int(norm_topk),
+                              routed_scale, ids.ctypes.data, w.ctypes.data)
+    return ids.reshape(s, k), w.reshape(s, k)
+
+
+def cache_route_select(choice, logit, k, route_j, route_m, resident=None):
+    """glm52::moe::cache_route_select on given choice/logit vectors -> [(id, weight)]."""
+    choice, logit = _f32(choice), _f32(logit)
+    ids = np.zeros(k, np.int32)
+    w = np.zeros(k, np.float32)
+    res = None if resident is None else np.ascontiguousarray(resident, np.uint8)
+    n = lib().orc_cache_route_select(choice, logit, choice.size, k, route_j, route_m,
+                                     res.ctypes.data if res is not None else None, ids, w)
+    return [(int(ids[j]), float(w[j])) for j in range(n)]
 
 
 def glm_route(x, router, bias, s, d, e, k, n_group, topk_group, norm_topk, routed_scale):

@@ -212,6 +212,122 @@ void orc_matmul_qt(float* y, const float* x, const uint8_t* data, const void* sc
     orc_matmul_i4_grouped(y, x, data, (const float*)scale, gs, s, i, o);
 }
 
+/* ---- the other QT kinds of matmul_qt (kernels.rs:1104-1132) */
+
+/* kernels.rs:301-309 qrow_i8: s = max(amax / 127, 1e-12), q = round_ties_even(x * (1 / s)) */
+float orc_qrow_i8(const float* x, size_t n, int8_t* q) {
+  float amax = 0.0f;
+  for (size_t k = 0; k < n; k++) amax = fmaxf(amax, fabsf(x[k]));
+  float sc = fmaxf(amax / 127.0f, 1e-12f);
+  float inv = 1.0f / sc;
+  for (size_t k = 0; k < n; k++) q[k] = (int8_t)(int32_t)nearbyintf(x[k] * inv);
+  return sc;
+}
+
+/* kernels.rs:331-337 */
+int32_t orc_dot_i8i8(const int8_t* w, const int8_t* x, size_t n) {
+  int32_t sum = 0;
+  for (size_t k = 0; k < n; k++) sum += (int32_t)w[k] * (int32_t)x[k];
+  return sum;
+}
+
+/* kernels.rs:355-368: nibble - 8 (low nibble first) times int8 */
+int32_t orc_dot_i4i8(const uint8_t* w4, const int8_t* x, size_t n) {
+  int32_t sum = 0;
+  for (size_t k = 0; k < n; k++) {
+    uint8_t b = w4[k >> 1];
+    int32_t v = (int32_t)((k & 1) ? (b >> 4) : (b & 0xF)) - 8;
+    sum += v * (int32_t)x[k];
+  }
+  return sum;
+}
+
+/* kernels.rs:135-148 matmul_q (int8 weights, per-row scale, float path): a = sum x * w from
+ * +0.0 (iterator sum), then a * scale */
+void orc_matmul_q(float* y, const float* x, const int8_t* q, const float* scale, size_t s, size_t i, size_t o) {
+#pragma omp parallel for schedule(static)
+  for (long oi = 0; oi < (long)o; oi++)
+    for (size_t si = 0; si < s; si++) {
+      float a = RUST_SUM_INIT;
+      for (size_t k = 0; k < i; k++) a = a + x[si * i + k] * (float)q[(size_t)oi * i + k];
+      y[si * o + oi] = a * scale[oi];
+    }
+}
+
+/* kernels.rs:167-193 matmul_i4_scalar: pairs a += x0 * lo + x1 * hi (left to right), tail
+ * nibble alone, then a * scale */
+void orc_matmul_i4(float* y, const float* x, const uint8_t* q4, const float* scale, size_t s, size_t i, size_t o) {
+  size_t rb = (i + 1) / 2;
+#pragma omp parallel for schedule(static)
+  for (long oi = 0; oi < (long)o; oi++)
+    for (size_t si = 0; si < s; si++) {
+      const uint8_t* w = q4 + (size_t)oi * rb;
+      const float* xs = x + si * i;
+      float a = 0.0f;
+      size_t k = 0;
+      for (; k + 1 < i; k += 2) {
+        uint8_t b = w[k >> 1];
+        float lo = (float)((int32_t)(b & 0xF) - 8), hi = (float)((int32_t)(b >> 4) - 8);
+        a = a + (xs[k] * lo + xs[k + 1] * hi);
+      }
+      if (k < i) a = a + xs[k] * (float)((int32_t)(w[k >> 1] & 0xF) - 8);
+      y[si * o + oi] = a * scale[oi];
+    }
+}
+
+/* kernels.rs:206-224 matmul_i2_scalar: 4 values per byte, low bits first, value + 2 stored */
+void orc_matmul_i2(float* y, const float* x, const uint8_t* q2, const float* scale, size_t s, size_t i, size_t o) {
+  size_t rb = (i + 3) / 4;
+#pragma omp parallel for schedule(static)
+  for (long oi = 0; oi < (long)o; oi++)
+    for (size_t si = 0; si < s; si++) {
+      const uint8_t* w = q2 + (size_t)oi * rb;
+      const float* xs = x + si * i;
+      float a = 0.0f;
+      for (size_t k = 0; k < i; k++) {
+        int32_t v = (int32_t)((w[k >> 2] >> ((k & 3) * 2)) & 3) - 2;
+        a = a + xs[k] * (float)v;
+      }
+      y[si * o + oi] = a * scale[oi];
+    }
+}
+
+/* kernels.rs:1063-1098 matmul_q_idot / matmul_i4_idot: activations quantized per row (qrow_i8),
+ * y = (float)dot * scale[o] * sx[s] */
+static void matmul_idot(float* y, const float* x, const void* w, int w4, const float* scale, size_t s, size_t i,
+                        size_t o) {
+  int8_t* xq = (int8_t*)malloc(s * i + 1);
+  float* sx = (float*)malloc((s + 1) * sizeof(float));
+  for (size_t si = 0; si < s; si++) sx[si] = orc_qrow_i8(x + si * i, i, xq + si * i);
+  size_t rb = w4 ? (i + 1) / 2 : i;
+#pragma omp parallel for schedule(static)
+  for (long oi = 0; oi < (long)o; oi++)
+    for (size_t si = 0; si < s; si++) {
+      int32_t d = w4 ? orc_dot_i4i8((const uint8_t*)w + (size_t)oi * rb, xq + si * i, i)
+                     : orc_dot_i8i8((const int8_t*)w + (size_t)oi * rb, xq + si * i, i);
+      y[si * o + oi] = (float)d * scale[oi] * sx[si];
+    }
+  free(xq);
+  free(sx);
+}
+
+/* kernels.rs:1104-1132 matmul_qt for every QT kind: 0 F32, 1 I8 (IDOT), 2 I4 (IDOT at s >= 2,
+ * else the float path), 3 I2, 4 I4Grouped, 5 MxFp4 */
+void orc_matmul_qt_kind(float* y, const float* x, int kind, const void* data, const void* scale, size_t gs,
+                        size_t s, size_t i, size_t o) {
+  switch (kind) {
+    case 0: orc_matmul_f32(y, x, (const float*)data, s, i, o); break;
+    case 1: matmul_idot(y, x, data, 0, (const float*)scale, s, i, o); break;
+    case 2:
+      if (s >= 2) matmul_idot(y, x, data, 1, (const float*)scale, s, i, o);
+      else orc_matmul_i4(y, x, (const uint8_t*)data, (const float*)scale, s, i, o);
+      break;
+    case 3: orc_matmul_i2(y, x, (const uint8_t*)data, (const float*)scale, s, i, o); break;
+    case 4: orc_matmul_i4_grouped(y, x, (const uint8_t*)data, (const float*)scale, gs, s, i, o); break;
+    default: orc_matmul_mxfp4(y, x, (const uint8_t*)data, (const uint8_t*)scale, s, i, o); break;
+  }
+}
+
 /* ------------------------------------------------------------------ activations */
 
 /* glm52/moe.rs:33-35 siluf == kimi_linear/ops.rs:22-24 swish */
@@ -363,6 +479,77 @@ void orc_glm_route(const float* x, const float* router, const float* bias, size_
       pi[j] = -1;
       pw[j] = 0.0f;
     }
+  }
+  free(logit);
+  free(choice);
+}
+
+/* glm52/moe.rs:293-323 cache_route_select: rank the top m = max(route_m, k) by choice
+ * (rank_top, :148-166), keep ranked[0..j), j = min(route_j, k, m), fill with resident ranked[j..]
+ * in order, then with any not-yet-picked ranked[j..] in order. resident NULL = every expert
+ * resident. Returns the number picked (ids/w: k entries, the rest -1 / 0). */
+size_t orc_cache_route_select(const float* choice, const float* logit, size_t e, size_t k, size_t route_j,
+                              size_t route_m, const uint8_t* resident, int32_t* ids, float* w) {
+  size_t m = route_m > k ? route_m : k;
+  if (m > e) m = e;
+  int32_t* rid = (int32_t*)malloc((m + 1) * sizeof(int32_t));
+  float* rw = (float*)malloc((m + 1) * sizeof(float));
+  rank_top_within(choice, logit, e, m, NULL, rid, rw);
+  size_t jj = route_j < k ? route_j : k;
+  if (jj > m) jj = m;
+  size_t n = 0;
+  for (size_t r = 0; r < jj; r++, n++) {
+    ids[n] = rid[r];
+    w[n] = rw[r];
+  }
+  for (size_t r = jj; r < m && n < k; r++)
+    if (!resident || resident[rid[r]]) {
+      ids[n] = rid[r];
+      w[n] = rw[r];
+      n++;
+    }
+  for (size_t r = jj; r < m && n < k; r++) {
+    int dup = 0;
+    for (size_t q = 0; q < n; q++) dup |= ids[q] == rid[r];
+    if (dup) continue;
+    ids[n] = rid[r];
+    w[n] = rw[r];
+    n++;
+  }
+  for (size_t j = n; j < k; j++) {
+    ids[j] = -1;
+    w[j] = 0.0f;
+  }
+  free(rid);
+  free(rw);
+  return n;
+}
+
+/* glm52/moe.rs:272-290 route_cache_aware: router_scores, cache_route_select, normalize_and_scale */
+void orc_glm_route_cache(const float* x, const float* router, const float* bias, size_t s, size_t d,
+                         size_t e, size_t k, size_t route_j, size_t route_m, const uint8_t* resident,
+                         int norm_topk, float routed_scale, int32_t* ids, float* w) {
+  float* logit = (float*)malloc(e * sizeof(float));
+  float* choice = (float*)malloc(e * sizeof(float));
+  for (size_t si = 0; si < s; si++) {
+    const float* xs = x + si * d;
+    for (size_t j = 0; j < e; j++) {
+      const float* wr = router + j * d;
+      float a = RUST_SUM_INIT;
+      for (size_t q = 0; q < d; q++) a = a + xs[q] * wr[q];
+      logit[j] = 1.0f / (1.0f + expf(-a));
+      choice[j] = logit[j] + bias[j];
+    }
+    int32_t* pi = ids + si * k;
+    float* pw = w + si * k;
+    size_t n = orc_cache_route_select(choice, logit, e, k, route_j, route_m, resident, pi, pw);
+    if (norm_topk) {
+      float sum = RUST_SUM_INIT;
+      for (size_t j = 0; j < n; j++) sum = sum + pw[j];
+      sum = sum + 1e-20f;
+      for (size_t j = 0; j < n; j++) pw[j] = pw[j] / sum;
+    }
+    for (size_t j = 0; j < n; j++) pw[j] = pw[j] * routed_scale;
   }
   free(logit);
   free(choice);

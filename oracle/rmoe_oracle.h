@@ -56,6 +56,11 @@ float orc_top2_sum(const float* vals, size_t n);       /* moe.rs:193-205 */
 size_t orc_rank_top_grouped(const float* choice, const float* logit, size_t e, size_t k,
                             size_t n_group, size_t topk_group, int32_t* ids, float* w);
 /* route() for s tokens: router matmul + sigmoid + bias + grouped top-k + normalize_and_scale */
+size_t orc_cache_route_select(const float* choice, const float* logit, size_t e, size_t k, size_t route_j,
+                              size_t route_m, const uint8_t* resident, int32_t* ids, float* w);
+void orc_glm_route_cache(const float* x, const float* router, const float* bias, size_t s, size_t d,
+                         size_t e, size_t k, size_t route_j, size_t route_m, const uint8_t* resident,
+                         int norm_topk, float routed_scale, int32_t* ids, float* w);
 void orc_glm_route(const float* x, const float* router, const float* bias, size_t s,
                    size_t d, size_t e, size_t k, size_t n_group, size_t topk_group,
                    int norm_topk, float routed_scale, int32_t* ids, float* w);
@@ -77,6 +82,14 @@ typedef struct orc_expert {
 } orc_expert;
 
 /* matmul_qt restricted to the two routed-expert formats. */
+float orc_qrow_i8(const float* x, size_t n, int8_t* q);
+int32_t orc_dot_i8i8(const int8_t* w, const int8_t* x, size_t n);
+int32_t orc_dot_i4i8(const uint8_t* w4, const int8_t* x, size_t n);
+void orc_matmul_q(float* y, const float* x, const int8_t* q, const float* scale, size_t s, size_t i, size_t o);
+void orc_matmul_i4(float* y, const float* x, const uint8_t* q4, const float* scale, size_t s, size_t i, size_t o);
+void orc_matmul_i2(float* y, const float* x, const uint8_t* q2, const float* scale, size_t s, size_t i, size_t o);
+void orc_matmul_qt_kind(float* y, const float* x, int kind, const void* data, const void* scale, size_t gs,
+                        size_t s, size_t i, size_t o);
 void orc_matmul_qt(float* y, const float* x, const uint8_t* data, const void* scale, int fmt,
                    size_t gs, size_t s, size_t i, size_t o);
 

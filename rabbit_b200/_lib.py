@@ -18,6 +18,7 @@ NAMINGS = {"glm52": 0, "glm52_fused_gate_up": 1, "kimi_linear": 2, "kimi_k3": 3,
            "qwen38_mxfp4": 5}
 FAMILIES = {"qwen38": 0, "glm52": 1}
 DTYPE_NAME_BYTES, MAX_TENSOR_DIMS = 16, 8
+QT_KINDS = {"f32": 0, "i8": 1, "i4": 2, "i2": 3, "i4_grouped": 4, "mxfp4": 5}
 
 
 class RmoeError(RuntimeError):
@@ -76,6 +77,7 @@ PROTOTYPES = {
     "rmoe_load_moe_weights": (C.c_int, [P, P, I32, I32]),
     "rmoe_layer_check": (C.c_int, [P, P]),
     "rmoe_layer_set_wait_limit": (C.c_int, [P, C.c_uint64]),
+    "rmoe_set_route_config": (C.c_int, [P, I32, I32, I32, P]),
     "rmoe_layer_set_profiling": (C.c_int, [P, C.c_int]),
     "rmoe_layer_get_profile": (C.c_int, [P, C.POINTER(Profile)]),
     "rmoe_upload_router": (C.c_int, [P, P, I32, SZ]),
@@ -96,6 +98,7 @@ PROTOTYPES = {
     "rmoe_matmul_mxfp4_noalloc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_i4_grouped": (C.c_int, [P, P, I32, P, P, I32, I32, I32, I32, I32, P]),
     "rmoe_matmul_f32": (C.c_int, [P, P, I32, P, I32, I32, I32, I32, P]),
+    "rmoe_matmul_qt": (C.c_int, [P, P, I32, I32, P, P, I32, I32, I32, I32, P]),
     "rmoe_synth_bytes": (C.c_int, [P, SZ, C.c_uint64, I32, I32, I32, P]),
 }
 

@@ -200,6 +200,12 @@ struct rmoe_layer {
   bool use_fused = true;                   // one token: the fused gate/up + down kernel (RMOE_DISABLE_FUSED=1: two kernels)
   unsigned long long spin_ns = kDefaultSpinNs;  // limit of the kernels' waits on other CTAs
   unsigned err_seen = 0;                   // device error flags already reported (and cleared)
+  // CACHE_ROUTE (sigmoid routers): keep the top route_j, prefer resident experts among the next
+  // ranked up to route_m (src/glm52/moe.rs:99-127)
+  bool cache_route = false;
+  int route_j = 2, route_m = 12;
+  uint8_t* resident = nullptr;   // [E] residency mask (device)
+  bool resident_all = true;      // no mask given: every expert resident
   bool diag_host = false;                  // RMOE_DIAG_HOST=1: kernel trace in mapped host memory
   void* diag_buf = nullptr;
   ~rmoe_layer() {
@@ -696,6 +702,21 @@ static rmoe_status drain_graph_profile(rmoe_layer* L, GraphEntry& g);
 // work on the layer's streams is done. Nonzero: the outputs of the calls since the last check
 // are invalid, and the persistent kernels' work counters may be left mid-count, so they are
 // zeroed (with the device idle) and the flags cleared: the next call runs normally.
+// Destroys the captured forward graphs (after the device is idle): a change of the layer's
+// kernel parameters or routing configuration is captured again on the next call.
+static rmoe_status drop_graphs(rmoe_layer* L) {
+  if (L->graphs.empty()) return RMOE_OK;
+  RMOE_CUDA(cudaDeviceSynchronize(), "drop graphs: synchronize");
+  for (auto& kv : L->graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+    for (cudaEvent_t e : kv.second.ev)
+      if (e) cudaEventDestroy(e);
+  }
+  L->graphs.clear();
+  return RMOE_OK;
+}
+
 static rmoe_status take_device_errors(rmoe_layer* L, const char* what) {
   unsigned ef = 0;
   RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
@@ -731,15 +752,36 @@ extern "C" rmoe_status rmoe_layer_set_wait_limit(rmoe_layer* L, uint64_t ns) {
   const unsigned long long v = ns ? ns : kDefaultSpinNs;
   if (v == L->spin_ns) return RMOE_OK;
   // the captured one-token graphs hold the old limit in their kernel arguments
-  RMOE_CUDA(cudaDeviceSynchronize(), "rmoe_layer_set_wait_limit synchronize");
-  for (auto& kv : L->graphs) {
-    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
-    for (cudaEvent_t e : kv.second.ev)
-      if (e) cudaEventDestroy(e);
-  }
-  L->graphs.clear();
+  rmoe_status s = drop_graphs(L);
+  if (s != RMOE_OK) return s;
   L->spin_ns = v;
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_set_route_config(rmoe_layer* L, int32_t cache_route, int32_t route_j, int32_t route_m,
+                                             const uint8_t* resident) {
+  const char* what = "rmoe_set_route_config";
+  if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
+  if (cache_route && L->desc.router_kind != RMOE_ROUTER_SIGMOID_GROUPED)
+    return fail(RMOE_NOT_SUPPORTED, "%s: CACHE_ROUTE applies to the sigmoid router only (the softmax router has none)", what);
+  if (cache_route && (route_j < 0 || route_m < 0 || std::max<int>(route_m, L->desc.topk) > 32))
+    return fail(RMOE_INVALID_ARG, "%s: route_j %d, route_m %d (0 <= route_j, max(route_m, k) <= 32)", what, route_j, route_m);
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  rmoe_status s = drop_graphs(L);
+  if (s != RMOE_OK) return s;
+  if (resident) {
+    if (!L->resident) {
+      void* p = nullptr;
+      RMOE_CUDA(cudaMalloc(&p, L->desc.n_experts), "rmoe_set_route_config resident mask");
+      L->arena.ptrs.push_back(p);
+      L->resident = static_cast<uint8_t*>(p);
+    }
+    RMOE_CUDA(cudaMemcpy(L->resident, resident, L->desc.n_experts, cudaMemcpyDefault), "resident mask");
+  }
+  L->cache_route = cache_route != 0;
+  L->route_j = route_j;
+  L->route_m = route_m;
+  L->resident_all = resident == nullptr;
   return RMOE_OK;
 }
 
@@ -960,6 +1002,10 @@ static rmoe_status route_into(rmoe_layer* L, const void* x, int x_dtype, int T, 
   if (D.router_kind == RMOE_ROUTER_SOFTMAX_TOPK)
     e = launch_topk_softmax(L->logits, L->has_bias ? L->router_bias : nullptr, T, D.n_experts, D.topk,
                             L->ids, L->rw, st);
+  else if (L->cache_route)
+    e = launch_topk_cache_route(L->logits, L->router_bias, T, D.n_experts, D.topk, L->route_j, L->route_m,
+                                L->resident_all ? nullptr : L->resident, D.norm_topk, D.routed_scale, L->ids, L->rw,
+                                st);
   else
     e = launch_topk_grouped(L->logits, L->router_bias, T, D.n_experts, D.topk, D.n_group,
                             D.topk_group, D.norm_topk, D.routed_scale, L->ids, L->rw, st);
@@ -1809,6 +1855,52 @@ extern "C" rmoe_status rmoe_matmul_f32(float* y, const void* x, int32_t x_dtype,
                                              static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rmoe_matmul_f32");
   return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_matmul_qt(float* y, const void* x, int32_t x_dtype, int32_t kind, const void* data,
+                                      const void* scale, int32_t group_size, int32_t s, int32_t i, int32_t o,
+                                      void* stream) {
+  const char* what = "rmoe_matmul_qt";
+  if (!y || !x || !data || (kind != RMOE_QT_F32 && !scale)) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  if (s < 0 || i <= 0 || o < 0) return fail(RMOE_INVALID_ARG, "%s: s=%d i=%d o=%d", what, s, i, o);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
+  switch (kind) {
+    case RMOE_QT_F32:
+      return rmoe_matmul_f32(y, x, x_dtype, data, RMOE_F32, s, i, o, stream);
+    case RMOE_QT_MXFP4:
+      return matmul_q(what, y, x, x_dtype, static_cast<const uint8_t*>(data), scale, ExpertFormat{kMxfp4, 32, kF32}, s, i,
+                      o, stream);
+    case RMOE_QT_I4_GROUPED:
+      if (group_size <= 0) return fail(RMOE_INVALID_ARG, "%s: group_size %d", what, group_size);
+      return matmul_q(what, y, x, x_dtype, static_cast<const uint8_t*>(data), scale,
+                      ExpertFormat{kInt4g, group_size, kF32}, s, i, o, stream);
+    case RMOE_QT_I2:
+    case RMOE_QT_I4:
+      // int4 at s >= 2 and int8 always take the integer-dot path, like the reference dispatcher
+      if (kind == RMOE_QT_I2 || s < 2) {
+        cudaError_t e = launch_matmul_qt_float(y, x, xdt, static_cast<const uint8_t*>(data), kind == RMOE_QT_I2 ? 2 : 4,
+                                               static_cast<const float*>(scale), s, i, o, st);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        return RMOE_OK;
+      }
+      [[fallthrough]];
+    case RMOE_QT_I8: {
+      if (s == 0 || o == 0) return RMOE_OK;
+      const size_t ws = matmul_idot_workspace_bytes(s, i);
+      void* buf = nullptr;
+      RMOE_CUDA(cudaMallocAsync(&buf, ws, st), "matmul_qt workspace");
+      cudaError_t e = launch_matmul_idot(y, x, xdt, data, kind == RMOE_QT_I4, static_cast<const float*>(scale), s, i, o,
+                                         buf, st);
+      cudaError_t e2 = cudaFreeAsync(buf, st);
+      if (e != cudaSuccess) return cuda_fail(e, what);
+      if (e2 != cudaSuccess) return cuda_fail(e2, what);
+      return RMOE_OK;
+    }
+    default:
+      return fail(RMOE_INVALID_ARG, "%s: kind %d", what, kind);
+  }
 }
 
 extern "C" rmoe_status rmoe_synth_bytes(void* dst, size_t n, uint64_t key, int32_t mode, int32_t lo,

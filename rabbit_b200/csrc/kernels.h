@@ -156,6 +156,19 @@ cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w
 cudaError_t launch_topk_softmax(const float* logits, const float* bias, int T, int E, int k,
                                 int32_t* ids, float* w, cudaStream_t st);
 // GLM noaux_tc: sigmoid, +bias for selection, group top-2 sums, grouped top-k, normalize.
+// matmul_qt's per-row quantized kinds (qt.cu): the integer-dot path (int8 or int4 weights, int8
+// activations quantized per row into `workspace` of matmul_idot_workspace_bytes) and the
+// float-weight int4 / int2 paths.
+size_t matmul_idot_workspace_bytes(int s, int i);
+cudaError_t launch_matmul_idot(float* y, const void* x, int x_dtype, const void* w, bool w4, const float* scale, int s,
+                               int i, int o, void* workspace, cudaStream_t st);
+cudaError_t launch_matmul_qt_float(float* y, const void* x, int x_dtype, const uint8_t* w, int bits, const float* scale,
+                                   int s, int i, int o, cudaStream_t st);
+// CACHE_ROUTE selection for the sigmoid router (glm52::moe::route_cache_aware); resident: [E]
+// bytes (nonzero = resident) or NULL (every expert resident).
+cudaError_t launch_topk_cache_route(const float* logits, const float* bias, int T, int E, int k, int route_j,
+                                    int route_m, const uint8_t* resident, int norm_topk, float routed_scale,
+                                    int32_t* ids, float* w, cudaStream_t st);
 cudaError_t launch_topk_grouped(const float* logits, const float* bias, int T, int E, int k,
                                 int n_group, int topk_group, int norm_topk, float routed_scale,
                                 int32_t* ids, float* w, cudaStream_t st);

@@ -534,4 +534,145 @@ cudaError_t launch_topk_grouped(const float* logits, const float* bias, int T, i
   return cudaGetLastError();
 }
 
+// CACHE_ROUTE (glm52::moe::route_cache_aware + cache_route_select, src/glm52/moe.rs:272-323):
+// rank the top m = max(route_m, k) experts by choice = sigmoid(logit) + bias (rank_top,
+// :148-166: strict '>' from -1e30, ties to the lower id), keep the top j = min(route_j, k)
+// always, fill the remaining slots with the resident experts among ranked[j..] in rank order,
+// then with the rest of ranked[j..] in rank order; weights are the plain sigmoids, normalized
+// and scaled (normalize_and_scale, :231-241). Like the reference it ranks over every expert (no
+// grouping). One warp per token; resident: [E] bytes, nonzero = resident (NULL = all).
+template <int PL>
+__global__ void topk_cache_route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
+                                        int k, int route_j, int route_m, const uint8_t* __restrict__ resident,
+                                        int norm_topk, float routed_scale, int32_t* __restrict__ ids,
+                                        float* __restrict__ wout) {
+  const int warps = blockDim.x / 32;
+  const int t = blockIdx.x * warps + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  float sg[PL], ch[PL];
+  const float* row = logits + static_cast<size_t>(t) * E;
+#pragma unroll
+  for (int q = 0; q < PL; q++) {
+    const int e = q * 32 + lane;
+    float sv = 0.0f, c = -INFINITY;
+    if (e < E) {
+      sv = sigmoid_ref(row[e]);
+      c = __fadd_rn(sv, bias ? bias[e] : 0.0f);
+    }
+    sg[q] = sv;
+    ch[q] = c;
+  }
+  const int m = min(max(route_m, k), E);
+  // ranked[r] (r < m) held by lane r: id, sigmoid, resident flag
+  int r_id = -1;
+  float r_w = 0.0f;
+  unsigned taken = 0;
+  for (int r = 0; r < m; r++) {
+    float bv = -1e30f;
+    int bid = 0x7fffffff;
+#pragma unroll
+    for (int q = 0; q < PL; q++) {
+      const int e = q * 32 + lane;
+      if (e >= E || ((taken >> q) & 1)) continue;
+      if (ch[q] > bv) {
+        bv = ch[q];
+        bid = e;
+      }
+    }
+    warp_argmax(bv, bid);
+    float wv = 0.0f;
+    if ((bid & 31) == lane) {
+      taken |= 1u << (bid >> 5);
+#pragma unroll
+      for (int q = 0; q < PL; q++)
+        if (q == (bid >> 5)) wv = sg[q];
+    }
+    wv = __shfl_sync(kFull, wv, bid & 31);
+    if (lane == r) {
+      r_id = bid;
+      r_w = wv;
+    }
+  }
+  const int j = min(min(route_j, k), m);
+  const bool res = lane < m && (!resident || resident[r_id] != 0);
+  // pass 1: ranked[0..j) always, then resident ranked[j..) in order, up to k slots
+  const unsigned res_mask = __ballot_sync(kFull, lane >= j && res);
+  const unsigned jmask = j >= 32 ? kFull : ((1u << j) - 1u);
+  unsigned pick = jmask;
+  int need = k - j;
+  unsigned rm = res_mask;
+  while (need > 0 && rm) {
+    const int b = __ffs(rm) - 1;
+    pick |= 1u << b;
+    rm &= rm - 1;
+    need--;
+  }
+  // pass 2: the rest of ranked[j..) in order
+  const unsigned mmask = m >= 32 ? kFull : ((1u << m) - 1u);
+  unsigned rest = mmask & ~pick;
+  while (need > 0 && rest) {
+    const int b = __ffs(rest) - 1;
+    pick |= 1u << b;
+    rest &= rest - 1;
+    need--;
+  }
+  // slot order: ranked[0..j), then pass-1 picks in rank order, then pass-2 picks in rank order
+  const unsigned p1 = pick & res_mask & ~jmask, p2 = pick & ~res_mask & ~jmask;
+  int slot = -1;
+  if ((pick >> lane) & 1u) {
+    const unsigned below = (1u << lane) - 1u;
+    if (lane < j) slot = lane;
+    else if ((p1 >> lane) & 1u) slot = j + __popc(p1 & below);
+    else slot = j + __popc(p1) + __popc(p2 & below);
+  }
+  const int kk = __popc(pick);
+  // gather per slot: lane s takes the entry whose slot is s
+  float w = 0.0f;
+  int id = -1;
+  for (int src = 0; src < 32; src++) {
+    const int sl = __shfl_sync(kFull, slot, src);
+    const int sid = __shfl_sync(kFull, r_id, src);
+    const float sw = __shfl_sync(kFull, r_w, src);
+    if (sl == lane) {
+      id = sid;
+      w = sw;
+    }
+  }
+  if (norm_topk) {
+    float sum = -0.0f;
+    for (int q = 0; q < kk; q++) sum = __fadd_rn(sum, __shfl_sync(kFull, w, q));
+    sum = __fadd_rn(sum, 1e-20f);
+    w = __fdiv_rn(w, sum);
+  }
+  w = __fmul_rn(w, routed_scale);
+  if (lane < k) {
+    ids[static_cast<size_t>(t) * k + lane] = lane < kk ? id : -1;
+    wout[static_cast<size_t>(t) * k + lane] = lane < kk ? w : 0.0f;
+  }
+}
+
+template <int PL>
+static void launch_cache_route_pl(const float* logits, const float* bias, int T, int E, int k, int route_j,
+                                  int route_m, const uint8_t* resident, int norm_topk, float routed_scale,
+                                  int32_t* ids, float* w, cudaStream_t st) {
+  const int warps = 8;
+  topk_cache_route_kernel<PL><<<(T + warps - 1) / warps, warps * 32, 0, st>>>(
+      logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w);
+}
+
+cudaError_t launch_topk_cache_route(const float* logits, const float* bias, int T, int E, int k, int route_j,
+                                    int route_m, const uint8_t* resident, int norm_topk, float routed_scale,
+                                    int32_t* ids, float* w, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (E > kMaxE || k > 32 || k < 1 || route_m > 32 || route_j < 0) return cudaErrorInvalidValue;
+  if (E <= 32) launch_cache_route_pl<1>(logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 64) launch_cache_route_pl<2>(logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 128) launch_cache_route_pl<4>(logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 256) launch_cache_route_pl<8>(logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w, st);
+  else if (E <= 512) launch_cache_route_pl<16>(logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w, st);
+  else launch_cache_route_pl<32>(logits, bias, T, E, k, route_j, route_m, resident, norm_topk, routed_scale, ids, w, st);
+  return cudaGetLastError();
+}
+
 }  // namespace rmoe

@@ -153,6 +153,12 @@ class MoeLayer:
         """Limit of the kernels' waits on other CTAs in nanoseconds (0: the default 2 s)."""
         check(self.lib.rmoe_layer_set_wait_limit(self.handle, int(ns)))
 
+    def set_route_config(self, cache_route: bool, route_j: int = 2, route_m: int = 12, resident=None):
+        """CACHE_ROUTE (glm52::moe::RouteConfig; sigmoid routers only). resident: [E] bool/uint8
+        array of resident experts, None = all."""
+        r = None if resident is None else np.ascontiguousarray(resident, np.uint8)
+        check(self.lib.rmoe_set_route_config(self.handle, int(cache_route), route_j, route_m, _ptr(r)))
+
     def set_profiling(self, on: bool = True):
         check(self.lib.rmoe_layer_set_profiling(self.handle, int(on)))
 
@@ -351,6 +357,15 @@ def matmul(y, x, w, s, i, o, stream=None):
     _require_cuda(y, x, w)
     check(_lib.load().rmoe_matmul_f32(_ptr(y), _ptr(x), _dtype_code(x), _ptr(w), _dtype_code(w),
                                       s, i, o, _stream(stream)))
+    return y
+
+
+def matmul_qt(y, x, kind: str, data, scale, s, i, o, group_size=32, stream=None):
+    """kernels::matmul_qt (src/kernels.rs:1104-1132) for a weight of QT kind `kind`
+    ("f32", "i8", "i4", "i2", "i4_grouped", "mxfp4")."""
+    _require_cuda(y, x, data)
+    check(_lib.load().rmoe_matmul_qt(_ptr(y), _ptr(x), _dtype_code(x), _lib.QT_KINDS[kind], _ptr(data), _ptr(scale),
+                                     group_size, s, i, o, _stream(stream)))
     return y
 
 

@@ -315,3 +315,121 @@ def test_moe_output_matches_independent_full_expert_sum():  # glm52/moe.rs:1037-
     assert sorted(ids[0].tolist()) == [0, 1, 2]
     assert np.max(np.abs(out - want)) < 1e-4
     assert rel_l2(out, want) < 1e-5
+
+
+# ---- CACHE_ROUTE (glm52::moe::cache_route_select), the reference's known answers
+def test_cache_route_keeps_true_top_j_on_a_cold_cache():  # glm52/moe.rs:719-728
+    choice = [0.0, 1.0, 2.0, 3.0, 4.0]
+    picked = orc.cache_route_select(choice, choice, 3, 2, 5, resident=np.zeros(5, bool))
+    assert [e for e, _ in picked] == [4, 3, 2]
+
+
+def test_cache_route_prefers_resident_experts():  # glm52/moe.rs:731-753
+    choice = [0.0, 1.0, 2.0, 3.0, 4.0]
+    res = np.zeros(5, bool)
+    res[[0, 1]] = True
+    picked = orc.cache_route_select(choice, choice, 3, 1, 5, resident=res)
+    assert [e for e, _ in picked] == [4, 1, 0]
+    assert all(w == choice[e] for e, w in picked)  # a substitute keeps its own plain sigmoid
+
+
+def test_cache_route_fills_resident_slots_then_falls_back():  # glm52/moe.rs:756-777
+    choice = [0.0, 1.0, 2.0, 3.0, 4.0]
+    res = np.zeros(5, bool)
+    res[0] = True
+    picked = orc.cache_route_select(choice, choice, 3, 1, 5, resident=res)
+    assert [e for e, _ in picked] == [4, 0, 3]
+
+
+def test_cache_route_all_resident_equals_plain_route():  # glm52/moe.rs:701-716, 780-830
+    """With every expert resident (or none: the cold cache), CACHE_ROUTE selects exactly the
+    ungrouped plain top-k, ids and weights bit for bit."""
+    import dataclasses
+
+    from rabbit_b200 import synth
+
+    cfg = dataclasses.replace(synth.CONFIGS["c0_tiny"], router="sigmoid_grouped", topk=4)
+    x, r, b = synth.activations(cfg), synth.router_weights(cfg), synth.correction_bias(cfg)
+    i0, w0 = orc.glm_route(x, r, b, 4, 256, 16, 4, 1, 1, True, 2.5)
+    for res in (None, np.ones(16, bool), np.zeros(16, bool)):
+        i1, w1 = orc.glm_route_cache(x, r, b, 4, 256, 16, 4, 2, 12, res, True, 2.5)
+        assert np.array_equal(i0, i1) and np.array_equal(w0, w1)
+
+
+# ---- matmul_qt's other QT kinds (kernels.rs tests), replayed on the restatement
+def _pack_nibbles(vals):
+    b = np.zeros((len(vals) + 1) // 2, np.uint8)
+    for idx, v in enumerate(vals):
+        b[idx // 2] |= np.uint8((v + 8) << (4 * (idx % 2)))
+    return b
+
+
+def test_matmul_i4_matches_manual_nibble_unpack():  # kernels.rs:1352-1370
+    vals = [3, -7, 0, 5, -2]
+    y = orc.matmul_qt(np.ones(5, np.float32), "i4", _pack_nibbles(vals), np.array([2.0], np.float32), 1, 5, 1)
+    assert y[0, 0] == sum(vals) * 2.0
+
+
+def test_matmul_i2_matches_manual_unpack():  # kernels.rs:1373-1386
+    vals = [-2, 1, 0, -1, 1]
+    b = np.zeros(2, np.uint8)
+    for idx, v in enumerate(vals):
+        b[idx // 4] |= np.uint8((v + 2) << ((idx % 4) * 2))
+    y = orc.matmul_qt(np.ones(5, np.float32), "i2", b, np.array([3.0], np.float32), 1, 5, 1)
+    assert y[0, 0] == sum(vals) * 3.0
+
+
+def test_dot_i8i8_and_i4i8_match_naive_sums():  # kernels.rs:1599-1621
+    w = np.array([(i % 7) - 3 for i in range(40)], np.int8)
+    x = np.array([(i % 5) - 2 for i in range(40)], np.int8)
+    assert orc.dot_i8i8(w, x) == int(np.dot(w.astype(np.int32), x.astype(np.int32)))
+    vals = [(i % 16) - 8 for i in range(41)]
+    x4 = np.array([(i % 5) - 2 for i in range(41)], np.int8)
+    assert orc.dot_i4i8(_pack_nibbles(vals), x4, 41) == int(np.dot(np.array(vals), x4.astype(np.int32)))
+
+
+def test_qrow_i8_round_trips_close_to_original():  # kernels.rs:1624-1632
+    x = random_vec(64, 5)
+    q, s = orc.qrow_i8(x)
+    assert np.all(np.abs(q.astype(np.float32) * s - x) < 0.02)
+
+
+def test_matmul_qt_i8_idot_is_close_to_the_float_path():  # kernels.rs:1652-1673 (and :1334-1349)
+    rows, cols, s = 4, 16, 2
+    w = random_vec(rows * cols, 21).reshape(rows, cols)
+    amax = np.abs(w).max(axis=1)
+    scale = np.maximum(amax / np.float32(127), np.float32(1e-12)).astype(np.float32)
+    q = np.clip(np.rint(w / scale[:, None]), -127, 127).astype(np.int8)
+    x = random_vec(s * cols, 22).reshape(s, cols)
+    direct = (x @ (q.astype(np.float32) * scale[:, None]).T).astype(np.float32)
+    y = orc.matmul_qt(x, "i8", q, scale, s, cols, rows)
+    assert np.max(np.abs(direct - y)) < 0.05
+    # integer-valued weights with scale 1 and x = 1: the IDOT path is exact (amax 127 -> scale 1)
+    qi = np.array([[10, -20, 30, 127]], np.int8)
+    y1 = orc.matmul_qt(np.ones(4, np.float32), "i8", qi, np.array([1.0], np.float32), 1, 4, 1)
+    assert y1[0, 0] == 147.0
+
+
+def test_matmul_qt_i4_gates_idot_by_seq_len():  # kernels.rs:1676-1700
+    rows, cols = 3, 10
+    rng = np.random.default_rng(31)
+    q4 = rng.integers(0, 256, rows * 5, dtype=np.uint8)
+    sc = (rng.random(rows) * 0.1).astype(np.float32)
+    x1 = random_vec(cols, 32)
+    y1 = orc.matmul_qt(x1, "i4", q4, sc, 1, cols, rows)  # s = 1: the float path
+    want = np.zeros(rows, np.float32)
+    for o in range(rows):
+        a = np.float32(0)
+        for k in range(0, cols, 2):
+            b = q4[o * 5 + k // 2]
+            a = np.float32(a + np.float32(np.float32(x1[k] * np.float32(int(b & 15) - 8))
+                                          + np.float32(x1[k + 1] * np.float32(int(b >> 4) - 8))))
+        want[o] = np.float32(a * sc[o])
+    assert np.array_equal(y1[0], want)
+    x2 = random_vec(2 * cols, 33).reshape(2, cols)  # s = 2: the integer-dot path
+    y2 = orc.matmul_qt(x2, "i4", q4, sc, 2, cols, rows)
+    for si in range(2):
+        xq, sx = orc.qrow_i8(x2[si])
+        for o in range(rows):
+            d = orc.dot_i4i8(q4[o * 5:(o + 1) * 5], xq, cols)
+            assert y2[si, o] == np.float32(np.float32(np.float32(d) * sc[o]) * sx)
