@@ -199,6 +199,14 @@ struct rmoe_layer {
   bool tc_trace_print = true;              // RMOE_TC_TRACE=2: record only (summary on get_stats)
   bool use_fused = true;                   // one token: the fused gate/up + down kernel (RMOE_DISABLE_FUSED=1: two kernels)
   unsigned long long spin_ns = kDefaultSpinNs;  // limit of the kernels' waits on other CTAs
+  // grouped-int4 layers on the tensor cores (i4_tc.cu), for batches of more than kI4MinTokens
+  bool use_i4tc = false;
+  uint8_t* i4_tiles = nullptr;   // tile-major copy of every slot's weights
+  size_t i4_stride = 0, i4_off_down = 0;
+  __half* i4_xh = nullptr;       // [P_max + 32][hidden] f16 activations per position
+  __half* i4_hh = nullptr;       // [P_max + 32][inter] f16 h per position
+  void* i4_map_x = nullptr;      // tensor maps of the two (host copies, 64-byte aligned)
+  void* i4_map_h = nullptr;
   unsigned err_seen = 0;                   // device error flags already reported (and cleared)
   // CACHE_ROUTE (sigmoid routers): keep the top route_j, prefer resident experts among the next
   // ranked up to route_m (src/glm52/moe.rs:99-127)
@@ -220,6 +228,8 @@ struct rmoe_layer {
     if (cap) cudaStreamDestroy(cap);
     if (diag_buf) cudaFreeHost(diag_buf);
     free(tc_plan);
+    free(i4_map_x);
+    free(i4_map_h);
   }
 };
 
@@ -567,6 +577,29 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
       return cleanup(fail(RMOE_CUDA_ERROR, "rmoe_layer_create: tensor map encoding failed"));
   }
   {
+    const char* no4 = getenv("RMOE_DISABLE_I4TC");
+    L->use_i4tc = f.fmt == kInt4g && !(no4 && no4[0] == '1') &&
+                  i4_tc_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is), f.group_size) &&
+                  (!L->has_shared || shared_in_table) && T > kI4MinTokens;
+  }
+  if (L->use_i4tc) {
+    L->i4_off_down = align_up(i4_tc_region_bytes(static_cast<int>(H), static_cast<int>(I), 0), 4096);
+    L->i4_stride = align_up(L->i4_off_down + i4_tc_region_bytes(static_cast<int>(H), static_cast<int>(I), 1), 4096);
+    ALLOC(L->i4_tiles, L->i4_stride * table_slots);
+    const size_t prow = static_cast<size_t>(L->P_max) + 32;
+    ALLOC(L->i4_xh, prow * H);
+    ALLOC(L->i4_hh, prow * I);
+    const size_t mb = (i4_act_map_bytes() + 63) / 64 * 64;
+    L->i4_map_x = aligned_alloc(64, mb);
+    L->i4_map_h = aligned_alloc(64, mb);
+    if (!L->i4_map_x || !L->i4_map_h) return cleanup(fail(RMOE_OUT_OF_MEMORY, "rmoe_layer_create: host allocation"));
+    if (cudaMemset(L->i4_xh, 0, prow * H * 2) != cudaSuccess || cudaMemset(L->i4_hh, 0, prow * I * 2) != cudaSuccess)
+      return cleanup(fail(RMOE_CUDA_ERROR, "rmoe_layer_create: cudaMemset"));
+    if (!i4_make_act_map(L->i4_map_x, L->i4_xh, static_cast<int>(H), static_cast<int>(prow)) ||
+        !i4_make_act_map(L->i4_map_h, L->i4_hh, static_cast<int>(I), static_cast<int>(prow)))
+      return cleanup(fail(RMOE_CUDA_ERROR, "rmoe_layer_create: tensor map encoding failed"));
+  }
+  {
     uint8_t* xd = nullptr;
     ALLOC(xd, static_cast<size_t>(T) * H * 4);
     L->x_dev = xd;
@@ -880,6 +913,21 @@ static rmoe_status put_tiled(rmoe_layer* L, const char* what, const void* gate, 
   return RMOE_OK;
 }
 
+// Grouped-int4 layers on the tensor cores: the slot's matrices (already uploaded in the
+// reference layout at gate/up/down) retiled into the slot's tile-major copy.
+static rmoe_status put_i4_tiles(rmoe_layer* L, const char* what, const uint8_t* gate, const uint8_t* up,
+                                const uint8_t* down, const void* gsc, const void* usc, const void* dsc, int slot) {
+  if (!L->use_i4tc) return RMOE_OK;
+  const int H = L->desc.hidden, I = L->desc.moe_inter, gs = L->fmt.group_size;
+  const int bf = L->fmt.scale_dtype == kBF16 ? 1 : 0;
+  uint8_t* dst = L->i4_tiles + L->i4_stride * slot;
+  cudaError_t e = launch_i4_relayout(0, gate, up, gsc, usc, bf, H, I, gs, dst, 0);
+  if (e == cudaSuccess) e = launch_i4_relayout(1, down, nullptr, dsc, nullptr, bf, H, I, gs, dst + L->i4_off_down, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return RMOE_OK;
+}
+
 static rmoe_status local_slot(const rmoe_layer* L, int32_t eid, const char* what, int* slot) {
   if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
   if (eid < 0 || eid >= L->desc.n_experts)
@@ -918,6 +966,9 @@ extern "C" rmoe_status rmoe_upload_expert(rmoe_layer* L, int32_t eid, const void
     return s;
   if ((s = put_matrix(L, "rmoe_upload_expert down", H, I, down, down_bytes, down_scale,
                       down_scale_bytes, b + L->tab.off_down, b + L->tab.off_ds)) != RMOE_OK)
+    return s;
+  if ((s = put_i4_tiles(L, "rmoe_upload_expert (int4 tiles)", b, b + L->tab.off_up, b + L->tab.off_down,
+                        b + L->tab.off_gs, b + L->tab.off_us, b + L->tab.off_ds, slot)) != RMOE_OK)
     return s;
   L->uploaded[slot] = 1;
   return RMOE_OK;
@@ -973,6 +1024,9 @@ extern "C" rmoe_status rmoe_upload_shared(rmoe_layer* L, const void* gate, size_
     return s;
   if ((s = put_matrix(L, "rmoe_upload_shared down", H, Is, down, down_bytes, down_scale, down_scale_bytes,
                       const_cast<uint8_t*>(p.down), (uint8_t*)p.down_scale)) != RMOE_OK)
+    return s;
+  if ((s = put_i4_tiles(L, "rmoe_upload_shared (int4 tiles)", p.gate, p.up, p.down, p.gate_scale, p.up_scale,
+                        p.down_scale, L->n_loc)) != RMOE_OK)
     return s;
   if (shared_gate && L->desc.shared_gated)
     RMOE_CUDA(cudaMemcpy(L->shared_gate_vec, shared_gate, H * 4, cudaMemcpyDefault), "rmoe_upload_shared gate vector");
@@ -1122,6 +1176,9 @@ static rmoe_status print_tc_trace(rmoe_layer* L, cudaStream_t st, const char* wh
 // gate/up, down and the combine into `out`. hs: the shared expert takes part (its positions are
 // in the dispatch); terms_done: the front end already wrote the token's activation terms;
 // fused_ok: the small-batch front end ran (one-token / fused down+combine paths allowed).
+// Batches of more than kI4MinTokens tokens of a grouped-int4 layer run on the tensor cores.
+static bool i4_path(const rmoe_layer* L, int T) { return L->use_i4tc && T > kI4MinTokens; }
+
 static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T, int mt, bool hs, bool terms_done,
                                    bool fused_ok, float* out, cudaStream_t st, StageMarks& marks, int* launches_io) {
   const rmoe_layer_desc& D = L->desc;
@@ -1131,6 +1188,27 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
   int& launches = *launches_io;
   const int P = T * k + (hs ? T : 0);
   const int n_slots = L->n_loc + (hs ? 1 : 0);
+  if (i4_path(L, T)) {
+    // grouped int4 on the tensor cores: x gathered per position (f16), gate/up (-> h per position,
+    // routing weight folded in), down (-> y per position), deterministic combine
+    e = launch_i4_gather_x(x, xdt, H, L->d.perm_tok, L->d.offsets + n_slots, L->P_max, L->i4_xh, st);
+    if (e != cudaSuccess) return cuda_fail(e, "int4 activations");
+    marks.mark();
+    e = launch_i4_moe(0, L->i4_map_x, L->d, L->d.offsets, H, D.moe_inter, L->i4_tiles, L->i4_stride, L->i4_hh,
+                      nullptr, L->fmt.act, L->dev_err, L->spin_ns, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gate/up (int4 tensor cores)");
+    marks.mark();
+    marks.mark();  // (h is formed in the gate/up epilogue)
+    e = launch_i4_moe(1, L->i4_map_h, L->d, L->d.offsets, H, D.moe_inter, L->i4_tiles + L->i4_off_down, L->i4_stride,
+                      nullptr, L->y, L->fmt.act, L->dev_err, L->spin_ns, st);
+    if (e != cudaSuccess) return cuda_fail(e, "down (int4 tensor cores)");
+    marks.mark();
+    e = launch_combine(L->y, L->d, nullptr, T, k, H, L->n_loc, hs ? 1 : 0, out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "combine");
+    marks.mark();
+    launches = 8;  // logits, top-k, prep, dispatch, gather, gate/up, down, combine
+    return RMOE_OK;
+  }
   if (L->use_tc) {
     // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
     // weight folded in), down: one token = combined row directly, else y per position + sum
@@ -1249,7 +1327,7 @@ static rmoe_status enqueue_forward(rmoe_layer* L, const void* x, int x_dtype, in
   const int H = D.hidden, k = D.topk;
   const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
   const bool gated = L->has_shared && D.shared_gated;
-  const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
+  const int mt = L->use_tc ? std::min(T, 32) : (i4_path(L, T) ? kI4Chunk : chunk_tokens(T));
   rmoe_status s = RMOE_OK;
   cudaError_t e = cudaSuccess;
   int launches = 10;
@@ -1617,7 +1695,7 @@ static rmoe_status experts_for_routing(rmoe_layer* L, const void* x, int xdt, in
                                        cudaStream_t st) {
   const rmoe_layer_desc& D = L->desc;
   const bool gated = hs && D.shared_gated;
-  const int mt = L->use_tc ? std::min(T, 32) : chunk_tokens(T);
+  const int mt = L->use_tc ? std::min(T, 32) : (i4_path(L, T) ? kI4Chunk : chunk_tokens(T));
   if (!L->use_tc || gated) {  // (the tensor-core path forms its own activation terms)
     cudaError_t e = launch_prep_tokens(x, xdt, T, D.hidden, L->fmt.fmt, gated ? L->shared_gate_vec : nullptr, L->xq,
                                        L->xexp, L->gate, st);

@@ -1,6 +1,7 @@
 // kernels.h -- host-side launchers of the routed-MoE kernels (internal to librmoe.so).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -156,6 +157,21 @@ cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w
 cudaError_t launch_topk_softmax(const float* logits, const float* bias, int T, int E, int k,
                                 int32_t* ids, float* w, cudaStream_t st);
 // GLM noaux_tc: sigmoid, +bias for selection, group top-2 sums, grouped top-k, normalize.
+// ---- grouped-int4 experts on the tensor cores (i4_tc.cu) ----
+constexpr int kI4MinTokens = 8;   // batches above this take the tensor-core path
+constexpr int kI4Chunk = 32;      // positions per chunk (the MMA's N)
+bool i4_tc_supported(int H, int I, int Is, int gs);
+size_t i4_tc_region_bytes(int H, int I, int down);
+cudaError_t launch_i4_relayout(int down, const uint8_t* m0, const uint8_t* m1, const void* s0, const void* s1,
+                               int scale_bf16, int H, int I, int gs, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_i4_gather_x(const void* x, int x_dtype, int H, const int32_t* perm_tok, const int32_t* total,
+                               int P_max, __half* xh, cudaStream_t st);
+bool i4_make_act_map(void* map, const void* base, int K, int rows);
+size_t i4_act_map_bytes();
+cudaError_t launch_i4_moe(int mode, const void* act_map, const DispatchBuffers& d, const int32_t* slot_offsets,
+                          int H, int I, const uint8_t* tiles, size_t stride, __half* h, float* y, ActParams act,
+                          unsigned* err, unsigned long long spin_ns, cudaStream_t st);
+
 // matmul_qt's per-row quantized kinds (qt.cu): the integer-dot path (int8 or int4 weights, int8
 // activations quantized per row into `workspace` of matmul_idot_workspace_bytes) and the
 // float-weight int4 / int2 paths.

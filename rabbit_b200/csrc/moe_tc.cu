@@ -112,14 +112,6 @@ constexpr int kRecRing = 4;
 constexpr int kBOff = (kTileBlock + 1023) & ~1023;
 
 // Shared-memory carve-up (offsets from the 1024-aligned base).
-// Completion of every tcgen05 operation this thread issued (MMAs, scale-factor copies) before
-// the CTA frees its TMEM: on a run that stopped early (a bounded wait ran out) no consumer waited
-// for the last ones. `bar` is a one-use mbarrier (count 1); the wait is bounded too.
-__device__ __forceinline__ void tc_drain(uint64_t* bar, unsigned* err) {
-  tc_commit(bar);
-  mbar_wait_bounded(bar, 0, err, 0x400000u);
-}
-
 struct MtLayout {
   int stage_pitch, off_bar, off_meta, off_rec, off_misc, off_ubuf, total;
 };

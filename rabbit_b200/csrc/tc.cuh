@@ -46,6 +46,14 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                : "memory");
 }
 
+// Completion of every tcgen05 operation this thread issued (MMAs, scale-factor copies) before
+// the CTA frees its TMEM: on a run that stopped early (a bounded wait ran out) no consumer waited
+// for the last ones. `bar` is a one-use mbarrier (count 1); the wait is bounded too.
+__device__ __forceinline__ void tc_drain(uint64_t* bar, unsigned* err) {
+  tc_commit(bar);
+  mbar_wait_bounded(bar, 0, err, 0x400000u);
+}
+
 // ---- shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart ----
 __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
   const uint64_t addr = smem_u32(tile);
