@@ -598,6 +598,10 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     if (!i4_make_act_map(L->i4_map_x, L->i4_xh, static_cast<int>(H), static_cast<int>(prow)) ||
         !i4_make_act_map(L->i4_map_h, L->i4_hh, static_cast<int>(I), static_cast<int>(prow)))
       return cleanup(fail(RMOE_CUDA_ERROR, "rmoe_layer_create: tensor map encoding failed"));
+    if (const char* tr = getenv("RMOE_TC_TRACE"); tr && tr[0] == '2' && !L->tc_trace) {
+      ALLOC(L->tc_trace, 8192);  // the int4 gate/up kernel's stage timeline (printed by get_stats)
+      if (cudaMemset(L->tc_trace, 0, 8192 * 8) != cudaSuccess) return cleanup(fail(RMOE_CUDA_ERROR, "trace"));
+    }
   }
   {
     uint8_t* xd = nullptr;
@@ -665,6 +669,20 @@ extern "C" rmoe_status rmoe_layer_get_stats(const rmoe_layer* L, rmoe_layer_stat
   unsigned op = 0;
   RMOE_CUDA(cudaMemcpy(&op, L->order_pending, 4, cudaMemcpyDeviceToHost), "read order counter");
   out->router_order_resolved = op;
+  if (L->tc_trace && L->use_i4tc) {
+    // diagnostics: the int4 gate/up kernel's first stages on CTA 0 (µs from the first copy)
+    static unsigned long long tr[4096];
+    RMOE_CUDA(cudaDeviceSynchronize(), "trace sync");
+    RMOE_CUDA(cudaMemcpy(tr, L->tc_trace, sizeof(tr), cudaMemcpyDeviceToHost), "trace read");
+    const unsigned long long t0 = tr[0];
+    auto rel = [&](unsigned long long t) { return t ? (double)(long long)(t - t0) * 1e-3 : -1.0; };
+    fprintf(stderr, "int4 gate/up stages (copies issued, weights landed, dequant start, dequant done, A ready at MMA, "
+                    "activations landed at MMA):\n");
+    for (int i = 0; i < 512; i += (i < 24 ? 1 : 32))
+      fprintf(stderr, "  %3d: %.2f %.2f %.2f %.2f %.2f %.2f\n", i, rel(tr[8 * i]), rel(tr[8 * i + 1]), rel(tr[8 * i + 2]),
+              rel(tr[8 * i + 3]), rel(tr[8 * i + 5]), rel(tr[8 * i + 4]));
+    return RMOE_OK;
+  }
   if (L->tc_trace && !L->tc_trace_print) {
     // diagnostics: the last one-token forward's kernel timeline (global timer, µs from the
     // front end's start)
@@ -1195,7 +1213,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
     if (e != cudaSuccess) return cuda_fail(e, "int4 activations");
     marks.mark();
     e = launch_i4_moe(0, L->i4_map_x, L->d, L->d.offsets, H, D.moe_inter, L->i4_tiles, L->i4_stride, L->i4_hh,
-                      nullptr, L->fmt.act, L->dev_err, L->spin_ns, st);
+                      nullptr, L->fmt.act, L->dev_err, L->spin_ns, st, L->tc_trace);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (int4 tensor cores)");
     marks.mark();
     marks.mark();  // (h is formed in the gate/up epilogue)

@@ -170,7 +170,8 @@ bool i4_make_act_map(void* map, const void* base, int K, int rows);
 size_t i4_act_map_bytes();
 cudaError_t launch_i4_moe(int mode, const void* act_map, const DispatchBuffers& d, const int32_t* slot_offsets,
                           int H, int I, const uint8_t* tiles, size_t stride, __half* h, float* y, ActParams act,
-                          unsigned* err, unsigned long long spin_ns, cudaStream_t st);
+                          unsigned* err, unsigned long long spin_ns, cudaStream_t st,
+                          unsigned long long* trace = nullptr);
 
 // matmul_qt's per-row quantized kinds (qt.cu): the integer-dot path (int8 or int4 weights, int8
 // activations quantized per row into `workspace` of matmul_idot_workspace_bytes) and the

@@ -52,7 +52,24 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
                                                   unsigned code, uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  for (unsigned n = 1;; n++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    // (the clock is read every 16th poll: many warps polling the global timer at once take issue
+    // slots from the warps doing the work)
+    if ((n & 15) == 0 && global_ns() - t0 > limit_ns) {
+      atomicOr(flag, code);
+      return false;
+    }
+  }
+}
+
+// The same for a wait expected to be long (a whole work unit): polls with a short sleep between.
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity, unsigned* flag,
+                                                        unsigned code, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
+    __nanosleep(200);
     if (global_ns() - t0 > limit_ns) {
       atomicOr(flag, code);
       return false;
