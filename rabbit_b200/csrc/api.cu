@@ -214,6 +214,7 @@ struct rmoe_layer {
   int route_j = 2, route_m = 12;
   uint8_t* resident = nullptr;   // [E] residency mask (device)
   bool resident_all = true;      // no mask given: every expert resident
+  bool use_cert_sigmoid = true;  // RMOE_DISABLE_CERT_SIGMOID=1: exact chains for every expert
   bool diag_host = false;                  // RMOE_DIAG_HOST=1: kernel trace in mapped host memory
   void* diag_buf = nullptr;
   ~rmoe_layer() {
@@ -502,6 +503,8 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     const char* off = getenv("RMOE_DISABLE_PIPE");
     L->use_pipe = pipe_supported(f, static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is)) &&
                   !(off && off[0] == '1');
+    const char* ncs = getenv("RMOE_DISABLE_CERT_SIGMOID");
+    L->use_cert_sigmoid = !(ncs && ncs[0] == '1');
     const char* nog = getenv("RMOE_DISABLE_GRAPH");
     L->use_graphs = !(nog && nog[0] == '1');
     L->rpt_gu = L->use_pipe ? 1 : 2;
@@ -1067,6 +1070,20 @@ static rmoe_status check_ready(const rmoe_layer* L, const char* what, int T, int
 static rmoe_status route_into(rmoe_layer* L, const void* x, int x_dtype, int T, cudaStream_t st,
                               StageMarks* marks = nullptr) {
   const rmoe_layer_desc& D = L->desc;
+  if (D.router_kind == RMOE_ROUTER_SIGMOID_GROUPED && D.n_group <= 1 && !L->cache_route && L->use_cert_sigmoid &&
+      L->hr % 256 == 0 && topk_sigmoid_certified_supported(T, L->hr, D.n_experts, D.topk)) {
+    // few tokens, ungrouped sigmoid router: certified fast logits, exact chains for contenders only
+    const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
+    cudaError_t e = launch_router_certified(x, xdt, L->router, L->router_dtype, L->logits, L->logit_err, T, L->hr,
+                                            D.n_experts, st);
+    if (e != cudaSuccess) return cuda_fail(e, "certified router");
+    if (marks) marks->mark();
+    e = launch_topk_sigmoid_certified(L->logits, L->logit_err, x, xdt, L->router, L->router_dtype, L->router_bias, T,
+                                      L->hr, D.n_experts, D.topk, D.norm_topk, D.routed_scale, L->ids, L->rw, nullptr,
+                                      st);
+    if (e != cudaSuccess) return cuda_fail(e, "certified sigmoid top-k");
+    return RMOE_OK;
+  }
   cudaError_t e = launch_router_logits_exact(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, L->router,
                                              L->router_dtype, L->logits, T, L->hr, D.n_experts, st);
   if (e != cudaSuccess) return cuda_fail(e, "router logits");
@@ -1812,11 +1829,16 @@ extern "C" rmoe_status rmoe_latent_moe(rmoe_layer* L, const void* x, int32_t x_d
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int H = L->desc.hidden, Hr = L->hr, k = L->desc.topk;
   const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
+  // x_latent = x . down^T (:91-92) on the side stream, beside the routing: the projection streams
+  // its weights from HBM while the router's exact chains are latency-bound
+  RMOE_CUDA(cudaEventRecord(L->ev_fork, st), "fork");
+  RMOE_CUDA(cudaStreamWaitEvent(L->side, L->ev_fork, 0), "fork wait");
+  cudaError_t e = launch_latent_proj(L->lat_down, L->lat_dtype, x, xdt, T, Hr, H, L->lat_x, L->side);
+  if (e != cudaSuccess) return cuda_fail(e, "latent down projection");
+  RMOE_CUDA(cudaEventRecord(L->ev_join, L->side), "join");
   // routing at the full width, on x itself (src/kimi_k3/moe.rs:84-86)
   if ((s = route_into(L, x, x_dtype, T, st)) != RMOE_OK) return s;
-  // x_latent = x . down^T (:91-92)
-  cudaError_t e = launch_latent_proj(L->lat_down, L->lat_dtype, x, xdt, T, Hr, H, L->lat_x, st);
-  if (e != cudaSuccess) return cuda_fail(e, "latent down projection");
+  RMOE_CUDA(cudaStreamWaitEvent(st, L->ev_join, 0), "join wait");
   // the routed experts at the latent width (:94-104); no shared expert here (the caller's)
   if ((s = experts_for_routing(L, L->lat_x, kF32, T, false, L->lat_y, st)) != RMOE_OK) return s;
   // RMSNorm of each token's summed routed row (:106-110), then out = y . up^T (:112)

@@ -354,3 +354,35 @@ def test_matmul_qt_every_kind(cuda_ctx, kind, s, i, o):
         assert rel_l2(got, want) < 2e-5
     else:  # (f16 activations on the GEMV path, as the dedicated tests)
         assert rel_l2(got, want) < 2e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("E,k,H", [(896, 16, 7168), (256, 8, 2048), (64, 6, 1024)])
+def test_certified_sigmoid_router_matches_reference(cuda_ctx, E, k, H):
+    """Few-token ungrouped sigmoid routing from certified logits (exact chains for the contenders
+    only) against the restated glm52::moe::route on 96 tokens routed 1, 3 and 8 at a time: ids
+    bit-exact, weights within 1e-6."""
+    import dataclasses
+
+    import torch
+
+    import rabbit_b200 as rb
+
+    cfg = dataclasses.replace(synth.CONFIGS["c0_tiny"], name="cert", router="sigmoid_grouped", n_experts=E, topk=k,
+                              tokens=96, hidden=H, bf16_inputs=True)
+    L = rb.MoeLayer(cuda_ctx, H, 128, E, k, router="sigmoid_grouped", routed_scale=2.5, max_tokens=8)
+    router, bias = synth.router_weights(cfg), synth.correction_bias(cfg)
+    L.upload_router(synth.f32_to_bf16_bits(router))
+    L.upload_router_bias(bias)
+    x = synth.activations(cfg)
+    xd = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    want_ids, want_w = orc.glm_route(x, router, bias, cfg.tokens, H, E, k, 1, 1, True, 2.5)
+    t0 = 0
+    for n in [1, 3, 8] * 8 + [1] * 24:
+        if t0 + n > cfg.tokens:
+            break
+        ids, w = L.route(xd[t0:t0 + n])
+        assert np.array_equal(ids.cpu().numpy(), want_ids[t0:t0 + n]), t0
+        assert np.max(np.abs(w.cpu().numpy() - want_w[t0:t0 + n])) < 1e-6
+        t0 += n
+    L.close()
