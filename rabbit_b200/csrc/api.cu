@@ -214,7 +214,6 @@ struct rmoe_layer {
   int route_j = 2, route_m = 12;
   uint8_t* resident = nullptr;   // [E] residency mask (device)
   bool resident_all = true;      // no mask given: every expert resident
-  bool use_cert_sigmoid = true;  // RMOE_DISABLE_CERT_SIGMOID=1: exact chains for every expert
   bool diag_host = false;                  // RMOE_DIAG_HOST=1: kernel trace in mapped host memory
   void* diag_buf = nullptr;
   ~rmoe_layer() {
@@ -503,8 +502,6 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     const char* off = getenv("RMOE_DISABLE_PIPE");
     L->use_pipe = pipe_supported(f, static_cast<int>(H), static_cast<int>(I), static_cast<int>(Is)) &&
                   !(off && off[0] == '1');
-    const char* ncs = getenv("RMOE_DISABLE_CERT_SIGMOID");
-    L->use_cert_sigmoid = !(ncs && ncs[0] == '1');
     const char* nog = getenv("RMOE_DISABLE_GRAPH");
     L->use_graphs = !(nog && nog[0] == '1');
     L->rpt_gu = L->use_pipe ? 1 : 2;
@@ -1070,20 +1067,6 @@ static rmoe_status check_ready(const rmoe_layer* L, const char* what, int T, int
 static rmoe_status route_into(rmoe_layer* L, const void* x, int x_dtype, int T, cudaStream_t st,
                               StageMarks* marks = nullptr) {
   const rmoe_layer_desc& D = L->desc;
-  if (D.router_kind == RMOE_ROUTER_SIGMOID_GROUPED && D.n_group <= 1 && !L->cache_route && L->use_cert_sigmoid &&
-      L->hr % 256 == 0 && topk_sigmoid_certified_supported(T, L->hr, D.n_experts, D.topk)) {
-    // few tokens, ungrouped sigmoid router: certified fast logits, exact chains for contenders only
-    const int xdt = x_dtype == RMOE_BF16 ? kBF16 : kF32;
-    cudaError_t e = launch_router_certified(x, xdt, L->router, L->router_dtype, L->logits, L->logit_err, T, L->hr,
-                                            D.n_experts, st);
-    if (e != cudaSuccess) return cuda_fail(e, "certified router");
-    if (marks) marks->mark();
-    e = launch_topk_sigmoid_certified(L->logits, L->logit_err, x, xdt, L->router, L->router_dtype, L->router_bias, T,
-                                      L->hr, D.n_experts, D.topk, D.norm_topk, D.routed_scale, L->ids, L->rw, nullptr,
-                                      st);
-    if (e != cudaSuccess) return cuda_fail(e, "certified sigmoid top-k");
-    return RMOE_OK;
-  }
   cudaError_t e = launch_router_logits_exact(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, L->router,
                                              L->router_dtype, L->logits, T, L->hr, D.n_experts, st);
   if (e != cudaSuccess) return cuda_fail(e, "router logits");

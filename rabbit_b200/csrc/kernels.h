@@ -181,13 +181,6 @@ cudaError_t launch_matmul_idot(float* y, const void* x, int x_dtype, const void*
                                int i, int o, void* workspace, cudaStream_t st);
 cudaError_t launch_matmul_qt_float(float* y, const void* x, int x_dtype, const uint8_t* w, int bits, const float* scale,
                                    int s, int i, int o, cudaStream_t st);
-// Ungrouped sigmoid router for T <= 8 from certified logits (launch_router_certified): exact
-// chains only for the contenders of the top k; n_contenders (may be null) counts them.
-bool topk_sigmoid_certified_supported(int T, int H, int E, int k);
-cudaError_t launch_topk_sigmoid_certified(const float* mid, const float* err, const void* x, int x_dtype,
-                                          const void* w, int w_dtype, const float* bias, int T, int H, int E, int k,
-                                          int norm_topk, float routed_scale, int32_t* ids, float* wout,
-                                          unsigned* n_contenders, cudaStream_t st);
 // CACHE_ROUTE selection for the sigmoid router (glm52::moe::route_cache_aware); resident: [E]
 // bytes (nonzero = resident) or NULL (every expert resident).
 cudaError_t launch_topk_cache_route(const float* logits, const float* bias, int T, int E, int k, int route_j,

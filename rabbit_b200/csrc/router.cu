@@ -505,152 +505,6 @@ __global__ void __launch_bounds__(1024) topk_sigmoid_block_kernel(const float* _
   }
 }
 
-// The reference's exact logit chain of expert e (x[k] * w[e][k] added from -0.0 in k order) by
-// one warp: per 1024-element chunk the lanes form the products into `buf` and lane 0 adds them
-// in order (as router_exact_warp_kernel). xs: the token's row in shared memory. Lane 0 returns it.
-template <int WD>
-__device__ float exact_chain_warp(const float* xs, const void* w, int e, int H, float* buf, int lane) {
-  const size_t wrow = static_cast<size_t>(e) * H;
-  float acc = -0.0f;
-  for (int c0 = 0; c0 < H; c0 += kRwChunk) {
-    float wv[4][8];
-#pragma unroll
-    for (int u = 0; u < 4; u++) load8_t<WD>(w, wrow + c0 + u * 256 + lane * 8, wv[u]);
-#pragma unroll
-    for (int u = 0; u < 4; u++)
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const int kk = u * 256 + lane * 8 + j;
-        buf[kk] = __fmul_rn(xs[c0 + kk], wv[u][j]);
-      }
-    __syncwarp();
-    if (lane == 0) {
-      float4 q[4], nq[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++) q[u] = *reinterpret_cast<const float4*>(buf + 4 * u);
-      for (int i = 0; i < kRwChunk; i += 16) {
-        if (i + 16 < kRwChunk) {
-#pragma unroll
-          for (int u = 0; u < 4; u++) nq[u] = *reinterpret_cast<const float4*>(buf + i + 16 + 4 * u);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          acc = __fadd_rn(acc, q[u].x);
-          acc = __fadd_rn(acc, q[u].y);
-          acc = __fadd_rn(acc, q[u].z);
-          acc = __fadd_rn(acc, q[u].w);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) q[u] = nq[u];
-      }
-    }
-    __syncwarp();
-  }
-  return acc;
-}
-
-// Ungrouped sigmoid router for a few tokens from certified logits (launch_router_certified: a
-// fast value and a rigorous bound on the distance of the reference's chain from it), one
-// 1024-thread block per token. Each expert's choice sigmoid(logit) + bias is bounded from the
-// logit interval (sigmoid is monotone; the single-precision evaluation is widened by 2^-20
-// relative as in topk_sigmoid_block_kernel); the experts whose upper bound reaches the k-th
-// largest lower bound are the only ones that can be among the reference's top k. Only those
-// contenders get the exact logit chain (one warp each, all in parallel), the reference's
-// sigmoid and the exact ranking by (choice desc, id asc); weights and scaling as
-// glm52::moe::route (src/glm52/moe.rs:131-260). Same ids and weights as the exact path.
-template <int XD, int WD>
-__global__ void __launch_bounds__(1024) topk_sigmoid_certified_kernel(
-    const float* __restrict__ mid, const float* __restrict__ err, const void* __restrict__ x,
-    const void* __restrict__ w, const float* __restrict__ bias, int T, int H, int E, int k, int norm_topk,
-    float routed_scale, int32_t* __restrict__ ids, float* __restrict__ wout, unsigned* __restrict__ n_contenders) {
-  extern __shared__ __align__(16) float tc_smem[];
-  float* xs = tc_smem;              // [H]
-  float* bufs = tc_smem + H;        // [32][kRwChunk]
-  __shared__ float c1[32 * 32], c2[32 * 32];
-  __shared__ int c1i[32 * 32], c2i[32 * 32];
-  __shared__ int sel_id[32], lo_id[32];
-  __shared__ float sel_v[32], lo_v[32];
-  __shared__ int cont[1024];
-  __shared__ int n_cont;
-  __shared__ float ex_logit[1024];
-  const int t = blockIdx.x, e = threadIdx.x, wi = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const bool valid = e < E;
-  const int id = valid ? e : 0x40000000 + e;
-  const int kk = min(k, E);
-  if (threadIdx.x == 0) n_cont = 0;
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-    float v[8];
-    load8_t<XD>(x, static_cast<size_t>(t) * H + i, v);
-#pragma unroll
-    for (int j = 0; j < 8; j++) xs[i + j] = v[j];
-  }
-  float b = 0.0f, lo = -INFINITY, hi = -INFINITY;
-  if (valid) {
-    const float l = mid[static_cast<size_t>(t) * E + e], r = err[static_cast<size_t>(t) * E + e];
-    b = bias ? bias[e] : 0.0f;
-    const float xl = __fsub_rd(l, r), xh = __fadd_ru(l, r);
-    const float sl = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-xl)));
-    const float sh = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-xh)));
-    lo = __fadd_rd(__fsub_rd(sl, fmaf(sl, 9.54e-7f, 1e-37f)), b);
-    hi = __fadd_ru(__fadd_ru(sh, fmaf(sh, 9.54e-7f, 1e-37f)), b);
-  }
-  block_select2(lo, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
-  const float Lk = sel_v[kk - 1];
-  if (valid && hi >= Lk) cont[atomicAdd(&n_cont, 1)] = e;
-  ex_logit[threadIdx.x] = 0.0f;
-  __syncthreads();
-  const int nc = n_cont;
-  for (int c = wi; c < nc; c += 32) {
-    const float v = exact_chain_warp<WD>(xs, w, cont[c], H, bufs + wi * kRwChunk, lane);
-    if (lane == 0) ex_logit[cont[c]] = v;
-  }
-  __syncthreads();
-  float sx = 0.0f, cx = -INFINITY;
-  if (valid && hi >= Lk) {
-    sx = sigmoid_ref(ex_logit[e]);
-    cx = __fadd_rn(sx, b);
-  }
-  ex_logit[threadIdx.x] = sx;  // (the exact sigmoid, read back as the weight)
-  __syncthreads();
-  block_select2(cx, cx, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
-  if (threadIdx.x < 32) {
-    float wv = lane < kk ? ex_logit[sel_id[lane]] : 0.0f;
-    if (norm_topk) {
-      float sum = -0.0f;
-      for (int j = 0; j < kk; j++) sum = __fadd_rn(sum, __shfl_sync(kFull, wv, j));
-      sum = __fadd_rn(sum, 1e-20f);
-      wv = __fdiv_rn(wv, sum);
-    }
-    wv = __fmul_rn(wv, routed_scale);
-    if (lane < k) {
-      ids[static_cast<size_t>(t) * k + lane] = lane < kk ? sel_id[lane] : -1;
-      wout[static_cast<size_t>(t) * k + lane] = lane < kk ? wv : 0.0f;
-    }
-    if (lane == 0 && n_contenders) atomicAdd(n_contenders, static_cast<unsigned>(nc));
-  }
-}
-
-bool topk_sigmoid_certified_supported(int T, int H, int E, int k) {
-  return T >= 1 && T <= 8 && H % kRwChunk == 0 && E <= 1024 && k <= 32 &&
-         (static_cast<size_t>(H) + 32 * kRwChunk) * 4 <= 200 * 1024;
-}
-
-cudaError_t launch_topk_sigmoid_certified(const float* mid, const float* err, const void* x, int x_dtype,
-                                          const void* w, int w_dtype, const float* bias, int T, int H, int E, int k,
-                                          int norm_topk, float routed_scale, int32_t* ids, float* wout,
-                                          unsigned* n_contenders, cudaStream_t st) {
-  if (!topk_sigmoid_certified_supported(T, H, E, k)) return cudaErrorInvalidValue;
-  const size_t smem = (static_cast<size_t>(H) + 32 * kRwChunk) * 4;
-  void (*kern)(const float*, const float*, const void*, const void*, const float*, int, int, int, int, int, float,
-               int32_t*, float*, unsigned*) =
-      x_dtype == kBF16 ? (w_dtype == kBF16 ? topk_sigmoid_certified_kernel<kBF16, kBF16> : topk_sigmoid_certified_kernel<kBF16, kF32>)
-                       : (w_dtype == kBF16 ? topk_sigmoid_certified_kernel<kF32, kBF16> : topk_sigmoid_certified_kernel<kF32, kF32>);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  kern<<<T, 1024, smem, st>>>(mid, err, x, w, bias, T, H, E, k, norm_topk, routed_scale, ids, wout, n_contenders);
-  return cudaGetLastError();
-}
-
 template <int PL>
 static void launch_grouped_pl(const float* logits, const float* bias, int T, int E, int k,
                               int n_group, int topk_group, int norm_topk, float routed_scale,

@@ -358,10 +358,10 @@ def test_matmul_qt_every_kind(cuda_ctx, kind, s, i, o):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("E,k,H", [(896, 16, 7168), (256, 8, 2048), (64, 6, 1024)])
-def test_certified_sigmoid_router_matches_reference(cuda_ctx, E, k, H):
-    """Few-token ungrouped sigmoid routing from certified logits (exact chains for the contenders
-    only) against the restated glm52::moe::route on 96 tokens routed 1, 3 and 8 at a time: ids
-    bit-exact, weights within 1e-6."""
+def test_few_token_sigmoid_router_matches_reference(cuda_ctx, E, k, H):
+    """Few-token ungrouped sigmoid routing (the latent layers' decode case) against the restated
+    glm52::moe::route on 96 tokens routed 1, 3 and 8 at a time: ids bit-exact, weights within
+    1e-6."""
     import dataclasses
 
     import torch
