@@ -215,6 +215,7 @@ struct rmoe_layer {
   uint8_t* resident = nullptr;   // [E] residency mask (device)
   bool resident_all = true;      // no mask given: every expert resident
   bool diag_host = false;                  // RMOE_DIAG_HOST=1: kernel trace in mapped host memory
+  unsigned* err_host = nullptr;            // pinned: the error flags, copied behind a host forward's outputs
   void* diag_buf = nullptr;
   ~rmoe_layer() {
     for (cudaEvent_t e : ev_free) cudaEventDestroy(e);
@@ -227,6 +228,7 @@ struct rmoe_layer {
     }
     if (cap) cudaStreamDestroy(cap);
     if (diag_buf) cudaFreeHost(diag_buf);
+    if (err_host) cudaFreeHost(err_host);
     free(tc_plan);
     free(i4_map_x);
     free(i4_map_h);
@@ -485,6 +487,12 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     L->tc_trace_print = false;
   }
   ALLOC(L->dev_err, 1);
+  {
+    void* hp = nullptr;
+    if (cudaHostAlloc(&hp, 64, cudaHostAllocDefault) != cudaSuccess) return cleanup(fail(RMOE_CUDA_ERROR, "error flag host copy"));
+    L->err_host = static_cast<unsigned*>(hp);
+    *L->err_host = 0;
+  }
   ALLOC(L->order_pending, 1);
   ALLOC(L->pending, std::min(T, 32));
   ALLOC(L->ids_final, static_cast<size_t>(T) * k);
@@ -768,9 +776,13 @@ static rmoe_status drop_graphs(rmoe_layer* L) {
   return RMOE_OK;
 }
 
-static rmoe_status take_device_errors(rmoe_layer* L, const char* what) {
+// ef_read: the flags already copied to the host behind the call's work (else read them here).
+static rmoe_status take_device_errors(rmoe_layer* L, const char* what, const unsigned* ef_read = nullptr) {
   unsigned ef = 0;
-  RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
+  if (ef_read)
+    ef = *ef_read;
+  else
+    RMOE_CUDA(cudaMemcpy(&ef, L->dev_err, 4, cudaMemcpyDeviceToHost), "read device error flags");
   if (!ef) return RMOE_OK;
   RMOE_CUDA(cudaDeviceSynchronize(), "timeout recovery: synchronize");
   const int T = L->max_tokens;
@@ -1877,6 +1889,8 @@ extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, 
             "out to host");
   if (ids_host) RMOE_CUDA(cudaMemcpyAsync(ids_host, L->ids_host_stage, n * 4, cudaMemcpyDeviceToHost, L->stream), "ids to host");
   if (w_host) RMOE_CUDA(cudaMemcpyAsync(w_host, L->w_host_stage, n * 4, cudaMemcpyDeviceToHost, L->stream), "weights to host");
+  // the error flags ride behind the outputs (no second round trip after the synchronize)
+  if (L->err_host) RMOE_CUDA(cudaMemcpyAsync(L->err_host, L->dev_err, 4, cudaMemcpyDeviceToHost, L->stream), "error flags to host");
   {
     cudaError_t e = cudaStreamSynchronize(L->stream);
     if (e != cudaSuccess) {
@@ -1884,7 +1898,7 @@ extern "C" rmoe_status rmoe_moe_forward_host(rmoe_layer* L, const void* x_host, 
       return cuda_fail(e, "rmoe_moe_forward_host synchronize");
     }
   }
-  return take_device_errors(L, "rmoe_moe_forward_host");
+  return take_device_errors(L, "rmoe_moe_forward_host", L->err_host);
 }
 
 // ------------------------------------------------------------------------------ matmuls

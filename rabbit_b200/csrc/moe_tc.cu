@@ -1284,49 +1284,77 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
 }
 
 // ---------------------------------------------------------------------- activation terms per position
-// xt rows 4p..4p+3 = terms of the token of position p. One warp per (token, 32-block): the terms
-// are computed once and stored at each of the token's routed positions (inv) and its shared one.
+// xt rows 4p..4p+3 = terms of the token of position p, stored at each of the token's routed
+// positions (inv) and its shared one. Activation terms of every (token, position) pair: one block per (token, 256 columns), one warp
+// per 32-column k-block computing its four E2M1 terms (amax by a warp reduction, each term
+// rounding what the previous ones left), staged in shared memory; then the block writes each of
+// the token's positions' term rows as whole 128-byte spans (8 k-blocks x 16 bytes) and 8-byte
+// scale runs, so every store fills its sectors.
 __global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __restrict__ x, int x_dtype, int H, int T,
                                                                 int k, const int32_t* __restrict__ inv,
                                                                 const int32_t* __restrict__ shared_pos0,
                                                                 uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
+  __shared__ uint4 sterm[4][8];       // [term][k-block of the span]
+  __shared__ uint8_t ssf[4][8];
+  __shared__ int spos[32];
   const int nb = H / 32;
-  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  if (wid >= T * nb) return;
-  const int t = wid / nb, b = wid % nb;
-  float r = load_elem(x, x_dtype, static_cast<size_t>(t) * H + b * 32 + lane);
-  // the token's positions: k routed slots (-1 when not local) and the shared one
-  int pos = -1;
-  if (lane < k) pos = __ldg(inv + t * k + lane);
-  else if (lane == k && shared_pos0) pos = __ldg(shared_pos0) + t;
-  uint32_t packed_w[4][4];
-  uint8_t sfb[4];
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(r))));
-    int e = 0;
-    uint32_t nib = 0;
-    if (amax > 0.0f) {
-      e = e2m1_block_exponent(amax);
-      const bool neg = r < 0.0f;
-      const int c = e2m1_nearest(fminf(fabsf(r) * exp2i(-e), 6.0f));
-      const float q = e2m1_magnitude(c) * exp2i(e);
-      r = neg ? r + q : r - q;
-      nib = static_cast<uint32_t>(c) | (neg && c ? 8u : 0u);
-    }
-    const uint32_t sh = nib << (4 * (lane & 7));
-#pragma unroll
-    for (int g = 0; g < 4; g++) packed_w[j][g] = __reduce_or_sync(kFull, (lane >> 3) == g ? sh : 0u);
-    sfb[j] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+  const int spans = (nb + 7) / 8;
+  const int t = blockIdx.x / spans, b0 = (blockIdx.x % spans) * 8;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nvb = min(8, nb - b0);  // k-blocks in this span
+  if (threadIdx.x < 32) {
+    int pos = -1;
+    if (lane < k) pos = __ldg(inv + t * k + lane);
+    else if (lane == k && shared_pos0) pos = __ldg(shared_pos0) + t;
+    spos[lane] = pos;
   }
-  // lanes holding a position each store the 4 term rows' 16 bytes + scale bytes there
-  if (pos >= 0) {
+  if (warp < nvb) {
+    const int b = b0 + warp;
+    float r = load_elem(x, x_dtype, static_cast<size_t>(t) * H + b * 32 + lane);
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const size_t row = static_cast<size_t>(4 * pos + j);
-      *reinterpret_cast<uint4*>(xt + row * (H / 2) + b * 16) =
-          make_uint4(packed_w[j][0], packed_w[j][1], packed_w[j][2], packed_w[j][3]);
-      xsf[row * nb + b] = sfb[j];
+      const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(r))));
+      int e = 0;
+      uint32_t nib = 0;
+      if (amax > 0.0f) {
+        e = e2m1_block_exponent(amax);
+        const bool neg = r < 0.0f;
+        const int c = e2m1_nearest(fminf(fabsf(r) * exp2i(-e), 6.0f));
+        const float q = e2m1_magnitude(c) * exp2i(e);
+        r = neg ? r + q : r - q;
+        nib = static_cast<uint32_t>(c) | (neg && c ? 8u : 0u);
+      }
+      const uint32_t sh = nib << (4 * (lane & 7));
+      uint32_t w[4];
+#pragma unroll
+      for (int g = 0; g < 4; g++) w[g] = __reduce_or_sync(kFull, (lane >> 3) == g ? sh : 0u);
+      if (lane == 0) {
+        sterm[j][warp] = make_uint4(w[0], w[1], w[2], w[3]);
+        ssf[j][warp] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+      }
+    }
+  }
+  __syncthreads();
+  // (position slot s, term j, k-block c): 8 lanes per term row, 4 rows per position
+  const int np = k + 1;
+  for (int i = threadIdx.x; i < np * 32; i += blockDim.x) {
+    const int s = i / 32, j = (i / 8) % 4, c = i % 8;
+    const int pos = spos[s];
+    if (pos < 0 || c >= nvb) continue;
+    const size_t row = static_cast<size_t>(4 * pos + j);
+    *reinterpret_cast<uint4*>(xt + row * (H / 2) + (b0 + c) * 16) = sterm[j][c];
+  }
+  for (int i = threadIdx.x; i < np * 4; i += blockDim.x) {
+    const int s = i / 4, j = i % 4;
+    const int pos = spos[s];
+    if (pos < 0) continue;
+    uint8_t* d = xsf + static_cast<size_t>(4 * pos + j) * nb + b0;
+    if (nvb == 8 && (reinterpret_cast<uintptr_t>(d) & 7) == 0) {
+      uint2 v;
+      memcpy(&v, ssf[j], 8);
+      *reinterpret_cast<uint2*>(d) = v;
+    } else {
+      for (int c = 0; c < nvb; c++) d[c] = ssf[j][c];
     }
   }
 }
@@ -1439,8 +1467,8 @@ cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, int T, i
                                      const int32_t* shared_pos0, uint8_t* xt, uint8_t* xsf, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   if (k > 31) return cudaErrorInvalidValue;
-  const long long n = static_cast<long long>(T) * (H / 32) * 32;
-  terms_by_position_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(x, x_dtype, H, T, k, inv, shared_pos0,
+  const long long n = static_cast<long long>(T) * ((H / 32 + 7) / 8);
+  terms_by_position_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(x, x_dtype, H, T, k, inv, shared_pos0,
                                                                                   xt, xsf);
   return cudaGetLastError();
 }

@@ -127,7 +127,8 @@ def test_matmul_i4_grouped_matches_oracle(cuda_ctx, s, i, o, gs, scale_dtype):
 
 
 @pytest.mark.parametrize("s,i,o,dt", [(1, 8192, 512, "bf16"), (4, 256, 16, "f32"),
-                                      (70, 512, 96, "bf16"), (130, 1000, 33, "f32")])
+                                      (70, 512, 96, "bf16"), (130, 1000, 33, "f32"),
+                                      (200, 2048, 130, "f32"), (96, 1024, 200, "mixed")])
 def test_router_matmul_is_bit_exact(cuda_ctx, s, i, o, dt):
     """kernels::matmul: every element must equal the reference's sequential f32 chain."""
     import torch
@@ -139,11 +140,15 @@ def test_router_matmul_is_bit_exact(cuda_ctx, s, i, o, dt):
     w = (rng.standard_normal((o, i)) * 0.02).astype(np.float32)
     if dt == "bf16":
         x, w = synth.round_bf16(x), synth.round_bf16(w)
+    if dt == "mixed":  # f32 activations, bf16 router rows (the C1/C2 layers' router)
+        w = synth.round_bf16(w)
     want = orc.matmul(x, w, s, i, o)
     y = torch.zeros((s, o), dtype=torch.float32, device="cuda")
     xt, wt = _t(x), _t(w)
     if dt == "bf16":
         xt, wt = xt.to(torch.bfloat16), wt.to(torch.bfloat16)
+    if dt == "mixed":
+        wt = wt.to(torch.bfloat16)
     rb.matmul(y, xt, wt, s, i, o)
     got = y.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
