@@ -115,6 +115,7 @@ struct rmoe_layer {
   // weights
   void* router = nullptr;
   int router_dtype = kF32;
+  uint8_t* router_slabs = nullptr;  // the router in the one-token exact kernel's slab layout
   int hr = 0;  // router width = width of the caller's x (the latent layers' full hidden size)
   // latent wrapper (router_hidden != hidden): projections, norm, activations between them
   void* lat_down = nullptr;   // [hidden][hr]
@@ -449,6 +450,8 @@ extern "C" rmoe_status rmoe_layer_create(rmoe_ctx* ctx, const rmoe_layer_desc* d
     uint8_t* r = nullptr;
     ALLOC(r, E * L->hr * 4);
     L->router = r;
+    const size_t sb = router_slab_bytes(static_cast<int>(E), L->hr, kF32);  // (f32 size: either dtype fits)
+    if (sb) ALLOC(L->router_slabs, sb);
   }
   if (L->hr != static_cast<int>(H)) {
     uint8_t* dp = nullptr;
@@ -885,6 +888,11 @@ extern "C" rmoe_status rmoe_upload_router(rmoe_layer* L, const void* w, int32_t 
   RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
   RMOE_CUDA(cudaMemcpy(L->router, w, bytes, cudaMemcpyDefault), "rmoe_upload_router copy");
   L->router_dtype = dtype == RMOE_BF16 ? kBF16 : kF32;
+  if (L->router_slabs) {
+    RMOE_CUDA(launch_router_slabs(L->router, L->router_dtype, L->desc.n_experts, L->hr, L->router_slabs, nullptr),
+              "router slab layout");
+    RMOE_CUDA(cudaDeviceSynchronize(), "router slab layout");
+  }
   L->has_router = true;
   return RMOE_OK;
 }
@@ -1080,7 +1088,8 @@ static rmoe_status route_into(rmoe_layer* L, const void* x, int x_dtype, int T, 
                               StageMarks* marks = nullptr) {
   const rmoe_layer_desc& D = L->desc;
   cudaError_t e = launch_router_logits_exact(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, L->router,
-                                             L->router_dtype, L->logits, T, L->hr, D.n_experts, st);
+                                             L->router_dtype, L->logits, T, L->hr, D.n_experts, st, L->dev_err,
+                                             L->router_slabs);
   if (e != cudaSuccess) return cuda_fail(e, "router logits");
   if (marks) marks->mark();
   if (D.router_kind == RMOE_ROUTER_SOFTMAX_TOPK)

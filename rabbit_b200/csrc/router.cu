@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "pipe.cuh"
 #include "select.cuh"
 
 namespace rmoe {
@@ -207,9 +208,247 @@ __global__ void __launch_bounds__(256) router_exact_warp_kernel(const void* __re
   if (lane == 0) logits[static_cast<size_t>(t) * E + e] = acc;
 }
 
+// One token: a block owns 32 experts. Three producer warps stream the 32 router rows through a ring
+// of slabs (one bulk copy per slab: the rows' 256-element pieces stored contiguously, rows 16
+// bytes apart beyond their length so 16-byte reads by the 32 lanes hit distinct banks -- the
+// slab layout written once at router upload) and form the products x[k] * w[e][k] of each slab
+// into a double-buffered [32][256] product tile; the chain warp's lane e then adds its expert's
+// products in k order. The chain is the reference's (fmul then fadd per element, from -0.0) and
+// its serial add latency -- H dependent adds, ~4.5 cycles each when fed from shared memory -- is
+// the kernel's bound: the chain lanes do nothing else and the 32 chains of a block advance
+// together. (Per-row 512-byte copies, 32 per slab, measured 3.5x slower: the copy engine's
+// per-request cost, not bandwidth, paced them.) Needs T == 1 and H % 256 == 0.
+constexpr int kRcSlabEl = 256;           // elements per slab
+constexpr int kRcProd = 3;               // producer warps (8-element pieces of every row slab, round robin)
+constexpr int kRcThreads = 32 * (kRcProd + 1);  // warps 0-2 producers, warp 3 the chains (its own scheduler)
+__device__ unsigned g_router_err;        // wait-timeout flags of calls without a layer
+#ifdef RMOE_RC_TRACE
+__device__ unsigned long long g_rc_trace[4 * 64];  // block 0: per slab producer / chain done
+#define RC_TRACE(i, v) \
+  if (blockIdx.x == 0 && (i) < 4 * 64) g_rc_trace[i] = (v)
+#else
+#define RC_TRACE(i, v)
+#endif
+
+// (d0, d1) = (a0 * b0, a1 * b1) on f32 bit patterns, each rounded to nearest even
+__device__ __forceinline__ void mul2_rn(uint32_t& d0, uint32_t& d1, uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
+  uint64_t d;
+  const uint64_t a = static_cast<uint64_t>(a0) | (static_cast<uint64_t>(a1) << 32);
+  const uint64_t b = static_cast<uint64_t>(b0) | (static_cast<uint64_t>(b1) << 32);
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  d0 = static_cast<uint32_t>(d);
+  d1 = static_cast<uint32_t>(d >> 32);
+}
+
+template <int WD>
+struct RcLayout {
+  static constexpr int esz = WD == kBF16 ? 2 : 4;
+  static constexpr int nring = WD == kBF16 ? 6 : 3;              // router-row slabs in flight
+  static constexpr int row_bytes = kRcSlabEl * esz;
+  static constexpr int pitch = row_bytes + 16;
+  static constexpr int ring = 0;                                  // [nring][32][pitch]
+  static constexpr int prod = ring + nring * 32 * pitch;        // [2][32][kRcSlabEl + 4] f32
+  static constexpr int prod_pitch = kRcSlabEl + 4;
+  static constexpr int xs = prod + 2 * 32 * prod_pitch * 4;       // [H] f32, then [H] bf16 staging
+  __host__ __device__ static size_t bars(int H) { return xs + static_cast<size_t>(H) * 6; }
+  static size_t bytes(int H) { return bars(H) + (nring + 5) * 8; }
+};
+
+// The slab layout: block b, slab j = rows 32 b .. 32 b + 31, elements 256 j .. 256 j + 255, row r at
+// byte r * pitch of the slab's 32 * pitch bytes (rows past E zero).
+__global__ void router_slab_relayout_kernel(const uint8_t* __restrict__ w, int esz, int E, int H,
+                                            uint8_t* __restrict__ dst) {
+  const int row_bytes = kRcSlabEl * esz, pitch = row_bytes + 16, nslab = H / kRcSlabEl;
+  const int chunks = row_bytes / 16;
+  const long long n = static_cast<long long>((E + 31) / 32) * nslab * 32 * chunks;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % chunks);
+    const long long rr = i / chunks;
+    const int r = static_cast<int>(rr % 32);
+    const long long bj = rr / 32;
+    const int j = static_cast<int>(bj % nslab), b = static_cast<int>(bj / nslab);
+    const int e = b * 32 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (e < E) v = *reinterpret_cast<const uint4*>(w + (static_cast<size_t>(e) * H + static_cast<size_t>(j) * kRcSlabEl) * esz + c * 16);
+    *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(bj) * 32 + r) * pitch + c * 16) = v;
+  }
+}
+
+size_t router_slab_bytes(int E, int H, int w_dtype) {
+  if (H % kRcSlabEl) return 0;
+  const int esz = w_dtype == kBF16 ? 2 : 4;
+  return static_cast<size_t>((E + 31) / 32) * (H / kRcSlabEl) * 32 * (kRcSlabEl * esz + 16);
+}
+
+cudaError_t launch_router_slabs(const void* w, int w_dtype, int E, int H, uint8_t* dst, cudaStream_t st) {
+  if (H % kRcSlabEl || reinterpret_cast<uintptr_t>(w) % 16) return cudaErrorInvalidValue;
+  router_slab_relayout_kernel<<<1184, 256, 0, st>>>(static_cast<const uint8_t*>(w), w_dtype == kBF16 ? 2 : 4, E, H, dst);
+  return cudaGetLastError();
+}
+
+template <int XD, int WD>
+__global__ void __launch_bounds__(kRcThreads) router_exact_chain_kernel(const void* __restrict__ x,
+                                                                        const uint8_t* __restrict__ wslab,
+                                                                        float* __restrict__ logits, int H, int E,
+                                                                        unsigned* err) {
+  using Lo = RcLayout<WD>;
+  extern __shared__ __align__(16) uint8_t rc_smem[];
+  uint8_t* ring = rc_smem + Lo::ring;
+  float* prod = reinterpret_cast<float*>(rc_smem + Lo::prod);
+  float* xs = reinterpret_cast<float*>(rc_smem + Lo::xs);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rc_smem + Lo::bars(H));
+  uint64_t* wfull = bars;                        // [Lo::nring] slab landed
+  uint64_t* pfull = bars + Lo::nring;            // [2] products formed (one arrival per producer thread)
+  uint64_t* pempty = bars + Lo::nring + 2;       // [2] products consumed (32 chain arrivals)
+  uint64_t* xbar = bars + Lo::nring + 4;         // the token's row landed
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nslab = H / kRcSlabEl;
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < Lo::nring; q++) mbar_init(&wfull[q], 1);
+    mbar_init(&pfull[0], 32 * kRcProd);
+    mbar_init(&pfull[1], 32 * kRcProd);
+    mbar_init(&pempty[0], 32);
+    mbar_init(&pempty[1], 32);
+    mbar_init(xbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) RC_TRACE(4 * 63 + 3, global_ns());
+  if (warp < kRcProd) {
+    // ---- producers: thread (warp h, lane r) forms row r's products of the slab's 8-element
+    // pieces h, h + kRcProd, ...
+    const int r = lane, h = warp;
+    const uint8_t* wblk = wslab + static_cast<size_t>(blockIdx.x) * nslab * 32 * Lo::pitch;
+    auto issue = [&](int j) {  // (warp 0, lane 0: the whole slab in one copy)
+      const int q = j % Lo::nring;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&wfull[q], 32 * Lo::pitch);
+        bulk_g2s_once(ring + q * 32 * Lo::pitch, wblk + static_cast<size_t>(j) * 32 * Lo::pitch, 32 * Lo::pitch, &wfull[q]);
+      }
+    };
+    // the token's row by one bulk copy (f32 straight into xs; bf16 into the staging area, then
+    // widened), so its latency overlaps the first slabs' instead of a chain of small loads
+    const int xbytes = H * (XD == kBF16 ? 2 : 4);
+    uint8_t* xdst = XD == kBF16 ? reinterpret_cast<uint8_t*>(xs + H) : reinterpret_cast<uint8_t*>(xs);
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(xbar, xbytes);
+      bulk_g2s(xdst, x, xbytes, xbar);
+    }
+    if (warp == 0)
+      for (int j = 0; j < min(Lo::nring, nslab); j++) issue(j);
+    bool ok = __all_sync(kFull, mbar_wait_bounded(xbar, 0, err, 0x1000000u));
+    if (XD == kBF16 && ok) {
+      const uint16_t* xb = reinterpret_cast<const uint16_t*>(xdst);
+      for (int i = threadIdx.x * 8; i < H; i += 32 * kRcProd * 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xb + i);
+        *reinterpret_cast<float4*>(xs + i) = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u),
+                                                         __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xFFFF0000u));
+        *reinterpret_cast<float4*>(xs + i + 4) = make_float4(__uint_as_float(raw.z << 16), __uint_as_float(raw.z & 0xFFFF0000u),
+                                                             __uint_as_float(raw.w << 16), __uint_as_float(raw.w & 0xFFFF0000u));
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kRcProd) : "memory");
+    int issued = min(Lo::nring, nslab);
+    for (int j = 0; j < nslab && ok; j++) {
+      const int q = j % Lo::nring, pb = j & 1;
+      ok = __all_sync(kFull, mbar_wait_bounded(&wfull[q], (j / Lo::nring) & 1, err, 0x1000000u));
+      if (ok && j >= 2) ok = __all_sync(kFull, mbar_wait_bounded(&pempty[pb], ((j - 2) >> 1) & 1, err, 0x2000000u));
+      if (!ok) break;
+      const uint8_t* src = ring + (q * 32 + r) * Lo::pitch;
+      const float* xk = xs + j * kRcSlabEl;
+      float* dst = prod + (pb * 32 + r) * Lo::prod_pitch;
+#pragma unroll
+      for (int c = 8 * h; c < kRcSlabEl; c += 8 * kRcProd) {
+        uint32_t wv[8];  // f32 bit patterns
+        if (WD == kBF16) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(src + c * 2);
+          wv[0] = raw.x << 16; wv[1] = raw.x & 0xFFFF0000u; wv[2] = raw.y << 16; wv[3] = raw.y & 0xFFFF0000u;
+          wv[4] = raw.z << 16; wv[5] = raw.z & 0xFFFF0000u; wv[6] = raw.w << 16; wv[7] = raw.w & 0xFFFF0000u;
+        } else {
+          const uint4 r0 = *reinterpret_cast<const uint4*>(src + c * 4);
+          const uint4 r1 = *reinterpret_cast<const uint4*>(src + c * 4 + 16);
+          wv[0] = r0.x; wv[1] = r0.y; wv[2] = r0.z; wv[3] = r0.w; wv[4] = r1.x; wv[5] = r1.y; wv[6] = r1.z; wv[7] = r1.w;
+        }
+        const uint4 x0 = *reinterpret_cast<const uint4*>(xk + c);
+        const uint4 x1 = *reinterpret_cast<const uint4*>(xk + c + 4);
+        // products two at a time (mul.rn.f32x2: each half rounded like __fmul_rn; stored, never fused)
+        uint4 p0, p1;
+        mul2_rn(p0.x, p0.y, x0.x, x0.y, wv[0], wv[1]);
+        mul2_rn(p0.z, p0.w, x0.z, x0.w, wv[2], wv[3]);
+        mul2_rn(p1.x, p1.y, x1.x, x1.y, wv[4], wv[5]);
+        mul2_rn(p1.z, p1.w, x1.z, x1.w, wv[6], wv[7]);
+        *reinterpret_cast<uint4*>(dst + c) = p0;
+        *reinterpret_cast<uint4*>(dst + c + 4) = p1;
+      }
+      mbar_arrive(&pfull[pb]);
+      if (lane == 0) RC_TRACE(4 * j + warp, global_ns());
+      // every producer warp is done with slot q: warp 0 refills it
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kRcProd) : "memory");
+      if (warp == 0 && j + Lo::nring < nslab) {
+        issue(j + Lo::nring);
+        issued = j + Lo::nring + 1;
+      }
+    }
+    if (!ok) {
+      if (warp == 0)  // copies still in flight land (bounded) before the block leaves
+        for (int j = max(0, issued - Lo::nring); j < issued; j++)
+          mbar_wait_bounded(&wfull[j % Lo::nring], (j / Lo::nring) & 1, err, 0x1000000u, 1000000ull);
+    }
+  } else {
+    // ---- chains: lane e adds its expert's products in k order
+    float acc = -0.0f;
+    bool ok = true;
+    for (int j = 0; j < nslab; j++) {
+      const int pb = j & 1;
+      ok = __all_sync(kFull, mbar_wait_bounded(&pfull[pb], (j >> 1) & 1, err, 0x4000000u));
+      if (!ok) break;
+      const float* pr = prod + (pb * 32 + lane) * Lo::prod_pitch;
+      // 16 products in registers while the next 16 load (the loads' latency stays off the chain)
+      float4 q[4], nq[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) q[u] = *reinterpret_cast<const float4*>(pr + 4 * u);
+#pragma unroll 2
+      for (int c = 0; c < kRcSlabEl; c += 16) {
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          nq[u] = c + 16 < kRcSlabEl ? *reinterpret_cast<const float4*>(pr + c + 16 + 4 * u) : q[u];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          acc = __fadd_rn(acc, q[u].x);
+          acc = __fadd_rn(acc, q[u].y);
+          acc = __fadd_rn(acc, q[u].z);
+          acc = __fadd_rn(acc, q[u].w);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) q[u] = nq[u];
+      }
+      mbar_arrive(&pempty[pb]);
+      if (lane == 0) RC_TRACE(4 * j + 2, global_ns());
+    }
+    const int e = blockIdx.x * 32 + lane;
+    if (ok && e < E) logits[e] = acc;
+  }
+}
+
 cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
-                                       float* logits, int T, int H, int E, cudaStream_t st) {
+                                       float* logits, int T, int H, int E, cudaStream_t st, unsigned* err,
+                                       const void* w_slabs) {
   if (T <= 0) return cudaSuccess;
+  if (T == 1 && w_slabs && H % kRcSlabEl == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && H * 4 < (1 << 20)) {
+    void (*kern)(const void*, const uint8_t*, float*, int, int, unsigned*) =
+        x_dtype == kBF16 ? (w_dtype == kBF16 ? router_exact_chain_kernel<kBF16, kBF16> : router_exact_chain_kernel<kBF16, kF32>)
+                         : (w_dtype == kBF16 ? router_exact_chain_kernel<kF32, kBF16> : router_exact_chain_kernel<kF32, kF32>);
+    const size_t smem = w_dtype == kBF16 ? RcLayout<kBF16>::bytes(H) : RcLayout<kF32>::bytes(H);
+    if (smem > 227 * 1024) goto other;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    unsigned* ef = err;
+    if (!ef && (e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ef), g_router_err)) != cudaSuccess) return e;
+    kern<<<(E + 31) / 32, kRcThreads, smem, st>>>(x, static_cast<const uint8_t*>(w_slabs), logits, H, E, ef);
+    return cudaGetLastError();
+  }
+other:
   const size_t warp_smem = (static_cast<size_t>(H) + 8 * kRwChunk) * 4;
   if (T <= 16 && H % kRwChunk == 0 && warp_smem <= 160 * 1024) {
     void (*kern)(const void*, const void*, float*, int, int, int) =
@@ -478,16 +717,51 @@ __global__ void __launch_bounds__(1024) topk_sigmoid_block_kernel(const float* _
     lo = __fadd_rd(__fsub_rd(sf, d), b);
     hi = __fadd_ru(__fadd_ru(sf, d), b);
   }
-  block_select2(lo, lo, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
-  const float Lk = sel_v[kk - 1];
+  // Lk, the kk-th largest lower bound, by a bitwise search over the order-preserving keys (one
+  // block count per bit); the contenders are the experts whose upper bound reaches it -- every
+  // member of the true top kk is one of them
+  const uint32_t klo = valid ? order_key(lo) : 0u;
+  uint32_t X = 0;
+  for (int bit = 31; bit >= 0; bit--) {
+    const uint32_t cand = X | (1u << bit);
+    if (__syncthreads_count(klo >= cand) >= kk) X = cand;
+  }
+  const bool cont = valid && order_key(hi) >= X;
   float sx = 0.0f, cx = -INFINITY;
-  if (valid && hi >= Lk) {
+  if (cont) {
     sx = sigmoid_ref(x);
     cx = __fadd_rn(sx, b);
   }
   s_sig[e] = sx;
-  __syncthreads();
-  block_select2(cx, cx, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  __shared__ int s_n;
+  if (threadIdx.x == 0) s_n = 0;
+  const int n_cont = __syncthreads_count(cont);
+  if (n_cont <= 32) {
+    // one warp ranks the contenders by (value desc, id asc): each lane counts those ahead of it
+    if (cont) {
+      const int slot = atomicAdd(&s_n, 1);
+      c1[slot] = cx;
+      c1i[slot] = e;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      const bool has = lane < n_cont;
+      const float v = has ? c1[lane] : -INFINITY;
+      const int vid = has ? c1i[lane] : 0x7fffffff;
+      const uint32_t kv = order_key(v);
+      int rank = 0;
+      for (int j = 0; j < n_cont; j++) {
+        const uint32_t kj = __shfl_sync(kFull, kv, j);
+        const int ij = __shfl_sync(kFull, vid, j);
+        rank += (kj > kv || (kj == kv && ij < vid)) ? 1 : 0;
+      }
+      if (has && rank < kk) sel_id[rank] = vid;
+    }
+    __syncthreads();
+  } else {
+    block_select2(cx, cx, id, kk, c1, c1i, c2, c2i, sel_id, sel_v, lo_id, lo_v);
+  }
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float w = lane < kk ? s_sig[sel_id[lane]] : 0.0f;

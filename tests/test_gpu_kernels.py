@@ -128,7 +128,8 @@ def test_matmul_i4_grouped_matches_oracle(cuda_ctx, s, i, o, gs, scale_dtype):
 
 @pytest.mark.parametrize("s,i,o,dt", [(1, 8192, 512, "bf16"), (4, 256, 16, "f32"),
                                       (70, 512, 96, "bf16"), (130, 1000, 33, "f32"),
-                                      (200, 2048, 130, "f32"), (96, 1024, 200, "mixed")])
+                                      (200, 2048, 130, "f32"), (96, 1024, 200, "mixed"),
+                                      (2, 7168, 896, "bf16"), (3, 2048, 70, "mixed"), (1, 4096, 33, "f32")])
 def test_router_matmul_is_bit_exact(cuda_ctx, s, i, o, dt):
     """kernels::matmul: every element must equal the reference's sequential f32 chain."""
     import torch
@@ -169,6 +170,27 @@ def _route_layer(ctx, logits_rows, topk, router="softmax", bias=None, **kw):
     x = np.zeros((T, H), np.float32)
     x[:, :E] = logits_rows
     return L, _t(x)
+
+
+@pytest.mark.parametrize("H,E,dt", [(2048, 70, "bf16"), (7168, 896, "bf16"), (4096, 128, "f32")])
+def test_one_token_route_uses_exact_logits(cuda_ctx, H, E, dt):
+    """One token through a layer's router (the one-token exact kernel on the slab layout): ids in
+    the reference's order and softmax weights equal to the oracle's on its exact logits."""
+    import rabbit_b200 as rb
+
+    rng = np.random.default_rng(H + E)
+    w = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    if dt == "bf16":
+        w = synth.round_bf16(w)
+    L = rb.MoeLayer(cuda_ctx, H, 32, E, 8, router="softmax", max_tokens=4)
+    L.upload_router(synth.f32_to_bf16_bits(w) if dt == "bf16" else w)
+    ids, wt = L.route(_t(x))
+    logits = orc.matmul(x, w, 1, H, E)
+    want = orc.qwen_route(logits[0], 8)
+    assert ids[0].cpu().tolist() == [i for i, _ in want]
+    assert np.max(np.abs(wt[0].cpu().numpy() - [v for _, v in want])) < 1e-6
+    L.close()
 
 
 def test_qwen_route_known_answers_on_gpu(cuda_ctx):  # qwen38/moe.rs:140-182
