@@ -4,8 +4,9 @@
 // src/kimi_linear/ops.rs:46-53), out = y . up^T after them.
 //
 // The projections are memory-bound matrix-vector products for decode-sized T: one warp per
-// output row streams that row of W once (16-byte loads, four in flight per lane) against the
-// tokens of x staged in shared memory, eight tokens per pass (larger T: several passes over W).
+// output row streams that row of W once (16-byte streaming loads, all of a 4096-element pass in
+// flight per lane) against the tokens of x staged in shared memory, eight tokens per pass
+// (larger T: several passes over W).
 #include <algorithm>
 
 #include "common.cuh"
@@ -34,58 +35,95 @@ __device__ __forceinline__ void load_w8(const void* w, size_t i, float (&v)[8]) 
 }
 
 constexpr int kProjTok = 8;        // tokens per pass over W
-constexpr int kProjWarps = 16;     // output rows per block
+constexpr int kProjWarps = 8;      // output rows per block
+constexpr int kProjLoads = 16;     // 16-byte weight loads in flight per lane
 constexpr int kProjSmem = 96 * 1024;
 
 // y[t][n] = sum_k x[t][k] w[n][k]; K % 8 == 0. Each block stages up to `tg` tokens of x in
 // shared memory (f32) and its 16 warps each stream one row of W against them.
-template <int WD, int XD>
+template <int WD, int XD, int TOK>
 __global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void* __restrict__ w,
                                                                       const void* __restrict__ x, int T, int K, int N,
                                                                       int tg, float* __restrict__ y) {
   extern __shared__ __align__(16) float px[];  // [tg][K]
   const int lane = threadIdx.x % 32, wi = threadIdx.x / 32;
+  // all tokens fit in one group: x is staged once and the block walks its rows
+  const bool once = T <= tg;
+  if (once) {
+    for (int i = threadIdx.x * 8; i < T * K; i += blockDim.x * 8) {
+      float v[8];
+      load_w8<XD>(x, i, v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) px[i + j] = v[j];
+    }
+    __syncthreads();
+  }
   for (int n0 = blockIdx.x * kProjWarps; n0 < N; n0 += gridDim.x * kProjWarps) {
     const int n = n0 + wi;
     for (int t0 = 0; t0 < T; t0 += tg) {
       const int nt = min(tg, T - t0);
-      __syncthreads();  // (the previous group's reads are done)
-      for (int i = threadIdx.x * 8; i < nt * K; i += blockDim.x * 8) {
-        float v[8];
-        load_w8<XD>(x, static_cast<size_t>(t0) * K + i, v);
+      if (!once) {
+        __syncthreads();  // (the previous group's reads are done)
+        for (int i = threadIdx.x * 8; i < nt * K; i += blockDim.x * 8) {
+          float v[8];
+          load_w8<XD>(x, static_cast<size_t>(t0) * K + i, v);
 #pragma unroll
-        for (int j = 0; j < 8; j++) px[i + j] = v[j];
+          for (int j = 0; j < 8; j++) px[i + j] = v[j];
+        }
+        __syncthreads();
       }
-      __syncthreads();
       if (n >= N) continue;
-      for (int ts = 0; ts < nt; ts += kProjTok) {
-        const int ns = min(kProjTok, nt - ts);
-        float acc[kProjTok];
+      for (int ts = 0; ts < nt; ts += TOK) {
+        const int ns = min(TOK, nt - ts);
+        float acc[TOK];
 #pragma unroll
-        for (int t = 0; t < kProjTok; t++) acc[t] = 0.0f;
-        for (int k0 = lane * 8; k0 < K; k0 += 4 * 256) {
-          float wv[4][8];  // four 16-byte weight loads in flight per lane
+        for (int t = 0; t < TOK; t++) acc[t] = 0.0f;
+        for (int k0 = lane * 8; k0 < K; k0 += kProjLoads * 256) {
+          // every 16-byte weight load of this pass in flight at once (a 7 KB bf16 row: one pass),
+          // converted when used
+          uint4 raw[kProjLoads][WD == kBF16 ? 1 : 2];
 #pragma unroll
-          for (int u = 0; u < 4; u++)
-            if (k0 + u * 256 < K) load_w8<WD>(w, static_cast<size_t>(n) * K + k0 + u * 256, wv[u]);
+          for (int u = 0; u < kProjLoads; u++)
+            if (k0 + u * 256 < K) {
+              const size_t i = static_cast<size_t>(n) * K + k0 + u * 256;
+              if (WD == kBF16) {
+                raw[u][0] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(w) + i));
+              } else {
+                raw[u][0] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const float*>(w) + i));
+                raw[u][WD == kBF16 ? 0 : 1] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const float*>(w) + i + 4));
+              }
+            }
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
+          for (int u = 0; u < kProjLoads; u++) {
             const int k = k0 + u * 256;
             if (k >= K) break;
+            float wv[8];
+            if (WD == kBF16) {
+              const uint32_t q[4] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w};
 #pragma unroll
-            for (int t = 0; t < kProjTok; t++) {
+              for (int j = 0; j < 4; j++) {
+                wv[2 * j] = __uint_as_float(q[j] << 16);
+                wv[2 * j + 1] = __uint_as_float(q[j] & 0xffff0000u);
+              }
+            } else {
+              const uint4 a = raw[u][0], b = raw[u][WD == kBF16 ? 0 : 1];
+              wv[0] = __uint_as_float(a.x); wv[1] = __uint_as_float(a.y); wv[2] = __uint_as_float(a.z); wv[3] = __uint_as_float(a.w);
+              wv[4] = __uint_as_float(b.x); wv[5] = __uint_as_float(b.y); wv[6] = __uint_as_float(b.z); wv[7] = __uint_as_float(b.w);
+            }
+#pragma unroll
+            for (int t = 0; t < TOK; t++) {
               if (t >= ns) break;
               const float* xr = px + static_cast<size_t>(ts + t) * K + k;
               const float4 a = *reinterpret_cast<const float4*>(xr);
               const float4 b = *reinterpret_cast<const float4*>(xr + 4);
               const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-              for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[u][j], acc[t]);
+              for (int j = 0; j < 8; j++) acc[t] = fmaf(xv[j], wv[j], acc[t]);
             }
           }
         }
 #pragma unroll
-        for (int t = 0; t < kProjTok; t++) {
+        for (int t = 0; t < TOK; t++) {
           if (t >= ns) break;
           const float sum = warp_sum(acc[t]);
           if (lane == 0) y[static_cast<size_t>(t0 + ts + t) * N + n] = sum;
@@ -135,14 +173,19 @@ cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_
   if (K % 8 || static_cast<size_t>(K) * 4 > kProjSmem) return cudaErrorInvalidValue;
   const int tg = std::min(T, static_cast<int>(kProjSmem / (static_cast<size_t>(K) * 4)));
   const size_t smem = static_cast<size_t>(tg) * K * 4;
+  // (one token: a one-token instance, whose fewer registers let two blocks share an SM)
   void (*kern)(const void*, const void*, int, int, int, int, float*) =
-      w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16> : latent_proj_kernel<kBF16, kF32>)
-                       : (x_dtype == kBF16 ? latent_proj_kernel<kF32, kBF16> : latent_proj_kernel<kF32, kF32>);
+      T == 1 ? (w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16, 1> : latent_proj_kernel<kBF16, kF32, 1>)
+                                 : (x_dtype == kBF16 ? latent_proj_kernel<kF32, kBF16, 1> : latent_proj_kernel<kF32, kF32, 1>))
+             : (w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16, kProjTok> : latent_proj_kernel<kBF16, kF32, kProjTok>)
+                                 : (x_dtype == kBF16 ? latent_proj_kernel<kF32, kBF16, kProjTok> : latent_proj_kernel<kF32, kF32, kProjTok>));
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, device_sm_count() * 4);
+  // one group of tokens: two resident blocks per SM walk the rows (x staged once per block);
+  // more tokens: a block per row group, x staged per group
+  const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, device_sm_count() * (T <= tg ? 2 : 8));
   kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y);
   return cudaGetLastError();
 }
