@@ -7,6 +7,8 @@
 // warp per expert prefix-sums the bitmap's popcounts, and a token's rank inside its expert is
 // that prefix plus the popcount of the lower bits of its own word. Ranks therefore equal the
 // ascending-token order by construction, independent of scheduling.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -80,8 +82,8 @@ __device__ int block_exclusive_scan(int v, int& excl) {
   return total;
 }
 
-// Single block (1024 threads): expert offsets, the chunk/task lists, first-occurrence order,
-// and the stable placement of every (token, slot) plus the shared expert's positions.
+// Single block (1024 threads): expert offsets, the chunk/task lists and the first-occurrence
+// order (the placement itself follows in dispatch_perm_kernel, spread over the grid).
 __global__ void __launch_bounds__(1024) dispatch_place_kernel(
     const int32_t* __restrict__ ids, const float* __restrict__ w, int T, int k, int e_begin,
     int n_loc, int words, int mt, int has_shared, const float* __restrict__ shared_gate_w,
@@ -161,37 +163,42 @@ __global__ void __launch_bounds__(1024) dispatch_place_kernel(
     }
     if (tid == 0) d.n_uniq[0] = carry;
   }
-  // stable placement
-  for (int q = tid; q < T * k; q += blockDim.x) {
+}
+
+// The stable placement of every (token, slot) and the shared expert's positions, one thread per
+// slot over the whole grid (after dispatch_place_kernel wrote the expert offsets): a slot's
+// position is its expert's offset plus the token's rank in the expert's bitmap.
+__global__ void dispatch_perm_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w, int T, int k,
+                                     int e_begin, int n_loc, int words, int has_shared,
+                                     const float* __restrict__ shared_gate_w, DispatchBuffers d) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q < T * k) {
     const int e = ids[q];
     const int el = e - e_begin;
     if (e < 0 || el < 0 || el >= n_loc) {
       d.inv[q] = -1;
-      continue;
+    } else {
+      const int t = q / k;
+      // a token that names an expert in two slots gets it once, with the first slot's weight
+      // (apply_single_expert takes the first matching pick, src/glm52/moe.rs:465-470)
+      bool dup = false;
+      for (int j = t * k; j < q; j++) dup |= ids[j] == e;
+      if (dup) {
+        d.inv[q] = -1;
+      } else {
+        const uint32_t word = d.bits[static_cast<size_t>(el) * words + (t >> 5)];
+        const int rank = d.wpre[static_cast<size_t>(el) * words + (t >> 5)] + __popc(word & ((1u << (t & 31)) - 1u));
+        const int pos = d.offsets[el] + rank;
+        d.perm_tok[pos] = t;
+        d.perm_w[pos] = w[q];
+        d.inv[q] = pos;
+      }
     }
-    const int t = q / k;
-    // a token that names an expert in two slots gets it once, with the first slot's weight
-    // (apply_single_expert takes the first matching pick, src/glm52/moe.rs:465-470)
-    bool dup = false;
-    for (int j = t * k; j < q; j++) dup |= ids[j] == e;
-    if (dup) {
-      d.inv[q] = -1;
-      continue;
-    }
-    const uint32_t word = d.bits[static_cast<size_t>(el) * words + (t >> 5)];
-    const int rank = d.wpre[static_cast<size_t>(el) * words + (t >> 5)] +
-                     __popc(word & ((1u << (t & 31)) - 1u));
-    const int pos = s_off[el] + rank;
-    d.perm_tok[pos] = t;
-    d.perm_w[pos] = w[q];
-    d.inv[q] = pos;
   }
-  if (has_shared) {
-    for (int t = tid; t < T; t += blockDim.x) {
-      const int pos = s_off[n_loc] + t;
-      d.perm_tok[pos] = t;
-      d.perm_w[pos] = shared_gate_w ? shared_gate_w[t] : 1.0f;
-    }
+  if (has_shared && q < T) {
+    const int pos = d.offsets[n_loc] + q;
+    d.perm_tok[pos] = q;
+    d.perm_w[pos] = shared_gate_w ? shared_gate_w[q] : 1.0f;
   }
 }
 
@@ -217,6 +224,10 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* w, int T, int k, in
   const int tpc_dn = hidden / rows_per_task_dn;
   dispatch_place_kernel<<<1, 1024, 0, st>>>(ids, w, T, k, e_begin, n_loc, d.words, mt, has_shared,
                                             shared_gate_w, tpc_gu, tpc_gu_sh, tpc_dn, d);
+  const int n = std::max(T * k, T);
+  if (n > 0)
+    dispatch_perm_kernel<<<(n + 255) / 256, 256, 0, st>>>(ids, w, T, k, e_begin, n_loc, d.words, has_shared,
+                                                          shared_gate_w, d);
   return cudaGetLastError();
 }
 

@@ -1285,32 +1285,42 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
 
 // ---------------------------------------------------------------------- activation terms per position
 // xt rows 4p..4p+3 = terms of the token of position p, stored at each of the token's routed
-// positions (inv) and its shared one. Activation terms of every (token, position) pair: one block per (token, 256 columns), one warp
-// per 32-column k-block computing its four E2M1 terms (amax by a warp reduction, each term
-// rounding what the previous ones left), staged in shared memory; then the block writes each of
-// the token's positions' term rows as whole 128-byte spans (8 k-blocks x 16 bytes) and 8-byte
-// scale runs, so every store fills its sectors.
+// positions (inv) and its shared one. One block per (token, 1024 columns): each warp computes the
+// four E2M1 terms of four 32-column k-blocks (amax by a warp reduction, each term rounding what
+// the previous ones left) into shared memory; then the block writes each of the token's
+// positions' term rows as 512-byte spans (32 k-blocks x 16 bytes, one 16-byte store per lane)
+// and 32-byte scale runs, so every store fills its sectors.
+constexpr int kTermSpan = 32;  // k-blocks per block
 __global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __restrict__ x, int x_dtype, int H, int T,
                                                                 int k, const int32_t* __restrict__ inv,
                                                                 const int32_t* __restrict__ shared_pos0,
                                                                 uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
-  __shared__ uint4 sterm[4][8];       // [term][k-block of the span]
-  __shared__ uint8_t ssf[4][8];
+  __shared__ uint4 sterm[4][kTermSpan];  // [term][k-block of the span]
+  __shared__ __align__(16) uint8_t ssf[4][kTermSpan];
   __shared__ int spos[32];
   const int nb = H / 32;
-  const int spans = (nb + 7) / 8;
-  const int t = blockIdx.x / spans, b0 = (blockIdx.x % spans) * 8;
+  const int spans = (nb + kTermSpan - 1) / kTermSpan;
+  const int t = blockIdx.x / spans, b0 = (blockIdx.x % spans) * kTermSpan;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nvb = min(8, nb - b0);  // k-blocks in this span
+  const int nvb = min(kTermSpan, nb - b0);  // k-blocks in this span
   if (threadIdx.x < 32) {
     int pos = -1;
     if (lane < k) pos = __ldg(inv + t * k + lane);
     else if (lane == k && shared_pos0) pos = __ldg(shared_pos0) + t;
     spos[lane] = pos;
   }
-  if (warp < nvb) {
-    const int b = b0 + warp;
-    float r = load_elem(x, x_dtype, static_cast<size_t>(t) * H + b * 32 + lane);
+  // the warp's k-blocks' activations loaded together, then their terms
+  float rv[kTermSpan / 8];
+#pragma unroll
+  for (int i = 0; i < kTermSpan / 8; i++) {
+    const int kb = warp + 8 * i;
+    rv[i] = kb < nvb ? load_elem(x, x_dtype, static_cast<size_t>(t) * H + (b0 + kb) * 32 + lane) : 0.0f;
+  }
+#pragma unroll
+  for (int i = 0; i < kTermSpan / 8; i++) {
+    const int kb = warp + 8 * i;
+    if (kb >= nvb) break;
+    float r = rv[i];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(r))));
@@ -1329,33 +1339,21 @@ __global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __re
 #pragma unroll
       for (int g = 0; g < 4; g++) w[g] = __reduce_or_sync(kFull, (lane >> 3) == g ? sh : 0u);
       if (lane == 0) {
-        sterm[j][warp] = make_uint4(w[0], w[1], w[2], w[3]);
-        ssf[j][warp] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
+        sterm[j][kb] = make_uint4(w[0], w[1], w[2], w[3]);
+        ssf[j][kb] = static_cast<uint8_t>(amax > 0.0f ? e + 127 : 127);
       }
     }
   }
   __syncthreads();
-  // (position slot s, term j, k-block c): 8 lanes per term row, 4 rows per position
+  // (position slot s, term j): one warp-wide 512-byte row span per item, 32-byte scale runs
   const int np = k + 1;
-  for (int i = threadIdx.x; i < np * 32; i += blockDim.x) {
-    const int s = i / 32, j = (i / 8) % 4, c = i % 8;
-    const int pos = spos[s];
-    if (pos < 0 || c >= nvb) continue;
-    const size_t row = static_cast<size_t>(4 * pos + j);
-    *reinterpret_cast<uint4*>(xt + row * (H / 2) + (b0 + c) * 16) = sterm[j][c];
-  }
-  for (int i = threadIdx.x; i < np * 4; i += blockDim.x) {
-    const int s = i / 4, j = i % 4;
+  for (int it = warp; it < np * 4; it += 8) {
+    const int s = it / 4, j = it % 4;
     const int pos = spos[s];
     if (pos < 0) continue;
-    uint8_t* d = xsf + static_cast<size_t>(4 * pos + j) * nb + b0;
-    if (nvb == 8 && (reinterpret_cast<uintptr_t>(d) & 7) == 0) {
-      uint2 v;
-      memcpy(&v, ssf[j], 8);
-      *reinterpret_cast<uint2*>(d) = v;
-    } else {
-      for (int c = 0; c < nvb; c++) d[c] = ssf[j][c];
-    }
+    const size_t row = static_cast<size_t>(4 * pos + j);
+    if (lane < nvb) *reinterpret_cast<uint4*>(xt + row * (H / 2) + (b0 + lane) * 16) = sterm[j][lane];
+    if (lane < nvb) xsf[row * nb + b0 + lane] = ssf[j][lane];
   }
 }
 
@@ -1467,7 +1465,7 @@ cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, int T, i
                                      const int32_t* shared_pos0, uint8_t* xt, uint8_t* xsf, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   if (k > 31) return cudaErrorInvalidValue;
-  const long long n = static_cast<long long>(T) * ((H / 32 + 7) / 8);
+  const long long n = static_cast<long long>(T) * ((H / 32 + kTermSpan - 1) / kTermSpan);
   terms_by_position_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(x, x_dtype, H, T, k, inv, shared_pos0,
                                                                                   xt, xsf);
   return cudaGetLastError();
