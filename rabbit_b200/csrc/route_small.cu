@@ -865,19 +865,23 @@ __global__ void __launch_bounds__(512, 2) decode_front_kernel(DecodeFront a) {
     if (wr < kk) s_cand[wi * kk + wr] = (static_cast<unsigned long long>(klo) << 32) | (0xffffffffu - e);
   }
   __syncthreads();
-  const int nc = (blockDim.x / 32) * kk;  // even
-  if (e < nc) {
-    const unsigned long long me = s_cand[e];
-    int gr = 0;
-#pragma unroll 8
-    for (int j = 0; j < nc; j += 2) {
-      const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(s_cand + j);
-      gr += (q.x > me ? 1 : 0) + (q.y > me ? 1 : 0);
-    }
-    if (gr < kk) {
-      const int idx = static_cast<int>(0xffffffffu - static_cast<uint32_t>(me));
-      s_top[gr] = idx;
-      if (gr == kk - 1) s_lk = s_lo[idx];
+  if (wi == 0) {
+    // warp 0 merges the 16 warps' sorted lists (lane w holds the head of warp w's list): each
+    // round takes the largest head -- (key, then the lower id) as one 64-bit value -- and
+    // advances that list
+    const int nw = blockDim.x / 32;
+    int h = 0;
+    for (int r = 0; r < kk; r++) {
+      const unsigned long long hv = lane < nw && h < kk ? s_cand[lane * kk + h] : 0ull;
+      const uint32_t hi = static_cast<uint32_t>(hv >> 32), lo32 = static_cast<uint32_t>(hv);
+      const uint32_t mhi = __reduce_max_sync(kFull, hi);
+      const uint32_t mlo = __reduce_max_sync(kFull, hi == mhi ? lo32 : 0u);
+      if (hv != 0ull && hi == mhi && lo32 == mlo) h++;
+      if (lane == 0) {
+        const int idx = static_cast<int>(0xffffffffu - mlo);
+        s_top[r] = idx;
+        if (r == kk - 1) s_lk = s_lo[idx];
+      }
     }
   }
   __syncthreads();
