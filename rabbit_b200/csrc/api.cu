@@ -1266,7 +1266,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
                   "fused counters");
       e = launch_moe_decode_fused(L->tc_plan, L->d, H, D.moe_inter, L->experts, L->tab.stride, L->tc_off_down, L->ht,
                                   L->hsf, L->partial, L->partial2, L->fused_cnt + 8, L->fused_cnt + 8 + L->fused_tiles,
-                                  L->fused_cnt, L->dev_err, out, L->fmt.act, terms_done && L->has_shared ? L->n_loc : -1, st,
+                                  L->fused_cnt, L->dev_err, out, L->fmt.act, terms_done && hs ? L->n_loc : -1, st,
                                   L->tc_trace ? L->tc_trace + 4096 + 2048 : nullptr, L->spin_ns);
       if (e != cudaSuccess) return cuda_fail(e, "fused experts (tensor cores)");
       marks.mark();
@@ -1741,11 +1741,15 @@ static rmoe_status experts_for_routing(rmoe_layer* L, const void* x, int xdt, in
     if (e != cudaSuccess) return cuda_fail(e, "prep tokens");
   }
   rmoe_status s = RMOE_OK;
+  bool prepared = false;
   if (T == 1 && L->use_tc && L->use_fused && (!L->tc_trace || !L->tc_trace_print) && D.topk <= 32) {
-    // (the one-token expert kernel reads only the chunk table: one warp builds it)
-    cudaError_t e = launch_dispatch_one_token(L->ids, L->rw, D.topk, L->e_begin, L->e_end, L->n_loc, hs ? 1 : 0,
-                                              gated ? L->gate : nullptr, L->d, st);
-    if (e != cudaSuccess) return cuda_fail(e, "one-token dispatch");
+    // (the one-token expert kernel reads only the chunk table, its zeroed counters and the token's
+    // four term rows: one launch prepares all three)
+    cudaError_t e = launch_one_token_prep(x, xdt, static_cast<int>(D.hidden), L->ids, L->rw, D.topk, L->e_begin, L->e_end,
+                                          L->n_loc, hs ? 1 : 0, gated ? L->gate : nullptr, L->d, L->fused_cnt,
+                                          8 + L->fused_tiles + RMOE_MAX_TOPK_DEV + 1, L->xt, L->xsf, st);
+    if (e != cudaSuccess) return cuda_fail(e, "one-token prep");
+    prepared = true;
   } else if ((s = dispatch_into(L, T, mt, gated ? L->gate : nullptr, st, hs)) != RMOE_OK) {
     return s;
   }
@@ -1753,7 +1757,7 @@ static rmoe_status experts_for_routing(rmoe_layer* L, const void* x, int xdt, in
   const bool prof = L->profiling;
   L->profiling = false;  // (stage events cover rmoe_moe_forward only)
   int launches = 0;
-  s = enqueue_experts(L, x, xdt, T, mt, hs, false, false, out, st, marks, &launches);
+  s = enqueue_experts(L, x, xdt, T, mt, hs, prepared, false, out, st, marks, &launches);
   L->profiling = prof;
   L->stats.kernel_launches += launches;
   return s;

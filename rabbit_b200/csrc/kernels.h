@@ -274,6 +274,12 @@ bool moe_tc_plan(void* plan, int H, int I, const uint8_t* xt, const uint8_t* xsf
 size_t moe_tc_region_bytes(int H, int I, int down);
 cudaError_t launch_tc_relayout(int down, const uint8_t* m0, const uint8_t* m1, const uint8_t* s0,
                                const uint8_t* s1, int H, int I, uint8_t* dst, cudaStream_t st);
+// One token on given routing (one launch): the one-token dispatch, the one-token expert kernel's
+// counters zeroed (zero_n ints), and x's four term rows (rows 0..3 of xt / xsf).
+cudaError_t launch_one_token_prep(const void* x, int x_dtype, int H, const int32_t* ids, const float* w, int k,
+                                  int e_begin, int e_end, int n_loc, int has_shared, const float* shared_gate_w,
+                                  const DispatchBuffers& d, int* zero_buf, int zero_n, uint8_t* xt, uint8_t* xsf,
+                                  cudaStream_t st);
 cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, int T, int k, const int32_t* inv,
                                      const int32_t* shared_pos0, uint8_t* xt, uint8_t* xsf, cudaStream_t st);
 // mode 0: gate/up (-> h terms), 1: down (-> y per position), 2: down of one token (-> out row)

@@ -1357,6 +1357,83 @@ __global__ void __launch_bounds__(256) terms_by_position_kernel(const void* __re
   }
 }
 
+// One token on given routing, one launch before the one-token expert kernel: block 0's first
+// warp builds the chunk table (positions by ascending expert id among the local slots, a
+// repeated expert once at its first slot, the shared expert last -- as the one-token dispatch),
+// block 0's other threads zero the expert kernel's counters, and every block writes the four
+// term rows of its 32 k-blocks of x once (rows 0..3: the one-token kernel reads the token's own
+// rows for every position).
+__global__ void __launch_bounds__(256) one_token_prep_kernel(const void* __restrict__ x, int x_dtype, int H,
+                                                             const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                                             int k, int e_begin, int e_end, int n_loc, int has_shared,
+                                                             const float* __restrict__ shared_gate_w, DispatchBuffers d,
+                                                             int* __restrict__ zero_buf, int zero_n,
+                                                             uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // the expert kernel launched next may start now: it waits for this grid before reading any of
+  // what it writes (as after the one-token front end)
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  if (blockIdx.x == 0 && warp == 0) {
+    const int sid = lane < k ? ids[lane] : -1;
+    const float wv = lane < k ? w[lane] : 0.0f;
+    bool first = true;
+    for (int j = 0; j < k; j++) {
+      const int o = __shfl_sync(kFull, sid, j);
+      first &= !(j < lane && o == sid);
+    }
+    const bool local = lane < k && first && sid >= e_begin && sid < e_end;
+    const uint32_t local_mask = __ballot_sync(kFull, local);
+    int pos = 0;
+    for (int j = 0; j < k; j++) {
+      const int o = __shfl_sync(kFull, sid, j);
+      pos += ((local_mask >> j) & 1u) && o < sid ? 1 : 0;
+    }
+    const int n_routed = __popc(local_mask);
+    if (lane < k) d.inv[lane] = local ? pos : -1;
+    if (local) {
+      d.ch_expert[pos] = sid - e_begin;
+      d.ch_pos[pos] = pos;
+      d.ch_n[pos] = 1;
+      d.perm_tok[pos] = 0;
+      d.perm_w[pos] = wv;
+    }
+    if (lane == 0) {
+      if (has_shared) {
+        d.ch_expert[n_routed] = n_loc;
+        d.ch_pos[n_routed] = n_routed;
+        d.ch_n[n_routed] = 1;
+        d.perm_tok[n_routed] = 0;
+        d.perm_w[n_routed] = shared_gate_w ? shared_gate_w[0] : 1.0f;
+      }
+      d.n_chunks[0] = n_routed + has_shared;
+      d.offsets[n_loc] = n_routed;
+      d.offsets[n_loc + has_shared] = n_routed + has_shared;
+    }
+  } else if (blockIdx.x == 0) {
+    for (int i = threadIdx.x - 32; i < zero_n; i += blockDim.x - 32) zero_buf[i] = 0;
+  }
+  const int nb = H / 32;
+  const int b0 = blockIdx.x * kTermSpan;
+#pragma unroll
+  for (int i = 0; i < kTermSpan / 8; i++) {
+    const int kb = warp + 8 * i;
+    if (b0 + kb >= nb) break;
+    const float r = load_elem(x, x_dtype, static_cast<size_t>(b0 + kb) * 32 + lane);
+    warp_terms4(r, xt + (b0 + kb) * 16, H / 2, xsf + b0 + kb, H / 32);
+  }
+}
+
+cudaError_t launch_one_token_prep(const void* x, int x_dtype, int H, const int32_t* ids, const float* w, int k,
+                                  int e_begin, int e_end, int n_loc, int has_shared, const float* shared_gate_w,
+                                  const DispatchBuffers& d, int* zero_buf, int zero_n, uint8_t* xt, uint8_t* xsf,
+                                  cudaStream_t st) {
+  if (k > 32 || H % 32) return cudaErrorInvalidValue;
+  const int blocks = (H / 32 + kTermSpan - 1) / kTermSpan;
+  one_token_prep_kernel<<<blocks, 256, 0, st>>>(x, x_dtype, H, ids, w, k, e_begin, e_end, n_loc, has_shared, shared_gate_w,
+                                                d, zero_buf, zero_n, xt, xsf);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------- host side
 bool make_tmap_sw128(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows);
 bool make_tmap_rows(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
