@@ -1850,9 +1850,12 @@ extern "C" rmoe_status rmoe_latent_moe(rmoe_layer* L, const void* x, int32_t x_d
   // the routed experts at the latent width (:94-104); no shared expert here (the caller's)
   if ((s = experts_for_routing(L, L->lat_x, kF32, T, false, L->lat_y, st)) != RMOE_OK) return s;
   // RMSNorm of each token's summed routed row (:106-110), then out = y . up^T (:112)
-  if (L->lat_has_norm && (e = launch_rmsnorm_rows(L->lat_y, T, H, L->lat_norm, L->lat_eps, st)) != cudaSuccess)
+  // (the norm folds into the up projection's staging of the rows when they fit in one group)
+  const bool fold = L->lat_has_norm && latent_proj_one_group(T, H);
+  if (L->lat_has_norm && !fold && (e = launch_rmsnorm_rows(L->lat_y, T, H, L->lat_norm, L->lat_eps, st)) != cudaSuccess)
     return cuda_fail(e, "latent norm");
-  if ((e = launch_latent_proj(L->lat_up, L->lat_dtype, L->lat_y, kF32, T, H, Hr, out, st)) != cudaSuccess)
+  if ((e = launch_latent_proj(L->lat_up, L->lat_dtype, L->lat_y, kF32, T, H, Hr, out, st, fold ? L->lat_norm : nullptr,
+                              L->lat_eps)) != cudaSuccess)
     return cuda_fail(e, "latent up projection");
   const size_t n = static_cast<size_t>(T) * k;
   if (ids_out) RMOE_CUDA(cudaMemcpyAsync(ids_out, L->ids, n * 4, cudaMemcpyDeviceToDevice, st), "latent ids");

@@ -307,8 +307,11 @@ cudaError_t launch_moe_decode_fused(const void* plan, const DispatchBuffers& d, 
 
 // ---- latent MoE wrapper (latent.cu) ----
 // y[T][N] = x[T][K] . w[N][K]^T (w bf16 or f32, x bf16 or f32; K % 8 == 0)
+// True when T rows of K fit the projection's one staging group (the norm can be folded in).
+bool latent_proj_one_group(int T, int K);
+// norm_w: RMSNorm each row of x first (weights [K], eps; the rows must fit in one staging group).
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
-                               cudaStream_t st);
+                               cudaStream_t st, const float* norm_w = nullptr, float eps = 0.0f);
 // v[r] *= w / sqrt(mean(v[r]^2) + eps) for each of `rows` rows of n
 cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st);
 

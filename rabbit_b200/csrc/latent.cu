@@ -44,12 +44,50 @@ constexpr int kProjSmem = 96 * 1024;
 template <int WD, int XD, int TOK>
 __global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void* __restrict__ w,
                                                                       const void* __restrict__ x, int T, int K, int N,
-                                                                      int tg, float* __restrict__ y) {
+                                                                      int tg, float* __restrict__ y,
+                                                                      const float* __restrict__ norm_w, float eps) {
   extern __shared__ __align__(16) float px[];  // [tg][K]
   const int lane = threadIdx.x % 32, wi = threadIdx.x / 32;
   // all tokens fit in one group: x is staged once and the block walks its rows
   const bool once = T <= tg;
-  if (once) {
+  if (once && norm_w) {
+    // RMSNorm of each row while it is staged (kimi_linear::ops::rmsnorm,
+    // src/kimi_linear/ops.rs:46-53): the row's values and the norm weights are loaded together,
+    // the mean of squares accumulated in f64, and px = v * (r * w) -- rmsnorm_rows_kernel's
+    // arithmetic, done by every block on its own copy of the rows
+    constexpr int kMaxC = 4;  // 8-element pieces per thread (K <= 8192)
+    __shared__ double part[kProjWarps];
+    for (int t = 0; t < T; t++) {
+      float v[kMaxC][8], nw[kMaxC][8];
+      double sq = 0.0;
+#pragma unroll
+      for (int c = 0; c < kMaxC; c++) {
+        const int i = (threadIdx.x + c * blockDim.x) * 8;
+        if (i < K) {
+          load_w8<XD>(x, static_cast<size_t>(t) * K + i, v[c]);
+          load_w8<kF32>(norm_w, i, nw[c]);
+#pragma unroll
+          for (int j = 0; j < 8; j++) sq += static_cast<double>(v[c][j]) * static_cast<double>(v[c][j]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
+      if (lane == 0) part[wi] = sq;
+      __syncthreads();
+      double tot = 0.0;
+      for (int q = 0; q < kProjWarps; q++) tot += part[q];
+      const float ms = static_cast<float>(tot / static_cast<double>(K));
+      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+#pragma unroll
+      for (int c = 0; c < kMaxC; c++) {
+        const int i = (threadIdx.x + c * blockDim.x) * 8;
+        if (i < K)
+#pragma unroll
+          for (int j = 0; j < 8; j++) px[static_cast<size_t>(t) * K + i + j] = v[c][j] * __fmul_rn(r, nw[c][j]);
+      }
+      __syncthreads();  // (the partials are read before the next row reuses them; px complete)
+    }
+  } else if (once) {
     for (int i = threadIdx.x * 8; i < T * K; i += blockDim.x * 8) {
       float v[8];
       load_w8<XD>(x, i, v);
@@ -168,13 +206,14 @@ __global__ void __launch_bounds__(1024) rmsnorm_rows_kernel(float* __restrict__ 
 }  // namespace
 
 cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_dtype, int T, int K, int N, float* y,
-                               cudaStream_t st) {
+                               cudaStream_t st, const float* norm_w, float eps) {
   if (T <= 0) return cudaSuccess;
   if (K % 8 || static_cast<size_t>(K) * 4 > kProjSmem) return cudaErrorInvalidValue;
   const int tg = std::min(T, static_cast<int>(kProjSmem / (static_cast<size_t>(K) * 4)));
+  if (norm_w && (tg < T || K > 8192)) return cudaErrorInvalidValue;  // (the norm stages every row at once)
   const size_t smem = static_cast<size_t>(tg) * K * 4;
   // (one token: a one-token instance, whose fewer registers let two blocks share an SM)
-  void (*kern)(const void*, const void*, int, int, int, int, float*) =
+  void (*kern)(const void*, const void*, int, int, int, int, float*, const float*, float) =
       T == 1 ? (w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16, 1> : latent_proj_kernel<kBF16, kF32, 1>)
                                  : (x_dtype == kBF16 ? latent_proj_kernel<kF32, kBF16, 1> : latent_proj_kernel<kF32, kF32, 1>))
              : (w_dtype == kBF16 ? (x_dtype == kBF16 ? latent_proj_kernel<kBF16, kBF16, kProjTok> : latent_proj_kernel<kBF16, kF32, kProjTok>)
@@ -186,8 +225,12 @@ cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_
   // one group of tokens: two resident blocks per SM walk the rows (x staged once per block);
   // more tokens: a block per row group, x staged per group
   const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, device_sm_count() * (T <= tg ? 2 : 8));
-  kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y);
+  kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y, norm_w, eps);
   return cudaGetLastError();
+}
+
+bool latent_proj_one_group(int T, int K) {
+  return T >= 1 && static_cast<size_t>(T) * K * 4 <= kProjSmem && K <= 8192 && K % 8 == 0;
 }
 
 cudaError_t launch_rmsnorm_rows(float* v, int rows, int n, const float* w, float eps, cudaStream_t st) {
