@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "pipe.cuh"
 
 namespace rmoe {
 
@@ -48,6 +49,8 @@ __global__ void __launch_bounds__(32 * kProjWarps) latent_proj_kernel(const void
                                                                       const float* __restrict__ norm_w, float eps) {
   extern __shared__ __align__(16) float px[];  // [tg][K]
   const int lane = threadIdx.x % 32, wi = threadIdx.x / 32;
+  // (launched as a programmatic dependent of the kernel that writes x: wait for it here)
+  griddep_wait();
   // all tokens fit in one group: x is staged once and the block walks its rows
   const bool once = T <= tg;
   if (once && norm_w) {
@@ -225,8 +228,17 @@ cudaError_t launch_latent_proj(const void* w, int w_dtype, const void* x, int x_
   // one group of tokens: two resident blocks per SM walk the rows (x staged once per block);
   // more tokens: a block per row group, x staged per group
   const int blocks = std::min((N + kProjWarps - 1) / kProjWarps, device_sm_count() * (T <= tg ? 2 : 8));
-  kern<<<blocks, 32 * kProjWarps, smem, st>>>(w, x, T, K, N, tg, y, norm_w, eps);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(32 * kProjWarps);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, w, x, T, K, N, tg, y, norm_w, eps);
 }
 
 bool latent_proj_one_group(int T, int K) {

@@ -314,6 +314,7 @@ __global__ void __launch_bounds__(kRcThreads) router_exact_chain_kernel(const vo
     mbar_fence_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) griddep_launch_dependents();  // (the top-k waits for this grid's logits)
   if (threadIdx.x == 0) RC_TRACE(4 * 63 + 3, global_ns());
   if (warp < kRcProd) {
     // ---- producers: thread (warp h, lane r) forms row r's products of the slab's 8-element
@@ -701,6 +702,8 @@ __global__ void __launch_bounds__(1024) topk_sigmoid_block_kernel(const float* _
   __shared__ int sel_id[32], lo_id[32];
   __shared__ float sel_v[32], lo_v[32];
   __shared__ float s_sig[1024];
+  // (launched as a programmatic dependent of the router logits: wait for them here)
+  griddep_wait();
   const int t = blockIdx.x, e = threadIdx.x;
   const bool valid = e < E;
   const int id = valid ? e : 0x40000000 + e;
@@ -796,8 +799,16 @@ cudaError_t launch_topk_grouped(const float* logits, const float* bias, int T, i
   if (E > kMaxE || k > 32 || k < 1 || n_group > 32) return cudaErrorInvalidValue;
   if (n_group > 1 && E % n_group != 0) return cudaErrorInvalidValue;
   if (n_group <= 1) {
-    topk_sigmoid_block_kernel<<<T, 1024, 0, st>>>(logits, bias, T, E, k, norm_topk, routed_scale, ids, w);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(T);
+    cfg.blockDim = dim3(1024);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, topk_sigmoid_block_kernel, logits, bias, T, E, k, norm_topk, routed_scale, ids, w);
   }
   if (E <= 32) launch_grouped_pl<1>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
   else if (E <= 64) launch_grouped_pl<2>(logits, bias, T, E, k, n_group, topk_group, norm_topk, routed_scale, ids, w, st);
