@@ -222,13 +222,6 @@ constexpr int kRcSlabEl = 256;           // elements per slab
 constexpr int kRcProd = 3;               // producer warps (8-element pieces of every row slab, round robin)
 constexpr int kRcThreads = 32 * (kRcProd + 1);  // warps 0-2 producers, warp 3 the chains (its own scheduler)
 __device__ unsigned g_router_err;        // wait-timeout flags of calls without a layer
-#ifdef RMOE_RC_TRACE
-__device__ unsigned long long g_rc_trace[4 * 64];  // block 0: per slab producer / chain done
-#define RC_TRACE(i, v) \
-  if (blockIdx.x == 0 && (i) < 4 * 64) g_rc_trace[i] = (v)
-#else
-#define RC_TRACE(i, v)
-#endif
 
 // (d0, d1) = (a0 * b0, a1 * b1) on f32 bit patterns, each rounded to nearest even
 __device__ __forceinline__ void mul2_rn(uint32_t& d0, uint32_t& d1, uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
@@ -315,7 +308,6 @@ __global__ void __launch_bounds__(kRcThreads) router_exact_chain_kernel(const vo
   }
   __syncthreads();
   if (threadIdx.x == 0) griddep_launch_dependents();  // (the top-k waits for this grid's logits)
-  if (threadIdx.x == 0) RC_TRACE(4 * 63 + 3, global_ns());
   if (warp < kRcProd) {
     // ---- producers: thread (warp h, lane r) forms row r's products of the slab's 8-element
     // pieces h, h + kRcProd, ...
@@ -383,7 +375,6 @@ __global__ void __launch_bounds__(kRcThreads) router_exact_chain_kernel(const vo
         *reinterpret_cast<uint4*>(dst + c + 4) = p1;
       }
       mbar_arrive(&pfull[pb]);
-      if (lane == 0) RC_TRACE(4 * j + warp, global_ns());
       // every producer warp is done with slot q: warp 0 refills it
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kRcProd) : "memory");
       if (warp == 0 && j + Lo::nring < nslab) {
@@ -425,7 +416,6 @@ __global__ void __launch_bounds__(kRcThreads) router_exact_chain_kernel(const vo
         for (int u = 0; u < 4; u++) q[u] = nq[u];
       }
       mbar_arrive(&pempty[pb]);
-      if (lane == 0) RC_TRACE(4 * j + 2, global_ns());
     }
     const int e = blockIdx.x * 32 + lane;
     if (ok && e < E) logits[e] = acc;
