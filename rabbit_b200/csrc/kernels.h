@@ -151,8 +151,8 @@ cudaError_t launch_prologue_small(const SmallPrologue& a, const DispatchBuffers&
 cudaError_t launch_resolve_order(const SmallPrologue& a, int32_t* ids_final, float* w_final, float* exact_v,
                                  int32_t* done_cnt, cudaStream_t st);
 // logits[T][E] = exact reference chain of x[t] . w[e] (fmul then fadd per element, from -0.0)
-// err: the layer's device error flags (a bounded copy wait that runs out sets a bit); null: a
-// module-wide word. w_slabs: the router in the slab layout (launch_router_slabs), used for T == 1.
+// err: the layer's device error flags (a bounded copy wait that runs out sets a bit). w_slabs: the
+// router in the slab layout (launch_router_slabs); with err, one token uses the slab kernel.
 cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w, int w_dtype,
                                        float* logits, int T, int H, int E, cudaStream_t st,
                                        unsigned* err = nullptr, const void* w_slabs = nullptr);

@@ -221,7 +221,6 @@ __global__ void __launch_bounds__(256) router_exact_warp_kernel(const void* __re
 constexpr int kRcSlabEl = 256;           // elements per slab
 constexpr int kRcProd = 3;               // producer warps (8-element pieces of every row slab, round robin)
 constexpr int kRcThreads = 32 * (kRcProd + 1);  // warps 0-2 producers, warp 3 the chains (its own scheduler)
-__device__ unsigned g_router_err;        // wait-timeout flags of calls without a layer
 
 // (d0, d1) = (a0 * b0, a1 * b1) on f32 bit patterns, each rounded to nearest even
 __device__ __forceinline__ void mul2_rn(uint32_t& d0, uint32_t& d1, uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
@@ -426,20 +425,18 @@ cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w
                                        float* logits, int T, int H, int E, cudaStream_t st, unsigned* err,
                                        const void* w_slabs) {
   if (T <= 0) return cudaSuccess;
-  if (T == 1 && w_slabs && H % kRcSlabEl == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && H * 4 < (1 << 20)) {
+  // one token through a layer (its router in the slab layout, its error flags for the waits)
+  const size_t chain_smem = w_dtype == kBF16 ? RcLayout<kBF16>::bytes(H) : RcLayout<kF32>::bytes(H);
+  if (T == 1 && w_slabs && err && H % kRcSlabEl == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+      chain_smem <= 227 * 1024) {
     void (*kern)(const void*, const uint8_t*, float*, int, int, unsigned*) =
         x_dtype == kBF16 ? (w_dtype == kBF16 ? router_exact_chain_kernel<kBF16, kBF16> : router_exact_chain_kernel<kBF16, kF32>)
                          : (w_dtype == kBF16 ? router_exact_chain_kernel<kF32, kBF16> : router_exact_chain_kernel<kF32, kF32>);
-    const size_t smem = w_dtype == kBF16 ? RcLayout<kBF16>::bytes(H) : RcLayout<kF32>::bytes(H);
-    if (smem > 227 * 1024) goto other;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(chain_smem));
     if (e != cudaSuccess) return e;
-    unsigned* ef = err;
-    if (!ef && (e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ef), g_router_err)) != cudaSuccess) return e;
-    kern<<<(E + 31) / 32, kRcThreads, smem, st>>>(x, static_cast<const uint8_t*>(w_slabs), logits, H, E, ef);
+    kern<<<(E + 31) / 32, kRcThreads, chain_smem, st>>>(x, static_cast<const uint8_t*>(w_slabs), logits, H, E, err);
     return cudaGetLastError();
   }
-other:
   const size_t warp_smem = (static_cast<size_t>(H) + 8 * kRwChunk) * 4;
   if (T <= 16 && H % kRwChunk == 0 && warp_smem <= 160 * 1024) {
     void (*kern)(const void*, const void*, float*, int, int, int) =
