@@ -127,6 +127,15 @@ def test_host_entry_point_matches_device_path(qwen_layer):
     pinned = torch.from_numpy(synth.f32_to_bf16_bits(x).view(np.int16)).pin_memory()
     out = L.moe_forward_host(pinned.view(torch.bfloat16))
     assert np.array_equal(dev, out)
+    # pinned buffers both ways, changing between calls
+    for T in (1, 4):
+        xt = synth.activations(cfg, tokens=T, token_offset=77 * T)
+        want = L.moe_forward(x_device(cfg, xt)).cpu().numpy()
+        for _ in range(2):
+            xp = torch.from_numpy(synth.f32_to_bf16_bits(xt).view(np.int16)).pin_memory()
+            op = torch.empty((T, cfg.hidden), dtype=torch.float32).pin_memory()
+            got = L.moe_forward_host(xp.view(torch.bfloat16), out=op)
+            assert np.array_equal(want, got.numpy())
 
 
 def test_graph_replays_bind_the_callers_buffers(qwen_layer):
@@ -235,6 +244,18 @@ def test_bounded_wait_reports_timeout_and_layer_recovers(cuda_ctx):
     again = L.moe_forward_host(x)
     assert np.array_equal(again, good)
     L.check()  # nothing pending
+    # the same with pinned buffers both ways
+    import torch
+
+    xp = torch.from_numpy(x.view(np.int16)).pin_memory()
+    op = torch.empty((1, cfg.hidden), dtype=torch.float32).pin_memory()
+    assert np.array_equal(L.moe_forward_host(xp.view(torch.bfloat16), out=op).numpy(), good)
+    L.set_wait_limit(100)
+    with pytest.raises(rb.RmoeError, match="TIMEOUT"):
+        L.moe_forward_host(xp.view(torch.bfloat16), out=op)
+    L.set_wait_limit(0)
+    assert np.array_equal(L.moe_forward_host(xp.view(torch.bfloat16), out=op).numpy(), good)
+    L.check()
     L.close()
 
 
