@@ -26,7 +26,7 @@ extern "C" {
 #define RMOE_API
 #endif
 
-#define RMOE_ABI_VERSION 3
+#define RMOE_ABI_VERSION 4
 #define RMOE_MAX_TOPK 32
 
 typedef enum rmoe_status {
@@ -322,6 +322,22 @@ RMOE_API rmoe_status rmoe_latent_moe(rmoe_layer* layer, const void* x, int32_t x
 RMOE_API rmoe_status rmoe_moe_forward_routed(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                                     const int32_t* ids, const float* weights, int32_t with_shared,
                                     float* out, void* stream);
+
+/* The activation operand of a tensor-core MXFP4 layer for T token rows, token-major: terms
+ * [T][4][hidden/2] (four E2M1 terms per row, each rounding what the previous ones left, low
+ * nibble first) and term_scales [T][4][hidden/32] (an E8M0 byte per term and 32 columns). No
+ * reference counterpart: it is what expert parallelism exchanges instead of x (17 bytes per 32
+ * columns against 128 for f32). RMOE_NOT_SUPPORTED on layers off the MXFP4 tensor-core path. */
+RMOE_API rmoe_status rmoe_activation_terms(rmoe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                                           uint8_t* terms, uint8_t* term_scales, void* stream);
+
+/* rmoe_moe_forward_routed (without the shared expert) on rows given as their activation terms
+ * (rmoe_activation_terms' layout): the same expert loop (apply_single_expert,
+ * src/glm52/moe.rs:463-513), the same outputs bit for bit as rmoe_moe_forward_routed on the x the
+ * terms were formed from. terms and out 16-byte aligned device pointers. */
+RMOE_API rmoe_status rmoe_moe_forward_routed_terms(rmoe_layer* layer, const uint8_t* terms, const uint8_t* term_scales,
+                                                   int32_t T, const int32_t* ids, const float* weights, float* out,
+                                                   void* stream);
 
 /* Owner-side combine of expert parallelism: out[r] = ((parts[0][r] + parts[1][r]) + ... +
  * parts[n_parts-1][r]) + last[r] for rows x hidden floats, parts [n_parts][rows][hidden] (each

@@ -8,6 +8,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "librmoe.so")
 
 RMOE_OK = 0
+RMOE_NOT_SUPPORTED = 6
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "SHAPE_MISMATCH", 3: "CUDA_ERROR", 4: "NCCL_ERROR",
                 5: "TIMEOUT", 6: "NOT_SUPPORTED", 7: "OUT_OF_MEMORY", 8: "IO_ERROR", 9: "MISSING_TENSOR"}
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_GROUPED = 0, 1
@@ -93,6 +94,8 @@ PROTOTYPES = {
     "rmoe_moe_forward_routed": (C.c_int, [P, P, I32, I32, P, P, I32, P, P]),
     "rmoe_moe_forward_host": (C.c_int, [P, P, I32, I32, P, P, P]),
     "rmoe_sum_rank_parts": (C.c_int, [P, P, I32, C.c_int64, I32, P, P]),
+    "rmoe_activation_terms": (C.c_int, [P, P, I32, I32, P, P, P]),
+    "rmoe_moe_forward_routed_terms": (C.c_int, [P, P, P, I32, P, P, P, P]),
     "rmoe_matmul_mxfp4": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_mxfp4_tc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),
     "rmoe_matmul_mxfp4_noalloc": (C.c_int, [P, P, I32, P, P, I32, I32, I32, P]),

@@ -1251,7 +1251,7 @@ static rmoe_status enqueue_experts(rmoe_layer* L, const void* x, int xdt, int T,
   if (L->use_tc) {
     // tensor-core experts: activation terms per position, gate/up (-> h terms with the routing
     // weight folded in), down: one token = combined row directly, else y per position + sum
-    if (!terms_done) {
+    if (!terms_done && x) {  // (x null: the caller already placed the position rows)
       e = launch_terms_by_position(x, xdt, H, T, k, L->d.inv, hs ? L->d.offsets + L->n_loc : nullptr,
                                    L->xt, L->xsf, st);
       if (e != cudaSuccess) return cuda_fail(e, "activation terms");
@@ -1802,6 +1802,58 @@ extern "C" rmoe_status rmoe_moe_forward_routed(rmoe_layer* L, const void* x, int
   L->stats.forward_calls++;
   L->stats.tokens_routed += T;
   return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_activation_terms(rmoe_layer* L, const void* x, int32_t x_dtype, int32_t T, uint8_t* terms,
+                                             uint8_t* term_scales, void* stream) {
+  const char* what = "rmoe_activation_terms";
+  if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
+  if (!L->use_tc) return fail(RMOE_NOT_SUPPORTED, "%s: the layer's experts are not on the MXFP4 tensor-core path", what);
+  if (x_dtype != RMOE_F32 && x_dtype != RMOE_BF16) return fail(RMOE_INVALID_ARG, "%s: x_dtype %d", what, x_dtype);
+  if (T < 0) return fail(RMOE_INVALID_ARG, "%s: T = %d", what, T);
+  if (T == 0) return RMOE_OK;
+  if (!x || !terms || !term_scales) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  RMOE_CUDA(launch_terms_rows(x, x_dtype == RMOE_BF16 ? kBF16 : kF32, L->desc.hidden, T, terms, term_scales,
+                              static_cast<cudaStream_t>(stream)),
+            what);
+  return RMOE_OK;
+}
+
+extern "C" rmoe_status rmoe_moe_forward_routed_terms(rmoe_layer* L, const uint8_t* terms, const uint8_t* term_scales,
+                                                     int32_t T, const int32_t* ids, const float* weights, float* out,
+                                                     void* stream) {
+  const char* what = "rmoe_moe_forward_routed_terms";
+  if (!L) return fail(RMOE_INVALID_ARG, "%s: null layer", what);
+  if (!L->use_tc) return fail(RMOE_NOT_SUPPORTED, "%s: the layer's experts are not on the MXFP4 tensor-core path", what);
+  if (T < 0 || T > L->max_tokens)
+    return fail(RMOE_INVALID_ARG, "%s: T = %d outside [0, max_tokens = %d]", what, T, L->max_tokens);
+  if (T == 0) return RMOE_OK;
+  if (!terms || !term_scales || !ids || !weights || !out) return fail(RMOE_INVALID_ARG, "%s: null pointer", what);
+  if (reinterpret_cast<uintptr_t>(terms) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(RMOE_INVALID_ARG, "%s: terms and out must be 16-byte aligned", what);
+  rmoe_status s = check_uploaded(L);
+  if (s != RMOE_OK) return s;
+  RMOE_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const rmoe_layer_desc& D = L->desc;
+  const int k = D.topk, mt = std::min(T, 32);
+  const size_t n = static_cast<size_t>(T) * k;
+  RMOE_CUDA(cudaMemcpyAsync(L->ids, ids, n * 4, cudaMemcpyDefault, st), "routed ids");
+  RMOE_CUDA(cudaMemcpyAsync(L->rw, weights, n * 4, cudaMemcpyDefault, st), "routed weights");
+  if ((s = dispatch_into(L, T, mt, nullptr, st, false)) != RMOE_OK) return s;
+  cudaError_t e = launch_terms_gather(terms, term_scales, D.hidden, T, k, L->d.inv, L->xt, L->xsf, st);
+  if (e != cudaSuccess) return cuda_fail(e, "position rows from terms");
+  StageMarks marks(L, st);
+  const bool prof = L->profiling;
+  L->profiling = false;
+  int launches = 0;
+  s = enqueue_experts(L, nullptr, kF32, T, mt, false, false, false, out, st, marks, &launches);
+  L->profiling = prof;
+  L->stats.kernel_launches += launches + 2;
+  L->stats.forward_calls++;
+  L->stats.tokens_routed += T;
+  return s;
 }
 
 extern "C" rmoe_status rmoe_upload_latent(rmoe_layer* L, const void* down_proj, const void* up_proj, int32_t proj_dtype,

@@ -280,6 +280,11 @@ cudaError_t launch_one_token_prep(const void* x, int x_dtype, int H, const int32
                                   int e_begin, int e_end, int n_loc, int has_shared, const float* shared_gate_w,
                                   const DispatchBuffers& d, int* zero_buf, int zero_n, uint8_t* xt, uint8_t* xsf,
                                   cudaStream_t st);
+// Token-major activation terms: rows 4t..4t+3 of xt ([4T][H/2]) / xsf ([4T][H/32]) are token t's.
+cudaError_t launch_terms_rows(const void* x, int x_dtype, int H, int T, uint8_t* xt, uint8_t* xsf, cudaStream_t st);
+// Position rows from token-major terms (inv [T][k]: each slot's position or -1).
+cudaError_t launch_terms_gather(const uint8_t* tt, const uint8_t* tsf, int H, int T, int k, const int32_t* inv,
+                                uint8_t* xt, uint8_t* xsf, cudaStream_t st);
 cudaError_t launch_terms_by_position(const void* x, int x_dtype, int H, int T, int k, const int32_t* inv,
                                      const int32_t* shared_pos0, uint8_t* xt, uint8_t* xsf, cudaStream_t st);
 // mode 0: gate/up (-> h terms), 1: down (-> y per position), 2: down of one token (-> out row)

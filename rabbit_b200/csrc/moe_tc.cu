@@ -1434,6 +1434,49 @@ cudaError_t launch_one_token_prep(const void* x, int x_dtype, int H, const int32
   return cudaGetLastError();
 }
 
+// Token-major activation terms (the payload expert parallelism exchanges): rows 4t..4t+3 of
+// xt / xsf are the four-term E2M1 expansion of token t. One warp per (token, 32-column k-block).
+__global__ void __launch_bounds__(256) terms_rows_kernel(const void* __restrict__ x, int x_dtype, int H, int T,
+                                                         uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
+  const int nb = H / 32;
+  const long long wid = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32;
+  if (wid >= static_cast<long long>(T) * nb) return;
+  const int t = static_cast<int>(wid / nb), b = static_cast<int>(wid % nb);
+  const float r = load_elem(x, x_dtype, static_cast<size_t>(t) * H + b * 32 + (threadIdx.x & 31));
+  warp_terms4(r, xt + static_cast<size_t>(4 * t) * (H / 2) + b * 16, H / 2, xsf + static_cast<size_t>(4 * t) * nb + b, nb);
+}
+
+cudaError_t launch_terms_rows(const void* x, int x_dtype, int H, int T, uint8_t* xt, uint8_t* xsf, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (H % 32) return cudaErrorInvalidValue;
+  const long long warps = static_cast<long long>(T) * (H / 32);
+  terms_rows_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, st>>>(x, x_dtype, H, T, xt, xsf);
+  return cudaGetLastError();
+}
+
+// The position rows of the expert kernels from token-major terms: position inv[t][j] (>= 0)
+// gets token t's four rows and their scales. One block per (token, slot).
+__global__ void __launch_bounds__(256) terms_gather_kernel(const uint8_t* __restrict__ tt, const uint8_t* __restrict__ tsf,
+                                                           int H, int k, const int32_t* __restrict__ inv,
+                                                           uint8_t* __restrict__ xt, uint8_t* __restrict__ xsf) {
+  const int q = blockIdx.x, t = q / k;
+  const int pos = inv[q];
+  if (pos < 0) return;
+  const size_t rb = static_cast<size_t>(H) / 2, nb = static_cast<size_t>(H) / 32;
+  const uint4* src = reinterpret_cast<const uint4*>(tt + static_cast<size_t>(4 * t) * rb);
+  uint4* dst = reinterpret_cast<uint4*>(xt + static_cast<size_t>(4 * pos) * rb);
+  for (size_t i = threadIdx.x; i < 4 * rb / 16; i += blockDim.x) dst[i] = src[i];
+  for (size_t i = threadIdx.x; i < 4 * nb; i += blockDim.x) xsf[static_cast<size_t>(4 * pos) * nb + i] = tsf[static_cast<size_t>(4 * t) * nb + i];
+}
+
+cudaError_t launch_terms_gather(const uint8_t* tt, const uint8_t* tsf, int H, int T, int k, const int32_t* inv,
+                                uint8_t* xt, uint8_t* xsf, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (H % 32 || reinterpret_cast<uintptr_t>(tt) % 16 || reinterpret_cast<uintptr_t>(xt) % 16) return cudaErrorInvalidValue;
+  terms_gather_kernel<<<T * k, 256, 0, st>>>(tt, tsf, H, k, inv, xt, xsf);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------- host side
 bool make_tmap_sw128(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows);
 bool make_tmap_rows(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,

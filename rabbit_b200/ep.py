@@ -6,8 +6,10 @@ One forward on every rank, with no host synchronisation (every size is fixed by 
 count is read back to the host, and every step is queued on the device):
 
 1. route the rank's own tokens with the replicated router (bit-exact, the one-GPU kernels);
-2. start the exchange of every rank's token rows and their routing: ``all_gather`` of x [T, H]
-   and of the routing row [T, 2k] (ids, and the weights' bits), asynchronously;
+2. start the exchange of every rank's token rows and their routing: ``all_gather`` of each row's
+   payload -- its activation terms on the MXFP4 tensor-core path (17 bytes per 32 columns, formed
+   once by the row's owner), else x [T, H] -- and of the routing row [T, 2k] (ids, and the
+   weights' bits), asynchronously;
 3. meanwhile compute the gated shared expert of the rank's own tokens (it needs no routing);
 4. run all N*T gathered rows through the local experts (``forward_routed``: rabbit's
    ``apply_single_expert`` loop, src/glm52/moe.rs:463-513): each row sums its slots whose expert
@@ -21,8 +23,9 @@ count is read back to the host, and every step is queued on the device):
 
 The exchanges are collectives the reference has no counterpart for (it runs on one host). The
 compute side is any object with ``route(x)``, ``forward_routed(x, ids, weights, with_shared, out)``,
-``sum_rank_parts(parts, last)`` and ``hidden``/``topk``/``n_experts`` attributes: the device layer
-(``MoeLayer``) on GPUs, or a CPU stand-in for the host-side tests.
+``sum_rank_parts(parts, last)`` and ``hidden``/``topk``/``n_experts`` attributes, optionally
+``row_payload(x)`` and ``forward_routed_payload(rows, ids, weights)`` for a cheaper row payload:
+the device layer (``MoeLayer``) on GPUs, or a CPU stand-in for the host-side tests.
 """
 from __future__ import annotations
 
@@ -61,18 +64,26 @@ class ExpertParallelMoe:
             self.last_exchange_bytes = 0
             return lay.forward_routed(x, ids, w, with_shared=True), ids, w
         meta = torch.cat([ids, w.view(torch.int32)], dim=1)     # [T, 2k] int32
-        x_all, wx = self._all_gather(x)
+        # what a row travels as: its activation terms where the layer has them (formed once, by
+        # the row's owner), else x
+        payload = lay.row_payload(x) if hasattr(lay, "row_payload") else (x,)
+        gathered = [self._all_gather(p) for p in payload]
         meta_all, wm = self._all_gather(meta)
         # the shared expert of the own tokens overlaps the exchange (it needs no routing)
         shared = lay.forward_routed(x, torch.full_like(ids, -1), torch.zeros_like(w), with_shared=True)
-        for work in (wx, wm):
+        for work in [g[1] for g in gathered] + [wm]:
             if work is not None:
                 work.wait()
         ids_all = meta_all[:, :k].contiguous()
         w_all = meta_all[:, k:].contiguous().view(torch.float32)
-        y = lay.forward_routed(x_all, ids_all, w_all, with_shared=False)   # [N*T, H] partial sums
+        rows = tuple(g[0] for g in gathered)
+        if hasattr(lay, "forward_routed_payload"):
+            y = lay.forward_routed_payload(rows, ids_all, w_all)             # [N*T, H] partial sums
+        else:
+            y = lay.forward_routed(rows[0], ids_all, w_all, with_shared=False)
         parts = torch.empty_like(y)
         dist.all_to_all_single(parts, y, group=self.group)      # block r: rank r's sums of my rows
-        self.last_exchange_bytes = (N - 1) * T * (H * x.element_size() + 2 * k * 4 + H * 4)
+        row_bytes = sum(q.numel() * q.element_size() for q in payload) // max(T, 1)
+        self.last_exchange_bytes = (N - 1) * T * (row_bytes + 2 * k * 4 + H * 4)
         out = lay.sum_rank_parts(parts.view(N, T, H), last=shared)
         return out, ids, w

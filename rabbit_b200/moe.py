@@ -269,6 +269,38 @@ class MoeLayer:
                                                1 if with_shared else 0, _ptr(out), _stream(stream)))
         return out
 
+    def row_payload(self, x, stream=None):
+        """What expert parallelism sends for rows x [T, H]: on the MXFP4 tensor-core path their
+        activation terms (rmoe_activation_terms: uint8 [T, 4 * H/2] and [T, 4 * H/32], 17 bytes per
+        32 columns), else x itself."""
+        _require_cuda(x)
+        if getattr(self, "_terms_ok", True):
+            T, H = x.shape[0], self.hidden
+            terms = torch.empty((T, 2 * H), dtype=torch.uint8, device=x.device)
+            scales = torch.empty((T, H // 8), dtype=torch.uint8, device=x.device)
+            st = self.lib.rmoe_activation_terms(self.handle, _ptr(x), _dtype_code(x), T, _ptr(terms), _ptr(scales),
+                                                _stream(stream))
+            if st == _lib.RMOE_NOT_SUPPORTED:
+                self._terms_ok = False
+            else:
+                check(st)
+                return (terms, scales)
+        return (x,)
+
+    def forward_routed_payload(self, payload, ids, weights, out=None, stream=None):
+        """forward_routed without the shared expert on rows given as row_payload() returned them
+        (gathered from every rank): the same outputs bit for bit."""
+        if len(payload) == 1:
+            return self.forward_routed(payload[0], ids, weights, with_shared=False, out=out, stream=stream)
+        terms, scales = payload
+        _require_cuda(terms, scales, ids, weights)
+        T = terms.shape[0]
+        if out is None:
+            out = torch.empty((T, self.hidden), dtype=torch.float32, device=terms.device)
+        check(self.lib.rmoe_moe_forward_routed_terms(self.handle, _ptr(terms.contiguous()), _ptr(scales.contiguous()), T,
+                                                     _ptr(ids), _ptr(weights), _ptr(out), _stream(stream)))
+        return out
+
     def sum_rank_parts(self, parts, last=None, out=None, stream=None):
         """parts [N, T, H] f32 -> out [T, H] = parts[0] + ... + parts[N-1] (+ last), in rank
         order (rmoe_sum_rank_parts): expert parallelism's owner-side combine."""

@@ -36,7 +36,7 @@ def test_abi_version_and_status_strings():
     from rabbit_b200 import _lib
 
     lib = _lib.load()
-    assert lib.rmoe_abi_version() == 3
+    assert lib.rmoe_abi_version() == 4
     assert lib.rmoe_status_string(2) == b"shape mismatch"
 
 

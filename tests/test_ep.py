@@ -52,6 +52,13 @@ class OracleLayer:
             w[t] = [v for _, v in r]
         return torch.from_numpy(ids), torch.from_numpy(w)
 
+    def row_payload(self, x):
+        """(the payload protocol: this stand-in sends x itself, as one tensor)"""
+        return (x,)
+
+    def forward_routed_payload(self, rows, ids, w, out=None):
+        return self.forward_routed(rows[0], ids, w, with_shared=False, out=out)
+
     def forward_routed(self, x, ids, w, with_shared=True, out=None):
         dst = out
         xn = x.numpy().astype(np.float32)
@@ -168,6 +175,31 @@ def test_ep_halves_on_one_gpu(cuda_ctx):
         L.close()
     got = parts[0] + parts[1] + shared
     assert rel_l2(got.cpu().numpy(), full.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 7, 40])
+def test_forward_routed_terms_is_forward_routed(cuda_ctx, T):
+    """The payload path of expert parallelism: rows sent as their activation terms
+    (rmoe_activation_terms, formed once by their owner) run through the expert loop to the same
+    bits as forward_routed on x without the shared expert -- on a full layer and on one EP half."""
+    import torch
+
+    cfg = _mid_cfg()
+    x = synth.x_device(cfg, synth.activations(cfg, tokens=T))
+    for ep in ((0, 1), (1, 2)):
+        L = synth.build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens, ep_rank=ep[0], ep_size=ep[1])
+        full_layer = L if ep[1] == 1 else synth.build_layer(cuda_ctx, cfg, max_tokens=cfg.tokens)
+        _, ids, w = full_layer.moe_forward(x, return_routing=True)
+        want = L.forward_routed(x, ids, w, with_shared=False)
+        payload = L.row_payload(x)
+        assert len(payload) == 2 and payload[0].dtype == torch.uint8
+        assert payload[0].shape == (T, 2 * cfg.hidden) and payload[1].shape == (T, cfg.hidden // 8)
+        got = L.forward_routed_payload(payload, ids, w)
+        assert torch.equal(got, want)
+        if full_layer is not L:
+            full_layer.close()
+        L.close()
 
 
 def _nccl_rank(rank, world, port, results):
