@@ -84,13 +84,27 @@ class OracleLayer:
         return out + last if last is not None else out
 
 
+class SplitPayloadLayer(OracleLayer):
+    """The same layer sending each row as two tensors (its two column halves, one of them as raw
+    bytes), like the device layer's terms and scales: the exchange gathers every tensor of the
+    payload and the receiver reassembles the rows."""
+
+    def row_payload(self, x):
+        h = self.hidden // 2
+        return (x[:, :h].contiguous(), x[:, h:].contiguous().view(torch.uint8))
+
+    def forward_routed_payload(self, rows, ids, w, out=None):
+        x = torch.cat([rows[0], rows[1].view(torch.float32)], dim=1)
+        return self.forward_routed(x, ids, w, with_shared=False, out=out)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, cfg_name, t_local, results):
+def _run(rank, world, port, cfg_name, t_local, results, split=False):
     from rabbit_b200.ep import ExpertParallelMoe
 
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
@@ -98,18 +112,18 @@ def _run(rank, world, port, cfg_name, t_local, results):
     cfg = synth.CONFIGS[cfg_name]
     x = synth.activations(cfg, tokens=world * t_local)
     mine = torch.from_numpy(x[rank * t_local:(rank + 1) * t_local].copy())
-    ep = ExpertParallelMoe(OracleLayer(cfg, rank, world))
+    ep = ExpertParallelMoe((SplitPayloadLayer if split else OracleLayer)(cfg, rank, world))
     out, ids, w = ep.forward(mine)
     results[rank] = (out.numpy(), ids.numpy())
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,t_local", [(2, 3), (4, 2)])
-def test_expert_parallel_matches_one_process(world, t_local):
+@pytest.mark.parametrize("world,t_local,split", [(2, 3, False), (4, 2, False), (2, 3, True)])
+def test_expert_parallel_matches_one_process(world, t_local, split):
     cfg = synth.CONFIGS["c0_tiny"]
     mgr = mp.Manager()
     results = mgr.dict()
-    mp.spawn(_run, args=(world, _free_port(), "c0_tiny", t_local, results), nprocs=world, join=True)
+    mp.spawn(_run, args=(world, _free_port(), "c0_tiny", t_local, results, split), nprocs=world, join=True)
     x = synth.activations(cfg, tokens=world * t_local)
     want, want_ids, _ = oracle_forward(cfg, x)
     got = np.concatenate([results[r][0] for r in range(world)])
