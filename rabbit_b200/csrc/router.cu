@@ -449,7 +449,10 @@ cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w
     kern<<<T * ((E + 7) / 8), 256, warp_smem, st>>>(x, w, logits, T, H, E);
     return cudaGetLastError();
   }
-  if (T >= 64) {
+  // 64 x 64 tiles when they fill the GPU; otherwise (fewer experts or tokens, e.g. 512 x 256)
+  // one chain per thread, so every SM gets blocks
+  const long long tiles = static_cast<long long>((E + 63) / 64) * ((T + 63) / 64);
+  if (T >= 64 && tiles >= device_sm_count()) {
     dim3 grid((E + 63) / 64, (T + 63) / 64);
     router_exact_tiled_kernel<<<grid, 256, 0, st>>>(x, x_dtype, w, w_dtype, logits, T, H, E);
   } else if (T == 1) {
