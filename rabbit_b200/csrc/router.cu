@@ -449,10 +449,17 @@ cudaError_t launch_router_logits_exact(const void* x, int x_dtype, const void* w
     kern<<<T * ((E + 7) / 8), 256, warp_smem, st>>>(x, w, logits, T, H, E);
     return cudaGetLastError();
   }
-  // 64 x 64 tiles when they fill the GPU; otherwise (fewer experts or tokens, e.g. 512 x 256)
-  // one chain per thread, so every SM gets blocks
+  // 64 x 64 tiles, or one chain per thread when that is faster: a tile block alone on an SM takes
+  // ~0.72 ms per 8192 columns (measured: the 512 x 256 GLM router, 32 blocks, 0.54 ms at 6144),
+  // a wave of them no longer; the one-chain kernel sustains ~2.5e9 chain steps per ms over the
+  // GPU (the same router, 0.32 ms). So the 512 x 256 GLM router takes one chain per thread,
+  // while 2048 x 512 (0.99 against 2.4 ms measured) and an expert-parallel rank's 512-1024 x 512
+  // keep the tiles.
+  const int sms = device_sm_count();
   const long long tiles = static_cast<long long>((E + 63) / 64) * ((T + 63) / 64);
-  if (T >= 64 && tiles >= device_sm_count()) {
+  const double t_tiled = static_cast<double>(H) / 8192.0 * 0.72 * static_cast<double>((tiles + sms - 1) / sms);
+  const double t_chain = static_cast<double>(T) * E * H / 2.5e9;
+  if (T >= 64 && t_tiled <= t_chain) {
     dim3 grid((E + 63) / 64, (T + 63) / 64);
     router_exact_tiled_kernel<<<grid, 256, 0, st>>>(x, x_dtype, w, w_dtype, logits, T, H, E);
   } else if (T == 1) {

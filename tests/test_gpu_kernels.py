@@ -129,7 +129,8 @@ def test_matmul_i4_grouped_matches_oracle(cuda_ctx, s, i, o, gs, scale_dtype):
 @pytest.mark.parametrize("s,i,o,dt", [(1, 8192, 512, "bf16"), (4, 256, 16, "f32"),
                                       (70, 512, 96, "bf16"), (130, 1000, 33, "f32"),
                                       (200, 2048, 130, "f32"), (96, 1024, 200, "mixed"),
-                                      (2, 7168, 896, "bf16"), (3, 2048, 70, "mixed"), (1, 4096, 33, "f32")])
+                                      (2, 7168, 896, "bf16"), (3, 2048, 70, "mixed"), (1, 4096, 33, "f32"),
+                                      (2048, 1024, 512, "mixed")])
 def test_router_matmul_is_bit_exact(cuda_ctx, s, i, o, dt):
     """kernels::matmul: every element must equal the reference's sequential f32 chain."""
     import torch
